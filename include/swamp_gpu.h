@@ -1,0 +1,152 @@
+/*
+ * swamp_gpu.h -- C ABI of libswamp_gpu.so, the B200 (sm_100a) drop-in for
+ * llamanyon.rs's quantized-linear hot path.
+ *
+ * It replaces, for GGUF Q4_0 (dtype 2) and Q4_K (dtype 12) tensors:
+ *   swamp-engine/src/linear.rs:14-90    forward_linear        -> sg_linear (batch 1)
+ *   swamp-engine/src/linear.rs:96-170   forward_linear_multi  -> sg_linear_multi
+ *   swamp-engine/src/linear.rs:176-239  forward_linear_batch  -> sg_linear (batch B)
+ *   swamp-engine/src/linear.rs:278-333  forward_gemvs         -> sg_linear_multi / sg_linear
+ *   swamp-kernels/src/fused_gemv_q4k.rs:59-82,527-554         -> sg_linear
+ *   swamp-kernels/src/fused_gemv_q4k.rs:799-823 swamp_fused_gemv_q4k -> sg_fused_gemv_q4k
+ *   swamp-gguf/src/quant/{q4_0.rs:11-38,q4_k.rs:21-33} dequant -> sg_dequant_f32
+ * and the swamp-gpu crate's loader/handle conventions
+ * (swamp-gpu/src/lib.rs:16-71: dlopen of libswamp_gpu.so, int status codes,
+ * opaque void* handles, host- and device-pointer entry points).
+ *
+ * Conventions
+ *  - Every entry returns an int status: SG_OK (0) or a negative SG_ERR_*;
+ *    sg_last_error() returns a message for the calling thread. Arguments are
+ *    validated on the host before anything is launched.
+ *  - Weights are uploaded once (sg_weight_register) and stay resident on the
+ *    GPU(s) until sg_weight_free; callers key the handle on the GGUF
+ *    TensorInfo.offset as the reference re-reads the mmap on every call
+ *    (swamp-engine/src/linear.rs:24).
+ *  - Output semantics are overwrite (forward_linear*, swamp_fused_gemv_q4k
+ *    zero-fill then accumulate, linear.rs:107,204-207, fused_gemv_q4k.rs:820)
+ *    unless SG_FLAG_ACCUMULATE asks for the batched kernel's out += W x
+ *    (fused_gemv_q4k.rs:696).
+ *  - Numerics: dequantized weights are bit-identical to swamp-gguf's. GEMV /
+ *    GEMM outputs accumulate in f32 with activations split into two 16-bit
+ *    parts; the tested bound is |y - y_ref| <= 1e-3 * max(|y_ref|, ||w.*x||_2)
+ *    per element against the reference's f32 result.
+ *  - Thread safety: calls are serialised on an internal mutex per library
+ *    instance; each device has one stream. Calls may come from any host
+ *    thread (the reference calls from rayon workers, linear.rs:35).
+ *  - There is no CPU fallback: without a usable sm_100 GPU, sg_init fails.
+ */
+#ifndef SWAMP_GPU_H
+#define SWAMP_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SG_API __attribute__((visibility("default")))
+#else
+#define SG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes (swamp-gpu/src/lib.rs:16-26 maps non-zero to GpuError) */
+#define SG_OK 0
+#define SG_ERR_INVALID_ARG (-1)
+#define SG_ERR_CUDA (-2)
+#define SG_ERR_NCCL (-3)
+#define SG_ERR_OOM (-4)
+#define SG_ERR_UNSUPPORTED (-5)
+#define SG_ERR_NOT_INITIALIZED (-6)
+#define SG_ERR_DEVICE_FAULT (-7) /* a kernel's bounded wait gave up; see sg_last_error */
+
+/* GgmlDType ids (swamp-gguf/src/dtype.rs:13,21) */
+#define SG_DTYPE_Q4_0 2
+#define SG_DTYPE_Q4_K 12
+
+/* tensor-parallel placement of a registered weight */
+#define SG_TP_REPLICATE 0 /* every rank holds the whole tensor */
+#define SG_TP_COLUMN 1    /* split N (output rows): Q/K/V/gate/up; outputs stay local */
+#define SG_TP_ROW 2       /* split K (reduction): O/down; outputs all-reduced (sum) */
+
+/* flags */
+#define SG_FLAG_DEVICE_PTRS 0x1 /* x/out pointers are device memory on this rank's device */
+#define SG_FLAG_ACCUMULATE 0x2  /* out += W x instead of out = W x */
+
+typedef struct sg_weight_s *sg_weight_t;
+
+/* ------------------------------------------------------------------ setup */
+
+/* Single-process mode (the reference engine is one process, one host thread,
+ * swamp-engine/src/executor.rs:292): use devices 0..n_gpus-1; for n_gpus > 1
+ * build an NCCL communicator over them (ncclCommInitAll). */
+SG_API int sg_init(int n_gpus);
+
+/* One-process-per-GPU mode: this process is `rank` of `world`, drives CUDA
+ * device `device`, and joins the NCCL communicator identified by the 128-byte
+ * id that rank 0 produced with sg_get_unique_id (shipped to the other ranks by
+ * the caller, e.g. over torch.distributed). */
+SG_API int sg_get_unique_id(void *id128);
+SG_API int sg_init_rank(int rank, int world, const void *id128, int device);
+
+SG_API int sg_shutdown(void);
+SG_API const char *sg_last_error(void);
+/* rank / world size / number of devices driven by this process */
+SG_API int sg_topology(int *rank, int *world, int *local_devices);
+
+/* ---------------------------------------------------------------- weights */
+
+/* Upload one GGUF tensor (host pointer to its raw block bytes, row-major:
+ * n_rows rows of n_cols/32*18 (Q4_0) or n_cols/256*144 (Q4_K) bytes) and
+ * repack it into the device tile layout. n_cols % 32 == 0 (Q4_0) or
+ * % 256 == 0 (Q4_K). tp_mode splits across the process's ranks/devices on
+ * whole blocks (SG_TP_ROW needs n_cols/world to stay a block multiple). */
+SG_API int sg_weight_register(const void *host_blocks, int dtype, int64_t n_rows, int64_t n_cols,
+                       int tp_mode, sg_weight_t *out);
+SG_API int sg_weight_free(sg_weight_t w);
+/* shape of the shard this rank holds: local rows/cols and their offsets */
+SG_API int sg_weight_shard(sg_weight_t w, int local_device, int64_t *n_rows, int64_t *n_cols,
+                    int64_t *row0, int64_t *col0);
+
+/* -------------------------------------------------------------- compute */
+
+/* forward_linear / forward_linear_batch: outs[b][r] = sum_k W[r][k] xs[b][k]
+ * for b < batch. Host pointers (default): xs[b] has n_cols floats, outs[b]
+ * n_rows floats (the whole tensor, whatever the TP split). With
+ * SG_FLAG_DEVICE_PTRS (single-device or rank mode only) xs/outs point at
+ * this rank's device and hold this rank's shard: x of n_cols_local, out of
+ * n_rows_local (column split) or n_rows (replicate / row split, all-reduced).
+ * Batches of 1..16 run the decode GEMV; larger batches the prefill GEMM. */
+SG_API int sg_linear(sg_weight_t w, const float *const *xs, float *const *outs, int batch, int flags);
+
+/* forward_linear_multi (linear.rs:96-170): several tensors, same x (K). */
+SG_API int sg_linear_multi(const sg_weight_t *ws, int n_weights, const float *x, float *const *outs,
+                    int flags);
+
+/* Device-resident, stream-ordered form for engines that keep activations on
+ * the GPU: x is [batch][ldx] (this rank's K-slice starts at x), y is
+ * [batch][ldy]. stream may be NULL (the library's stream for this device).
+ * Returns once the work is enqueued. */
+SG_API int sg_linear_device(sg_weight_t w, const float *x, int64_t ldx, float *y, int64_t ldy, int batch,
+                     void *stream, int flags);
+SG_API int sg_linear_multi_device(const sg_weight_t *ws, int n_weights, const float *x, int64_t ldx,
+                           float *const *ys, const int64_t *ldys, int batch, void *stream, int flags);
+
+/* Dequantize the whole tensor to f32 [n_rows][n_cols] (host pointer, or this
+ * rank's shard into device memory with SG_FLAG_DEVICE_PTRS). Bit-exact with
+ * swamp-gguf's dequant. */
+SG_API int sg_dequant_f32(sg_weight_t w, float *dst, int flags);
+
+/* swamp_fused_gemv_q4k (fused_gemv_q4k.rs:799-823): raw Q4_K host bytes on
+ * every call, x of n_cols, out of n_rows (overwritten). Unlike the Rust
+ * symbol it reports errors instead of silently returning. */
+SG_API int sg_fused_gemv_q4k(const uint8_t *w_raw, const float *x, float *out, int n_rows, int n_cols);
+
+/* Wait for this process's devices and surface any device-side error flag. */
+SG_API int sg_synchronize(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SWAMP_GPU_H */

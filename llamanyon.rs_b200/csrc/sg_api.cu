@@ -1,0 +1,705 @@
+// sg_api.cu -- the C ABI of libswamp_gpu.so (declared in include/swamp_gpu.h).
+//
+// Host-side mirror of swamp-engine's linear dispatch (swamp-engine/src/linear.rs)
+// for Q4_0/Q4_K, routed to the B200 kernels with no CPU fallback. Weight
+// handles own device shards; tensor parallelism splits rows (SG_TP_COLUMN) or
+// K (SG_TP_ROW, followed by an NCCL sum all-reduce over NVLink). NCCL is
+// loaded lazily with dlopen("libnccl.so.2") only when more than one rank
+// exists, so the single-GPU library has no NCCL dependency and shares the
+// process's NCCL (e.g. torch's) when one is already loaded.
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/swamp_gpu.h"
+#include "sg_gemm.cuh"
+#include "sg_gemv.cuh"
+
+// ---------------------------------------------------------------- NCCL shim
+namespace {
+typedef struct ncclComm* ncclComm_t;
+typedef struct {
+  char internal[128];
+} ncclUniqueId;
+typedef int ncclResult_t;
+enum { kNcclFloat = 7, kNcclSum = 0 };
+
+struct NcclApi {
+  void* h = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommInitAll)(ncclComm_t*, int, const int*) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+  bool load(std::string& err) {
+    if (h) return true;
+    h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      err = "cannot dlopen libnccl.so.2";
+      return false;
+    }
+#define SG_SYM(f, name)                                 \
+  f = reinterpret_cast<decltype(f)>(dlsym(h, name));    \
+  if (!f) {                                             \
+    err = std::string("libnccl missing symbol ") + name; \
+    return false;                                       \
+  }
+    SG_SYM(GetUniqueId, "ncclGetUniqueId");
+    SG_SYM(CommInitRank, "ncclCommInitRank");
+    SG_SYM(CommInitAll, "ncclCommInitAll");
+    SG_SYM(AllReduce, "ncclAllReduce");
+    SG_SYM(GroupStart, "ncclGroupStart");
+    SG_SYM(GroupEnd, "ncclGroupEnd");
+    SG_SYM(CommDestroy, "ncclCommDestroy");
+    SG_SYM(GetErrorString, "ncclGetErrorString");
+#undef SG_SYM
+    return true;
+  }
+};
+NcclApi g_nccl;
+
+// ------------------------------------------------------------------ state
+struct DevState {
+  int device = -1;
+  int num_sms = 0;
+  cudaStream_t stream = nullptr;
+  ncclComm_t comm = nullptr;
+  void* scratch = nullptr;  // GEMV/GEMM scratch
+  size_t scratch_bytes = 0;
+  float* xbuf = nullptr;  // staging for host-pointer calls
+  size_t xbuf_bytes = 0;
+  float* ybuf = nullptr;
+  size_t ybuf_bytes = 0;
+  float* hbuf = nullptr;  // pinned host staging
+  size_t hbuf_bytes = 0;
+};
+
+struct Ctx {
+  std::mutex mu;
+  bool inited = false;
+  int rank_base = 0;  // global rank of devs[0]
+  int world = 1;
+  std::vector<DevState> devs;
+};
+Ctx g_ctx;
+
+thread_local std::string t_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+#define CUDA_TRY(expr)                                                                          \
+  do {                                                                                          \
+    cudaError_t _e = (expr);                                                                    \
+    if (_e != cudaSuccess) return fail(SG_ERR_CUDA, "%s: %s (%s:%d)", #expr, cudaGetErrorString(_e), \
+                                       __FILE__, __LINE__);                                     \
+  } while (0)
+
+}  // namespace
+
+struct Shard {
+  int dev_idx = 0;
+  int64_t row0 = 0, col0 = 0;
+  SgDevWeight w = {};
+};
+
+struct sg_weight_s {
+  int dtype = 0;
+  int64_t n_rows = 0, n_cols = 0;
+  int tp_mode = SG_TP_REPLICATE;
+  std::vector<Shard> shards;  // one per local device
+};
+
+namespace {
+
+int64_t block_of(int dtype) { return dtype == SG_DTYPE_Q4_0 ? 32 : 256; }
+int64_t block_bytes(int dtype) { return dtype == SG_DTYPE_Q4_0 ? 18 : 144; }
+
+int ensure_buf(void** p, size_t* have, size_t need) {
+  if (*have >= need) return SG_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *have = 0;
+  size_t sz = std::max(need, (size_t)1 << 20);
+  if (cudaMalloc(p, sz) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SG_ERR_OOM, "cudaMalloc(%zu) failed", sz);
+  }
+  *have = sz;
+  return SG_OK;
+}
+
+int ensure_host(DevState& d, size_t need) {
+  if (d.hbuf_bytes >= need) return SG_OK;
+  if (d.hbuf) cudaFreeHost(d.hbuf);
+  d.hbuf = nullptr;
+  d.hbuf_bytes = 0;
+  size_t sz = std::max(need, (size_t)1 << 20);
+  if (cudaMallocHost((void**)&d.hbuf, sz) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SG_ERR_OOM, "cudaMallocHost(%zu) failed", sz);
+  }
+  d.hbuf_bytes = sz;
+  return SG_OK;
+}
+
+int check_device_error(DevState& d) {
+  int v = 0;
+  CUDA_TRY(cudaSetDevice(d.device));
+  CUDA_TRY(cudaMemcpyFromSymbol(&v, g_sg_error, sizeof(int)));
+  if (v != 0) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_sg_error, &z, sizeof(int));
+    return fail(SG_ERR_DEVICE_FAULT, "device %d: kernel wait gave up (code 0x%x)", d.device, v);
+  }
+  return SG_OK;
+}
+
+int init_devices(const std::vector<int>& devices, int rank_base, int world) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return fail(SG_ERR_UNSUPPORTED, "no CUDA device (this library has no CPU fallback)");
+  }
+  g_ctx.devs.clear();
+  for (int dev : devices) {
+    if (dev < 0 || dev >= n) return fail(SG_ERR_INVALID_ARG, "device %d out of range (%d devices)", dev, n);
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+    if (prop.major != 10)
+      return fail(SG_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a (B200)", dev, prop.major,
+                  prop.minor);
+    DevState d;
+    d.device = dev;
+    d.num_sms = prop.multiProcessorCount;
+    CUDA_TRY(cudaSetDevice(dev));
+    CUDA_TRY(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
+    g_ctx.devs.push_back(d);
+  }
+  g_ctx.rank_base = rank_base;
+  g_ctx.world = world;
+  return SG_OK;
+}
+
+void release_devices() {
+  for (auto& d : g_ctx.devs) {
+    cudaSetDevice(d.device);
+    if (d.comm && g_nccl.CommDestroy) g_nccl.CommDestroy(d.comm);
+    if (d.scratch) cudaFree(d.scratch);
+    if (d.xbuf) cudaFree(d.xbuf);
+    if (d.ybuf) cudaFree(d.ybuf);
+    if (d.hbuf) cudaFreeHost(d.hbuf);
+    if (d.stream) cudaStreamDestroy(d.stream);
+  }
+  g_ctx.devs.clear();
+  g_ctx.inited = false;
+}
+
+// ---------------------------------------------------------- the core launch
+// y[b][*] (ldy) = W_shard x[b][*] (ldx) on one device, stream-ordered.
+int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* x, int64_t ldx,
+               float* const* ys, const int64_t* ldys, int batch, cudaStream_t st, bool accumulate) {
+  const int64_t K = ws[0]->n_cols;
+  if (batch <= 16) {
+    int rc = ensure_buf(&d.scratch, &d.scratch_bytes, sg_gemv_scratch_bytes(K));
+    if (rc) return rc;
+    SgGemvMat mats[SG_GEMV_MAX_MATS];
+    for (int i = 0; i < n_w; ++i) mats[i] = {ws[i], ys[i], ldys[i]};
+    CUDA_TRY(sg_gemv(mats, n_w, x, ldx, batch, accumulate, d.scratch, d.scratch_bytes, d.num_sms, st));
+    return SG_OK;
+  }
+  // prefill GEMM (or accumulate): one launch per matrix
+  for (int i = 0; i < n_w; ++i) {
+    const size_t need = sg_gemm_scratch_bytes(batch, K);
+    int rc = ensure_buf(&d.scratch, &d.scratch_bytes, need);
+    if (rc) return rc;
+    CUDA_TRY(sg_gemm(ws[i], x, ldx, ys[i], ldys[i], batch, accumulate, d.scratch, d.scratch_bytes, d.num_sms, st));
+  }
+  return SG_OK;
+}
+
+int allreduce_local(const std::vector<float*>& bufs, size_t count) {
+  if (g_ctx.world <= 1) return SG_OK;
+  if (!g_nccl.AllReduce) return fail(SG_ERR_NCCL, "NCCL not initialised");
+  ncclResult_t r = g_nccl.GroupStart();
+  for (size_t i = 0; i < g_ctx.devs.size() && r == 0; ++i) {
+    DevState& d = g_ctx.devs[i];
+    cudaSetDevice(d.device);
+    r = g_nccl.AllReduce(bufs[i], bufs[i], count, kNcclFloat, kNcclSum, d.comm, d.stream);
+  }
+  ncclResult_t r2 = g_nccl.GroupEnd();
+  if (r || r2) return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r ? r : r2));
+  return SG_OK;
+}
+
+int validate_weight(sg_weight_t w) {
+  if (!g_ctx.inited) return fail(SG_ERR_NOT_INITIALIZED, "sg_init not called");
+  if (!w) return fail(SG_ERR_INVALID_ARG, "null weight handle");
+  if (w->shards.size() != g_ctx.devs.size()) return fail(SG_ERR_INVALID_ARG, "weight registered under another init");
+  return SG_OK;
+}
+
+// host-pointer linear over all local devices (also the multi form)
+int linear_host(const sg_weight_t* ws, int n_w, const float* const* xs, float* const* outs, int batch, int flags) {
+  const int64_t K = ws[0]->n_cols;
+  const int tp = ws[0]->tp_mode;
+  for (int i = 0; i < n_w; ++i) {
+    int rc = validate_weight(ws[i]);
+    if (rc) return rc;
+    if (ws[i]->n_cols != K || ws[i]->dtype != ws[0]->dtype)
+      return fail(SG_ERR_INVALID_ARG, "multi: tensors must share dtype and n_cols");
+    if (ws[i]->tp_mode != tp) return fail(SG_ERR_INVALID_ARG, "multi: tensors must share tp_mode");
+  }
+  if (n_w > SG_GEMV_MAX_MATS) return fail(SG_ERR_INVALID_ARG, "at most %d tensors per multi call", SG_GEMV_MAX_MATS);
+  const bool accumulate = (flags & SG_FLAG_ACCUMULATE) != 0;
+  const size_t nd = g_ctx.devs.size();
+  std::vector<std::vector<float*>> ydev(nd, std::vector<float*>(n_w));
+  std::vector<std::vector<int64_t>> ld(nd, std::vector<int64_t>(n_w));
+  // 1. stage inputs and launch on every local device
+  for (size_t di = 0; di < nd; ++di) {
+    DevState& d = g_ctx.devs[di];
+    const Shard& s0 = ws[0]->shards[di];
+    const int64_t kl = s0.w.n_cols, c0 = s0.col0;
+    CUDA_TRY(cudaSetDevice(d.device));
+    int64_t ytot = 0;
+    for (int i = 0; i < n_w; ++i) ytot += (int64_t)batch * (tp == SG_TP_ROW ? ws[i]->n_rows : ws[i]->shards[di].w.n_rows);
+    int rc = ensure_buf((void**)&d.xbuf, &d.xbuf_bytes, (size_t)batch * kl * sizeof(float));
+    if (rc) return rc;
+    rc = ensure_buf((void**)&d.ybuf, &d.ybuf_bytes, (size_t)ytot * sizeof(float));
+    if (rc) return rc;
+    const size_t hx = (size_t)batch * kl * sizeof(float);
+    rc = ensure_host(d, std::max(hx, (size_t)ytot * sizeof(float)));
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(d.stream));  // pinned staging reuse
+    for (int b = 0; b < batch; ++b) memcpy(d.hbuf + (size_t)b * kl, xs[b] + c0, (size_t)kl * sizeof(float));
+    CUDA_TRY(cudaMemcpyAsync(d.xbuf, d.hbuf, hx, cudaMemcpyHostToDevice, d.stream));
+    int64_t off = 0;
+    const SgDevWeight* sw[SG_GEMV_MAX_MATS];
+    for (int i = 0; i < n_w; ++i) {
+      sw[i] = &ws[i]->shards[di].w;
+      ydev[di][i] = d.ybuf + off;
+      ld[di][i] = tp == SG_TP_ROW ? ws[i]->n_rows : sw[i]->n_rows;
+      off += (int64_t)batch * ld[di][i];
+    }
+    rc = run_linear(d, sw, n_w, d.xbuf, kl, ydev[di].data(), ld[di].data(), batch, d.stream, false);
+    if (rc) return rc;
+  }
+  // 2. row split: sum partial outputs across ranks
+  if (tp == SG_TP_ROW && g_ctx.world > 1) {
+    std::vector<float*> bufs(nd);
+    size_t count = 0;
+    for (int i = 0; i < n_w; ++i) count += (size_t)batch * ws[i]->n_rows;
+    for (size_t di = 0; di < nd; ++di) bufs[di] = g_ctx.devs[di].ybuf;
+    int rc = allreduce_local(bufs, count);
+    if (rc) return rc;
+  }
+  // 3. copy back: column split -> every device its rows; otherwise device 0
+  for (size_t di = 0; di < nd; ++di) {
+    if (tp != SG_TP_COLUMN && di > 0) break;
+    DevState& d = g_ctx.devs[di];
+    CUDA_TRY(cudaSetDevice(d.device));
+    int64_t tot = 0;
+    for (int i = 0; i < n_w; ++i) tot += (int64_t)batch * ld[di][i];
+    CUDA_TRY(cudaMemcpyAsync(d.hbuf, d.ybuf, (size_t)tot * sizeof(float), cudaMemcpyDeviceToHost, d.stream));
+    CUDA_TRY(cudaStreamSynchronize(d.stream));
+    int rc = check_device_error(d);
+    if (rc) return rc;
+    int64_t off = 0;
+    for (int i = 0; i < n_w; ++i) {
+      const Shard& s = ws[i]->shards[di];
+      const int64_t r0 = tp == SG_TP_COLUMN ? s.row0 : 0;
+      const int64_t nr = ld[di][i];
+      for (int b = 0; b < batch; ++b) {
+        float* dst = outs[(size_t)i * batch + b] + r0;
+        const float* src = d.hbuf + off + (size_t)b * nr;
+        if (accumulate)
+          for (int64_t r = 0; r < nr; ++r) dst[r] += src[r];
+        else
+          memcpy(dst, src, (size_t)nr * sizeof(float));
+      }
+      off += (int64_t)batch * nr;
+    }
+  }
+  for (size_t di = 1; di < nd; ++di) {
+    cudaSetDevice(g_ctx.devs[di].device);
+    CUDA_TRY(cudaStreamSynchronize(g_ctx.devs[di].stream));
+    int rc = check_device_error(g_ctx.devs[di]);
+    if (rc) return rc;
+  }
+  return SG_OK;
+}
+
+}  // namespace
+
+// ====================================================================== ABI
+extern "C" {
+
+const char* sg_last_error(void) { return t_err.c_str(); }
+
+int sg_init(int n_gpus) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (g_ctx.inited) return fail(SG_ERR_INVALID_ARG, "already initialised; call sg_shutdown first");
+  if (n_gpus < 1) return fail(SG_ERR_INVALID_ARG, "n_gpus must be >= 1");
+  std::vector<int> devs;
+  for (int i = 0; i < n_gpus; ++i) devs.push_back(i);
+  int rc = init_devices(devs, 0, n_gpus);
+  if (rc) {
+    release_devices();
+    return rc;
+  }
+  if (n_gpus > 1) {
+    std::string err;
+    if (!g_nccl.load(err)) {
+      release_devices();
+      return fail(SG_ERR_NCCL, "%s", err.c_str());
+    }
+    std::vector<ncclComm_t> comms(n_gpus);
+    ncclResult_t r = g_nccl.CommInitAll(comms.data(), n_gpus, devs.data());
+    if (r) {
+      release_devices();
+      return fail(SG_ERR_NCCL, "ncclCommInitAll: %s", g_nccl.GetErrorString(r));
+    }
+    for (int i = 0; i < n_gpus; ++i) g_ctx.devs[i].comm = comms[i];
+  }
+  g_ctx.inited = true;
+  return SG_OK;
+}
+
+int sg_get_unique_id(void* id128) {
+  if (!id128) return fail(SG_ERR_INVALID_ARG, "null id buffer");
+  std::string err;
+  if (!g_nccl.load(err)) return fail(SG_ERR_NCCL, "%s", err.c_str());
+  ncclUniqueId id;
+  ncclResult_t r = g_nccl.GetUniqueId(&id);
+  if (r) return fail(SG_ERR_NCCL, "ncclGetUniqueId: %s", g_nccl.GetErrorString(r));
+  memcpy(id128, &id, sizeof id);
+  return SG_OK;
+}
+
+int sg_init_rank(int rank, int world, const void* id128, int device) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (g_ctx.inited) return fail(SG_ERR_INVALID_ARG, "already initialised; call sg_shutdown first");
+  if (world < 1 || rank < 0 || rank >= world) return fail(SG_ERR_INVALID_ARG, "bad rank %d / world %d", rank, world);
+  if (world > 1 && !id128) return fail(SG_ERR_INVALID_ARG, "world > 1 needs the NCCL unique id");
+  int rc = init_devices({device}, rank, world);
+  if (rc) {
+    release_devices();
+    return rc;
+  }
+  if (world > 1) {
+    std::string err;
+    if (!g_nccl.load(err)) {
+      release_devices();
+      return fail(SG_ERR_NCCL, "%s", err.c_str());
+    }
+    ncclUniqueId id;
+    memcpy(&id, id128, sizeof id);
+    cudaSetDevice(device);
+    ncclResult_t r = g_nccl.CommInitRank(&g_ctx.devs[0].comm, world, id, rank);
+    if (r) {
+      release_devices();
+      return fail(SG_ERR_NCCL, "ncclCommInitRank: %s", g_nccl.GetErrorString(r));
+    }
+  }
+  g_ctx.inited = true;
+  return SG_OK;
+}
+
+int sg_shutdown(void) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  for (auto& d : g_ctx.devs) {
+    cudaSetDevice(d.device);
+    cudaStreamSynchronize(d.stream);
+  }
+  release_devices();
+  return SG_OK;
+}
+
+int sg_topology(int* rank, int* world, int* local_devices) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!g_ctx.inited) return fail(SG_ERR_NOT_INITIALIZED, "sg_init not called");
+  if (rank) *rank = g_ctx.rank_base;
+  if (world) *world = g_ctx.world;
+  if (local_devices) *local_devices = (int)g_ctx.devs.size();
+  return SG_OK;
+}
+
+int sg_weight_register(const void* host_blocks, int dtype, int64_t n_rows, int64_t n_cols, int tp_mode,
+                       sg_weight_t* out) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!g_ctx.inited) return fail(SG_ERR_NOT_INITIALIZED, "sg_init not called");
+  if (!host_blocks || !out) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (dtype != SG_DTYPE_Q4_0 && dtype != SG_DTYPE_Q4_K)
+    return fail(SG_ERR_UNSUPPORTED, "dtype %d not supported (Q4_0=2, Q4_K=12)", dtype);
+  if (n_rows <= 0 || n_cols <= 0) return fail(SG_ERR_INVALID_ARG, "empty tensor %lld x %lld", (long long)n_rows,
+                                              (long long)n_cols);
+  const int64_t bs = block_of(dtype), bb = block_bytes(dtype);
+  if (n_cols % bs) return fail(SG_ERR_INVALID_ARG, "n_cols %lld not a multiple of %lld", (long long)n_cols, (long long)bs);
+  if (tp_mode < SG_TP_REPLICATE || tp_mode > SG_TP_ROW) return fail(SG_ERR_INVALID_ARG, "bad tp_mode %d", tp_mode);
+  const int W = g_ctx.world;
+  const int64_t nblk = n_cols / bs;
+  if (tp_mode == SG_TP_ROW && nblk < W) return fail(SG_ERR_INVALID_ARG, "row split: %lld blocks < %d ranks", (long long)nblk, W);
+  if (tp_mode == SG_TP_COLUMN && n_rows < W) return fail(SG_ERR_INVALID_ARG, "column split: %lld rows < %d ranks", (long long)n_rows, W);
+  const size_t row_bytes = (size_t)nblk * bb;
+  auto* w = new sg_weight_s();
+  w->dtype = dtype;
+  w->n_rows = n_rows;
+  w->n_cols = n_cols;
+  w->tp_mode = tp_mode;
+  int rc = SG_OK;
+  for (size_t di = 0; di < g_ctx.devs.size() && rc == SG_OK; ++di) {
+    DevState& d = g_ctx.devs[di];
+    const int R = g_ctx.rank_base + (int)di;
+    Shard s;
+    s.dev_idx = (int)di;
+    int64_t nr = n_rows, nc = n_cols;
+    if (tp_mode == SG_TP_COLUMN) {
+      s.row0 = (int64_t)R * n_rows / W;
+      nr = (int64_t)(R + 1) * n_rows / W - s.row0;
+    } else if (tp_mode == SG_TP_ROW) {
+      const int64_t b0 = (int64_t)R * nblk / W, b1 = (int64_t)(R + 1) * nblk / W;
+      s.col0 = b0 * bs;
+      nc = (b1 - b0) * bs;
+    }
+    cudaSetDevice(d.device);
+    if (sg_layout_alloc(&s.w, dtype, nr, nc)) {
+      cudaGetLastError();
+      rc = fail(SG_ERR_OOM, "device %d: cannot allocate %zu bytes for weights", d.device,
+                sg_layout_bytes(dtype, nr, nc));
+      break;
+    }
+    const size_t lrow = (size_t)(nc / bs) * bb;
+    uint8_t* raw = nullptr;
+    if (cudaMalloc(&raw, lrow * nr) != cudaSuccess) {
+      cudaGetLastError();
+      sg_layout_free(&s.w);
+      rc = fail(SG_ERR_OOM, "device %d: cannot allocate upload staging", d.device);
+      break;
+    }
+    const uint8_t* src = static_cast<const uint8_t*>(host_blocks) + (size_t)s.row0 * row_bytes +
+                         (size_t)(s.col0 / bs) * bb;
+    cudaError_t e = cudaMemcpy2DAsync(raw, lrow, src, row_bytes, lrow, nr, cudaMemcpyHostToDevice, d.stream);
+    if (e == cudaSuccess) e = sg_layout_repack(&s.w, raw, d.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d.stream);
+    cudaFree(raw);
+    if (e != cudaSuccess) {
+      sg_layout_free(&s.w);
+      rc = fail(SG_ERR_CUDA, "upload/repack on device %d: %s", d.device, cudaGetErrorString(e));
+      break;
+    }
+    w->shards.push_back(s);
+  }
+  if (rc != SG_OK) {
+    for (auto& s : w->shards) {
+      cudaSetDevice(g_ctx.devs[s.dev_idx].device);
+      sg_layout_free(&s.w);
+    }
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return SG_OK;
+}
+
+int sg_weight_free(sg_weight_t w) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!w) return fail(SG_ERR_INVALID_ARG, "null weight handle");
+  for (auto& s : w->shards) {
+    if (s.dev_idx < (int)g_ctx.devs.size()) {
+      cudaSetDevice(g_ctx.devs[s.dev_idx].device);
+      cudaStreamSynchronize(g_ctx.devs[s.dev_idx].stream);
+    }
+    sg_layout_free(&s.w);
+  }
+  delete w;
+  return SG_OK;
+}
+
+int sg_weight_shard(sg_weight_t w, int local_device, int64_t* n_rows, int64_t* n_cols, int64_t* row0, int64_t* col0) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  int rc = validate_weight(w);
+  if (rc) return rc;
+  if (local_device < 0 || local_device >= (int)w->shards.size()) return fail(SG_ERR_INVALID_ARG, "bad local device");
+  const Shard& s = w->shards[local_device];
+  if (n_rows) *n_rows = s.w.n_rows;
+  if (n_cols) *n_cols = s.w.n_cols;
+  if (row0) *row0 = s.row0;
+  if (col0) *col0 = s.col0;
+  return SG_OK;
+}
+
+int sg_linear(sg_weight_t w, const float* const* xs, float* const* outs, int batch, int flags) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  int rc = validate_weight(w);
+  if (rc) return rc;
+  if (batch < 0) return fail(SG_ERR_INVALID_ARG, "negative batch");
+  if (batch == 0) return SG_OK;  // forward_linear_batch with no inputs (linear.rs:184)
+  if (!xs || !outs) return fail(SG_ERR_INVALID_ARG, "null xs/outs");
+  for (int b = 0; b < batch; ++b)
+    if (!xs[b] || !outs[b]) return fail(SG_ERR_INVALID_ARG, "null xs[%d]/outs[%d]", b, b);
+  if (flags & SG_FLAG_DEVICE_PTRS) {
+    if (g_ctx.devs.size() != 1) return fail(SG_ERR_INVALID_ARG, "device pointers need one device per process");
+    // xs/outs are arrays of device pointers; contiguous [batch][K] layout required
+    for (int b = 1; b < batch; ++b)
+      if (xs[b] != xs[0] + (size_t)b * w->shards[0].w.n_cols)
+        return fail(SG_ERR_INVALID_ARG, "device xs must be one contiguous [batch][n_cols] array");
+    DevState& d = g_ctx.devs[0];
+    const SgDevWeight* sw = &w->shards[0].w;
+    const int64_t ldy = w->tp_mode == SG_TP_ROW ? w->n_rows : sw->n_rows;
+    for (int b = 1; b < batch; ++b)
+      if (outs[b] != outs[0] + (size_t)b * ldy)
+        return fail(SG_ERR_INVALID_ARG, "device outs must be one contiguous [batch][rows] array");
+    CUDA_TRY(cudaSetDevice(d.device));
+    float* y0 = outs[0];
+    rc = run_linear(d, &sw, 1, xs[0], sw->n_cols, &y0, &ldy, batch, d.stream, (flags & SG_FLAG_ACCUMULATE) != 0);
+    if (rc) return rc;
+    if (w->tp_mode == SG_TP_ROW && g_ctx.world > 1) {
+      rc = allreduce_local({outs[0]}, (size_t)batch * ldy);
+      if (rc) return rc;
+    }
+    CUDA_TRY(cudaStreamSynchronize(d.stream));
+    return check_device_error(d);
+  }
+  return linear_host(&w, 1, xs, outs, batch, flags);
+}
+
+int sg_linear_multi(const sg_weight_t* ws, int n_weights, const float* x, float* const* outs, int flags) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!ws || !x || !outs || n_weights < 1) return fail(SG_ERR_INVALID_ARG, "bad arguments");
+  if (flags & SG_FLAG_DEVICE_PTRS) return fail(SG_ERR_INVALID_ARG, "use sg_linear_multi_device for device pointers");
+  for (int i = 0; i < n_weights; ++i)
+    if (!outs[i]) return fail(SG_ERR_INVALID_ARG, "null outs[%d]", i);
+  const float* xs[1] = {x};
+  // chunk into groups of SG_GEMV_MAX_MATS tensors sharing x
+  for (int i0 = 0; i0 < n_weights; i0 += SG_GEMV_MAX_MATS) {
+    const int n = std::min(SG_GEMV_MAX_MATS, n_weights - i0);
+    int rc = linear_host(ws + i0, n, xs, outs + i0, 1, flags);
+    if (rc) return rc;
+  }
+  return SG_OK;
+}
+
+int sg_linear_device(sg_weight_t w, const float* x, int64_t ldx, float* y, int64_t ldy, int batch, void* stream,
+                     int flags) {
+  const int64_t ldys[1] = {ldy};
+  return sg_linear_multi_device(&w, 1, x, ldx, &y, ldys, batch, stream, flags);
+}
+
+int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x, int64_t ldx, float* const* ys,
+                           const int64_t* ldys, int batch, void* stream, int flags) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!ws || !x || !ys || !ldys || n_weights < 1 || n_weights > SG_GEMV_MAX_MATS)
+    return fail(SG_ERR_INVALID_ARG, "bad arguments");
+  if (g_ctx.devs.size() != 1) return fail(SG_ERR_INVALID_ARG, "device entry points need one device per process");
+  if (batch < 0) return fail(SG_ERR_INVALID_ARG, "negative batch");
+  if (batch == 0) return SG_OK;
+  const bool acc = (flags & SG_FLAG_ACCUMULATE) != 0;
+  const SgDevWeight* sw[SG_GEMV_MAX_MATS];
+  for (int i = 0; i < n_weights; ++i) {
+    int rc = validate_weight(ws[i]);
+    if (rc) return rc;
+    sw[i] = &ws[i]->shards[0].w;
+    if (sw[i]->n_cols != sw[0]->n_cols || sw[i]->dtype != sw[0]->dtype || ws[i]->tp_mode != ws[0]->tp_mode)
+      return fail(SG_ERR_INVALID_ARG, "multi: tensors must share dtype, n_cols and tp_mode");
+    const int64_t need = ws[i]->tp_mode == SG_TP_ROW ? ws[i]->n_rows : sw[i]->n_rows;
+    if (!ys[i] || ldys[i] < need) return fail(SG_ERR_INVALID_ARG, "y[%d]: ldy %lld < %lld rows", i, (long long)ldys[i], (long long)need);
+    if (acc && ws[i]->tp_mode == SG_TP_ROW && g_ctx.world > 1)
+      return fail(SG_ERR_UNSUPPORTED, "SG_FLAG_ACCUMULATE with a row-split tensor");
+  }
+  if (ldx < sw[0]->n_cols) return fail(SG_ERR_INVALID_ARG, "ldx %lld < n_cols %lld", (long long)ldx, (long long)sw[0]->n_cols);
+  DevState& d = g_ctx.devs[0];
+  CUDA_TRY(cudaSetDevice(d.device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : d.stream;
+  int rc = run_linear(d, sw, n_weights, x, ldx, ys, ldys, batch, st, acc);
+  if (rc) return rc;
+  if (ws[0]->tp_mode == SG_TP_ROW && g_ctx.world > 1) {
+    if (!g_nccl.AllReduce) return fail(SG_ERR_NCCL, "NCCL not initialised");
+    for (int i = 0; i < n_weights; ++i) {
+      const int64_t nr = ws[i]->n_rows;
+      const int calls = ldys[i] == nr ? 1 : batch;
+      const size_t count = ldys[i] == nr ? (size_t)batch * nr : (size_t)nr;
+      for (int b = 0; b < calls; ++b) {
+        float* yb = ys[i] + (size_t)b * ldys[i];
+        ncclResult_t r = g_nccl.AllReduce(yb, yb, count, kNcclFloat, kNcclSum, d.comm, st);
+        if (r) return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
+      }
+    }
+  }
+  return SG_OK;
+}
+
+int sg_dequant_f32(sg_weight_t w, float* dst, int flags) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  int rc = validate_weight(w);
+  if (rc) return rc;
+  if (!dst) return fail(SG_ERR_INVALID_ARG, "null dst");
+  if (flags & SG_FLAG_DEVICE_PTRS) {
+    if (g_ctx.devs.size() != 1) return fail(SG_ERR_INVALID_ARG, "device pointers need one device per process");
+    DevState& d = g_ctx.devs[0];
+    CUDA_TRY(cudaSetDevice(d.device));
+    const SgDevWeight& s = w->shards[0].w;
+    CUDA_TRY(sg_layout_dequant(&s, dst, s.n_cols, d.stream));
+    CUDA_TRY(cudaStreamSynchronize(d.stream));
+    return SG_OK;
+  }
+  for (size_t di = 0; di < w->shards.size(); ++di) {
+    const Shard& sh = w->shards[di];
+    if (w->tp_mode == SG_TP_REPLICATE && di > 0) break;
+    DevState& d = g_ctx.devs[sh.dev_idx];
+    CUDA_TRY(cudaSetDevice(d.device));
+    const size_t n = (size_t)sh.w.n_rows * sh.w.n_cols;
+    rc = ensure_buf((void**)&d.ybuf, &d.ybuf_bytes, n * sizeof(float));
+    if (rc) return rc;
+    CUDA_TRY(sg_layout_dequant(&sh.w, d.ybuf, sh.w.n_cols, d.stream));
+    // place the shard into the full [n_rows][n_cols] host matrix
+    CUDA_TRY(cudaMemcpy2DAsync(dst + (size_t)sh.row0 * w->n_cols + sh.col0, (size_t)w->n_cols * sizeof(float), d.ybuf,
+                               (size_t)sh.w.n_cols * sizeof(float), (size_t)sh.w.n_cols * sizeof(float),
+                               (size_t)sh.w.n_rows, cudaMemcpyDeviceToHost, d.stream));
+    CUDA_TRY(cudaStreamSynchronize(d.stream));
+  }
+  return SG_OK;
+}
+
+int sg_fused_gemv_q4k(const uint8_t* w_raw, const float* x, float* out, int n_rows, int n_cols) {
+  if (!w_raw || !x || !out) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (n_rows <= 0 || n_cols <= 0 || n_cols % 256) return fail(SG_ERR_INVALID_ARG, "n_cols %d not a positive multiple of 256", n_cols);
+  sg_weight_t w = nullptr;
+  int rc = sg_weight_register(w_raw, SG_DTYPE_Q4_K, n_rows, n_cols, SG_TP_REPLICATE, &w);
+  if (rc) return rc;
+  const float* xs[1] = {x};
+  float* outs[1] = {out};
+  rc = sg_linear(w, xs, outs, 1, 0);
+  int rc2 = sg_weight_free(w);
+  return rc ? rc : rc2;
+}
+
+int sg_synchronize(void) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!g_ctx.inited) return fail(SG_ERR_NOT_INITIALIZED, "sg_init not called");
+  for (auto& d : g_ctx.devs) {
+    CUDA_TRY(cudaSetDevice(d.device));
+    CUDA_TRY(cudaStreamSynchronize(d.stream));
+    int rc = check_device_error(d);
+    if (rc) return rc;
+  }
+  return SG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,246 @@
+// sg_layout.cu -- repack GGUF Q4_0/Q4_K blocks into the device tile layout,
+// and the bit-exact dequantizer that reads the tile layout back to f32.
+//
+// Dequant arithmetic follows swamp-gguf exactly:
+//   Q4_0 (swamp-gguf/src/quant/q4_0.rs:24-35):  w = (float)(q - 8) * d
+//   Q4_K (swamp-gguf/src/quant/q4_k.rs:297-317): w = RN(RN(d*sc) * q) - RN(dmin*m)
+// with no FMA contraction, so the result is the reference's f32 bit pattern.
+#include "sg_layout.cuh"
+
+namespace {
+
+__device__ __forceinline__ uint32_t raw_nibble(int dtype, const uint8_t* raw, int64_t n_rows, int64_t n_cols,
+                                               int64_t row, int64_t k) {
+  if (row >= n_rows || k >= n_cols) return 0u;
+  if (dtype == SG_DTYPE_Q4_0) {
+    const int64_t nb = n_cols / 32;
+    const int64_t b = k >> 5;
+    const int i = (int)(k & 31);
+    const uint8_t byte = raw[(row * nb + b) * 18 + 2 + (i >> 1)];  // q4_0.rs:31
+    return (i & 1) ? (byte >> 4) : (byte & 15u);                    // q4_0.rs:32
+  } else {
+    const int64_t nsb = n_cols / 256;
+    const int64_t sb = k >> 8;
+    const int e = (int)(k & 255), p = e >> 6, h = (e >> 5) & 1, i = e & 31;
+    const uint8_t byte = raw[(row * nsb + sb) * 144 + 16 + 32 * p + i];  // q4_k.rs:292,302,315
+    return h ? (byte >> 4) : (byte & 15u);
+  }
+}
+
+__global__ void repack_qs_kernel(int dtype, const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
+                                 int64_t n_rb, int64_t n_ch, uint32_t* __restrict__ qs) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = n_rb * n_ch * 256;
+  if (tid >= total) return;
+  const int lane = (int)(tid & 31);
+  const int rt = (int)((tid >> 5) & 7);
+  const int64_t tile = tid >> 8;  // rb * n_ch + c
+  const int64_t rb = tile / n_ch, c = tile % n_ch;
+  const int g = lane >> 2, t = lane & 3;
+  uint32_t words[4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      const int64_t row = rb * 128 + rt * 16 + g + ((p & 1) ? 8 : 0);
+      const int64_t k = c * 64 + 16 * s + 2 * t + (((p >> 1) & 1) ? 8 : 0) + ((p >> 2) & 1);
+      w |= raw_nibble(dtype, raw, n_rows, n_cols, row, k) << (4 * p);
+    }
+    words[s] = w;
+  }
+  reinterpret_cast<uint4*>(qs)[tid] = make_uint4(words[0], words[1], words[2], words[3]);
+}
+
+// Q4_0 scales: one thread per (rb, chunk, rt, g) writes 4 halves [blk][hl].
+__global__ void repack_q4_0_scales_kernel(const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
+                                          int64_t n_rb, int64_t n_ch, uint16_t* __restrict__ sc) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = n_rb * n_ch * 64;
+  if (tid >= total) return;
+  const int g = (int)(tid & 7), rt = (int)((tid >> 3) & 7);
+  const int64_t tile = tid >> 6, rb = tile / n_ch, c = tile % n_ch;
+  const int64_t nb = n_cols / 32;
+  uint16_t v[4];
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk)
+#pragma unroll
+    for (int hl = 0; hl < 2; ++hl) {
+      const int64_t row = rb * 128 + rt * 16 + g + 8 * hl;
+      const int64_t b = c * 2 + blk;
+      uint16_t d = 0;
+      if (row < n_rows && b < nb) {
+        const uint8_t* p = raw + (row * nb + b) * 18;
+        d = (uint16_t)(p[0] | (p[1] << 8));
+      }
+      v[blk * 2 + hl] = d;
+    }
+  uint2 out;
+  out.x = v[0] | ((uint32_t)v[1] << 16);
+  out.y = v[2] | ((uint32_t)v[3] << 16);
+  reinterpret_cast<uint2*>(sc)[tid] = out;
+}
+
+// unpack_scales (swamp-gguf/src/quant/q4_k.rs:37-53)
+__device__ __forceinline__ void q4k_unpack(const uint8_t* s, int j, uint32_t& sc, uint32_t& m) {
+  if (j < 4) {
+    sc = s[j] & 63u;
+    m = s[j + 4] & 63u;
+  } else {
+    sc = (s[j + 4] & 0xFu) | ((uint32_t)(s[j - 4] >> 6) << 4);
+    m = (uint32_t)(s[j + 4] >> 4) | ((uint32_t)(s[j] >> 6) << 4);
+  }
+}
+
+// Q4_K scm: one thread per (rb, chunk, rt, g, hl).
+__global__ void repack_q4k_scm_kernel(const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
+                                      int64_t n_rb, int64_t n_ch, uint32_t* __restrict__ scm) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = n_rb * n_ch * 128;
+  if (tid >= total) return;
+  const int hl = (int)(tid & 1), g = (int)((tid >> 1) & 7), rt = (int)((tid >> 4) & 7);
+  const int64_t tile = tid >> 7, rb = tile / n_ch, c = tile % n_ch;
+  const int64_t row = rb * 128 + rt * 16 + g + 8 * hl;
+  const int64_t nsb = n_cols / 256;
+  uint32_t out = 0;
+  if (row < n_rows) {
+    const uint8_t* blk = raw + (row * nsb + (c >> 2)) * 144;
+    const int a = 2 * (int)(c & 3);
+    uint32_t sa, ma, sb, mb;
+    q4k_unpack(blk + 4, a, sa, ma);
+    q4k_unpack(blk + 4, a + 1, sb, mb);
+    out = sa | (sb << 8) | (ma << 16) | (mb << 24);
+  }
+  scm[tid] = out;
+}
+
+// Q4_K dd: one thread per (rb, superblock, rt, g, hl).
+__global__ void repack_q4k_dd_kernel(const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
+                                     int64_t n_rb, int64_t n_sb, uint32_t* __restrict__ dd) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = n_rb * n_sb * 128;
+  if (tid >= total) return;
+  const int hl = (int)(tid & 1), g = (int)((tid >> 1) & 7), rt = (int)((tid >> 4) & 7);
+  const int64_t tile = tid >> 7, rb = tile / n_sb, sb = tile % n_sb;
+  const int64_t row = rb * 128 + rt * 16 + g + 8 * hl;
+  uint32_t out = 0;
+  if (row < n_rows) {
+    const uint8_t* blk = raw + (row * n_sb + sb) * 144;
+    out = (uint32_t)blk[0] | ((uint32_t)blk[1] << 8) | ((uint32_t)blk[2] << 16) | ((uint32_t)blk[3] << 24);
+  }
+  dd[tid] = out;
+}
+
+// Dequantize 8 consecutive k of one row per thread.
+__global__ void dequant_kernel(SgDevWeight w, float* __restrict__ dst, int64_t ld) {
+  const int64_t kq = w.n_cols / 8;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (tid >= w.n_rows * kq) return;
+  const int64_t row = tid / kq;
+  const int64_t k0 = (tid % kq) * 8;
+  const int64_t rb = row >> 7;
+  const int r = (int)(row & 127);
+  const int64_t c = k0 >> 6;
+  const int kk0 = (int)(k0 & 63);
+  const uint32_t* tile = w.qs + (rb * w.n_ch + c) * 1024;
+  const int rt = r >> 4, g = r & 7, hl = (r >> 3) & 1;
+  float out[8];
+  if (w.dtype == SG_DTYPE_Q4_0) {
+    const __half* sc = reinterpret_cast<const __half*>(w.sc) + (rb * w.n_ch + c) * 256;
+    const float d = __half2float(sc[rt * 32 + g * 4 + (kk0 >> 5) * 2 + hl]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int q = (int)tile_nibble(tile, r, kk0 + i);
+      out[i] = __fmul_rn((float)(q - 8), d);
+    }
+  } else {
+    const uint32_t scm = reinterpret_cast<const uint32_t*>(w.sc)[(rb * w.n_ch + c) * 128 + rt * 16 + g * 2 + hl];
+    const uint32_t ddw = w.dd[(rb * w.n_sb + (c >> 2)) * 128 + rt * 16 + g * 2 + hl];
+    const float d = __half2float(__ushort_as_half((unsigned short)(ddw & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(ddw >> 16)));
+    const int sub = kk0 >> 5;
+    const float sv = __fmul_rn(d, (float)((scm >> (8 * sub)) & 0xFFu));
+    const float mv = __fmul_rn(dmin, (float)((scm >> (16 + 8 * sub)) & 0xFFu));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int q = (int)tile_nibble(tile, r, kk0 + i);
+      out[i] = __fsub_rn(__fmul_rn(sv, (float)q), mv);
+    }
+  }
+  float4* o = reinterpret_cast<float4*>(dst + row * ld + k0);
+  o[0] = make_float4(out[0], out[1], out[2], out[3]);
+  o[1] = make_float4(out[4], out[5], out[6], out[7]);
+}
+
+inline unsigned nblocks(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+}  // namespace
+
+size_t sg_layout_bytes(int dtype, int64_t n_rows, int64_t n_cols) {
+  const int64_t n_rb = (n_rows + 127) / 128;
+  const int64_t n_ch = (n_cols + 63) / 64;
+  size_t b = (size_t)(n_rb * n_ch) * (SG_CHUNK_QS + SG_CHUNK_SC);
+  if (dtype == SG_DTYPE_Q4_K) b += (size_t)(n_rb * (n_cols / 256)) * SG_SB_DD;
+  return b;
+}
+
+int sg_layout_alloc(SgDevWeight* w, int dtype, int64_t n_rows, int64_t n_cols) {
+  w->dtype = dtype;
+  w->n_rows = n_rows;
+  w->n_cols = n_cols;
+  w->n_rb = (n_rows + 127) / 128;
+  w->n_ch = (n_cols + 63) / 64;
+  w->n_sb = dtype == SG_DTYPE_Q4_K ? n_cols / 256 : 0;
+  w->qs = nullptr;
+  w->sc = nullptr;
+  w->dd = nullptr;
+  const size_t qs_bytes = (size_t)(w->n_rb * w->n_ch) * SG_CHUNK_QS;
+  const size_t sc_bytes = (size_t)(w->n_rb * w->n_ch) * SG_CHUNK_SC;
+  const size_t dd_bytes = (size_t)(w->n_rb * w->n_sb) * SG_SB_DD;
+  if (cudaMalloc(&w->qs, qs_bytes) != cudaSuccess) return -1;
+  if (cudaMalloc(&w->sc, sc_bytes) != cudaSuccess) {
+    sg_layout_free(w);
+    return -1;
+  }
+  if (dd_bytes && cudaMalloc(&w->dd, dd_bytes) != cudaSuccess) {
+    sg_layout_free(w);
+    return -1;
+  }
+  return 0;
+}
+
+void sg_layout_free(SgDevWeight* w) {
+  if (w->qs) cudaFree(w->qs);
+  if (w->sc) cudaFree(w->sc);
+  if (w->dd) cudaFree(w->dd);
+  w->qs = nullptr;
+  w->sc = nullptr;
+  w->dd = nullptr;
+}
+
+cudaError_t sg_layout_repack(const SgDevWeight* w, const uint8_t* raw_dev, cudaStream_t st) {
+  const int T = 256;
+  const int64_t nq = w->n_rb * w->n_ch * 256;
+  repack_qs_kernel<<<nblocks(nq, T), T, 0, st>>>(w->dtype, raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch,
+                                                 w->qs);
+  if (w->dtype == SG_DTYPE_Q4_0) {
+    const int64_t ns = w->n_rb * w->n_ch * 64;
+    repack_q4_0_scales_kernel<<<nblocks(ns, T), T, 0, st>>>(raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch,
+                                                            reinterpret_cast<uint16_t*>(w->sc));
+  } else {
+    const int64_t ns = w->n_rb * w->n_ch * 128;
+    repack_q4k_scm_kernel<<<nblocks(ns, T), T, 0, st>>>(raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch,
+                                                        reinterpret_cast<uint32_t*>(w->sc));
+    const int64_t nd = w->n_rb * w->n_sb * 128;
+    repack_q4k_dd_kernel<<<nblocks(nd, T), T, 0, st>>>(raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_sb, w->dd);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t sg_layout_dequant(const SgDevWeight* w, float* dst, int64_t ld, cudaStream_t st) {
+  const int T = 256;
+  const int64_t n = w->n_rows * (w->n_cols / 8);
+  if (n == 0) return cudaSuccess;
+  dequant_kernel<<<nblocks(n, T), T, 0, st>>>(*w, dst, ld);
+  return cudaGetLastError();
+}

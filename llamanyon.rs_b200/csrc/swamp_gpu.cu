@@ -1,0 +1,9 @@
+// swamp_gpu.cu -- unity translation unit for libswamp_gpu.so.
+//
+// The library is compiled as one translation unit so that device globals
+// (the per-device error flag) have exactly one definition without relocatable
+// device code.
+#include "sg_layout.cu"
+#include "sg_gemv.cu"
+#include "sg_gemm.cu"
+#include "sg_api.cu"

@@ -1,0 +1,250 @@
+"""Python binding of libswamp_gpu.so (the C ABI in include/swamp_gpu.h).
+
+Mirrors the reference's linear-layer interface (swamp-engine/src/linear.rs):
+``forward_linear``, ``forward_linear_multi``, ``forward_linear_batch`` and
+``forward_gemvs`` take a registered tensor (the GGUF TensorInfo + raw block
+bytes) and f32 activations, with the same overwrite semantics and errors
+raised as exceptions (the Rust functions return anyhow::Result). There is no
+CPU fallback: if the shared library or a usable sm_100 GPU is missing, every
+entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from typing import Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libswamp_gpu.so")
+
+SG_OK = 0
+SG_DTYPE_Q4_0 = 2
+SG_DTYPE_Q4_K = 12
+SG_TP_REPLICATE, SG_TP_COLUMN, SG_TP_ROW = 0, 1, 2
+SG_FLAG_DEVICE_PTRS = 0x1
+SG_FLAG_ACCUMULATE = 0x2
+
+BLOCK = {SG_DTYPE_Q4_0: 32, SG_DTYPE_Q4_K: 256}
+BLOCK_BYTES = {SG_DTYPE_Q4_0: 18, SG_DTYPE_Q4_K: 144}
+
+# every symbol include/swamp_gpu.h declares
+EXPORTS = (
+    "sg_init", "sg_get_unique_id", "sg_init_rank", "sg_shutdown", "sg_last_error", "sg_topology",
+    "sg_weight_register", "sg_weight_free", "sg_weight_shard", "sg_linear", "sg_linear_multi",
+    "sg_linear_device", "sg_linear_multi_device", "sg_dequant_f32", "sg_fused_gemv_q4k",
+    "sg_synchronize",
+)
+
+
+class SwampGpuError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"swamp_gpu error {code}: {msg}")
+        self.code = code
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    if not os.path.exists(path):
+        raise SwampGpuError(-5, f"{path} is missing; run llamanyon.rs_b200/build_lib.py (no CPU fallback)")
+    L = ctypes.CDLL(path)
+    P, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    L.sg_init.argtypes = [i32]
+    L.sg_get_unique_id.argtypes = [P]
+    L.sg_init_rank.argtypes = [i32, i32, P, i32]
+    L.sg_shutdown.argtypes = []
+    L.sg_last_error.restype = ctypes.c_char_p
+    L.sg_topology.argtypes = [P, P, P]
+    L.sg_weight_register.argtypes = [P, i32, i64, i64, i32, P]
+    L.sg_weight_free.argtypes = [P]
+    L.sg_weight_shard.argtypes = [P, i32, P, P, P, P]
+    L.sg_linear.argtypes = [P, P, P, i32, i32]
+    L.sg_linear_multi.argtypes = [P, i32, P, P, i32]
+    L.sg_linear_device.argtypes = [P, P, i64, P, i64, i32, P, i32]
+    L.sg_linear_multi_device.argtypes = [P, i32, P, i64, P, P, i32, P, i32]
+    L.sg_dequant_f32.argtypes = [P, P, i32]
+    L.sg_fused_gemv_q4k.argtypes = [P, P, P, i32, i32]
+    L.sg_synchronize.argtypes = []
+    for name in EXPORTS:
+        getattr(L, name).restype = ctypes.c_char_p if name == "sg_last_error" else ctypes.c_int
+    return L
+
+
+def row_bytes(dtype: int, n_cols: int) -> int:
+    return n_cols // BLOCK[dtype] * BLOCK_BYTES[dtype]
+
+
+@dataclass
+class TensorInfo:
+    """swamp-gguf TensorInfo (tensor_info.rs:10-16): shape[0] = n_cols (K),
+    shape[1] = n_rows (N)."""
+    name: str
+    shape: tuple
+    dtype: int
+
+    @property
+    def n_cols(self) -> int:
+        return int(self.shape[0])
+
+    @property
+    def n_rows(self) -> int:
+        return int(self.shape[1])
+
+
+class Weight:
+    """A GGUF tensor resident on the GPU(s) (sg_weight_t)."""
+
+    def __init__(self, lib: "SwampGpu", handle: int, dtype: int, n_rows: int, n_cols: int, tp_mode: int):
+        self.lib, self.handle = lib, handle
+        self.dtype, self.n_rows, self.n_cols, self.tp_mode = dtype, n_rows, n_cols, tp_mode
+
+    def shard(self, local_device: int = 0):
+        v = [ctypes.c_int64() for _ in range(4)]
+        self.lib._check(self.lib.L.sg_weight_shard(self.handle, local_device, *[ctypes.byref(a) for a in v]))
+        return tuple(int(a.value) for a in v)  # n_rows, n_cols, row0, col0
+
+    def free(self):
+        if self.handle:
+            self.lib._check(self.lib.L.sg_weight_free(self.handle))
+            self.handle = None
+
+
+class SwampGpu:
+    """One loaded libswamp_gpu.so with its init state."""
+
+    def __init__(self, path: str = LIB_PATH):
+        self.L = load_library(path)
+
+    def _check(self, rc: int):
+        if rc != SG_OK:
+            raise SwampGpuError(rc, self.L.sg_last_error().decode(errors="replace"))
+
+    # ---------------------------------------------------------- setup
+    def init(self, n_gpus: int = 1):
+        self._check(self.L.sg_init(n_gpus))
+        return self
+
+    def get_unique_id(self) -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        self._check(self.L.sg_get_unique_id(buf))
+        return buf.raw
+
+    def init_rank(self, rank: int, world: int, uid: bytes | None, device: int):
+        buf = ctypes.create_string_buffer(uid, 128) if uid is not None else None
+        self._check(self.L.sg_init_rank(rank, world, buf, device))
+        return self
+
+    def shutdown(self):
+        self._check(self.L.sg_shutdown())
+
+    def topology(self):
+        r, w, n = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        self._check(self.L.sg_topology(ctypes.byref(r), ctypes.byref(w), ctypes.byref(n)))
+        return r.value, w.value, n.value
+
+    def synchronize(self):
+        self._check(self.L.sg_synchronize())
+
+    # --------------------------------------------------------- weights
+    def register(self, blocks: np.ndarray, dtype: int, n_rows: int, n_cols: int,
+                 tp_mode: int = SG_TP_REPLICATE) -> Weight:
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        if blocks.size < n_rows * row_bytes(dtype, n_cols):
+            raise SwampGpuError(-1, f"blocks hold {blocks.size} bytes, tensor needs {n_rows * row_bytes(dtype, n_cols)}")
+        h = ctypes.c_void_p()
+        self._check(self.L.sg_weight_register(blocks.ctypes.data, dtype, n_rows, n_cols, tp_mode, ctypes.byref(h)))
+        return Weight(self, h.value, dtype, n_rows, n_cols, tp_mode)
+
+    # --------------------------------------------------------- compute
+    def linear(self, w: Weight, xs: np.ndarray, accumulate_into: np.ndarray | None = None) -> np.ndarray:
+        """outs[b] = W xs[b] (host arrays); xs is (K,) or (B, K)."""
+        xs = np.ascontiguousarray(xs, dtype=np.float32)
+        single = xs.ndim == 1
+        if single:
+            xs = xs[None]
+        B = xs.shape[0]
+        if xs.shape[1] < w.n_cols:
+            raise SwampGpuError(-1, "forward_linear shape mismatch")  # linear.rs:23
+        if accumulate_into is not None:
+            outs = np.ascontiguousarray(accumulate_into, dtype=np.float32).reshape(B, w.n_rows)
+            flags = SG_FLAG_ACCUMULATE
+        else:
+            outs = np.zeros((B, w.n_rows), np.float32)
+            flags = 0
+        xp = (ctypes.c_void_p * B)(*[xs[b].ctypes.data for b in range(B)])
+        op = (ctypes.c_void_p * B)(*[outs[b].ctypes.data for b in range(B)])
+        self._check(self.L.sg_linear(w.handle, xp, op, B, flags))
+        return outs[0] if single else outs
+
+    def linear_multi(self, ws: Sequence[Weight], x: np.ndarray) -> list:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        outs = [np.zeros(w.n_rows, np.float32) for w in ws]
+        hp = (ctypes.c_void_p * len(ws))(*[w.handle for w in ws])
+        op = (ctypes.c_void_p * len(ws))(*[o.ctypes.data for o in outs])
+        self._check(self.L.sg_linear_multi(hp, len(ws), x.ctypes.data, op, 0))
+        return outs
+
+    def linear_device(self, w: Weight, x_ptr: int, ldx: int, y_ptr: int, ldy: int, batch: int,
+                      stream: int = 0, flags: int = 0):
+        """Stream-ordered device call (pointers are raw device addresses)."""
+        self._check(self.L.sg_linear_device(w.handle, x_ptr, ldx, y_ptr, ldy, batch, stream or None, flags))
+
+    def linear_multi_device(self, ws: Sequence[Weight], x_ptr: int, ldx: int, y_ptrs: Sequence[int],
+                            ldys: Sequence[int], batch: int, stream: int = 0, flags: int = 0):
+        n = len(ws)
+        hp = (ctypes.c_void_p * n)(*[w.handle for w in ws])
+        yp = (ctypes.c_void_p * n)(*y_ptrs)
+        lp = (ctypes.c_int64 * n)(*ldys)
+        self._check(self.L.sg_linear_multi_device(hp, n, x_ptr, ldx, yp, lp, batch, stream or None, flags))
+
+    def dequant(self, w: Weight) -> np.ndarray:
+        out = np.empty((w.n_rows, w.n_cols), np.float32)
+        self._check(self.L.sg_dequant_f32(w.handle, out.ctypes.data, 0))
+        return out
+
+    def dequant_device(self, w: Weight, dst_ptr: int):
+        self._check(self.L.sg_dequant_f32(w.handle, dst_ptr, SG_FLAG_DEVICE_PTRS))
+
+    def fused_gemv_q4k(self, w_raw: np.ndarray, x: np.ndarray, n_rows: int, n_cols: int) -> np.ndarray:
+        """swamp_fused_gemv_q4k (fused_gemv_q4k.rs:799-823)."""
+        w_raw = np.ascontiguousarray(w_raw, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty(n_rows, np.float32)
+        self._check(self.L.sg_fused_gemv_q4k(w_raw.ctypes.data, x.ctypes.data, out.ctypes.data, n_rows, n_cols))
+        return out
+
+
+# ---------------------------------------------------------------------------
+# swamp-engine/src/linear.rs call shapes
+# ---------------------------------------------------------------------------
+
+def forward_linear(gpu: SwampGpu, tensor: Weight, x: np.ndarray, out: np.ndarray) -> None:
+    """linear.rs:14-90: out[..n_rows] = W x (x has >= n_cols entries)."""
+    if x.shape[0] < tensor.n_cols or out.shape[0] < tensor.n_rows:
+        raise SwampGpuError(-1, "forward_linear shape mismatch")
+    out[: tensor.n_rows] = gpu.linear(tensor, x[: tensor.n_cols])
+
+
+def forward_linear_multi(gpu: SwampGpu, tensors: Sequence[Weight], x: np.ndarray, outputs: Sequence[np.ndarray]) -> None:
+    """linear.rs:96-170: several tensors over one x; outputs overwritten."""
+    res = gpu.linear_multi(tensors, x)
+    for o, r in zip(outputs, res):
+        o[: r.shape[0]] = r
+
+
+def forward_linear_batch(gpu: SwampGpu, tensor: Weight, xs: Sequence[np.ndarray], outputs: Sequence[np.ndarray]) -> None:
+    """linear.rs:176-239: batch of inputs; bs != outputs.len() is an error (:185-187)."""
+    if len(xs) != len(outputs):
+        raise SwampGpuError(-1, f"forward_linear_batch: {len(xs)} inputs != {len(outputs)} outputs")
+    if len(xs) == 0:
+        return
+    res = gpu.linear(tensor, np.stack([np.asarray(x[: tensor.n_cols], np.float32) for x in xs]))
+    for o, r in zip(outputs, res):
+        o[: tensor.n_rows] = r
+
+
+def forward_gemvs(gpu: SwampGpu, specs: Sequence[tuple]) -> None:
+    """linear.rs:278-333: list of (tensor, x, out); outputs zero-filled then written."""
+    for tensor, x, out in specs:
+        forward_linear(gpu, tensor, x, out)

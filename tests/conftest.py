@@ -1,0 +1,64 @@
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+for p in (os.path.join(ROOT, "oracle"), os.path.join(ROOT, "llamanyon.rs_b200"), ROOT):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+SEED = 0x5EED1A11
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU; runs the CUDA path through the C ABI")
+
+
+@pytest.fixture(scope="session")
+def oracle():
+    import oracle as orc
+    orc.build()
+    return orc
+
+
+@pytest.fixture(scope="session")
+def gpu():
+    """The library on cuda:0. A GPU test without a usable GPU fails (no fallback)."""
+    import swamp_gpu
+    import build_lib as libbuild
+    libbuild.build()
+    lib = swamp_gpu.SwampGpu()
+    lib.init(1)
+    yield lib
+    lib.shutdown()
+
+
+def reference_gate(y, ref, l2dot, rtol=1e-3):
+    """Per-element parity bound used by every GEMV/GEMM test:
+
+        |y - ref| <= rtol * max(|ref|, ||w_r .* x_b||_2)
+
+    ref is the reference's f32 result (scalar Q4_K kernel / engine Q4_0
+    route); ||w.*x||_2 is the natural magnitude of the dot product (a sum of
+    K terms of random sign has |ref| of about that size), so elements whose
+    true value cancels to ~0 are judged against the scale of their terms
+    instead of an arbitrarily small |ref|. Returns the worst ratio."""
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    denom = np.maximum(np.abs(ref), np.asarray(l2dot, np.float64))
+    denom = np.where(denom == 0, 1.0, denom)
+    ratio = np.abs(y - ref) / denom
+    worst = float(ratio.max()) if ratio.size else 0.0
+    assert np.all(np.isfinite(y)), "non-finite outputs"
+    assert worst <= rtol, f"parity bound exceeded: max |y-ref|/max(|ref|,||w.*x||) = {worst:.3e} > {rtol}"
+    return worst
+
+
+def reference_outputs(orc, dtype, w, x, n_rows, n_cols):
+    """(ref f32 [B,N], l2dot [B,N]) from the oracle."""
+    x = np.atleast_2d(np.asarray(x, np.float32))
+    ref = orc.reference_linear(dtype, w, x, n_rows, n_cols)
+    l2 = np.stack([orc.gemv_f64(dtype, w, x[b], n_rows, n_cols)[2] for b in range(x.shape[0])])
+    return ref, l2
