@@ -153,42 +153,63 @@ def cpu_sample(threads, seconds_budget=20.0, max_calls=None):
 
 
 def reference_arm(args):
+    """The reference's CPU route on the host cores, same metric and config.
+
+    Each step runs the layer's 7 tensors through forward_linear at batch 1
+    (one token, the engine's decode call) on a row slice sized so that the
+    whole --steps/--warmup run stays within about two minutes; GB/s counts the
+    sliced bytes. Rank 0 only."""
     rank = env_int("RANK", 0)
     if rank != 0:
         return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.build()
     threads = os.cpu_count() or 1
-    per_step = []
+    ws = [(k, n, oracle.gen_weight(Q40, SEED, 500 + i, n, k)) for i, (_, k, n) in enumerate(LAYER)]
+    x = {k: oracle.gen_x(SEED, 900 + k, (k,)) for _, k, _ in LAYER}
+    t0 = time.perf_counter()
+    for k, n, w in ws:  # calibration pass (also pages the weights in)
+        oracle.forward_linear(Q40, w, x[k], n, k, threads)
+    t_layer = time.perf_counter() - t0
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    frac = min(1.0, budget / t_layer)
+    sl = []
+    for k, n, w in ws:
+        rows = max(128, int(n * frac) // 128 * 128)
+        rb = oracle.row_bytes(Q40, k)
+        sl.append((k, rows, w[: rows * rb]))
+    step_b = sum(wbytes(k, r) + (k + r) * 4 for k, r, _ in sl)
     for _ in range(args.warmup):
-        cpu_sample(threads, seconds_budget=0.0, max_calls=len(LAYER))
-    total_bytes = 0
+        for k, r, w in sl:
+            oracle.forward_linear(Q40, w, x[k], r, k, threads)
+    per_step = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        gbs, calls, el = cpu_sample(threads, seconds_budget=0.0, max_calls=len(LAYER))
+        for k, r, w in sl:
+            oracle.forward_linear(Q40, w, x[k], r, k, threads)
         per_step.append(time.perf_counter() - t0)
-    gbs_steps = [(sum(wbytes(k, n) + (k + n) * 4 for _, k, n in LAYER)) / t / 1e9 for t in per_step]
-    value = statistics.median(gbs_steps)
-    sample = ("one Llama-2-7B layer's 7 Q4_0 linears at batch 1 per step through the reference route "
-              "(forward_linear: full-tensor dequant + f32 row dots, linear.rs:68-87)")
+    tot = sum(per_step)
+    value = step_b * len(per_step) / tot / 1e9
+    sample = (f"per step: the layer's 7 Q4_0 tensors, first {sl[0][1]}/{LAYER[0][2]} .. rows "
+              f"({100 * frac:.1f}% of each), batch 1, through forward_linear's Q4_0 route "
+              f"(full-slice dequant + f32 row dots, swamp-engine/src/linear.rs:68-87) on {threads} threads")
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * statistics.median(per_step), 3),
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * tot / len(per_step), 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "configs[1] Q4_0 Llama-2-7B layer decode (CPU sample: batch 1)",
-                   "host_threads": threads},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+        "config": {"workload": "configs[1]: Llama-2-7B layer Q4_0 linears at decode (CPU sample: batch 1)",
+                   "host_threads": threads, "bytes_per_step": step_b},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-# ---------------------------------------------------------------------------
-# GPU arm
-# ---------------------------------------------------------------------------
-
-def gpu_arm(args):
-    import numpy as np
+def setup_gpu(args):
+    """torch.distributed (one rank per GPU) + the library on this rank's GPU."""
     import torch
     import swamp_gpu as sg
     import build_lib
@@ -213,15 +234,39 @@ def gpu_arm(args):
         gpu.init_rank(rank, world, bytes(t.cpu().numpy().tobytes()), local)
     else:
         gpu.init(1)
+    return torch, gpu, dist, rank, world, local
+
+
+def graph_of(torch, fn):
+    """Capture fn() (stream-ordered library calls on the current stream) into a CUDA graph."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def time_graphs(torch, graphs, reps, st):
+    """Replay graphs round-robin `reps` times; device ms between two events."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for j in range(reps):
+        graphs[j % len(graphs)].replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def gpu_arm(args):
+    import numpy as np
+    torch, gpu, dist, rank, world, local = setup_gpu(args)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle  # weight generator (host-side synthetic data only)
+    import oracle  # host-side synthetic weight generator only
 
     n_layers = world  # weak scaling: per-GPU bytes fixed
     l2 = torch.cuda.get_device_properties(local).L2_cache_size
     layer_b = sum(wbytes(k, n) for _, k, n in LAYER)
-    copies = max(5, int(np.ceil(4.5 * l2 / (layer_b / world))) + 1)
-    copies = max(copies, n_layers)
-    # register: copies x layer tensors (TP-split when world > 1)
+    copies = max(5, int(np.ceil(4.5 * l2 / (layer_b / world))) + 1, n_layers)
     model = []
     for c in range(copies):
         layer = {}
@@ -229,142 +274,124 @@ def gpu_arm(args):
             w = oracle.gen_weight(Q40, SEED, 1000 + 16 * c + i, n, k)
             layer[name] = gpu.register(w, Q40, n, k, TP_MODE[name] if world > 1 else 0)
         model.append(layer)
-    # activations / outputs (device, this rank's shard shapes)
-    st = torch.cuda.current_stream()
-    sp = st.cuda_stream
-
-    def shard(w):
-        return w.shard(0)  # n_rows, n_cols, row0, col0
-
     xs = {b: torch.randn(b, 11008, device="cuda") for b in BATCHES}
     ys = {b: {name: torch.empty(b, 11008, device="cuda") for name, _, _ in LAYER} for b in BATCHES}
-    launches_per_call = 2
+    LD = 11008
+    kernels_per_call = 1  # the GEMV kernel
 
-    def run_layer(layer, b):
-        x = xs[b]
-        q, kk, v = layer["q"], layer["k"], layer["v"]
-        ldx = 11008
-        gpu.linear_multi_device([q, kk, v], x.data_ptr(), ldx,
-                                [ys[b]["q"].data_ptr(), ys[b]["k"].data_ptr(), ys[b]["v"].data_ptr()],
-                                [11008] * 3, b, stream=sp)
-        gpu.linear_device(layer["o"], x.data_ptr(), ldx, ys[b]["o"].data_ptr(), 11008, b, stream=sp)
-        gpu.linear_multi_device([layer["gate"], layer["up"]], x.data_ptr(), ldx,
-                                [ys[b]["gate"].data_ptr(), ys[b]["up"].data_ptr()], [11008] * 2, b, stream=sp)
-        gpu.linear_device(layer["down"], x.data_ptr(), ldx, ys[b]["down"].data_ptr(), 11008, b, stream=sp)
+    def run_layer(layer, b, st):
+        x, y = xs[b].data_ptr(), ys[b]
+        gpu.linear_multi_device([layer["q"], layer["k"], layer["v"]], x, LD,
+                                [y["q"].data_ptr(), y["k"].data_ptr(), y["v"].data_ptr()], [LD] * 3, b, stream=st)
+        gpu.linear_device(layer["o"], x, LD, y["o"].data_ptr(), LD, b, stream=st)
+        gpu.linear_multi_device([layer["gate"], layer["up"]], x, LD, [y["gate"].data_ptr(), y["up"].data_ptr()],
+                                [LD] * 2, b, stream=st)
+        gpu.linear_device(layer["down"], x, LD, y["down"].data_ptr(), LD, b, stream=st)
         return 4
 
-    state = {"i": 0}
-
-    def step():
+    def step(j):
+        """one step = batches 1, 4, 16 over n_layers layers; copies rotate with j"""
+        st = torch.cuda.current_stream().cuda_stream
         calls = 0
-        for b in BATCHES:
-            for _ in range(n_layers):
-                layer = model[state["i"] % copies]
-                state["i"] += 1
-                calls += run_layer(layer, b)
+        for bi, b in enumerate(BATCHES):
+            for li in range(n_layers):
+                calls += run_layer(model[(j * len(BATCHES) * n_layers + bi * n_layers + li) % copies], b, st)
         return calls
 
-    # warmup
-    for _ in range(args.warmup):
-        step()
+    # warmup (eager: allocates the scratch once), then one graph per rotation offset
+    for j in range(args.warmup):
+        step(j)
+    torch.cuda.synchronize()
+    calls_per_step = step(0)
+    torch.cuda.synchronize()
+    graphs = [graph_of(torch, lambda j=j: step(j)) for j in range(copies)] if not args.eager else None
+    for j in range(args.warmup):
+        graphs[j % copies].replay() if graphs else step(j)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
 
     # ------------------------------------------------------------ timed
+    st = torch.cuda.current_stream()
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
         dist.barrier()
-    torch.cuda.synchronize()
-    ev0.record(st)
-    calls = 0
-    for _ in range(args.steps):
-        calls += step()
-    ev1.record(st)
-    torch.cuda.synchronize()
+    if graphs:
+        ms = time_graphs(torch, graphs, args.steps, st)
+    else:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for j in range(args.steps):
+            step(j)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
     if dist:
         dist.barrier()
     clocks = sampler.stop()
-    ms = ev0.elapsed_time(ev1)
     if dist:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    total_bytes = step_bytes(n_layers) * args.steps
-    value = total_bytes / (ms / 1e3) / 1e9
+    value = step_bytes(n_layers) * args.steps / (ms / 1e3) / 1e9
 
     # ------------------------------------------ per-launch roofline pass
-    # events around each GEMV call of one pass (each call = activation prep +
-    # the GEMV kernel, no overlap with its neighbours in this pass)
-    per = {}
+    # for each (shape, batch): a graph of `copies` back-to-back single-tensor
+    # GEMVs over rotating copies, timed with events; average device time per
+    # launch in steady state
+    tot_by, tot_us, per_shape = 0.0, 0.0, {}
+    reps = 20
     for b in BATCHES:
-        layer = model[state["i"] % copies]
-        state["i"] += 1
-        for name, k, n in LAYER:
-            if name in ("k", "v", "up"):
-                continue
-        # time single-tensor calls for the roofline
-        for name, k, n in LAYER:
-            w = layer[name]
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            gpu.linear_device(w, xs[b].data_ptr(), 11008, ys[b][name].data_ptr(), 11008, b, stream=sp)
-            e1.record(st)
-            per.setdefault(b, []).append((name, k, n, e0, e1))
-    torch.cuda.synchronize()
-    launch_gbs, launch_us = [], []
-    for b, lst in per.items():
-        for name, k, n, e0, e1 in lst:
-            us = e0.elapsed_time(e1) * 1e3
+        for name, k, n in (("q", 4096, 4096), ("gate", 4096, 11008), ("down", 11008, 4096)):
+            mult = {"q": 4, "gate": 2, "down": 1}[name]
+
+            def one(name=name, b=b):
+                stp = torch.cuda.current_stream().cuda_stream
+                for c in range(copies):
+                    gpu.linear_device(model[c][name], xs[b].data_ptr(), LD, ys[b][name].data_ptr(), LD, b, stream=stp)
+            g = graph_of(torch, one)
+            g.replay()
+            ms1 = time_graphs(torch, [g], reps, st)
+            us = ms1 * 1e3 / (reps * copies)
             by = (wbytes(k, n) + b * (k + n) * 4) / world
-            launch_gbs.append(by / (us * 1e-6) / 1e9)
-            launch_us.append(us)
-    tot_by = sum((wbytes(k, n) + b * (k + n) * 4) / world for b, lst in per.items() for (_, k, n, _, _) in lst)
-    tot_us = sum(launch_us)
+            per_shape[f"{k}x{n}_b{b}"] = round(by / (us * 1e-6) / 1e9, 1)
+            tot_by += by * mult
+            tot_us += us * mult
+            del g
     achieved = tot_by / (tot_us * 1e-6) / 1e9
     peak, peak_kind = measured_peaks()
 
     # -------------------------------------------------------------- e2e
-    # through the host-pointer C ABI: x copied in and y read back per call
+    # the public host-pointer C ABI: x copied in and y read back on every call
     e2e = None
     if world == 1:
         xh = {b: np.ascontiguousarray(xs[b].cpu().numpy()) for b in BATCHES}
-        torch.cuda.synchronize()
         h2d = d2h = 0
+        e2e_steps = max(1, min(args.steps, args.e2e_steps))
         t0 = time.perf_counter()
-        e2e_steps = max(1, min(args.steps, 10))
-        for _ in range(e2e_steps):
-            for b in BATCHES:
-                layer = model[state["i"] % copies]
-                state["i"] += 1
-                x4096 = xh[b][:, :4096]
-                outs = gpu.linear_multi([layer["q"], layer["k"], layer["v"]], x4096[0]) if b == 1 else None
+        for j in range(e2e_steps):
+            for bi, b in enumerate(BATCHES):
+                layer = model[(j * len(BATCHES) + bi) % copies]
+                x4096 = np.ascontiguousarray(xh[b][:, :4096])
                 if b == 1:
-                    h2d += 4096 * 4
-                    d2h += 3 * 4096 * 4
+                    gpu.linear_multi([layer["q"], layer["k"], layer["v"]], x4096[0])
+                    gpu.linear_multi([layer["gate"], layer["up"]], x4096[0])
                 else:
-                    for name in ("q", "k", "v"):
+                    for name in ("q", "k", "v", "gate", "up"):
                         gpu.linear(layer[name], x4096)
-                        h2d += b * 4096 * 4
-                        d2h += b * 4096 * 4
                 gpu.linear(layer["o"], x4096)
-                h2d += b * 4096 * 4
-                d2h += b * 4096 * 4
-                for name in ("gate", "up"):
-                    gpu.linear(layer[name], x4096)
-                    h2d += b * 4096 * 4
-                    d2h += b * 11008 * 4
                 gpu.linear(layer["down"], xh[b])
-                h2d += b * 11008 * 4
-                d2h += b * 4096 * 4
+                h2d += b * 4096 * 4 * (2 if b == 1 else 6) + b * 11008 * 4
+                d2h += b * 4 * (5 * 4096 + 2 * 11008)
         el = time.perf_counter() - t0
         e2e = {"value": round(step_bytes(1) * e2e_steps / el / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": h2d // e2e_steps, "d2h_bytes_per_step": d2h // e2e_steps,
-               "path": "sg_linear / sg_linear_multi with host buffers (pinned staging, H2D + D2H per call)"}
+               "steps": e2e_steps,
+               "path": "sg_linear / sg_linear_multi, host buffers (copy in, launch, copy out, sync per call)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -377,25 +404,28 @@ def gpu_arm(args):
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16x2-split/f32-acc (Q4_0 weights)",
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u4 weights, bf16 hi+lo activations, f32 accumulate",
             "data": "synthetic (seeded random-init Q4_0 blocks, N(0,1) activations)",
             "config": {"workload": "configs[1]: Llama-2-7B layer Q4_0 linears (4x 4096->4096, 2x 4096->11008, "
                                    "11008->4096) at decode batch 1, 4, 16",
-                       "layers_per_step": n_layers, "tp": world, "parallelism": f"tp{world}" if world > 1 else "none",
+                       "layers_per_step": n_layers, "parallelism": f"tp{world}" if world > 1 else "none",
+                       "execution": "eager" if args.eager else "CUDA graph per step (PDL edges kept)",
                        "l2_policy": f"inputs larger than L2: {copies} rotating layer copies "
                                     f"({copies * layer_b / world / 1e6:.0f} MB per GPU vs L2 {l2 / 1e6:.0f} MB)",
                        "bytes_per_step": step_bytes(n_layers)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
-                         "kernel": "gemv_main (decode GEMV) incl. its activation-prep launch",
-                         "peak_kind": peak_kind, "per_launch_gbs_median": round(statistics.median(launch_gbs), 1)},
+                         "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "gemv_kernel (one launch per GEMV), back-to-back launches in a CUDA graph",
+                         "per_shape_gbs": per_shape},
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clocks,
-            "gpu_launches": calls * launches_per_call,
+            "gpu_launches": calls_per_step * kernels_per_call * args.steps,
         }
         print(json.dumps(line), flush=True)
+    graphs = None
+    torch.cuda.synchronize()
     for layer in model:
         for w in layer.values():
             w.free()
@@ -406,19 +436,57 @@ def gpu_arm(args):
     return 0
 
 
+def profile_arm(args):
+    """One tensor shape, eager back-to-back launches (for ncu; not a bench line)."""
+    import numpy as np
+    torch, gpu, dist, rank, world, local = setup_gpu(args)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    k, n, b = (int(v) for v in args.profile.split(","))
+    dtype = Q4K if args.dtype == "q4k" else Q40
+    copies = 4
+    ws = [gpu.register(oracle.gen_weight(dtype, SEED, 3000 + c, n, k), dtype, n, k) for c in range(copies)]
+    x = torch.randn(b, k, device="cuda")
+    y = torch.empty(b, n, device="cuda")
+    st = torch.cuda.current_stream()
+    for i in range(args.warmup + args.steps):
+        if i == args.warmup:
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+        gpu.linear_device(ws[i % copies], x.data_ptr(), k, y.data_ptr(), n, b, stream=st.cuda_stream)
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    by = (n * k * (18 if dtype == Q40 else 144) // (32 if dtype == Q40 else 256)) + b * (k + n) * 4
+    print(json.dumps({"profile": args.profile, "dtype": args.dtype, "us_per_call": round(us, 2),
+                      "gbs": round(by / us / 1e3, 1), "note": "eager, host-launch bound; for ncu only"}))
+    for w in ws:
+        w.free()
+    gpu.shutdown()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="no CUDA graphs")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--profile", default=None, help="K,N,B: single-shape eager launches (for ncu)")
+    ap.add_argument("--dtype", default="q4_0", choices=["q4_0", "q4k"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return reference_arm(args)
+    if args.profile:
+        return profile_arm(args)
     return gpu_arm(args)
 
 

@@ -126,7 +126,7 @@ SG_API int sg_linear_multi(const sg_weight_t *ws, int n_weights, const float *x,
 
 /* Device-resident, stream-ordered form for engines that keep activations on
  * the GPU: x is [batch][ldx] (this rank's K-slice starts at x), y is
- * [batch][ldy]. stream may be NULL (the library's stream for this device).
+ * [batch][ldy]. stream is a cudaStream_t; NULL means CUDA's default stream.
  * Returns once the work is enqueued. */
 SG_API int sg_linear_device(sg_weight_t w, const float *x, int64_t ldx, float *y, int64_t ldy, int batch,
                      void *stream, int flags);

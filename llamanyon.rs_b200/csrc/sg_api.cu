@@ -74,7 +74,7 @@ struct DevState {
   int num_sms = 0;
   cudaStream_t stream = nullptr;
   ncclComm_t comm = nullptr;
-  void* scratch = nullptr;  // GEMV/GEMM scratch
+  void* scratch = nullptr;  // prefill GEMM scratch (grows on demand)
   size_t scratch_bytes = 0;
   float* xbuf = nullptr;  // staging for host-pointer calls
   size_t xbuf_bytes = 0;
@@ -217,18 +217,18 @@ void release_devices() {
 int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* x, int64_t ldx,
                float* const* ys, const int64_t* ldys, int batch, cudaStream_t st, bool accumulate) {
   const int64_t K = ws[0]->n_cols;
+  if (((uintptr_t)x & 15) || (ldx & 3))
+    return fail(SG_ERR_INVALID_ARG, "x must be 16-byte aligned with a row stride that is a multiple of 4 floats");
   if (batch <= 16) {
-    int rc = ensure_buf(&d.scratch, &d.scratch_bytes, sg_gemv_scratch_bytes(K));
-    if (rc) return rc;
     SgGemvMat mats[SG_GEMV_MAX_MATS];
     for (int i = 0; i < n_w; ++i) mats[i] = {ws[i], ys[i], ldys[i]};
-    CUDA_TRY(sg_gemv(mats, n_w, x, ldx, batch, accumulate, d.scratch, d.scratch_bytes, d.num_sms, st));
+    CUDA_TRY(sg_gemv(mats, n_w, x, ldx, batch, accumulate, d.num_sms, st));
     return SG_OK;
   }
-  // prefill GEMM (or accumulate): one launch per matrix
+  // prefill GEMM: one launch per matrix
   for (int i = 0; i < n_w; ++i) {
     const size_t need = sg_gemm_scratch_bytes(batch, K);
-    int rc = ensure_buf(&d.scratch, &d.scratch_bytes, need);
+    int rc = need ? ensure_buf(&d.scratch, &d.scratch_bytes, need) : SG_OK;
     if (rc) return rc;
     CUDA_TRY(sg_gemm(ws[i], x, ldx, ys[i], ldys[i], batch, accumulate, d.scratch, d.scratch_bytes, d.num_sms, st));
   }
@@ -626,7 +626,9 @@ int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x,
   if (ldx < sw[0]->n_cols) return fail(SG_ERR_INVALID_ARG, "ldx %lld < n_cols %lld", (long long)ldx, (long long)sw[0]->n_cols);
   DevState& d = g_ctx.devs[0];
   CUDA_TRY(cudaSetDevice(d.device));
-  cudaStream_t st = stream ? (cudaStream_t)stream : d.stream;
+  // a NULL stream is CUDA's default stream (the CUDA convention), not the
+  // library's internal stream, so callers on the default stream stay ordered
+  cudaStream_t st = (cudaStream_t)stream;
   int rc = run_linear(d, sw, n_weights, x, ldx, ys, ldys, batch, st, acc);
   if (rc) return rc;
   if (ws[0]->tp_mode == SG_TP_ROW && g_ctx.world > 1) {

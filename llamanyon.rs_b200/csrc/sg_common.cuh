@@ -1,9 +1,10 @@
 // sg_common.cuh -- shared device helpers for the swamp-gpu B200 kernels.
 //
-// Every spin-wait in these kernels is bounded: after SG_WAIT_LIMIT polls the
-// waiting thread records an error code in the per-device flag g_sg_error and
-// returns false, and the caller abandons its loop. The host reads the flag
-// (sg_check_device_error) after a kernel instead of the GPU hanging.
+// Every spin-wait in these kernels is bounded: after SG_WAIT_NS of wall time
+// (%globaltimer) the waiting thread records an error code in the per-device
+// flag g_sg_error and returns false, and the caller abandons its loop. The
+// host reads the flag after a call (SG_ERR_DEVICE_FAULT) instead of the GPU
+// hanging.
 #pragma once
 
 #include <cuda.h>
@@ -26,10 +27,6 @@
 // Error codes written to g_sg_error.
 #define SG_DEVERR_WAIT_TIMEOUT 0x100
 #define SG_DEVERR_BAD_ARGS 0x200
-
-#ifndef SG_WAIT_LIMIT
-#define SG_WAIT_LIMIT (1u << 26)
-#endif
 
 // The library is built as one translation unit (swamp_gpu.cu), so this is the
 // single definition of the per-device error flag.
@@ -65,6 +62,8 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
       : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting thread sleeps (it does not
+// spin and issue) until the phase completes or the hint expires.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -72,17 +71,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(0x989680u)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
 
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Bounded wait: returns false (and records SG_DEVERR_WAIT_TIMEOUT | tag) if the
-// phase with the given parity does not complete within SG_WAIT_LIMIT polls.
+// phase with the given parity has not completed after SG_WAIT_NS nanoseconds
+// of wall time (or after another thread already recorded an error).
+#ifndef SG_WAIT_NS
+#define SG_WAIT_NS 4000000000ull
+#endif
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int tag) {
-  for (uint32_t i = 0; i < SG_WAIT_LIMIT; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && *(volatile int*)&g_sg_error != 0) return false;
+    if (*(volatile int*)&g_sg_error != 0) return false;
+    if (globaltimer_ns() - t0 > SG_WAIT_NS) break;
   }
   sg_set_error(SG_DEVERR_WAIT_TIMEOUT | tag);
   return false;
@@ -135,6 +147,16 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ------------------------------------------------ programmatic dependent launch
+// Host switch: SG_PDL=0 in the environment launches every kernel without the
+// programmatic-serialization attribute (plain stream order).
+#include <cstdlib>
+inline bool sg_pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SG_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -11,15 +11,18 @@
 
 size_t sg_gemm_scratch_bytes(int64_t m, int64_t n_cols) {
   (void)m;
-  return sg_gemv_scratch_bytes(n_cols);
+  (void)n_cols;
+  return 0;
 }
 
 cudaError_t sg_gemm(const SgDevWeight* w, const float* x, int64_t ldx, float* y, int64_t ldy, int m, bool accumulate,
                     void* scratch, size_t scratch_bytes, int num_sms, cudaStream_t st) {
+  (void)scratch;
+  (void)scratch_bytes;
   for (int t0 = 0; t0 < m; t0 += 16) {
     const int nb = m - t0 < 16 ? m - t0 : 16;
     SgGemvMat mat = {w, y + (int64_t)t0 * ldy, ldy};
-    cudaError_t e = sg_gemv(&mat, 1, x + (int64_t)t0 * ldx, ldx, nb, accumulate, scratch, scratch_bytes, num_sms, st);
+    cudaError_t e = sg_gemv(&mat, 1, x + (int64_t)t0 * ldx, ldx, nb, accumulate, num_sms, st);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

@@ -5,481 +5,496 @@
 // (:527-698) and the engine's Q4_0 route (swamp-engine/src/linear.rs:68-87).
 // out[b][r] = sum_k W[r][k] * x[b][k], W dequantized exactly as swamp-gguf.
 //
-// Two kernels per call, chained with programmatic dependent launch:
+// One kernel per call (up to 4 matrices sharing x in one launch). The grid is
+// (row-block of 128 rows) x (split K slices), sized to one wave of 4 CTAs per
+// SM; the `split` CTAs of a row-block form one thread-block cluster.
 //
-// 1. gemv_xprep: one CTA per output column. Scales x[b] by a power of two
-//    2^e (so max|x| lands in [2^13, 2^14)), splits it into f16 hi + lo parts
-//    (16+ significant bits together; the exact split makes the activation
-//    error ~2^-22 relative instead of the 2^-11 of a single f16), and writes
-//    them in m16n8k16 B-fragment order. Column 2b holds x_hi[b], column 2b+1
-//    x_lo[b], so each thread's C fragment carries both halves of one batch.
-//    Also zeroes y and (Q4_K) writes per-32 sums of the scaled x.
-//
-// 2. gemv_main: persistent, 4 consumer warps + 1 producer warp per CTA. The
-//    work list is (matrix, row-block of 128 rows, 64-wide K chunk) units in
-//    that order; CTA i takes units [i*U/G, (i+1)*U/G). The producer streams
-//    each unit's 4.5 KB of packed weights plus the chunk's activation
-//    fragments into a 6-deep shared-memory ring with cp.async.bulk
-//    (evict-first for weights), completing on mbarriers. Consumers decode
-//    nibbles straight into f16 A fragments (lop3 + one f16x2 op per pair;
-//    q-8 resp. q is exact in f16), run mma.sync m16n8k16 with f32
-//    accumulation per 32-element block, apply the block's scale in f32 and
-//    accumulate. A row-block's partial sums are added to y with red.add when
-//    the CTA leaves the row-block (row-blocks split across CTAs at most at
-//    the ends of each CTA's range).
-//
-// The weight loads are issued before griddepcontrol.wait, so a GEMV launched
-// behind another kernel starts streaming its (immutable) weights while the
-// previous kernel drains; activation-dependent loads come after the wait.
+//  * Each of the 4 warps owns two 16-row tiles of the row-block and streams
+//    its K slice with 128-bit loads straight into registers (16 B of nibbles
+//    + the scales per tile per 64-wide chunk per lane), prefetched 4 chunks
+//    ahead. The first prefetches are issued before griddepcontrol.wait:
+//    weights never depend on the previous kernel, so they stream while that
+//    kernel drains.
+//  * After the wait, the CTA splits its K slice of x exactly into bf16 hi + lo
+//    (16 significant bits, full f32 range) in shared memory, laid out as
+//    m16n8k16 B fragments. Batch <= 4: one n-tile whose column 2b holds
+//    x_hi[b] and 2b+1 x_lo[b] (one mma per k-step); batch 5..16: n-tiles of 8
+//    batch columns with separate hi and lo fragments accumulated into the
+//    same f32 partial (half the epilogue work of interleaving).
+//  * Nibbles decode into bf16 A fragments (shift + lop3 + one bf16x2 fma per
+//    pair; q-8 / q are exact in bf16). Per 32-element block, mma.sync
+//    accumulates in f32; the block partial is scaled in f32 by d (Q4_0) or
+//    d*sc minus the min term dmin*m*sum(x) (Q4_K).
+//  * The cluster's K-slice partials are summed on chip through distributed
+//    shared memory (each CTA reduces a fixed share of the rows in rank order,
+//    so results are reproducible) and written to y. No global scratch, no
+//    atomics and no spin-waits: the only synchronisation is __syncthreads and
+//    the hardware cluster barrier, which every thread of the cluster reaches.
 #include <algorithm>
 
 #include "sg_gemv.cuh"
 
 namespace {
 
-constexpr int kStages = 6;
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kCtasPerSm = 4;
+constexpr int kMaxSmem = 55 * 1024;        // fits 4 CTAs per SM
+constexpr int kMaxSmemLarge = 110 * 1024;  // hard limit (2 CTAs per SM)
 
-template <int DT, int NT>
-struct StageGeom {
-  static constexpr int qs = 4096;
-  static constexpr int sc = 512;
-  static constexpr int dd = (DT == SG_DTYPE_Q4_K) ? 512 : 0;
-  static constexpr int xf = NT * 1024;
-  static constexpr int xs = (DT == SG_DTYPE_Q4_K) ? 128 : 0;
-  static constexpr int off_sc = qs;
-  static constexpr int off_dd = off_sc + sc;
-  static constexpr int off_xf = off_dd + dd;
-  static constexpr int off_xs = off_xf + xf;
-  static constexpr int bytes = off_xs + xs;
+// MODE 0: batch <= 4, [hi|lo] interleaved columns, 1 n-tile
+// MODE 1: batch <= 8, hi and lo fragments, 1 n-tile of 8 batches
+// MODE 2: batch <= 16, hi and lo fragments, 2 n-tiles
+template <int MODE>
+struct Frag {
+  static constexpr int nt = MODE == 2 ? 2 : 1;        // n-tiles
+  static constexpr int nfr = MODE == 0 ? 1 : 2;       // fragments per n-tile (hi, lo)
+  static constexpr int chunk_bytes = 4 * nt * nfr * 256;  // per 64-wide chunk
+  static constexpr int ncol = MODE == 0 ? 4 : 8 * nt;     // batch columns covered
 };
 
-__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], const uint32_t b[2], const float z[4]) {
+// One packed word -> the four bf16x2 A-fragment registers of m16n8k16 as raw
+// magic values: 128+q on rows g (fragment registers 0, 2) and 128+8q on rows
+// g+8 (registers 1, 3), both exact in bf16. The kernel removes the 128 (and
+// the Q4_0 bias of 8) in the f32 epilogue with the block sum of x.
+__device__ __forceinline__ void decode_frag_raw(uint32_t w, uint32_t a[4]) {
+  a[0] = lop3_and_or(w, 0x000F000Fu, 0x43004300u);
+  a[1] = lop3_and_or(w >> 1, 0x00780078u, 0x43004300u);
+  a[2] = lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u);
+  a[3] = lop3_and_or(w >> 9, 0x00780078u, 0x43004300u);
+}
+
+__device__ __forceinline__ void mma_bf16(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1,
+                                         const float z[4]) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%11,%12,%13};"
       : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "f"(z[0]), "f"(z[1]), "f"(z[2]),
-        "f"(z[3]));
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z[0]), "f"(z[1]), "f"(z[2]), "f"(z[3]));
 }
 
-__device__ __forceinline__ void unit_decode(const SgGemvParams& p, int64_t u, int& m, int64_t& rb, int64_t& c) {
-  m = 0;
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(const float* local, int rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// Per-warp weight ring: each warp streams its two row-tiles' share of every
+// chunk (1 KB of nibbles, 128 B of scales, Q4_K also 128 B of d|dmin) with
+// cp.async.bulk into a private ring of kStages stages; a stage is refilled by
+// the same warp right after it consumed it, so no warp ever waits on another.
+constexpr int kStages = 6;
+template <int DT>
+struct Ring {
+  static constexpr int nib = 1024, sc = 128, dd = DT == SG_DTYPE_Q4_K ? 128 : 0;
+  static constexpr int stage = nib + sc + dd;
+  static constexpr int warp_bytes = kStages * stage;
+  static constexpr int bytes = kWarps * warp_bytes;
+};
+
+template <int DT>
+__device__ __forceinline__ void issue_chunk(uint8_t* st, const uint8_t* tile, const uint32_t* dd_src, int warp,
+                                            uint64_t* bar, uint64_t pol) {
+  using R = Ring<DT>;
+  mbar_arrive_expect_tx(bar, R::stage);
+  bulk_g2s_evict_first(st, tile + warp * 1024, R::nib, bar, pol);
+  bulk_g2s_evict_first(st + R::nib, tile + SG_TILE_SC_OFF + warp * 128, R::sc, bar, pol);
+  if (DT == SG_DTYPE_Q4_K) bulk_g2s(st + R::nib + R::sc, dd_src + warp * 32, R::dd, bar);
+}
+
+// x (this CTA's chunks [c0, c0+nc)) -> bf16 hi/lo B fragments in smem, plus
+// the per-32 sums of x (of the hi+lo parts the mma sees) for the epilogue.
+template <int DT, int MODE>
+__device__ __forceinline__ void prepare_x(const SgGemvParams& p, int c0, int nc, uint8_t* smem) {
+  using F = Frag<MODE>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // zero the fragments and sums (columns past the batch must read as 0)
+  uint4* z = reinterpret_cast<uint4*>(smem);
+  const int nz = nc * (F::chunk_bytes + 128) / 16;
+  for (int i = threadIdx.x; i < nz; i += kThreads) z[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+  uint32_t* xf = reinterpret_cast<uint32_t*>(smem);
+  float* xs = reinterpret_cast<float*>(smem + (size_t)nc * F::chunk_bytes);
+  const int s4 = lane >> 3, tt = lane & 3, half = (lane >> 2) & 1;
+  const int items = nc * p.batch;  // (chunk, live column), one warp each
+  for (int it = warp; it < items; it += kWarps) {
+    const int i = it / p.batch, b = it - i * p.batch;
+    const int k = 64 * (c0 + i) + 2 * lane;
+    float2 v = make_float2(0.f, 0.f);
+    if (k < p.n_cols) v = *reinterpret_cast<const float2*>(p.x + (int64_t)b * p.ldx + k);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(v.x, v.y);
+    const float2 hf = __bfloat1622float2(hi);
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x - hf.x, v.y - hf.y);
+    const uint32_t hiw = *reinterpret_cast<const uint32_t*>(&hi), low = *reinterpret_cast<const uint32_t*>(&lo);
+    uint32_t* cf = xf + (size_t)i * (F::chunk_bytes / 4);
+    if (MODE == 0) {
+      // [s4][lane] uint2; column g = 2b (hi) / 2b+1 (lo)
+      cf[(s4 * 32 + 4 * (2 * b) + tt) * 2 + half] = hiw;
+      cf[(s4 * 32 + 4 * (2 * b + 1) + tt) * 2 + half] = low;
+    } else {
+      // [s4][nn][hl][lane] uint2; column g = b % 8 of n-tile b / 8
+      const int nn = b >> 3, gg = b & 7;
+      uint32_t* e = cf + (((s4 * F::nt + nn) * 2) * 32 + 4 * gg + tt) * 2 + half;
+      e[0] = hiw;
+      e[64] = low;
+    }
+    {
+      const float2 lf = __bfloat1622float2(lo);
+      float sum = (hf.x + lf.x) + (hf.y + lf.y);
+#pragma unroll
+      for (int o = 8; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if ((lane & 15) == 0) xs[(i * 2 + (lane >> 4)) * 16 + b] = sum;
+    }
+  }
+}
+
+template <int DT, int MODE>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(SgGemvParams p) {
+  using F = Frag<MODE>;
+  constexpr int NT = F::nt;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int split = p.split;
+  const int rbg = blockIdx.x / split, ks = blockIdx.x - rbg * split;
+  int m = 0;
 #pragma unroll
   for (int i = 1; i < SG_GEMV_MAX_MATS; ++i)
-    if (i < p.n_mats && u >= p.mats[i].unit0) m = i;
-  const int64_t local = u - p.mats[m].unit0;
-  rb = local / p.n_ch;
-  c = local - rb * p.n_ch;
-}
-
-// --------------------------------------------------------------------------
-// activation prep
-// --------------------------------------------------------------------------
-template <int DT>
-__global__ void __launch_bounds__(256) gemv_xprep_kernel(SgGemvParams p, const float* __restrict__ x, int64_t ldx,
-                                                          int NT) {
-  pdl_launch_dependents();
-  pdl_wait();  // x may be the previous kernel's output; the scratch may still be in use by the previous GEMV
-  const int ncols = 4 * NT;
-  const int b = blockIdx.x;
-  if (b >= ncols) {
-    // zero the outputs (the GEMV accumulates with red.add); skipped when the
-    // caller asked for out += W x
-    const int64_t zid = (int64_t)(b - ncols) * blockDim.x + threadIdx.x;
-    const int64_t zstride = (int64_t)(gridDim.x - ncols) * blockDim.x;
-    for (int mi = 0; mi < p.n_mats; ++mi) {
-      const int64_t n = p.mats[mi].n_rows;
-      const int64_t tot = n * p.batch;
-      for (int64_t i = zid; i < tot; i += zstride) {
-        const int64_t bb = i / n, r = i - bb * n;
-        p.mats[mi].y[bb * p.mats[mi].ldy + r] = 0.f;
-      }
-    }
-    return;
-  }
-  const bool live = b < p.batch;
-  const int64_t K = p.n_cols;
-  const float* xb = x + (int64_t)(live ? b : 0) * ldx;
-  __shared__ float red[8];
-  __shared__ float s_scale;
-  float mx = 0.f;
-  if (live)
-    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(xb[k]));
-  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float m2 = 0.f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m2 = fmaxf(m2, red[i]);
-    int e = 0;
-    if (m2 > 0.f && m2 <= 3.0e38f) {
-      int ex;
-      frexpf(m2, &ex);  // m2 = f * 2^ex, f in [0.5, 1)
-      e = 14 - ex;      // m2 * 2^e in [2^13, 2^14)
-      e = max(-120, min(120, e));
-    }
-    const float s = live ? ldexpf(1.f, e) : 0.f;
-    s_scale = s;
-    if (live) p.inv_scale[b] = ldexpf(1.f, -e);
-  }
-  __syncthreads();
-  const float s = s_scale;
-  // fragment entries: (chunk c, k16-step s4, t) -> lanes (4*g + t), g = 2*(b%4) + {0 hi, 1 lo}
-  const int n = b >> 2;
-  const int ghi = 2 * (b & 3);
-  const int64_t items = p.n_ch * 16;
-  for (int64_t it = threadIdx.x; it < items; it += blockDim.x) {
-    const int t = (int)(it & 3);
-    const int s4 = (int)((it >> 2) & 3);
-    const int64_t c = it >> 4;
-    const int64_t k0 = c * 64 + 16 * s4 + 2 * t;
-    float v[4];
-    const int64_t ks[4] = {k0, k0 + 1, k0 + 8, k0 + 9};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = (live && ks[j] < K) ? xb[ks[j]] * s : 0.f;
-    __half hi[4], lo[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      hi[j] = __float2half_rn(v[j]);
-      lo[j] = __float2half_rn(v[j] - __half2float(hi[j]));
-    }
-    uint2 whi, wlo;
-    whi.x = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16);
-    whi.y = (uint32_t)__half_as_ushort(hi[2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
-    wlo.x = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16);
-    wlo.y = (uint32_t)__half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
-    uint2* base = p.xfrag + ((c * 4 + s4) * NT + n) * 32;
-    base[4 * ghi + t] = whi;
-    base[4 * (ghi + 1) + t] = wlo;
-  }
-  if (DT == SG_DTYPE_Q4_K) {
-    // per-32 sums of the scaled activations: xsum[c][j][b]
-    const int64_t nsub = p.n_ch * 2;
-    for (int64_t it = threadIdx.x; it < nsub; it += blockDim.x) {
-      float acc = 0.f;
-      const int64_t k0 = it * 32;
-      if (live)
-        for (int i = 0; i < 32; ++i)
-          if (k0 + i < K) acc += xb[k0 + i] * s;
-      p.xsum[it * 16 + b] = acc;
-    }
-  }
-}
-
-// --------------------------------------------------------------------------
-// main persistent GEMV
-// --------------------------------------------------------------------------
-template <int DT, int NT>
-__global__ void __launch_bounds__(kThreads) gemv_main_kernel(SgGemvParams p) {
-  using G = StageGeom<DT, NT>;
-  extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full_bar[kStages];
-  __shared__ __align__(8) uint64_t empty_bar[kStages];
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t U = p.n_units;
-  const int64_t u0 = (int64_t)blockIdx.x * U / gridDim.x;
-  const int64_t u1 = (int64_t)(blockIdx.x + 1) * U / gridDim.x;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kConsumerWarps);
-    }
+    if (i < p.n_mats && rbg >= p.mats[i].rb0) m = i;
+  const SgGemvMatP& M = p.mats[m];
+  const int rb = rbg - M.rb0;
+  const int c0 = (int)((int64_t)ks * p.n_ch / split), c1 = (int)((int64_t)(ks + 1) * p.n_ch / split);
+  const int nc = c1 - c0;
+  const uint8_t* tb = M.tiles + ((int64_t)rb * p.n_ch + c0) * SG_TILE_BYTES;
+  // dd of (row-block, super-block) for this chunk: [rt 8][g 8][hl 2] words
+  const uint32_t* ddb = DT == SG_DTYPE_Q4_K ? M.dd + (int64_t)rb * M.n_sb * 128 : nullptr;
+  using R = Ring<DT>;
+  const size_t xbytes = (size_t)nc * (F::chunk_bytes + 128);
+  const size_t ring_off = (xbytes + 127) & ~(size_t)127;
+  uint8_t* ring = smem + ring_off + (size_t)warp * R::warp_bytes;
+  __shared__ __align__(8) uint64_t wbar[kWarps][kStages];
+  uint64_t* bars = wbar[warp];
+  const uint64_t pol = policy_evict_first();
+  // weights do not depend on the previous kernel: start streaming them now
+  if (lane == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
     mbar_fence_init();
+    for (int d = 0; d < kStages && d < nc; ++d)
+      issue_chunk<DT>(ring + d * R::stage, tb + (int64_t)d * SG_TILE_BYTES, ddb + ((c0 + d) >> 2) * 128, warp, &bars[d],
+                      pol);
   }
-  __syncthreads();
-
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer
-    if (elect_one()) {
-      const uint64_t pol = policy_evict_first();
-      const int64_t n = u1 - u0;
-      const int64_t pre = n < kStages ? n : kStages;
-      // weights of the first stages before the grid dependency resolves
-      for (int64_t i = 0; i < pre; ++i) {
-        int m;
-        int64_t rb, c;
-        unit_decode(p, u0 + i, m, rb, c);
-        const SgGemvMatP& M = p.mats[m];
-        uint8_t* st = smem + i * G::bytes;
-        mbar_arrive_expect_tx(&full_bar[i], G::bytes);
-        const int64_t tile = rb * p.n_ch + c;
-        bulk_g2s_evict_first(st, M.qs + tile * 1024, G::qs, &full_bar[i], pol);
-        bulk_g2s_evict_first(st + G::off_sc, (const uint8_t*)M.sc + tile * 512, G::sc, &full_bar[i], pol);
-        if (DT == SG_DTYPE_Q4_K)
-          bulk_g2s(st + G::off_dd, (const uint8_t*)M.dd + (rb * M.n_sb + (c >> 2)) * 512, G::dd, &full_bar[i]);
-      }
-      pdl_wait();
-      for (int64_t i = 0; i < pre; ++i) {
-        int m;
-        int64_t rb, c;
-        unit_decode(p, u0 + i, m, rb, c);
-        uint8_t* st = smem + i * G::bytes;
-        bulk_g2s(st + G::off_xf, p.xfrag + c * (4 * NT * 32), G::xf, &full_bar[i]);
-        if (DT == SG_DTYPE_Q4_K) bulk_g2s(st + G::off_xs, p.xsum + c * 32, G::xs, &full_bar[i]);
-      }
-      for (int64_t i = pre; i < n; ++i) {
-        const int s = (int)(i % kStages);
-        const uint32_t ph = (uint32_t)((i / kStages) & 1);
-        if (!mbar_wait(&empty_bar[s], ph ^ 1u, 1)) break;
-        int m;
-        int64_t rb, c;
-        unit_decode(p, u0 + i, m, rb, c);
-        const SgGemvMatP& M = p.mats[m];
-        uint8_t* st = smem + s * G::bytes;
-        mbar_arrive_expect_tx(&full_bar[s], G::bytes);
-        const int64_t tile = rb * p.n_ch + c;
-        bulk_g2s_evict_first(st, M.qs + tile * 1024, G::qs, &full_bar[s], pol);
-        bulk_g2s_evict_first(st + G::off_sc, (const uint8_t*)M.sc + tile * 512, G::sc, &full_bar[s], pol);
-        if (DT == SG_DTYPE_Q4_K)
-          bulk_g2s(st + G::off_dd, (const uint8_t*)M.dd + (rb * M.n_sb + (c >> 2)) * 512, G::dd, &full_bar[s]);
-        bulk_g2s(st + G::off_xf, p.xfrag + c * (4 * NT * 32), G::xf, &full_bar[s]);
-        if (DT == SG_DTYPE_Q4_K) bulk_g2s(st + G::off_xs, p.xsum + c * 32, G::xs, &full_bar[s]);
-      }
-      // drain: wait until the consumers released every stage still in flight,
-      // so no bulk copy outlives the CTA
-      for (int64_t i = (n > kStages ? n - kStages : 0); i < n; ++i) {
-        const int s = (int)(i % kStages);
-        if (!mbar_wait(&empty_bar[s], (uint32_t)((i / kStages) & 1), 2)) break;
-      }
-    }
-    return;
-  }
-
-  // -------------------------------------------------------------- consumers
+  __syncwarp();
   pdl_wait();
-  const int g = lane >> 2, t = lane & 3;
-  const uint32_t bias_lo = DT == SG_DTYPE_Q4_0 ? SG_BIAS_LO_Q4_0 : SG_BIAS_LO_Q4_K;
-  const uint32_t bias_hi = DT == SG_DTYPE_Q4_0 ? SG_BIAS_HI_Q4_0 : SG_BIAS_HI_Q4_K;
+  prepare_x<DT, MODE>(p, c0, nc, smem);
+  __syncthreads();
+  const float* xs = reinterpret_cast<const float*>(smem + (size_t)nc * F::chunk_bytes);
+
+  // ---- stream the K slice
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
   float acc[2][NT][4];
 #pragma unroll
   for (int r = 0; r < 2; ++r)
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
+    for (int nn = 0; nn < NT; ++nn)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[r][n][j] = 0.f;
+      for (int j = 0; j < 4; ++j) acc[r][nn][j] = 0.f;
+  const uint2* xfr2 = reinterpret_cast<const uint2*>(smem);
 
-  int cur_m = -1;
-  int64_t cur_rb = -1;
-  auto flush = [&]() {
-    if (cur_m < 0) return;
-    const SgGemvMatP& M = p.mats[cur_m];
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int64_t row = cur_rb * 128 + (2 * warp + r) * 16 + g;
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        const int b = 4 * n + t;
-        if (b < p.batch) {
-          const float inv = p.inv_scale[b];
-          float* yb = M.y + (int64_t)b * M.ldy;
-          if (row < M.n_rows) red_add_f32(yb + row, (acc[r][n][0] + acc[r][n][1]) * inv);
-          if (row + 8 < M.n_rows) red_add_f32(yb + row + 8, (acc[r][n][2] + acc[r][n][3]) * inv);
+  bool ok = true;
+  int issued = nc < kStages ? nc : kStages;
+  int i = 0;
+  for (; i < nc; ++i) {
+    {
+      {
+        const int slot = i % kStages;
+        // every lane acquires the stage; the vote keeps the warp converged even
+        // if one lane's bounded wait gave up
+        const bool lane_ok = mbar_wait(&bars[slot], (i / kStages) & 1, 6);
+        if (!__all_sync(0xffffffffu, lane_ok)) {
+          ok = false;
+          break;
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[r][n][j] = 0.f;
-      }
-    }
-  };
-
-  const int64_t n = u1 - u0;
-  for (int64_t i = 0; i < n; ++i) {
-    const int s = (int)(i % kStages);
-    const uint32_t ph = (uint32_t)((i / kStages) & 1);
-    int m;
-    int64_t rb, c;
-    unit_decode(p, u0 + i, m, rb, c);
-    if (m != cur_m || rb != cur_rb) {
-      flush();
-      cur_m = m;
-      cur_rb = rb;
-    }
-    if (!mbar_wait(&full_bar[s], ph, 3)) break;
-    const uint8_t* st = smem + s * G::bytes;
-    const uint2* xf = reinterpret_cast<const uint2*>(st + G::off_xf);
-    uint4 wq[2];
-    float dsc[2][2][2];  // [r][blk or sub][hl] : Q4_0 d, Q4_K sv
-    float dmn[2][2][2];  // Q4_K mv
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int rt = 2 * warp + r;
-      wq[r] = reinterpret_cast<const uint4*>(st)[rt * 32 + lane];
-      if (DT == SG_DTYPE_Q4_0) {
-        const uint2 dv = *reinterpret_cast<const uint2*>(st + G::off_sc + rt * 64 + g * 8);
-        dsc[r][0][0] = __half2float(__ushort_as_half((unsigned short)(dv.x & 0xFFFFu)));
-        dsc[r][0][1] = __half2float(__ushort_as_half((unsigned short)(dv.x >> 16)));
-        dsc[r][1][0] = __half2float(__ushort_as_half((unsigned short)(dv.y & 0xFFFFu)));
-        dsc[r][1][1] = __half2float(__ushort_as_half((unsigned short)(dv.y >> 16)));
-      } else {
-        const uint2 scm = *reinterpret_cast<const uint2*>(st + G::off_sc + (rt * 16 + g * 2) * 4);
-        const uint2 ddv = *reinterpret_cast<const uint2*>(st + G::off_dd + (rt * 16 + g * 2) * 4);
-        const uint32_t sw[2] = {scm.x, scm.y};
-        const uint32_t dw[2] = {ddv.x, ddv.y};
-#pragma unroll
-        for (int hl = 0; hl < 2; ++hl) {
-          const float d = __half2float(__ushort_as_half((unsigned short)(dw[hl] & 0xFFFFu)));
-          const float dm = __half2float(__ushort_as_half((unsigned short)(dw[hl] >> 16)));
-#pragma unroll
-          for (int sub = 0; sub < 2; ++sub) {
-            dsc[r][sub][hl] = d * (float)((sw[hl] >> (8 * sub)) & 0xFFu);
-            dmn[r][sub][hl] = dm * (float)((sw[hl] >> (16 + 8 * sub)) & 0xFFu);
-          }
-        }
-      }
-    }
-    float tmp[2][NT][4];
-#pragma unroll
-    for (int s4 = 0; s4 < 4; ++s4) {
-      uint32_t bf[NT][2];
-#pragma unroll
-      for (int nn = 0; nn < NT; ++nn) {
-        const uint2 v = xf[(s4 * NT + nn) * 32 + lane];
-        bf[nn][0] = v.x;
-        bf[nn][1] = v.y;
-      }
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const uint32_t w = s4 == 0 ? wq[r].x : s4 == 1 ? wq[r].y : s4 == 2 ? wq[r].z : wq[r].w;
-        uint32_t a[4];
-        decode_frag(w, bias_lo, bias_hi, a);
-#pragma unroll
-        for (int nn = 0; nn < NT; ++nn) mma16816(tmp[r][nn], a, bf[nn], (s4 & 1) ? tmp[r][nn] : zero4);
-      }
-      if (s4 & 1) {
-        const int blk = s4 >> 1;
+        const uint8_t* st = ring + slot * R::stage;
+        struct {
+          uint4 q[2];
+          uint2 sc[2];
+          uint2 dd[2];
+        } cur;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-          const float d0 = dsc[r][blk][0], d1 = dsc[r][blk][1];
+          cur.q[r] = *reinterpret_cast<const uint4*>(st + r * 512 + lane * 16);
+          cur.sc[r] = *reinterpret_cast<const uint2*>(st + R::nib + r * 64 + g * 8);
+          if (DT == SG_DTYPE_Q4_K) cur.dd[r] = *reinterpret_cast<const uint2*>(st + R::nib + R::sc + r * 64 + g * 8);
+        }
+        // the stage is in registers now: refill it with the chunk kStages ahead
+        __syncwarp();
+        if (i + kStages < nc) {
+          if (lane == 0) {
+            fence_proxy_async_smem();
+            issue_chunk<DT>(ring + slot * R::stage, tb + (int64_t)(i + kStages) * SG_TILE_BYTES,
+                            ddb + ((c0 + i + kStages) >> 2) * 128, warp, &bars[slot], pol);
+          }
+          ++issued;
+        }
+        // per (row-tile, 32-block, row half): acc += alpha * T - beta * S, where
+        // T is the mma of the raw magic values (128+q on rows g, 128+8q on rows
+        // g+8) and S the block's sum of x, so the bias never enters the decode
+        float alpha[2][2][2], beta[2][2][2];  // [r][32-block][hl]
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          if (DT == SG_DTYPE_Q4_0) {
+            const float2 d0 = __half22float2(*reinterpret_cast<const __half2*>(&cur.sc[r].x));
+            const float2 d1 = __half22float2(*reinterpret_cast<const __half2*>(&cur.sc[r].y));
+            const float dv[2][2] = {{d0.x, d0.y}, {d1.x, d1.y}};
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+              alpha[r][blk][0] = dv[blk][0];
+              alpha[r][blk][1] = dv[blk][1] * 0.125f;
+              beta[r][blk][0] = dv[blk][0] * 136.f;  // d * (128 + 8)
+              beta[r][blk][1] = dv[blk][1] * 24.f;   // d * (128/8 + 8)
+            }
+          } else {
+            const uint32_t scw[2] = {cur.sc[r].x, cur.sc[r].y};
+            const uint32_t ddw[2] = {cur.dd[r].x, cur.dd[r].y};
+#pragma unroll
+            for (int hl = 0; hl < 2; ++hl) {
+              const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddw[hl]));
+#pragma unroll
+              for (int sub = 0; sub < 2; ++sub) {
+                const float sv = dm.x * (float)((scw[hl] >> (8 * sub)) & 0xFFu);
+                const float mv = dm.y * (float)((scw[hl] >> (16 + 8 * sub)) & 0xFFu);
+                alpha[r][sub][hl] = hl ? sv * 0.125f : sv;
+                beta[r][sub][hl] = fmaf(sv, hl ? 16.f : 128.f, mv);
+              }
+            }
+          }
+        }
+        const uint2* xfr = xfr2 + (size_t)i * (F::chunk_bytes / 8);
+        float tmp[2][NT][4];
+#pragma unroll
+        for (int s4 = 0; s4 < 4; ++s4) {
+          uint2 bh[NT], bl[NT];
 #pragma unroll
           for (int nn = 0; nn < NT; ++nn) {
-            acc[r][nn][0] = fmaf(d0, tmp[r][nn][0], acc[r][nn][0]);
-            acc[r][nn][1] = fmaf(d0, tmp[r][nn][1], acc[r][nn][1]);
-            acc[r][nn][2] = fmaf(d1, tmp[r][nn][2], acc[r][nn][2]);
-            acc[r][nn][3] = fmaf(d1, tmp[r][nn][3], acc[r][nn][3]);
-            if (DT == SG_DTYPE_Q4_K) {
-              const float xs = reinterpret_cast<const float*>(st + G::off_xs)[blk * 16 + 4 * nn + t];
-              acc[r][nn][0] = fmaf(-dmn[r][blk][0], xs, acc[r][nn][0]);
-              acc[r][nn][2] = fmaf(-dmn[r][blk][1], xs, acc[r][nn][2]);
+            if (MODE == 0) {
+              bh[nn] = xfr[s4 * 32 + lane];
+            } else {
+              bh[nn] = xfr[((s4 * NT + nn) * 2 + 0) * 32 + lane];
+              bl[nn] = xfr[((s4 * NT + nn) * 2 + 1) * 32 + lane];
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const uint32_t w = s4 == 0 ? cur.q[r].x : s4 == 1 ? cur.q[r].y : s4 == 2 ? cur.q[r].z : cur.q[r].w;
+            uint32_t a[4];
+            decode_frag_raw(w, a);
+#pragma unroll
+            for (int nn = 0; nn < NT; ++nn) {
+              mma_bf16(tmp[r][nn], a, bh[nn].x, bh[nn].y, (s4 & 1) ? tmp[r][nn] : zero4);
+              if (MODE != 0) mma_bf16(tmp[r][nn], a, bl[nn].x, bl[nn].y, tmp[r][nn]);
+            }
+          }
+          if (s4 & 1) {
+            const int blk = s4 >> 1;
+#pragma unroll
+            for (int nn = 0; nn < NT; ++nn) {
+              // MODE 0: thread t owns batch t (hi col 2t, lo col 2t+1); others: batches 8nn+2t, +1
+              float2 sx;
+              if (MODE == 0) {
+                sx.x = xs[(i * 2 + blk) * 16 + t];
+                sx.y = 0.f;
+              } else {
+                sx = *reinterpret_cast<const float2*>(xs + (i * 2 + blk) * 16 + 8 * nn + 2 * t);
+              }
+#pragma unroll
+              for (int r = 0; r < 2; ++r) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[r][nn][j] = fmaf(alpha[r][blk][j >> 1], tmp[r][nn][j], acc[r][nn][j]);
+                // the S term applies once per batch column: the hi column only in MODE 0
+                acc[r][nn][0] = fmaf(-beta[r][blk][0], sx.x, acc[r][nn][0]);
+                acc[r][nn][2] = fmaf(-beta[r][blk][1], sx.x, acc[r][nn][2]);
+                if (MODE != 0) {
+                  acc[r][nn][1] = fmaf(-beta[r][blk][0], sx.y, acc[r][nn][1]);
+                  acc[r][nn][3] = fmaf(-beta[r][blk][1], sx.y, acc[r][nn][3]);
+                }
+              }
             }
           }
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[s]);
   }
-  flush();
+  // a stage that timed out: wait (bounded) for the copies still in flight so
+  // none lands after the CTA has exited
+  if (!ok)
+    for (int j = i; j < issued; ++j)
+      if (!mbar_wait(&bars[j % kStages], (j / kStages) & 1, 7)) break;
+  pdl_launch_dependents();
+
+  // ---- results: value of (row-tile r, half hl, n-tile nn, column jc) and its batch
+  auto out_val = [&](int r, int hl, int nn, int jc, int& b) -> float {
+    if (MODE == 0) {
+      b = t;  // jc selects hi/lo which are summed below
+      return acc[r][nn][2 * hl] + acc[r][nn][2 * hl + 1];
+    }
+    b = 8 * nn + 2 * t + jc;
+    return acc[r][nn][2 * hl + jc];
+  };
+  constexpr int NJC = MODE == 0 ? 1 : 2;
+  if (split == 1) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl) {
+        const int row = rb * 128 + (2 * warp + r) * 16 + g + 8 * hl;
+        if (row < M.n_rows)
+#pragma unroll
+          for (int nn = 0; nn < NT; ++nn)
+#pragma unroll
+            for (int jc = 0; jc < NJC; ++jc) {
+              int b;
+              const float v = out_val(r, hl, nn, jc, b);
+              if (b < p.batch) {
+                float* yp = M.y + (int64_t)b * M.ldy + row;
+                *yp = p.accumulate ? *yp + v : v;
+              }
+            }
+      }
+    return;
+  }
+  // split-K: partials through distributed shared memory, fixed rank order
+  __syncthreads();  // every warp is done with the fragment area
+  float* P = reinterpret_cast<float*>(smem);  // [128 rows][16 cols]
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+      for (int nn = 0; nn < NT; ++nn)
+#pragma unroll
+        for (int jc = 0; jc < NJC; ++jc) {
+          int b;
+          const float v = out_val(r, hl, nn, jc, b);
+          P[((2 * warp + r) * 16 + g + 8 * hl) * 16 + b] = v;
+        }
+  cluster_sync_all();
+  const int r0 = ks * 128 / split, r1 = (ks + 1) * 128 / split;
+  const int nitems = (r1 - r0) * p.batch;
+  for (int it = threadIdx.x; it < nitems; it += kThreads) {
+    const int rl = r0 + it / p.batch, b = it % p.batch;
+    float v = 0.f;
+    for (int q = 0; q < split; ++q) v += ld_dsmem_f32(P + rl * 16 + b, q);
+    const int row = rb * 128 + rl;
+    if (row < M.n_rows) {
+      float* yp = M.y + (int64_t)b * M.ldy + row;
+      *yp = p.accumulate ? *yp + v : v;
+    }
+  }
+  cluster_sync_all();  // keep this CTA's partials alive until the whole cluster has read them
 }
 
-template <int DT, int NT>
-cudaError_t launch_main(const SgGemvParams& p, int grid, cudaStream_t st, bool pdl) {
-  using G = StageGeom<DT, NT>;
-  const size_t smem = (size_t)kStages * G::bytes;
-  auto kern = gemv_main_kernel<DT, NT>;
-  static bool attr_set = false;  // per (DT,NT) instantiation
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+template <int DT, int MODE>
+size_t smem_bytes(int nc_max) {
+  // [x fragments + per-32 sums][per-warp weight rings]; the split-K partials
+  // (8 KB) reuse the front once the rings are drained
+  const size_t frag = ((size_t)nc_max * (Frag<MODE>::chunk_bytes + 128) + 127) & ~(size_t)127;
+  return std::max<size_t>(frag + Ring<DT>::bytes, 128 * 16 * sizeof(float));
+}
+
+// cudaFuncSetAttribute is per device; remember which devices are done.
+template <int DT, int MODE>
+cudaError_t set_attrs() {
+  static uint64_t done_mask = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 64 && ((done_mask >> dev) & 1)) return cudaSuccess;
+  e = cudaFuncSetAttribute(gemv_kernel<DT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmemLarge);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemv_kernel<DT, MODE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess && dev < 64) done_mask |= (1ull << dev);
+  return e;
+}
+
+template <int DT, int MODE>
+cudaError_t launch(SgGemvParams& p, int total_rb, int num_sms, cudaStream_t st) {
+  cudaError_t e = set_attrs<DT, MODE>();
+  if (e != cudaSuccess) return e;
+  // split: the most K slices per row-block that still fit one wave of CTAs,
+  // keeping >= 2 chunks per slice and the fragments within the smem budget
+  const int slots = num_sms * kCtasPerSm;
+  int split = std::max(1, std::min(16, slots / std::max(1, total_rb)));
+  split = std::min(split, std::max(1, p.n_ch / 2));
+  while (split < 16 && smem_bytes<DT, MODE>((p.n_ch + split - 1) / split) > (size_t)kMaxSmem) ++split;
+  // very long K at batch > 8 may still exceed the 4-CTA budget: run fewer CTAs per SM
+  if (smem_bytes<DT, MODE>((p.n_ch + split - 1) / split) > (size_t)kMaxSmemLarge) return cudaErrorInvalidConfiguration;
+  p.split = split;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(total_rb * split);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = smem_bytes<DT, MODE>((p.n_ch + split - 1) / split);
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, p);
-}
-
-template <int DT>
-cudaError_t launch_xprep(const SgGemvParams& p, const float* x, int64_t ldx, int NT, bool accumulate, cudaStream_t st,
-                         bool pdl) {
-  int64_t ytot = 0;
-  for (int i = 0; i < p.n_mats; ++i) ytot += p.mats[i].n_rows * p.batch;
-  int zb = (int)std::min<int64_t>(64, (ytot + 2047) / 2048);
-  if (zb < 1) zb = 1;
-  if (accumulate) zb = 0;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(4 * NT + zb);
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_xprep_kernel<DT>, p, x, ldx, NT);
-}
-
-template <int DT>
-cudaError_t launch_dt(const SgGemvParams& p, int NT, int grid, cudaStream_t st, bool pdl) {
-  switch (NT) {
-    case 1: return launch_main<DT, 1>(p, grid, st, pdl);
-    case 2: return launch_main<DT, 2>(p, grid, st, pdl);
-    case 3: return launch_main<DT, 3>(p, grid, st, pdl);
-    default: return launch_main<DT, 4>(p, grid, st, pdl);
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = sg_pdl_enabled() ? 1 : 0;
+  ++na;
+  if (split > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = split;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<DT, MODE>, p);
+}
+
+template <int DT>
+cudaError_t launch_dt(SgGemvParams& p, int total_rb, int num_sms, cudaStream_t st) {
+  if (p.batch <= 4) return launch<DT, 0>(p, total_rb, num_sms, st);
+  if (p.batch <= 8) return launch<DT, 1>(p, total_rb, num_sms, st);
+  return launch<DT, 2>(p, total_rb, num_sms, st);
 }
 
 }  // namespace
 
-size_t sg_gemv_scratch_bytes(int64_t n_cols) {
-  const int64_t n_ch = (n_cols + 63) / 64;
-  const size_t xf = (size_t)n_ch * 4 * 4 * 32 * sizeof(uint2);  // NT = 4 worst case
-  const size_t xs = (size_t)n_ch * 32 * sizeof(float);
-  return ((xf + 255) & ~(size_t)255) + ((xs + 255) & ~(size_t)255) + 256;
-}
-
-int sg_gemv_max_ctas_per_sm() { return 2; }
-
 cudaError_t sg_gemv(const SgGemvMat* mats, int n_mats, const float* x, int64_t ldx, int batch, bool accumulate,
-                    void* scratch, size_t scratch_bytes, int num_sms, cudaStream_t st) {
+                    int num_sms, cudaStream_t st) {
   if (n_mats < 1 || n_mats > SG_GEMV_MAX_MATS || batch < 1 || batch > 16) return cudaErrorInvalidValue;
+  if (((uintptr_t)x & 7) || (ldx & 1)) return cudaErrorInvalidValue;
   const int dtype = mats[0].w->dtype;
   const int64_t K = mats[0].w->n_cols;
+  if (K > (1 << 30)) return cudaErrorInvalidValue;
   SgGemvParams p = {};
   p.n_mats = n_mats;
-  p.n_cols = K;
-  p.n_ch = mats[0].w->n_ch;
+  p.n_cols = (int)K;
+  p.n_ch = (int)mats[0].w->n_ch;
   p.batch = batch;
-  int64_t units = 0;
+  p.accumulate = accumulate ? 1 : 0;
+  p.x = x;
+  p.ldx = ldx;
+  int64_t rbs = 0;
   for (int i = 0; i < n_mats; ++i) {
     const SgDevWeight* w = mats[i].w;
     if (w->dtype != dtype || w->n_cols != K) return cudaErrorInvalidValue;
-    p.mats[i].qs = w->qs;
-    p.mats[i].sc = w->sc;
+    p.mats[i].tiles = w->tiles;
     p.mats[i].dd = w->dd;
-    p.mats[i].n_sb = w->n_sb;
-    p.mats[i].n_rows = w->n_rows;
-    p.mats[i].unit0 = units;
+    p.mats[i].n_sb = (int)w->n_sb;
+    p.mats[i].n_rb = (int)w->n_rb;
+    p.mats[i].n_rows = (int)w->n_rows;
+    p.mats[i].rb0 = (int)rbs;
     p.mats[i].y = mats[i].y;
     p.mats[i].ldy = mats[i].ldy;
-    units += w->n_rb * w->n_ch;
+    rbs += w->n_rb;
   }
-  p.n_units = units;
-  if (scratch_bytes < sg_gemv_scratch_bytes(K)) return cudaErrorInvalidValue;
-  uint8_t* sp = static_cast<uint8_t*>(scratch);
-  const size_t xf = (size_t)p.n_ch * 4 * 4 * 32 * sizeof(uint2);
-  p.xfrag = reinterpret_cast<uint2*>(sp);
-  sp += (xf + 255) & ~(size_t)255;
-  p.xsum = reinterpret_cast<float*>(sp);
-  sp += (((size_t)p.n_ch * 32 * sizeof(float)) + 255) & ~(size_t)255;
-  p.inv_scale = reinterpret_cast<float*>(sp);
-  const int NT = (batch + 3) / 4;
-  int grid = (int)std::min<int64_t>(units, (int64_t)num_sms * sg_gemv_max_ctas_per_sm());
-  if (grid < 1) grid = 1;
-  cudaError_t e = dtype == SG_DTYPE_Q4_0 ? launch_xprep<SG_DTYPE_Q4_0>(p, x, ldx, NT, accumulate, st, true)
-                                         : launch_xprep<SG_DTYPE_Q4_K>(p, x, ldx, NT, accumulate, st, true);
-  if (e != cudaSuccess) return e;
-  return dtype == SG_DTYPE_Q4_0 ? launch_dt<SG_DTYPE_Q4_0>(p, NT, grid, st, true)
-                                : launch_dt<SG_DTYPE_Q4_K>(p, NT, grid, st, true);
+  if (rbs * 16 > (1ll << 31)) return cudaErrorInvalidValue;
+  return dtype == SG_DTYPE_Q4_0 ? launch_dt<SG_DTYPE_Q4_0>(p, (int)rbs, num_sms, st)
+                                : launch_dt<SG_DTYPE_Q4_K>(p, (int)rbs, num_sms, st);
 }

@@ -27,8 +27,9 @@ __device__ __forceinline__ uint32_t raw_nibble(int dtype, const uint8_t* raw, in
   }
 }
 
+// one thread per (tile, rt, lane): the 16-byte nibble vector of that lane
 __global__ void repack_qs_kernel(int dtype, const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
-                                 int64_t n_rb, int64_t n_ch, uint32_t* __restrict__ qs) {
+                                 int64_t n_rb, int64_t n_ch, uint8_t* __restrict__ tiles) {
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = n_rb * n_ch * 256;
   if (tid >= total) return;
@@ -49,36 +50,8 @@ __global__ void repack_qs_kernel(int dtype, const uint8_t* __restrict__ raw, int
     }
     words[s] = w;
   }
-  reinterpret_cast<uint4*>(qs)[tid] = make_uint4(words[0], words[1], words[2], words[3]);
-}
-
-// Q4_0 scales: one thread per (rb, chunk, rt, g) writes 4 halves [blk][hl].
-__global__ void repack_q4_0_scales_kernel(const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
-                                          int64_t n_rb, int64_t n_ch, uint16_t* __restrict__ sc) {
-  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t total = n_rb * n_ch * 64;
-  if (tid >= total) return;
-  const int g = (int)(tid & 7), rt = (int)((tid >> 3) & 7);
-  const int64_t tile = tid >> 6, rb = tile / n_ch, c = tile % n_ch;
-  const int64_t nb = n_cols / 32;
-  uint16_t v[4];
-#pragma unroll
-  for (int blk = 0; blk < 2; ++blk)
-#pragma unroll
-    for (int hl = 0; hl < 2; ++hl) {
-      const int64_t row = rb * 128 + rt * 16 + g + 8 * hl;
-      const int64_t b = c * 2 + blk;
-      uint16_t d = 0;
-      if (row < n_rows && b < nb) {
-        const uint8_t* p = raw + (row * nb + b) * 18;
-        d = (uint16_t)(p[0] | (p[1] << 8));
-      }
-      v[blk * 2 + hl] = d;
-    }
-  uint2 out;
-  out.x = v[0] | ((uint32_t)v[1] << 16);
-  out.y = v[2] | ((uint32_t)v[3] << 16);
-  reinterpret_cast<uint2*>(sc)[tid] = out;
+  *reinterpret_cast<uint4*>(tiles + tile * SG_TILE_BYTES + (rt * 32 + lane) * 16) =
+      make_uint4(words[0], words[1], words[2], words[3]);
 }
 
 // unpack_scales (swamp-gguf/src/quant/q4_k.rs:37-53)
@@ -92,26 +65,46 @@ __device__ __forceinline__ void q4k_unpack(const uint8_t* s, int j, uint32_t& sc
   }
 }
 
-// Q4_K scm: one thread per (rb, chunk, rt, g, hl).
-__global__ void repack_q4k_scm_kernel(const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
-                                      int64_t n_rb, int64_t n_ch, uint32_t* __restrict__ scm) {
+// one thread per (tile, rt, g): the two scale words of rows g and g+8
+__global__ void repack_scales_kernel(int dtype, const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
+                                     int64_t n_rb, int64_t n_ch, uint8_t* __restrict__ tiles) {
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t total = n_rb * n_ch * 128;
+  const int64_t total = n_rb * n_ch * 64;
   if (tid >= total) return;
-  const int hl = (int)(tid & 1), g = (int)((tid >> 1) & 7), rt = (int)((tid >> 4) & 7);
-  const int64_t tile = tid >> 7, rb = tile / n_ch, c = tile % n_ch;
-  const int64_t row = rb * 128 + rt * 16 + g + 8 * hl;
-  const int64_t nsb = n_cols / 256;
-  uint32_t out = 0;
-  if (row < n_rows) {
-    const uint8_t* blk = raw + (row * nsb + (c >> 2)) * 144;
-    const int a = 2 * (int)(c & 3);
-    uint32_t sa, ma, sb, mb;
-    q4k_unpack(blk + 4, a, sa, ma);
-    q4k_unpack(blk + 4, a + 1, sb, mb);
-    out = sa | (sb << 8) | (ma << 16) | (mb << 24);
+  const int g = (int)(tid & 7), rt = (int)((tid >> 3) & 7);
+  const int64_t tile = tid >> 6, rb = tile / n_ch, c = tile % n_ch;
+  uint32_t w[2] = {0u, 0u};
+  if (dtype == SG_DTYPE_Q4_0) {
+    const int64_t nb = n_cols / 32;
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk)
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl) {
+        const int64_t row = rb * 128 + rt * 16 + g + 8 * hl;
+        const int64_t b = c * 2 + blk;
+        uint32_t d = 0;
+        if (row < n_rows && b < nb) {
+          const uint8_t* p = raw + (row * nb + b) * 18;
+          d = (uint32_t)p[0] | ((uint32_t)p[1] << 8);
+        }
+        w[blk] |= d << (16 * hl);
+      }
+  } else {
+    const int64_t nsb = n_cols / 256;
+#pragma unroll
+    for (int hl = 0; hl < 2; ++hl) {
+      const int64_t row = rb * 128 + rt * 16 + g + 8 * hl;
+      if (row < n_rows) {
+        const uint8_t* blk = raw + (row * nsb + (c >> 2)) * 144;
+        const int a = 2 * (int)(c & 3);
+        uint32_t sa, ma, sb, mb;
+        q4k_unpack(blk + 4, a, sa, ma);
+        q4k_unpack(blk + 4, a + 1, sb, mb);
+        w[hl] = sa | (sb << 8) | (ma << 16) | (mb << 24);
+      }
+    }
   }
-  scm[tid] = out;
+  *reinterpret_cast<uint2*>(tiles + tile * SG_TILE_BYTES + SG_TILE_SC_OFF + (rt * 8 + g) * 8) = make_uint2(w[0], w[1]);
 }
 
 // Q4_K dd: one thread per (rb, superblock, rt, g, hl).
@@ -142,19 +135,20 @@ __global__ void dequant_kernel(SgDevWeight w, float* __restrict__ dst, int64_t l
   const int r = (int)(row & 127);
   const int64_t c = k0 >> 6;
   const int kk0 = (int)(k0 & 63);
-  const uint32_t* tile = w.qs + (rb * w.n_ch + c) * 1024;
+  const uint8_t* tile = w.tiles + (rb * w.n_ch + c) * SG_TILE_BYTES;
   const int rt = r >> 4, g = r & 7, hl = (r >> 3) & 1;
+  const uint32_t* scw = reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF) + (rt * 8 + g) * 2;
   float out[8];
   if (w.dtype == SG_DTYPE_Q4_0) {
-    const __half* sc = reinterpret_cast<const __half*>(w.sc) + (rb * w.n_ch + c) * 256;
-    const float d = __half2float(sc[rt * 32 + g * 4 + (kk0 >> 5) * 2 + hl]);
+    const uint32_t dw = scw[kk0 >> 5];
+    const float d = __half2float(__ushort_as_half((unsigned short)(hl ? (dw >> 16) : (dw & 0xFFFFu))));
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int q = (int)tile_nibble(tile, r, kk0 + i);
       out[i] = __fmul_rn((float)(q - 8), d);
     }
   } else {
-    const uint32_t scm = reinterpret_cast<const uint32_t*>(w.sc)[(rb * w.n_ch + c) * 128 + rt * 16 + g * 2 + hl];
+    const uint32_t scm = scw[hl];
     const uint32_t ddw = w.dd[(rb * w.n_sb + (c >> 2)) * 128 + rt * 16 + g * 2 + hl];
     const float d = __half2float(__ushort_as_half((unsigned short)(ddw & 0xFFFFu)));
     const float dmin = __half2float(__ushort_as_half((unsigned short)(ddw >> 16)));
@@ -179,8 +173,8 @@ inline unsigned nblocks(int64_t n, int t) { return (unsigned)((n + t - 1) / t); 
 size_t sg_layout_bytes(int dtype, int64_t n_rows, int64_t n_cols) {
   const int64_t n_rb = (n_rows + 127) / 128;
   const int64_t n_ch = (n_cols + 63) / 64;
-  size_t b = (size_t)(n_rb * n_ch) * (SG_CHUNK_QS + SG_CHUNK_SC);
-  if (dtype == SG_DTYPE_Q4_K) b += (size_t)(n_rb * (n_cols / 256)) * SG_SB_DD;
+  size_t b = (size_t)(n_rb * n_ch) * SG_TILE_BYTES;
+  if (dtype == SG_DTYPE_Q4_K) b += (size_t)(n_rb * (n_cols / 256)) * 512;
   return b;
 }
 
@@ -191,17 +185,11 @@ int sg_layout_alloc(SgDevWeight* w, int dtype, int64_t n_rows, int64_t n_cols) {
   w->n_rb = (n_rows + 127) / 128;
   w->n_ch = (n_cols + 63) / 64;
   w->n_sb = dtype == SG_DTYPE_Q4_K ? n_cols / 256 : 0;
-  w->qs = nullptr;
-  w->sc = nullptr;
+  w->tiles = nullptr;
   w->dd = nullptr;
-  const size_t qs_bytes = (size_t)(w->n_rb * w->n_ch) * SG_CHUNK_QS;
-  const size_t sc_bytes = (size_t)(w->n_rb * w->n_ch) * SG_CHUNK_SC;
-  const size_t dd_bytes = (size_t)(w->n_rb * w->n_sb) * SG_SB_DD;
-  if (cudaMalloc(&w->qs, qs_bytes) != cudaSuccess) return -1;
-  if (cudaMalloc(&w->sc, sc_bytes) != cudaSuccess) {
-    sg_layout_free(w);
-    return -1;
-  }
+  const size_t tile_bytes = (size_t)(w->n_rb * w->n_ch) * SG_TILE_BYTES;
+  const size_t dd_bytes = (size_t)(w->n_rb * w->n_sb) * 512;
+  if (cudaMalloc(&w->tiles, tile_bytes) != cudaSuccess) return -1;
   if (dd_bytes && cudaMalloc(&w->dd, dd_bytes) != cudaSuccess) {
     sg_layout_free(w);
     return -1;
@@ -210,11 +198,9 @@ int sg_layout_alloc(SgDevWeight* w, int dtype, int64_t n_rows, int64_t n_cols) {
 }
 
 void sg_layout_free(SgDevWeight* w) {
-  if (w->qs) cudaFree(w->qs);
-  if (w->sc) cudaFree(w->sc);
+  if (w->tiles) cudaFree(w->tiles);
   if (w->dd) cudaFree(w->dd);
-  w->qs = nullptr;
-  w->sc = nullptr;
+  w->tiles = nullptr;
   w->dd = nullptr;
 }
 
@@ -222,15 +208,11 @@ cudaError_t sg_layout_repack(const SgDevWeight* w, const uint8_t* raw_dev, cudaS
   const int T = 256;
   const int64_t nq = w->n_rb * w->n_ch * 256;
   repack_qs_kernel<<<nblocks(nq, T), T, 0, st>>>(w->dtype, raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch,
-                                                 w->qs);
-  if (w->dtype == SG_DTYPE_Q4_0) {
-    const int64_t ns = w->n_rb * w->n_ch * 64;
-    repack_q4_0_scales_kernel<<<nblocks(ns, T), T, 0, st>>>(raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch,
-                                                            reinterpret_cast<uint16_t*>(w->sc));
-  } else {
-    const int64_t ns = w->n_rb * w->n_ch * 128;
-    repack_q4k_scm_kernel<<<nblocks(ns, T), T, 0, st>>>(raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch,
-                                                        reinterpret_cast<uint32_t*>(w->sc));
+                                                 w->tiles);
+  const int64_t ns = w->n_rb * w->n_ch * 64;
+  repack_scales_kernel<<<nblocks(ns, T), T, 0, st>>>(w->dtype, raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch,
+                                                     w->tiles);
+  if (w->dtype == SG_DTYPE_Q4_K) {
     const int64_t nd = w->n_rb * w->n_sb * 128;
     repack_q4k_dd_kernel<<<nblocks(nd, T), T, 0, st>>>(raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_sb, w->dd);
   }

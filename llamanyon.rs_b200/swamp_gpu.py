@@ -150,7 +150,7 @@ class SwampGpu:
     def register(self, blocks: np.ndarray, dtype: int, n_rows: int, n_cols: int,
                  tp_mode: int = SG_TP_REPLICATE) -> Weight:
         blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
-        if blocks.size < n_rows * row_bytes(dtype, n_cols):
+        if dtype in BLOCK and blocks.size < n_rows * row_bytes(dtype, n_cols):
             raise SwampGpuError(-1, f"blocks hold {blocks.size} bytes, tensor needs {n_rows * row_bytes(dtype, n_cols)}")
         h = ctypes.c_void_p()
         self._check(self.L.sg_weight_register(blocks.ctypes.data, dtype, n_rows, n_cols, tp_mode, ctypes.byref(h)))
