@@ -100,6 +100,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int ta
   return false;
 }
 
+// Drain wait used on the error path: waits (bounded, ignoring the error flag)
+// for a phase whose asynchronous copies or MMAs are still in flight, so that
+// none of them lands after the CTA has released its shared memory or TMEM.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > SG_WAIT_NS) return false;
+  }
+}
+
 // ------------------------------------------------------------ bulk copies
 // 1-D bulk async copy global -> shared, completion counted on an mbarrier.
 // Both addresses 16-byte aligned, size a multiple of 16.

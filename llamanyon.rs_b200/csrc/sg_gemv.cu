@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(SgGemvParams
   // none lands after the CTA has exited
   if (!ok)
     for (int j = i; j < issued; ++j)
-      if (!mbar_wait(&bars[j % kStages], (j / kStages) & 1, 7)) break;
+      if (!mbar_wait_drain(&bars[j % kStages], (j / kStages) & 1)) break;
   pdl_launch_dependents();
 
   // ---- results: value of (row-tile r, half hl, n-tile nn, column jc) and its batch

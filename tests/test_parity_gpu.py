@@ -97,6 +97,50 @@ def test_prefill_batches(gpu, oracle, dtype, batch):
         W.free()
 
 
+@pytest.mark.parametrize("dtype,n,k,m", [
+    (Q40, 200, 352, 300),   # K % 64 == 32 (half-padded chunk), two token tiles, ragged last tile
+    (Q40, 77, 64, 33),      # one chunk, ragged rows
+    (Q4K, 129, 256, 257),   # one super-block, 257 tokens (one token in the second tile)
+    (Q4K, 300, 768, 100),
+])
+def test_prefill_shapes(gpu, oracle, dtype, n, k, m):
+    w = _weights(oracle, dtype, n, k, tid=6)
+    x = oracle.gen_x(SEED, 300 + m, (m, k))
+    W = gpu.register(w, dtype, n, k)
+    try:
+        y = gpu.linear(W, x)
+        ref, l2 = reference_outputs(oracle, dtype, w, x, n, k)
+        reference_gate(y, ref, l2)
+    finally:
+        W.free()
+
+
+@pytest.mark.parametrize("dtype", [Q40, Q4K])
+def test_prefill_device_strided_accumulate(gpu, oracle, dtype):
+    """Device entry, batch > 16: padded leading dimensions, y += W x (split-K
+    reduction onto existing values), and two calls in a row on one stream."""
+    torch = pytest.importorskip("torch")
+    n, k, m = 256, 2048, 40
+    w = _weights(oracle, dtype, n, k, tid=21)
+    x = oracle.gen_x(SEED, 21, (m, k))
+    W = gpu.register(w, dtype, n, k)
+    try:
+        ldx, ldy = k + 4, n + 3
+        xd = torch.zeros((m, ldx), dtype=torch.float32, device="cuda")
+        xd[:, :k] = torch.from_numpy(x)
+        y0 = torch.linspace(-2, 2, m * ldy, device="cuda").reshape(m, ldy)
+        yd = y0.clone()
+        gpu.linear_device(W, xd.data_ptr(), ldx, yd.data_ptr(), ldy, m, flags=2)  # SG_FLAG_ACCUMULATE
+        gpu.linear_device(W, xd.data_ptr(), ldx, yd.data_ptr(), ldy, m, flags=2)
+        torch.cuda.synchronize()
+        got = (yd - y0).cpu().numpy()
+        ref, l2 = reference_outputs(oracle, dtype, w, x, n, k)
+        reference_gate(got[:, :n] / 2, ref, l2)
+        assert np.array_equal(got[:, n:], np.zeros((m, ldy - n), np.float32))  # padding untouched
+    finally:
+        W.free()
+
+
 def test_activation_ranges(gpu, oracle):
     """Large, tiny and mixed-magnitude activations (the f16 split is rescaled per column)."""
     n, k = 96, 512
