@@ -124,6 +124,31 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch, from an ncu
+# capture of the current kernels (None where no capture exists yet):
+# decode GEMV 4096->11008 batch 1 (algorithmic 25,406,976 B); prefill GEMM
+# Q4_K 4096->14336 M=512 (algorithmic weight + activation bytes 41,418,752 B).
+NCU_TRAFFIC = {"gemv_4096x11008_b1": 25_406_976, "gemm_q4k_4096x14336_m512": 43_897_600}
+
+
+def measured_tensor_peak():
+    """(burst, sustained) dense bf16 TFLOP/s and where they come from."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    return 1590.0, 1400.0, "fallback"
+
+
+# configs[2]: Q4_K prefill at M=512 over the Llama-3-8B linear shapes (K, N)
+PREFILL_M = 512
+PREFILL_SHAPES = [(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)]
+
+
+def prefill_flops():
+    return sum(2 * PREFILL_M * n * k for k, n in PREFILL_SHAPES)
+
+
 # ---------------------------------------------------------------------------
 # reference arm / CPU baseline
 # ---------------------------------------------------------------------------
@@ -150,6 +175,31 @@ def cpu_sample(threads, seconds_budget=20.0, max_calls=None):
         if el > seconds_budget or (max_calls and calls >= max_calls):
             break
     return nbytes / el / 1e9, calls, el
+
+
+def cpu_prefill_sample(threads, seconds_budget=8.0):
+    """The reference's batched Q4_K path (fused_gemv_q4k_batched, scalar
+    order; swamp-engine forward_linear_batch) on a token/row sample of the
+    configs[2] shapes. Returns (GFLOP/s, sample description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.build()
+    toks, rows = 16, 512
+    ws = [(k, oracle.gen_weight(Q4K, SEED, 700 + i, rows, k)) for i, (k, _) in enumerate(PREFILL_SHAPES)]
+    xs = {k: oracle.gen_x(SEED, 800 + k, (toks, k)) for k, _ in PREFILL_SHAPES}
+    oracle.forward_linear_batch(Q4K, ws[0][1], xs[ws[0][0]], rows, ws[0][0], threads)  # page-in
+    t0 = time.perf_counter()
+    flops, calls = 0, 0
+    while True:
+        for k, w in ws:
+            oracle.forward_linear_batch(Q4K, w, xs[k], rows, k, threads)
+            flops += 2 * toks * rows * k
+            calls += 1
+        el = time.perf_counter() - t0
+        if el > seconds_budget:
+            break
+    return flops / el / 1e12, (f"{calls} forward_linear_batch calls (Q4_K, {toks} tokens x {rows} rows of each "
+                               f"configs[2] shape) in {el:.1f} s on {threads} host threads")
 
 
 def reference_arm(args):
@@ -365,6 +415,9 @@ def gpu_arm(args):
     achieved = tot_by / (tot_us * 1e-6) / 1e9
     peak, peak_kind = measured_peaks()
 
+    # ---------------------------------------------- prefill
+    prefill = prefill_bench(torch, gpu, oracle, st, args) if world == 1 and not args.no_prefill else None
+
     # -------------------------------------------------------------- e2e
     # the public host-pointer C ABI: x copied in and y read back on every call
     e2e = None
@@ -415,13 +468,15 @@ def gpu_arm(args):
                                     f"({copies * layer_b / world / 1e6:.0f} MB per GPU vs L2 {l2 / 1e6:.0f} MB)",
                        "bytes_per_step": step_bytes(n_layers)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC["gemv_4096x11008_b1"],
+                         "traffic_launch": "4096x11008 batch 1 (algorithmic 25,406,976 B)", "peak_kind": peak_kind,
                          "kernel": "gemv_kernel (one launch per GEMV), back-to-back launches in a CUDA graph",
                          "per_shape_gbs": per_shape},
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": calls_per_step * kernels_per_call * args.steps,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     graphs = None
@@ -434,6 +489,60 @@ def gpu_arm(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def prefill_bench(torch, gpu, oracle, st, args):
+    """Q4_K prefill GEMM, M=512, the four Llama-3-8B shapes. Two
+    rotating weight copies per shape (156 MB > L2); each shape timed as a CUDA
+    graph of back-to-back calls. TFLOP/s counts 2*M*N*K (one product); the
+    kernel issues three bf16 products per k-step (hi/lo operand split), so the
+    tensor pipe does 3x that work."""
+    import numpy as np
+    copies = 2
+    M = PREFILL_M
+    ws = {(k, n): [gpu.register(oracle.gen_weight(Q4K, SEED, 2000 + 8 * c + i, n, k), Q4K, n, k)
+                   for c in range(copies)] for i, (k, n) in enumerate(PREFILL_SHAPES)}
+    x = torch.randn(M, 14336, device="cuda")
+    y = torch.empty(M, 14336, device="cuda")
+    reps = max(3, min(50, args.prefill_reps))
+    per_shape, tot_us = {}, 0.0
+    for (k, n), wl in ws.items():
+        def one(wl=wl, k=k, n=n):
+            stp = torch.cuda.current_stream().cuda_stream
+            for w in wl * 2:
+                gpu.linear_device(w, x.data_ptr(), k, y.data_ptr(), n, M, stream=stp)
+        one()  # eager first call: scratch, kernel attributes
+        torch.cuda.synchronize()
+        g = graph_of(torch, one)
+        for _ in range(3):
+            g.replay()
+        ms = time_graphs(torch, [g], reps, st)
+        us = ms * 1e3 / (reps * 2 * copies)
+        tot_us += us
+        per_shape[f"{k}x{n}"] = {"us": round(us, 2), "tflops": round(2 * M * n * k / us / 1e6, 1)}
+        del g
+    achieved = prefill_flops() / tot_us / 1e6
+    burst, sustained, kind = measured_tensor_peak()
+    cpu = None
+    if not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        tf, sample = cpu_prefill_sample(threads, seconds_budget=min(8.0, args.cpu_seconds))
+        cpu = {"value": round(tf * 1e3, 3), "unit": "GFLOP/s", "cores": threads, "kind": "port", "sample": sample}
+    for wl in ws.values():
+        for w in wl:
+            w.free()
+    return {"metric": "Q4_K prefill GEMM TFLOP/s (configs[2]: Llama-3-8B linears, M=512)",
+            "value": round(achieved, 1), "unit": "TFLOP/s", "flops_per_pass": prefill_flops(),
+            "us_per_pass": round(tot_us, 1), "per_shape": per_shape,
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": burst, "unit": "TFLOP/s",
+                         "frac": round(achieved / burst, 4), "peak_kind": f"{kind} bf16 dense burst",
+                         "tensor_pipe_frac": round(3 * achieved / burst, 4),
+                         "traffic": NCU_TRAFFIC["gemm_q4k_4096x14336_m512"],
+                         "traffic_launch": "4096x14336 M=512 (weights 33.0 MB + bf16 hi/lo x 8.4 MB)",
+                         "kernel": "gemm_kernel (tcgen05 M128 N256 K16 bf16, 3 products per k-step) "
+                                   "+ gemm_xprep_kernel"},
+            "cpu_baseline": cpu,
+            "gpu_launches_per_call": 2}
 
 
 def profile_arm(args):
@@ -480,6 +589,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--profile", default=None, help="K,N,B: single-shape eager launches (for ncu)")
     ap.add_argument("--dtype", default="q4_0", choices=["q4_0", "q4k"])
+    ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] prefill measurement")
+    ap.add_argument("--prefill-reps", type=int, default=20)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -28,7 +28,8 @@
  *    (fused_gemv_q4k.rs:696).
  *  - Numerics: dequantized weights are bit-identical to swamp-gguf's. GEMV /
  *    GEMM outputs accumulate in f32 with activations split into two 16-bit
- *    parts; the tested bound is |y - y_ref| <= 1e-3 * max(|y_ref|, ||w.*x||_2)
+ *    parts (the prefill GEMM splits the dequantized weights the same way);
+ *    the tested bound is |y - y_ref| <= 1e-3 * max(|y_ref|, ||w.*x||_2)
  *    per element against the reference's f32 result.
  *  - Thread safety: calls are serialised on an internal mutex per library
  *    instance; each device has one stream. Calls may come from any host
@@ -105,6 +106,13 @@ SG_API int sg_topology(int *rank, int *world, int *local_devices);
 SG_API int sg_weight_register(const void *host_blocks, int dtype, int64_t n_rows, int64_t n_cols,
                        int tp_mode, sg_weight_t *out);
 SG_API int sg_weight_free(sg_weight_t w);
+/* The slice rank `rank` of `world` holds under tp_mode, computed on the host
+ * (no GPU or init needed): rows [row0, row0+rows) and columns
+ * [col0, col0+cols). Column split: rows [rank*N/world, (rank+1)*N/world);
+ * row split: whole blocks [rank*nblk/world, (rank+1)*nblk/world) of every
+ * row (nblk = n_cols/32 or /256). Same validation as sg_weight_register. */
+SG_API int sg_tp_shard(int dtype, int64_t n_rows, int64_t n_cols, int tp_mode, int world, int rank,
+                       int64_t *row0, int64_t *rows, int64_t *col0, int64_t *cols);
 /* shape of the shard this rank holds: local rows/cols and their offsets */
 SG_API int sg_weight_shard(sg_weight_t w, int local_device, int64_t *n_rows, int64_t *n_cols,
                     int64_t *row0, int64_t *col0);

@@ -132,6 +132,41 @@ namespace {
 int64_t block_of(int dtype) { return dtype == SG_DTYPE_Q4_0 ? 32 : 256; }
 int64_t block_bytes(int dtype) { return dtype == SG_DTYPE_Q4_0 ? 18 : 144; }
 
+// The slice of an n_rows x n_cols tensor that rank R of W holds: column split
+// (SG_TP_COLUMN) takes rows [R*N/W, (R+1)*N/W); row split (SG_TP_ROW) takes
+// whole blocks [R*nblk/W, (R+1)*nblk/W) of every row; replicate takes all.
+// Returns SG_OK or SG_ERR_INVALID_ARG / SG_ERR_UNSUPPORTED with a message.
+int shard_plan(int dtype, int64_t n_rows, int64_t n_cols, int tp_mode, int W, int R, int64_t* row0, int64_t* nr,
+               int64_t* col0, int64_t* nc) {
+  if (dtype != SG_DTYPE_Q4_0 && dtype != SG_DTYPE_Q4_K)
+    return fail(SG_ERR_UNSUPPORTED, "dtype %d not supported (Q4_0=2, Q4_K=12)", dtype);
+  if (n_rows <= 0 || n_cols <= 0)
+    return fail(SG_ERR_INVALID_ARG, "empty tensor %lld x %lld", (long long)n_rows, (long long)n_cols);
+  const int64_t bs = block_of(dtype);
+  if (n_cols % bs)
+    return fail(SG_ERR_INVALID_ARG, "n_cols %lld not a multiple of %lld", (long long)n_cols, (long long)bs);
+  if (tp_mode < SG_TP_REPLICATE || tp_mode > SG_TP_ROW) return fail(SG_ERR_INVALID_ARG, "bad tp_mode %d", tp_mode);
+  if (W < 1 || R < 0 || R >= W) return fail(SG_ERR_INVALID_ARG, "rank %d of world %d", R, W);
+  const int64_t nblk = n_cols / bs;
+  if (tp_mode == SG_TP_ROW && nblk < W)
+    return fail(SG_ERR_INVALID_ARG, "row split: %lld blocks < %d ranks", (long long)nblk, W);
+  if (tp_mode == SG_TP_COLUMN && n_rows < W)
+    return fail(SG_ERR_INVALID_ARG, "column split: %lld rows < %d ranks", (long long)n_rows, W);
+  *row0 = 0;
+  *col0 = 0;
+  *nr = n_rows;
+  *nc = n_cols;
+  if (tp_mode == SG_TP_COLUMN) {
+    *row0 = (int64_t)R * n_rows / W;
+    *nr = (int64_t)(R + 1) * n_rows / W - *row0;
+  } else if (tp_mode == SG_TP_ROW) {
+    const int64_t b0 = (int64_t)R * nblk / W, b1 = (int64_t)(R + 1) * nblk / W;
+    *col0 = b0 * bs;
+    *nc = (b1 - b0) * bs;
+  }
+  return SG_OK;
+}
+
 int ensure_buf(void** p, size_t* have, size_t need) {
   if (*have >= need) return SG_OK;
   if (*p) cudaFree(*p);
@@ -446,17 +481,14 @@ int sg_weight_register(const void* host_blocks, int dtype, int64_t n_rows, int64
   std::lock_guard<std::mutex> lk(g_ctx.mu);
   if (!g_ctx.inited) return fail(SG_ERR_NOT_INITIALIZED, "sg_init not called");
   if (!host_blocks || !out) return fail(SG_ERR_INVALID_ARG, "null pointer");
-  if (dtype != SG_DTYPE_Q4_0 && dtype != SG_DTYPE_Q4_K)
-    return fail(SG_ERR_UNSUPPORTED, "dtype %d not supported (Q4_0=2, Q4_K=12)", dtype);
-  if (n_rows <= 0 || n_cols <= 0) return fail(SG_ERR_INVALID_ARG, "empty tensor %lld x %lld", (long long)n_rows,
-                                              (long long)n_cols);
-  const int64_t bs = block_of(dtype), bb = block_bytes(dtype);
-  if (n_cols % bs) return fail(SG_ERR_INVALID_ARG, "n_cols %lld not a multiple of %lld", (long long)n_cols, (long long)bs);
-  if (tp_mode < SG_TP_REPLICATE || tp_mode > SG_TP_ROW) return fail(SG_ERR_INVALID_ARG, "bad tp_mode %d", tp_mode);
   const int W = g_ctx.world;
+  for (int R = 0; R < W; ++R) {  // validates the arguments for every rank's slice
+    int64_t r0, nr, c0, nc;
+    const int rc = shard_plan(dtype, n_rows, n_cols, tp_mode, W, R, &r0, &nr, &c0, &nc);
+    if (rc != SG_OK) return rc;
+  }
+  const int64_t bs = block_of(dtype), bb = block_bytes(dtype);
   const int64_t nblk = n_cols / bs;
-  if (tp_mode == SG_TP_ROW && nblk < W) return fail(SG_ERR_INVALID_ARG, "row split: %lld blocks < %d ranks", (long long)nblk, W);
-  if (tp_mode == SG_TP_COLUMN && n_rows < W) return fail(SG_ERR_INVALID_ARG, "column split: %lld rows < %d ranks", (long long)n_rows, W);
   const size_t row_bytes = (size_t)nblk * bb;
   auto* w = new sg_weight_s();
   w->dtype = dtype;
@@ -470,14 +502,7 @@ int sg_weight_register(const void* host_blocks, int dtype, int64_t n_rows, int64
     Shard s;
     s.dev_idx = (int)di;
     int64_t nr = n_rows, nc = n_cols;
-    if (tp_mode == SG_TP_COLUMN) {
-      s.row0 = (int64_t)R * n_rows / W;
-      nr = (int64_t)(R + 1) * n_rows / W - s.row0;
-    } else if (tp_mode == SG_TP_ROW) {
-      const int64_t b0 = (int64_t)R * nblk / W, b1 = (int64_t)(R + 1) * nblk / W;
-      s.col0 = b0 * bs;
-      nc = (b1 - b0) * bs;
-    }
+    shard_plan(dtype, n_rows, n_cols, tp_mode, W, R, &s.row0, &nr, &s.col0, &nc);
     cudaSetDevice(d.device);
     if (sg_layout_alloc(&s.w, dtype, nr, nc)) {
       cudaGetLastError();
@@ -530,6 +555,12 @@ int sg_weight_free(sg_weight_t w) {
   }
   delete w;
   return SG_OK;
+}
+
+int sg_tp_shard(int dtype, int64_t n_rows, int64_t n_cols, int tp_mode, int world, int rank, int64_t* row0,
+                int64_t* rows, int64_t* col0, int64_t* cols) {
+  if (!row0 || !rows || !col0 || !cols) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  return shard_plan(dtype, n_rows, n_cols, tp_mode, world, rank, row0, rows, col0, cols);
 }
 
 int sg_weight_shard(sg_weight_t w, int local_device, int64_t* n_rows, int64_t* n_cols, int64_t* row0, int64_t* col0) {

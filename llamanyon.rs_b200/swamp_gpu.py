@@ -33,7 +33,7 @@ BLOCK_BYTES = {SG_DTYPE_Q4_0: 18, SG_DTYPE_Q4_K: 144}
 # every symbol include/swamp_gpu.h declares
 EXPORTS = (
     "sg_init", "sg_get_unique_id", "sg_init_rank", "sg_shutdown", "sg_last_error", "sg_topology",
-    "sg_weight_register", "sg_weight_free", "sg_weight_shard", "sg_linear", "sg_linear_multi",
+    "sg_weight_register", "sg_weight_free", "sg_tp_shard", "sg_weight_shard", "sg_linear", "sg_linear_multi",
     "sg_linear_device", "sg_linear_multi_device", "sg_dequant_f32", "sg_fused_gemv_q4k",
     "sg_synchronize",
 )
@@ -58,6 +58,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     L.sg_topology.argtypes = [P, P, P]
     L.sg_weight_register.argtypes = [P, i32, i64, i64, i32, P]
     L.sg_weight_free.argtypes = [P]
+    L.sg_tp_shard.argtypes = [i32, i64, i64, i32, i32, i32, P, P, P, P]
     L.sg_weight_shard.argtypes = [P, i32, P, P, P, P]
     L.sg_linear.argtypes = [P, P, P, i32, i32]
     L.sg_linear_multi.argtypes = [P, i32, P, P, i32]
@@ -119,6 +120,12 @@ class SwampGpu:
     def _check(self, rc: int):
         if rc != SG_OK:
             raise SwampGpuError(rc, self.L.sg_last_error().decode(errors="replace"))
+
+    def tp_shard(self, dtype: int, n_rows: int, n_cols: int, tp_mode: int, world: int, rank: int):
+        """(row0, rows, col0, cols) of rank's slice; host-only, needs no GPU."""
+        v = [ctypes.c_int64() for _ in range(4)]
+        self._check(self.L.sg_tp_shard(dtype, n_rows, n_cols, tp_mode, world, rank, *[ctypes.byref(a) for a in v]))
+        return tuple(a.value for a in v)
 
     # ---------------------------------------------------------- setup
     def init(self, n_gpus: int = 1):
