@@ -74,7 +74,7 @@ struct DevState {
   int num_sms = 0;
   cudaStream_t stream = nullptr;
   ncclComm_t comm = nullptr;
-  void* scratch = nullptr;  // prefill GEMM scratch (grows on demand)
+  void* scratch = nullptr;  // activation scratch of the GEMV / GEMM kernels (grows on demand)
   size_t scratch_bytes = 0;
   float* xbuf = nullptr;  // staging for host-pointer calls
   size_t xbuf_bytes = 0;
@@ -254,10 +254,18 @@ int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* 
   const int64_t K = ws[0]->n_cols;
   if (((uintptr_t)x & 15) || (ldx & 3))
     return fail(SG_ERR_INVALID_ARG, "x must be 16-byte aligned with a row stride that is a multiple of 4 floats");
-  if (batch <= 16) {
-    SgGemvMat mats[SG_GEMV_MAX_MATS];
-    for (int i = 0; i < n_w; ++i) mats[i] = {ws[i], ys[i], ldys[i]};
-    CUDA_TRY(sg_gemv(mats, n_w, x, ldx, batch, accumulate, d.num_sms, st));
+  if (batch <= SG_GEMV_MAX_BATCH) {
+    int rc = ensure_buf(&d.scratch, &d.scratch_bytes, sg_gemv_scratch_bytes(K));
+    if (rc) return rc;
+    // one launch per run of consecutive same-dtype matrices
+    for (int i0 = 0; i0 < n_w;) {
+      int i1 = i0 + 1;
+      while (i1 < n_w && i1 - i0 < SG_GEMV_MAX_MATS && ws[i1]->dtype == ws[i0]->dtype) ++i1;
+      SgGemvMat mats[SG_GEMV_MAX_MATS];
+      for (int i = i0; i < i1; ++i) mats[i - i0] = {ws[i], ys[i], ldys[i]};
+      CUDA_TRY(sg_gemv(mats, i1 - i0, x, ldx, batch, accumulate, d.scratch, d.scratch_bytes, d.num_sms, st));
+      i0 = i1;
+    }
     return SG_OK;
   }
   // prefill GEMM: one launch per matrix

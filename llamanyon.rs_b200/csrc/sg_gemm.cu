@@ -4,35 +4,42 @@
 // Replaces swamp-kernels fused_gemv_q4k_batched (fused_gemv_q4k.rs:527-698),
 // which the engine's prefill issues through forward_linear_batch
 // (swamp-engine/src/linear.rs:176-239, executor.rs:106-181):
-//   y[t][r] = sum_k W[r][k] x[t][k],  W dequantized exactly as swamp-gguf.
+//   y[t][r] = sum_k W[r][k] x[t][k],  W dequantized as swamp-gguf does.
 //
 // Precision: the reference computes in f32. A Q4_K weight needs up to 24
 // significant bits and an activation 24, neither fits one 16-bit operand, and
 // a single bf16 product errs by ~2^-9 -- far outside the 1e-3 parity bound. So
-// both operands are split exactly into bf16 hi + lo parts (16 bits each; Q4_0
-// weights have at most 15 bits and split without error) and every k-step runs
-// three MMAs: A_hi*X_hi + A_hi*X_lo + A_lo*X_hi (A_lo*X_lo is ~2^-16 relative
-// and dropped), all accumulating in f32 in TMEM.
+// both operands are split into bf16 hi + lo parts and every k-step runs three
+// MMAs: A_hi*X_hi + A_hi*X_lo + A_lo*X_hi (A_lo*X_lo is ~2^-16 relative and
+// dropped), all accumulating in f32 in TMEM. The weight split truncates (hi =
+// top 16 bits of the f32, lo = the exact remainder rounded to bf16: error
+// <= 2^-15 relative); the activation split rounds.
 //
 // Two kernels, chained with programmatic dependent launch:
-//  1. gemm_xprep: x (f32) -> X_hi, X_lo (bf16, [m][K]) in scratch; zeroes y
-//     when the K dimension is split across CTAs.
-//  2. gemm_kernel: one CTA per (128-row block, 256-token tile, K slice).
+//  1. gemm_xprep_kernel: x (f32) -> X_hi, X_lo (bf16, [m][K]) in scratch;
+//     zeroes the output tiles that more than one CTA reduces into.
+//  2. gemm_kernel: persistent, one CTA per SM. Work = tiles of 128 weight
+//     rows x 256 tokens, each a run of 64-wide K chunks. Whole tiles are dealt
+//     round-robin (data parallel); the tiles left over are cut into equal
+//     chunk ranges across all CTAs (stream-K), so every SM gets the same work.
 //     warp 0     producer: TMA 2-D loads of X_hi/X_lo tiles (32 K x 256
 //                tokens, 64-byte swizzle) and bulk copies of the packed
-//                weight tiles (4.5 KB per 64-wide chunk, + Q4_K d|dmin).
-//     warp 1     allocates 256 TMEM columns; one thread issues tcgen05.mma
-//                (M=128, N=256, K=16, bf16 -> f32) and tcgen05.commit.
-//     warps 2-5  dequantize each 128 x 32 weight slab to exact f32, split it
-//                into bf16 hi/lo and write both straight into the UMMA
-//                K-major 64-byte-swizzled layout; then the epilogue: tcgen05.ld
-//                of the accumulator, stores (or red.add for split K) to y.
+//                weight tiles (4.5 KB per 128 x 64, + Q4_K d|dmin).
+//     warp 1     allocates 512 TMEM columns (two 128 x 256 f32
+//                accumulators); one thread issues tcgen05.mma (M=128, N=256,
+//                K=16, bf16 -> f32) and tcgen05.commit.
+//     warps 2-5  dequantize: one weight row per thread, 32 K per stage,
+//                exact f32 via FMA from the f16 magic-number decode, split
+//                into bf16 hi/lo, 16-byte stores into the swizzled A tiles.
+//     warps 6-9  epilogue: tcgen05.ld of the finished accumulator (while the
+//                MMAs fill the other one), stores -- or red.add for a tile
+//                shared with another CTA.
 //  Four 48 KB stages (A_hi, A_lo, X_hi, X_lo) + a 3-chunk raw weight ring.
 //  Every mbarrier wait is bounded (sg_common.cuh).
 #include <algorithm>
-#include <mutex>
 
 #include "sg_gemm.cuh"
+#include "sg_tc.cuh"
 
 namespace gemm_tc {
 
@@ -44,62 +51,48 @@ constexpr int X_BYTES = BN * BK * 2;  // 16 KB
 constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * X_BYTES;
 constexpr int RAW_BYTES = SG_TILE_BYTES + 512;
 constexpr int SMEM_BYTES = kS * STAGE_BYTES + kR * RAW_BYTES + 1024;  // + alignment slack
-constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kIdesc = sg_idesc_bf16(BM, BN);
 
 struct GemmParams {
   const uint8_t* tiles;
   const uint32_t* dd;
   int dtype;
-  int n_rows, n_cols, n_ch, n_sb;
-  int m;       // tokens
-  int n_tt;    // token tiles
-  int split;   // K slices
+  int n_rows, n_ch, n_sb;
+  int m;      // tokens
+  int n_tt;   // token tiles
+  int dp;     // whole tiles per CTA (data-parallel rounds)
+  int64_t rem_iters;  // chunk iterations of the leftover tiles, shared by all CTAs
   int accumulate;
   float* y;
   int64_t ldy;
 };
 
-// UMMA shared-memory descriptor: K-major, 64-byte swizzle, 8-row atoms 512 B apart.
-__device__ __forceinline__ uint64_t sdesc_sw64(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1 << 16;           // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(512 >> 4) << 32;  // stride byte offset: 8 rows x 64 B
-  d |= (uint64_t)1 << 46;           // descriptor version (sm_100)
-  d |= (uint64_t)4 << 61;           // SWIZZLE_64B
-  return d;
-}
-
-// instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major, M = 128, N = 256
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// byte offset of element (row, k) in a K-major 64-byte-swizzled tile (rows of 32 bf16)
-__device__ __forceinline__ uint32_t sw64_off(int row, int k) {
-  return (uint32_t)((row >> 3) * 512 + (row & 7) * 64 + ((((k >> 3) ^ (row >> 1)) & 3) << 4) + (k & 7) * 2);
+// The CTA's work as a sequence of segments (tile, chunk range). Every warp
+// walks the same sequence.
+template <typename F>
+__device__ __forceinline__ void for_each_segment(const GemmParams& p, F&& f) {
+  const int G = gridDim.x, c = blockIdx.x;
+  for (int s = 0; s < p.dp; ++s) f(c + s * G, 0, p.n_ch);
+  const int base = p.dp * G;
+  const int64_t it0 = (int64_t)c * p.rem_iters / G, it1 = (int64_t)(c + 1) * p.rem_iters / G;
+  for (int64_t it = it0; it < it1;) {
+    const int tile = base + (int)(it / p.n_ch);
+    const int k0 = (int)(it % p.n_ch);
+    const int64_t left = it1 - it;
+    const int k1 = left < (int64_t)(p.n_ch - k0) ? k0 + (int)left : p.n_ch;
+    f(tile, k0, k1);
+    it += k1 - k0;
+  }
 }
 
 // ---------------------------------------------------------------- x prep
 __global__ void __launch_bounds__(256) gemm_xprep_kernel(const float* __restrict__ x, int64_t ldx, int m, int K,
                                                           __nv_bfloat16* __restrict__ xh, __nv_bfloat16* __restrict__ xl,
-                                                          float* __restrict__ y, int64_t ldy, int n_rows, int zero_y) {
+                                                          GemmParams p, int G) {
   pdl_launch_dependents();
-  pdl_wait();
+  pdl_wait();  // scratch / y may still be in use by the previous kernel
   const int64_t n8 = (int64_t)m * (K / 8);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += stride) {
@@ -120,13 +113,33 @@ __global__ void __launch_bounds__(256) gemm_xprep_kernel(const float* __restrict
     *reinterpret_cast<uint4*>(xh + t * K + k) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     *reinterpret_cast<uint4*>(xl + t * K + k) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
-  if (zero_y) {
-    const int64_t tot = (int64_t)m * n_rows;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < tot; i += stride) {
-      const int64_t t = i / n_rows, r = i - t * n_rows;
-      y[t * ldy + r] = 0.f;
+  // zero the tiles that a stream-K boundary cuts (reduced with red.add):
+  // one warp per (boundary, 32-token slice of the tile)
+  if (!p.accumulate && p.rem_iters > 0) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarp = stride >> 5;
+    const int64_t tot = (int64_t)(G - 1) * (BN / 32);
+    for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < tot; i += nwarp) {
+      const int cb = 1 + (int)(i / (BN / 32)), ts = (int)(i % (BN / 32));
+      const int64_t it = (int64_t)cb * p.rem_iters / G;
+      if (it % p.n_ch == 0) continue;
+      const int tile = p.dp * G + (int)(it / p.n_ch);
+      const int rb = tile / p.n_tt, tt = tile % p.n_tt;
+      const int nr = min(BM, p.n_rows - rb * BM);
+      for (int j = 0; j < 32; ++j) {
+        const int tok = tt * BN + ts * 32 + j;
+        if (tok >= p.m) break;
+        float* yr = p.y + (int64_t)tok * p.ldy + (int64_t)rb * BM;
+        for (int r = lane; r < nr; r += 32) yr[r] = 0.f;
+      }
     }
   }
+}
+
+// byte offset of the 16-byte chunk j (8 K) of row r in a K-major
+// 64-byte-swizzled tile (rows of 32 elements, 8-row atoms of 512 B)
+__device__ __forceinline__ uint32_t sw64_chunk(int r, int j) {
+  return (uint32_t)((r >> 3) * 512 + (r & 7) * 64 + (((j ^ (r >> 1)) & 3) << 4));
 }
 
 // ---------------------------------------------------------------- GEMM
@@ -134,16 +147,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo, GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(8) uint64_t x_full[kS], a_full[kS], s_empty[kS], raw_full[kR], raw_empty[kR], acc_full;
+  __shared__ __align__(8) uint64_t x_full[kS], a_full[kS], s_empty[kS], raw_full[kR], raw_empty[kR], acc_full[2],
+      acc_empty[2];
   __shared__ uint32_t tmem_base_sh;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int per_rb = p.n_tt * p.split;
-  const int rb = blockIdx.x / per_rb;
-  const int rem = blockIdx.x - rb * per_rb;
-  const int tt = rem / p.split, ks = rem - tt * p.split;
-  const int c0 = (int)((int64_t)ks * p.n_ch / p.split), c1 = (int)((int64_t)(ks + 1) * p.n_ch / p.split);
-  const int nchunk = c1 - c0, nk = 2 * nchunk;
   uint8_t* raw_ring = smem + kS * STAGE_BYTES;
 
   if (threadIdx.x == 0) {
@@ -156,163 +164,203 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&raw_full[r], 1);
       mbar_init(&raw_empty[r], 4);
     }
-    mbar_init(&acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
     mbar_fence_init();
     prefetch_tensormap(&map_hi);
     prefetch_tensormap(&map_lo);
   }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
-                 "r"(kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  tc_fence_before();
+  if (warp == 1) sg_tmem_alloc(&tmem_base_sh, kTmemCols);
+  sg_tc_fence_before();
   __syncthreads();
-  tc_fence_after();
+  sg_tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
 
   if (warp == 0) {
     // ================================================================ producer
     if (lane == 0) {
       pdl_wait();  // X_hi/X_lo come from the activation-prep kernel
-      const int kx0 = 64 * c0, t0 = tt * BN;
-      int x_issued = 0, raw_issued = 0;
-      for (int kk = 0; kk < nk; ++kk) {
-        const int s = kk % kS;
-        if (kk >= kS && !mbar_wait(&s_empty[s], ((kk / kS) & 1) ^ 1, 0x11)) break;
-        uint8_t* st = smem + s * STAGE_BYTES;
-        mbar_arrive_expect_tx(&x_full[s], 2 * X_BYTES);
-        tma_load_2d(st + 2 * A_BYTES, &map_hi, kx0 + kk * BK, t0, &x_full[s]);
-        tma_load_2d(st + 2 * A_BYTES + X_BYTES, &map_lo, kx0 + kk * BK, t0, &x_full[s]);
-        x_issued = kk + 1;
-        if ((kk & 1) == 0) {
-          const int c = kk >> 1, r = c % kR;
-          if (c >= kR && !mbar_wait(&raw_empty[r], ((c / kR) & 1) ^ 1, 0x12)) break;
-          raw_issued = c + 1;
+      int g = 0, rc = 0;  // k-step and raw-chunk counters
+      bool ok = true;
+      for_each_segment(p, [&](int tile, int k0, int k1) {
+        if (!ok) return;
+        const int rb = tile / p.n_tt, tt = tile % p.n_tt;
+        for (int ch = k0; ch < k1 && ok; ++ch) {
+          const int r = rc % kR;
+          if (rc >= kR && !mbar_wait(&raw_empty[r], ((rc / kR) & 1) ^ 1, 0x12)) {
+            ok = false;
+            break;
+          }
           uint8_t* rw = raw_ring + r * RAW_BYTES;
-          const int ch = c0 + c;
           mbar_arrive_expect_tx(&raw_full[r], SG_TILE_BYTES + (p.dtype == SG_DTYPE_Q4_K ? 512 : 0));
           bulk_g2s(rw, p.tiles + ((int64_t)rb * p.n_ch + ch) * SG_TILE_BYTES, SG_TILE_BYTES, &raw_full[r]);
           if (p.dtype == SG_DTYPE_Q4_K)
             bulk_g2s(rw + SG_TILE_BYTES, p.dd + ((int64_t)rb * p.n_sb + (ch >> 2)) * 128, 512, &raw_full[r]);
+          ++rc;
+          for (int h = 0; h < 2; ++h) {
+            const int s = g % kS;
+            if (g >= kS && !mbar_wait(&s_empty[s], ((g / kS) & 1) ^ 1, 0x11)) {
+              ok = false;
+              break;
+            }
+            uint8_t* st = smem + s * STAGE_BYTES;
+            mbar_arrive_expect_tx(&x_full[s], 2 * X_BYTES);
+            tma_load_2d(st + 2 * A_BYTES, &map_hi, 64 * ch + BK * h, tt * BN, &x_full[s]);
+            tma_load_2d(st + 2 * A_BYTES + X_BYTES, &map_lo, 64 * ch + BK * h, tt * BN, &x_full[s]);
+            ++g;
+          }
         }
-      }
+      });
       if (*(volatile int*)&g_sg_error != 0) {
         // error path: let every copy still in flight land before the CTA exits
         // (each barrier has at most one phase outstanding)
-        for (int j = max(0, x_issued - kS); j < x_issued; ++j) mbar_wait_drain(&x_full[j % kS], (j / kS) & 1);
-        for (int j = max(0, raw_issued - kR); j < raw_issued; ++j)
-          mbar_wait_drain(&raw_full[j % kR], (j / kR) & 1);
+        for (int j = max(0, g - kS); j < g; ++j) mbar_wait_drain(&x_full[j % kS], (j / kS) & 1);
+        for (int j = max(0, rc - kR); j < rc; ++j) mbar_wait_drain(&raw_full[j % kR], (j / kR) & 1);
       }
     }
   } else if (warp == 1) {
     // ============================================================ MMA issuer
     if (lane == 0) {
-      for (int kk = 0; kk < nk; ++kk) {
-        const int s = kk % kS;
-        const uint32_t ph = (kk / kS) & 1;
-        if (!mbar_wait(&x_full[s], ph, 0x13) || !mbar_wait(&a_full[s], ph, 0x14)) break;
-        tc_fence_after();
-        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-        const uint64_t ah = sdesc_sw64(base), al = sdesc_sw64(base + A_BYTES);
-        const uint64_t xh = sdesc_sw64(base + 2 * A_BYTES), xl = sdesc_sw64(base + 2 * A_BYTES + X_BYTES);
-#pragma unroll
-        for (int j = 0; j < BK / 16; ++j) {
-          const uint64_t o = (uint64_t)(j * 32 >> 4);  // K step of 16 bf16 = 32 bytes
-          umma_bf16(tmem, ah + o, xh + o, (kk | j) ? 1u : 0u);
-          umma_bf16(tmem, ah + o, xl + o, 1u);
-          umma_bf16(tmem, al + o, xh + o, 1u);
-        }
-        umma_commit(&s_empty[s]);
-      }
-      umma_commit(&acc_full);  // fires when every MMA above has completed
-    }
-  } else {
-    // ====================================================== dequant warps
-    const int dw = warp - 2;
-    const int g = lane >> 2, t = lane & 3;
-    for (int kk = 0; kk < nk; ++kk) {
-      const int s = kk % kS, c = kk >> 1, h = kk & 1, r = c % kR;
+      int g = 0, seg = 0;
       bool ok = true;
-      if (h == 0) ok = mbar_wait(&raw_full[r], (c / kR) & 1, 0x15);
-      if (ok && kk >= kS) ok = mbar_wait(&s_empty[s], ((kk / kS) & 1) ^ 1, 0x16);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      const uint8_t* rw = raw_ring + r * RAW_BYTES;
-      uint8_t* a_hi = smem + s * STAGE_BYTES;
-      uint8_t* a_lo = a_hi + A_BYTES;
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int rt = 2 * dw + rr;
-        const uint2 wv = *reinterpret_cast<const uint2*>(rw + (rt * 32 + lane) * 16 + 8 * h);
-        const uint2 scw = *reinterpret_cast<const uint2*>(rw + SG_TILE_SC_OFF + (rt * 8 + g) * 8);
-        float mul[2], sub[2];  // row g, row g+8: w = mul * q - sub
-        if (p.dtype == SG_DTYPE_Q4_0) {
-          const uint32_t dword = h ? scw.y : scw.x;
-          const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&dword));
-          mul[0] = d.x;
-          mul[1] = d.y;
-          sub[0] = 8.f * d.x;  // (q - 8) * d == q*d - 8d exactly (both terms exact in f32)
-          sub[1] = 8.f * d.y;
-        } else {
-          const uint2 ddv = *reinterpret_cast<const uint2*>(rw + SG_TILE_BYTES + (rt * 16 + g * 2) * 4);
-          const uint32_t sc2[2] = {scw.x, scw.y}, dd2[2] = {ddv.x, ddv.y};
-#pragma unroll
-          for (int hl = 0; hl < 2; ++hl) {
-            const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dd2[hl]));
-            mul[hl] = __fmul_rn(dm.x, (float)((sc2[hl] >> (8 * h)) & 0xFFu));
-            sub[hl] = __fmul_rn(dm.y, (float)((sc2[hl] >> (16 + 8 * h)) & 0xFFu));
-          }
+      for_each_segment(p, [&](int tile, int k0, int k1) {
+        (void)tile;
+        if (!ok) return;
+        const int b = seg & 1;
+        if (seg >= 2 && !mbar_wait(&acc_empty[b], ((seg >> 1) & 1) ^ 1, 0x18)) {
+          ok = false;
+          return;
         }
-#pragma unroll
-        for (int sw = 0; sw < 2; ++sw) {
-          const uint32_t w32 = sw ? wv.y : wv.x;
-#pragma unroll
-          for (int pp = 0; pp < 4; ++pp) {  // nibble pairs (p, p+4): same row, k and k+1
-            const int hl = pp & 1;
-            const int row = rt * 16 + g + 8 * hl;
-            const int k = 16 * sw + 2 * t + 8 * ((pp >> 1) & 1);
-            const float q0 = (float)((w32 >> (4 * pp)) & 15u), q1 = (float)((w32 >> (4 * pp + 16)) & 15u);
-            const float v0 = __fsub_rn(__fmul_rn(mul[hl], q0), sub[hl]);
-            const float v1 = __fsub_rn(__fmul_rn(mul[hl], q1), sub[hl]);
-            const __nv_bfloat162 hi = __floats2bfloat162_rn(v0, v1);
-            const float2 hf = __bfloat1622float2(hi);
-            const __nv_bfloat162 lo = __floats2bfloat162_rn(v0 - hf.x, v1 - hf.y);
-            const uint32_t off = sw64_off(row, k);
-            *reinterpret_cast<__nv_bfloat162*>(a_hi + off) = hi;
-            *reinterpret_cast<__nv_bfloat162*>(a_lo + off) = lo;
+        sg_tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * BN);
+        for (int kk = 0; kk < 2 * (k1 - k0); ++kk) {
+          const int s = g % kS;
+          const uint32_t ph = (g / kS) & 1;
+          if (!mbar_wait(&x_full[s], ph, 0x13) || !mbar_wait(&a_full[s], ph, 0x14)) {
+            ok = false;
+            break;
           }
+          sg_tc_fence_after();
+          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+          const uint64_t ah = sg_sdesc(base, SG_SW64), al = sg_sdesc(base + A_BYTES, SG_SW64);
+          const uint64_t xh = sg_sdesc(base + 2 * A_BYTES, SG_SW64);
+          const uint64_t xl = sg_sdesc(base + 2 * A_BYTES + X_BYTES, SG_SW64);
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j) {
+            const uint64_t o = (uint64_t)(j * 2);  // K step of 16 bf16 = 32 bytes
+            sg_umma(d, ah + o, xh + o, kIdesc, (kk | j) ? 1u : 0u);
+            sg_umma(d, ah + o, xl + o, kIdesc, 1u);
+            sg_umma(d, al + o, xh + o, kIdesc, 1u);
+          }
+          sg_umma_commit(&s_empty[s]);
+          ++g;
         }
-      }
-      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[s]);
-        if (h == 1 || kk == nk - 1) mbar_arrive(&raw_empty[r]);
-      }
+        sg_umma_commit(&acc_full[b]);  // fires when this segment's MMAs have completed
+        ++seg;
+      });
+      // every MMA issued must have completed before TMEM is freed: each k-step
+      // ends with a commit, so the last one covers all (also on the error path)
+      if (g > 0) mbar_wait_drain(&s_empty[(g - 1) % kS], ((g - 1) / kS) & 1);
     }
-    // ============================================================== epilogue
-    pdl_wait();  // y may have been zeroed by the activation-prep kernel
-    const bool ok = mbar_wait(&acc_full, 0, 0x17);
-    if (!ok) mbar_wait_drain(&acc_full, 0);  // the issuer always commits: MMAs must finish before TMEM is freed
-    tc_fence_after();
-    if (__all_sync(0xffffffffu, ok)) {
-      const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31 belong to this warp
-      const int row_l = quad * 32 + lane;
+  } else if (warp < 6) {
+    // ====================================================== dequant warps
+    const int row = (warp & 3) * 32 + lane;
+    int g = 0, rc = 0;
+    bool ok = true;
+    for_each_segment(p, [&](int tile, int k0, int k1) {
+      (void)tile;
+      if (!ok) return;
+      for (int ch = k0; ch < k1 && ok; ++ch, ++rc) {
+        const int r = rc % kR;
+        const uint8_t* rw = raw_ring + r * RAW_BYTES;
+        for (int h = 0; h < 2; ++h) {
+          const int s = g % kS;
+          bool w = true;
+          if (h == 0) w = mbar_wait(&raw_full[r], (rc / kR) & 1, 0x15);
+          if (w && g >= kS) w = mbar_wait(&s_empty[s], ((g / kS) & 1) ^ 1, 0x16);
+          if (!__all_sync(0xffffffffu, w)) {
+            ok = false;
+            break;
+          }
+          const uint4 nv = *reinterpret_cast<const uint4*>(rw + h * 2048 + row * 16);
+          const uint32_t scw = *reinterpret_cast<const uint32_t*>(rw + SG_TILE_SC_OFF + row * 4);
+          float sv, mv;  // w = sv*q - mv
+          if (p.dtype == SG_DTYPE_Q4_0) {
+            sv = __half2float(__ushort_as_half((unsigned short)(h ? (scw >> 16) : (scw & 0xFFFFu))));
+            mv = 8.f * sv;
+          } else {
+            const uint32_t ddw = *reinterpret_cast<const uint32_t*>(rw + SG_TILE_BYTES + row * 4);
+            const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddw));
+            sv = __fmul_rn(dm.x, (float)((scw >> (8 * h)) & 0xFFu));
+            mv = __fmul_rn(dm.y, (float)((scw >> (16 + 8 * h)) & 0xFFu));
+          }
+          // f = 1024+q (k%8 in {0,1,4,5}) or 1024+16q ({2,3,6,7}):
+          //   w = f*sv - (1024 sv + mv)   or   w = f*(sv/16) - (64 sv + mv)
+          const float mulA = sv, addA = -__fadd_rn(1024.f * sv, mv);
+          const float mulB = sv * 0.0625f, addB = -__fadd_rn(64.f * sv, mv);
+          uint8_t* a_hi = smem + s * STAGE_BYTES;
+          uint8_t* a_lo = a_hi + A_BYTES;
+          const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 f16 = sg_decode_word_f16(nw[j]);
+            const uint32_t fp[4] = {f16.x, f16.y, f16.z, f16.w};
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&fp[e]));
+              const float mul = (e & 1) ? mulB : mulA, add = (e & 1) ? addB : addA;
+              const float w0 = fmaf(f.x, mul, add), w1 = fmaf(f.y, mul, add);
+              const uint32_t u0 = __float_as_uint(w0), u1 = __float_as_uint(w1);
+              hi[e] = __byte_perm(u0, u1, 0x7632);  // truncated bf16 pair (top halves)
+              const __nv_bfloat162 l = __floats2bfloat162_rn(w0 - __uint_as_float(u0 & 0xFFFF0000u),
+                                                             w1 - __uint_as_float(u1 & 0xFFFF0000u));
+              lo[e] = *reinterpret_cast<const uint32_t*>(&l);
+            }
+            const uint32_t off = sw64_chunk(row, j);
+            *reinterpret_cast<uint4*>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          }
+          fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&a_full[s]);
+            if (h == 1) mbar_arrive(&raw_empty[r]);
+          }
+          ++g;
+        }
+      }
+    });
+  } else {
+    // ============================================================ epilogue warps
+    const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+    const int row_l = quad * 32 + lane;
+    int seg = 0;
+    bool ok = true;
+    bool waited = false;
+    for_each_segment(p, [&](int tile, int k0, int k1) {
+      if (!ok) return;
+      const int b = seg & 1;
+      const bool w = mbar_wait(&acc_full[b], (seg >> 1) & 1, 0x17);
+      if (!__all_sync(0xffffffffu, w)) {
+        ok = false;
+        return;
+      }
+      sg_tc_fence_after();
+      if (!waited) {
+        pdl_wait();  // y: zeroing by the prep kernel, readers of the previous kernel
+        waited = true;
+      }
+      const int rb = tile / p.n_tt, tt = tile % p.n_tt;
       const int row = rb * BM + row_l;
-      const bool use_red = p.split > 1;
+      const bool whole = (k0 == 0 && k1 == p.n_ch);
 #pragma unroll 1
       for (int cb = 0; cb < BN / 32; ++cb) {
         uint32_t v[32];
-        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(cb * 32);
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
-            "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-              "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-              "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        sg_tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BN + cb * 32), v);
+        sg_tmem_ld_wait();
         if (row < p.n_rows) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -320,54 +368,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (tok < p.m) {
               float* yp = p.y + (int64_t)tok * p.ldy + row;
               const float val = __uint_as_float(v[j]);
-              if (use_red) red_add_f32(yp, val);
+              if (!whole) red_add_f32(yp, val);
               else *yp = p.accumulate ? *yp + val : val;
             }
           }
         }
       }
-    }
+      sg_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      ++seg;
+    });
   }
   pdl_launch_dependents();
-  tc_fence_before();
+  sg_tc_fence_before();
   __syncthreads();
   if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    sg_tc_fence_after();
+    sg_tmem_dealloc(tmem, kTmemCols);
   }
 }
 
 // ------------------------------------------------------------ host side
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(f);
-  });
-  return fn;
-}
-
-// 2-D map over a [rows][K] bf16 matrix, box 32 (K) x 256 (rows), 64-byte swizzle.
-bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t K) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BN};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 cudaError_t set_gemm_attr() {
   static uint64_t done_mask = 0;
   int dev = 0;
@@ -383,7 +405,8 @@ cudaError_t launch(const SgDevWeight* w, const float* x, int64_t ldx, float* y, 
                    void* scratch, size_t scratch_bytes, int num_sms, cudaStream_t st) {
   if (m < 1 || !w || !x || !y) return cudaErrorInvalidValue;
   const int64_t K = w->n_cols;
-  if ((K & 31) || ((uintptr_t)x & 15) || (ldx & 3) || K > (1 << 30) || (int64_t)m * K > (1ll << 40))
+  if ((K & 31) || ((uintptr_t)x & 15) || (ldx & 3) || ldx < K || K > (1 << 30) || (int64_t)m * K > (1ll << 40) ||
+      ldy < w->n_rows)
     return cudaErrorInvalidValue;
   if (scratch_bytes < sg_gemm_scratch_bytes(m, K)) return cudaErrorInvalidValue;
   __nv_bfloat16* xh = static_cast<__nv_bfloat16*>(scratch);
@@ -394,7 +417,6 @@ cudaError_t launch(const SgDevWeight* w, const float* x, int64_t ldx, float* y, 
   p.dd = w->dd;
   p.dtype = w->dtype;
   p.n_rows = (int)w->n_rows;
-  p.n_cols = (int)K;
   p.n_ch = (int)w->n_ch;
   p.n_sb = (int)w->n_sb;
   p.m = m;
@@ -403,11 +425,11 @@ cudaError_t launch(const SgDevWeight* w, const float* x, int64_t ldx, float* y, 
   p.y = y;
   p.ldy = ldy;
   const int64_t tiles = w->n_rb * p.n_tt;
-  int split = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms / std::max<int64_t>(1, tiles), p.n_ch / 4));
-  p.split = std::max(1, split);
-  const bool zero_y = p.split > 1 && !accumulate;
+  // persistent grid: one CTA per SM (at least one chunk each)
+  const int G = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms, tiles * p.n_ch));
+  p.dp = (int)(tiles / G);
+  p.rem_iters = (tiles - (int64_t)p.dp * G) * p.n_ch;
 
-  // 1. activation split (+ zero y for the split-K reduction)
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = sg_pdl_enabled() ? 1 : 0;
@@ -418,17 +440,17 @@ cudaError_t launch(const SgDevWeight* w, const float* x, int64_t ldx, float* y, 
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_xprep_kernel, x, ldx, m, (int)K, xh, xl, y, ldy, p.n_rows,
-                                     zero_y ? 1 : 0);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_xprep_kernel, x, ldx, m, (int)K, xh, xl, p, G);
   if (e != cudaSuccess) return e;
 
-  // 2. GEMM
   CUtensorMap mh, ml;
-  if (!make_map(&mh, xh, m, K) || !make_map(&ml, xl, m, K)) return cudaErrorInvalidValue;
+  if (!sg_make_map_16(&mh, xh, m, K, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B, false) ||
+      !sg_make_map_16(&ml, xl, m, K, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B, false))
+    return cudaErrorInvalidValue;
   e = set_gemm_attr();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t g = {};
-  g.gridDim = dim3((unsigned)(tiles * p.split));
+  g.gridDim = dim3((unsigned)G);
   g.blockDim = dim3(kThreads);
   g.dynamicSmemBytes = SMEM_BYTES;
   g.stream = st;

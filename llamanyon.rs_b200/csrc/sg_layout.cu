@@ -27,30 +27,29 @@ __device__ __forceinline__ uint32_t raw_nibble(int dtype, const uint8_t* raw, in
   }
 }
 
-// one thread per (tile, rt, lane): the 16-byte nibble vector of that lane
+// one thread per (tile, half, row): the 16-byte nibble vector of that row
 __global__ void repack_qs_kernel(int dtype, const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
                                  int64_t n_rb, int64_t n_ch, uint8_t* __restrict__ tiles) {
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = n_rb * n_ch * 256;
   if (tid >= total) return;
-  const int lane = (int)(tid & 31);
-  const int rt = (int)((tid >> 5) & 7);
+  const int r = (int)(tid & 127);
+  const int h = (int)((tid >> 7) & 1);
   const int64_t tile = tid >> 8;  // rb * n_ch + c
   const int64_t rb = tile / n_ch, c = tile % n_ch;
-  const int g = lane >> 2, t = lane & 3;
+  const int64_t row = rb * 128 + r;
   uint32_t words[4];
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    uint32_t w = 0;
+  for (int w = 0; w < 4; ++w) {
+    uint32_t v = 0;
 #pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      const int64_t row = rb * 128 + rt * 16 + g + ((p & 1) ? 8 : 0);
-      const int64_t k = c * 64 + 16 * s + 2 * t + (((p >> 1) & 1) ? 8 : 0) + ((p >> 2) & 1);
-      w |= raw_nibble(dtype, raw, n_rows, n_cols, row, k) << (4 * p);
+    for (int j = 0; j < 8; ++j) {
+      const int64_t k = c * 64 + 32 * h + 8 * w + j;
+      v |= raw_nibble(dtype, raw, n_rows, n_cols, row, k) << sg_nib_pos(j);
     }
-    words[s] = w;
+    words[w] = v;
   }
-  *reinterpret_cast<uint4*>(tiles + tile * SG_TILE_BYTES + (rt * 32 + lane) * 16) =
+  *reinterpret_cast<uint4*>(tiles + tile * SG_TILE_BYTES + (h * 128 + r) * 16) =
       make_uint4(words[0], words[1], words[2], words[3]);
 }
 
@@ -65,60 +64,52 @@ __device__ __forceinline__ void q4k_unpack(const uint8_t* s, int j, uint32_t& sc
   }
 }
 
-// one thread per (tile, rt, g): the two scale words of rows g and g+8
+// one thread per (tile, row): the row's scale word
 __global__ void repack_scales_kernel(int dtype, const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
                                      int64_t n_rb, int64_t n_ch, uint8_t* __restrict__ tiles) {
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t total = n_rb * n_ch * 64;
+  const int64_t total = n_rb * n_ch * 128;
   if (tid >= total) return;
-  const int g = (int)(tid & 7), rt = (int)((tid >> 3) & 7);
-  const int64_t tile = tid >> 6, rb = tile / n_ch, c = tile % n_ch;
-  uint32_t w[2] = {0u, 0u};
-  if (dtype == SG_DTYPE_Q4_0) {
-    const int64_t nb = n_cols / 32;
+  const int r = (int)(tid & 127);
+  const int64_t tile = tid >> 7, rb = tile / n_ch, c = tile % n_ch;
+  const int64_t row = rb * 128 + r;
+  uint32_t out = 0;
+  if (row < n_rows) {
+    if (dtype == SG_DTYPE_Q4_0) {
+      const int64_t nb = n_cols / 32;
 #pragma unroll
-    for (int blk = 0; blk < 2; ++blk)
-#pragma unroll
-      for (int hl = 0; hl < 2; ++hl) {
-        const int64_t row = rb * 128 + rt * 16 + g + 8 * hl;
+      for (int blk = 0; blk < 2; ++blk) {
         const int64_t b = c * 2 + blk;
-        uint32_t d = 0;
-        if (row < n_rows && b < nb) {
-          const uint8_t* p = raw + (row * nb + b) * 18;
-          d = (uint32_t)p[0] | ((uint32_t)p[1] << 8);
+        if (b < nb) {
+          const uint8_t* p = raw + (row * nb + b) * 18;  // q4_0.rs:24
+          out |= ((uint32_t)p[0] | ((uint32_t)p[1] << 8)) << (16 * blk);
         }
-        w[blk] |= d << (16 * hl);
       }
-  } else {
-    const int64_t nsb = n_cols / 256;
-#pragma unroll
-    for (int hl = 0; hl < 2; ++hl) {
-      const int64_t row = rb * 128 + rt * 16 + g + 8 * hl;
-      if (row < n_rows) {
-        const uint8_t* blk = raw + (row * nsb + (c >> 2)) * 144;
-        const int a = 2 * (int)(c & 3);
-        uint32_t sa, ma, sb, mb;
-        q4k_unpack(blk + 4, a, sa, ma);
-        q4k_unpack(blk + 4, a + 1, sb, mb);
-        w[hl] = sa | (sb << 8) | (ma << 16) | (mb << 24);
-      }
+    } else {
+      const int64_t nsb = n_cols / 256;
+      const uint8_t* blk = raw + (row * nsb + (c >> 2)) * 144;
+      const int a = 2 * (int)(c & 3);
+      uint32_t sa, ma, sb, mb;
+      q4k_unpack(blk + 4, a, sa, ma);
+      q4k_unpack(blk + 4, a + 1, sb, mb);
+      out = sa | (sb << 8) | (ma << 16) | (mb << 24);
     }
   }
-  *reinterpret_cast<uint2*>(tiles + tile * SG_TILE_BYTES + SG_TILE_SC_OFF + (rt * 8 + g) * 8) = make_uint2(w[0], w[1]);
+  reinterpret_cast<uint32_t*>(tiles + tile * SG_TILE_BYTES + SG_TILE_SC_OFF)[r] = out;
 }
 
-// Q4_K dd: one thread per (rb, superblock, rt, g, hl).
+// Q4_K dd: one thread per (rb, superblock, row).
 __global__ void repack_q4k_dd_kernel(const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
                                      int64_t n_rb, int64_t n_sb, uint32_t* __restrict__ dd) {
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = n_rb * n_sb * 128;
   if (tid >= total) return;
-  const int hl = (int)(tid & 1), g = (int)((tid >> 1) & 7), rt = (int)((tid >> 4) & 7);
+  const int r = (int)(tid & 127);
   const int64_t tile = tid >> 7, rb = tile / n_sb, sb = tile % n_sb;
-  const int64_t row = rb * 128 + rt * 16 + g + 8 * hl;
+  const int64_t row = rb * 128 + r;
   uint32_t out = 0;
   if (row < n_rows) {
-    const uint8_t* blk = raw + (row * n_sb + sb) * 144;
+    const uint8_t* blk = raw + (row * n_sb + sb) * 144;  // q4_k.rs:281-282
     out = (uint32_t)blk[0] | ((uint32_t)blk[1] << 8) | ((uint32_t)blk[2] << 16) | ((uint32_t)blk[3] << 24);
   }
   dd[tid] = out;
@@ -136,20 +127,19 @@ __global__ void dequant_kernel(SgDevWeight w, float* __restrict__ dst, int64_t l
   const int64_t c = k0 >> 6;
   const int kk0 = (int)(k0 & 63);
   const uint8_t* tile = w.tiles + (rb * w.n_ch + c) * SG_TILE_BYTES;
-  const int rt = r >> 4, g = r & 7, hl = (r >> 3) & 1;
-  const uint32_t* scw = reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF) + (rt * 8 + g) * 2;
+  const uint32_t scw = reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF)[r];
   float out[8];
   if (w.dtype == SG_DTYPE_Q4_0) {
-    const uint32_t dw = scw[kk0 >> 5];
-    const float d = __half2float(__ushort_as_half((unsigned short)(hl ? (dw >> 16) : (dw & 0xFFFFu))));
+    const uint32_t dw = (kk0 >> 5) ? (scw >> 16) : (scw & 0xFFFFu);
+    const float d = __half2float(__ushort_as_half((unsigned short)dw));
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int q = (int)tile_nibble(tile, r, kk0 + i);
       out[i] = __fmul_rn((float)(q - 8), d);
     }
   } else {
-    const uint32_t scm = scw[hl];
-    const uint32_t ddw = w.dd[(rb * w.n_sb + (c >> 2)) * 128 + rt * 16 + g * 2 + hl];
+    const uint32_t scm = scw;
+    const uint32_t ddw = w.dd[(rb * w.n_sb + (c >> 2)) * 128 + r];
     const float d = __half2float(__ushort_as_half((unsigned short)(ddw & 0xFFFFu)));
     const float dmin = __half2float(__ushort_as_half((unsigned short)(ddw >> 16)));
     const int sub = kk0 >> 5;
@@ -209,7 +199,7 @@ cudaError_t sg_layout_repack(const SgDevWeight* w, const uint8_t* raw_dev, cudaS
   const int64_t nq = w->n_rb * w->n_ch * 256;
   repack_qs_kernel<<<nblocks(nq, T), T, 0, st>>>(w->dtype, raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch,
                                                  w->tiles);
-  const int64_t ns = w->n_rb * w->n_ch * 64;
+  const int64_t ns = w->n_rb * w->n_ch * 128;
   repack_scales_kernel<<<nblocks(ns, T), T, 0, st>>>(w->dtype, raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch,
                                                      w->tiles);
   if (w->dtype == SG_DTYPE_Q4_K) {
