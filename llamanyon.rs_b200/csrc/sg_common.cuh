@@ -102,12 +102,12 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 #define SG_WAIT_NS 4000000000ull
 #endif
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int tag) {
-  if (mbar_test(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
 #pragma unroll 1
-    for (int i = 0; i < 64; ++i)
-      if (mbar_test(bar, parity)) return true;
+    for (int i = 0; i < 16; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
     if (*(volatile int*)&g_sg_error != 0) return false;
     if (globaltimer_ns() - t0 > SG_WAIT_NS) break;
   }
@@ -176,6 +176,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* m
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
       "[%4];" ::"r"(smem_u32(dst_smem)),
       "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 4-D tiled TMA load (no multicast), completion on an mbarrier.
+__device__ __forceinline__ void tma_load_4d(void* dst_smem, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(smem_u32(dst_smem)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
 }
 

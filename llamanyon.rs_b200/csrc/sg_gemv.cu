@@ -18,31 +18,39 @@
 // block's constant part (precomputed per token from the same hi + lo values,
 // so the 1024 offset cancels exactly) and applies the block scale in f32.
 //
+// Data movement is built around one measured fact of the copy engine: each
+// issuing thread completes bulk copies one after another at a roughly fixed
+// cost per copy, so bandwidth comes from large copies. Work is therefore cut
+// in units of 4 chunks (128 rows x 256 K) -- 18 KB of packed weights,
+// contiguous in the tile layout -- and each unit's weights and activations
+// arrive in one bulk copy each.
+//
 // Kernels, chained with programmatic dependent launch:
-//  1. gemv_xprep_kernel: one CTA per token -- power-of-two scale, f16 hi/lo
-//     activations, per-block sums, zeroing of the output rows that several
-//     CTAs share.
-//  2. gemv_kernel<dtype, BP>: balanced split -- CTA c takes iterations
-//     [c*T/G, (c+1)*T/G) of the T = row-blocks x K-chunks space, crossing
+//  1. gemv_xprep_kernel: power-of-two scale per token, f16 hi/lo activation
+//     parts written directly in the swizzled UMMA operand layout, unit by
+//     unit, with each unit's per-block sums appended; zeroing of the output
+//     rows that several CTAs reduce into.
+//  2. gemv_kernel<dtype, BP>: one CTA per SM, balanced split -- CTA c takes
+//     units [c*T/G, (c+1)*T/G) of the T = row-blocks x units space, crossing
 //     row-block (and matrix) boundaries; a row-block seen whole is stored, a
 //     shared one is reduced with red.add.
-//       warp 0     producer: cp.async.bulk of packed weight tiles (4.5 KB per
-//                  128 rows x 64 K) into a 7-slot ring -- the first ones
-//                  before the wait on the previous kernel, weights do not
-//                  depend on it -- then TMA of the activation tiles and block
-//                  sums per chunk.
-//       warp 1     TMEM owner; one thread issues tcgen05.mma (M=128,
-//                  N=2*BP: BP hi token rows + BP lo token rows, K=16, f16 ->
-//                  f32), two per 32-block, into a ring of TMEM slots.
-//       warps 2-5  dequant: one weight row per thread, 16-byte nibble loads,
-//                  4 lop3 per 8 weights into the 128-byte-swizzled A tile.
-//       warps 6-9  epilogue: per chunk, tcgen05.ld of the two block
-//                  accumulators of its TMEM lane quadrant (warp % 4), block
-//                  scales in f32, output rows stored or reduced.
-// Rings decouple the roles: weight tiles (freed by the dequant warps), A
-// tiles and activation tiles (freed by the MMA commit) and TMEM slots with
-// their block sums and row scales (freed by the epilogue); the producer
-// serves the weight and activation queues without blocking on either.
+//       warp 0      weight producer: one cp.async.bulk per unit into a
+//                   4-slot ring (issued before the wait on the previous
+//                   kernel: weights do not depend on it).
+//       warp 10     activation producer: one cp.async.bulk per unit (4
+//                   operand tiles + block sums) into a 3-slot ring.
+//       warp 1      TMEM owner; one thread issues tcgen05.mma (A from TMEM,
+//                   M=128, N=2*BP: BP hi token rows + BP lo token rows,
+//                   K=16, f16 -> f32), two per 32-block, into a ring of TMEM
+//                   accumulator slots.
+//       warps 2-5   dequant: one weight row per thread, two 16-byte reads
+//                   and 8 lop3 + 2 shifts per 64 K, written with one
+//                   tcgen05.st into a tensor-memory A tile (lane = row), so
+//                   the dequantized operand never passes through shared
+//                   memory.
+//       warps 6-9   epilogue: per chunk, tcgen05.ld of the two block
+//                   accumulators of its TMEM lane quadrant (warp % 4), block
+//                   scales in f32, output rows stored or reduced.
 // Every mbarrier wait is bounded (sg_common.cuh).
 #include <algorithm>
 
@@ -51,26 +59,38 @@
 
 namespace gemv_tc {
 
-constexpr int kSA = 3;                // dequantized A tiles (freed by the MMA commit)
-constexpr int kPD = 4;                // weight chunks in flight per dequant thread (registers)
-constexpr int kA = 128 * 128;         // 128 rows x 64 K f16
-constexpr int kThreads = 320;
-constexpr int kXLag = 2;              // activation chunks in flight per producer lane
+constexpr int kUC = 4;                     // chunks per unit
+constexpr int kRW = 4;                     // weight unit ring
+constexpr int kRX = 3;                     // activation unit ring
+constexpr int kACols = 32;                 // TMEM columns of one A tile: 128 lanes x 64 K f16
+constexpr int kWU = kUC * SG_TILE_BYTES + 512;  // packed weights of a unit + Q4_K d|dmin
+constexpr int kThreads = 352;
+constexpr int kMaskWords = 32;             // split row-block bitmask (row-blocks 0..1023)
 
 template <int BP>
 struct Cfg {
   static constexpr int N = 2 * BP;                   // MMA N: hi rows then lo rows
-  static constexpr int SD = BP == 8 ? 8 : 4;         // TMEM slots / block sums / row scales in flight
-  static constexpr int SX = BP == 8 ? 6 : 4;         // activation tiles (freed by the MMA commit)
-  static constexpr int X = N * 128;                  // activation tile bytes
-  static constexpr int SUM = 256;                    // [blk 2][2][16] f32
-  static constexpr int SCAL = 1024;                  // [2][128] u32 row scale words
-  static constexpr int OFF_X = kSA * kA;
-  static constexpr int OFF_SUM = OFF_X + SX * X;
-  static constexpr int OFF_SCAL = OFF_SUM + SD * SUM;
-  static constexpr int SMEM = OFF_SCAL + SD * SCAL + 1024;
-  static constexpr uint32_t TMEM_COLS = SD * 2 * N;  // 256
+  static constexpr int CPG = BP == 8 ? 4 : 2;        // chunks per group (one hand-off between roles)
+  static constexpr int GPU = kUC / CPG;              // groups per unit
+  static constexpr int SG = 2;                       // groups in flight: A tiles and accumulators in TMEM
+  static constexpr int T = N * 128;                  // activation tile bytes (one chunk)
+  static constexpr int XU = kUC * T + kUC * 256;     // activation unit: 4 tiles + 4 x block sums
+  static constexpr int SCAL = 1024;                  // per chunk: [2][128] u32 row scale words
+  static constexpr int OFF_X = 0;
+  static constexpr int OFF_W = OFF_X + kRX * XU;
+  static constexpr int OFF_SCAL = OFF_W + kRW * kWU;
+  // Each CTA takes all 512 TMEM columns, so two CTAs must never share an SM
+  // (the second would wait in tcgen05.alloc): ask for more than half of the
+  // SM's shared memory.
+  static constexpr int SMEM_USED = OFF_SCAL + SG * CPG * SCAL + 1024;
+  static constexpr int SMEM = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
+  static constexpr uint32_t A_COLS = CPG * kACols;   // TMEM columns of a group's A tiles
+  static constexpr uint32_t D_COLS = CPG * 2 * N;    // TMEM columns of a group's block accumulators
+  static constexpr uint32_t D_COL0 = SG * A_COLS;    // A tiles first, then the accumulators
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(D_COL0 + SG * D_COLS <= TMEM_COLS, "TMEM budget");
   static constexpr uint32_t IDESC = sg_idesc_f16(128, N);
+  static_assert(XU % 1024 == 0, "activation units must keep 1024-byte tile alignment");
 };
 
 struct Mat {
@@ -81,17 +101,12 @@ struct Mat {
   int n_rb, n_rows, n_sb, rb0;
 };
 
-constexpr int kMaskWords = 32;  // split row-block bitmask (row-blocks 0..1023)
-
 struct Params {
   Mat mats[SG_GEMV_MAX_MATS];
-  int n_mats, batch, n_ch, accumulate;
-  int64_t total;      // row-blocks x chunks
-  const float* sums;  // [2*n_ch][2][16]
-  const float* inv;   // [16] per-token 2^-e
-  const __half* xh;   // [batch][K] activation parts
-  const __half* xl;
-  int K;
+  int n_mats, batch, n_ch, n_sc, accumulate;
+  int64_t total;          // row-blocks x units
+  const uint8_t* xunits;  // activation units (xprep layout)
+  const float* inv;       // [16] per-token 2^-e
   int total_rb;
   int zero_all;                  // more row-blocks than the mask holds: zero every split candidate
   uint32_t split[kMaskWords];    // bit rbg: row-block reduced by more than one CTA (zeroed first)
@@ -105,30 +120,59 @@ __device__ __forceinline__ int find_mat(const Params& p, int rbg) {
   return m;
 }
 
+// Unit cursor: walks the CTA's units without divisions.
+struct Cursor {
+  int rbg, sc, mi, rb;  // global row-block, unit within it, matrix, row-block within the matrix
+  __device__ __forceinline__ void init(const Params& p, int64_t gu) {
+    rbg = (int)(gu / p.n_sc);
+    sc = (int)(gu % p.n_sc);
+    mi = find_mat(p, rbg);
+    rb = rbg - p.mats[mi].rb0;
+  }
+  __device__ __forceinline__ int chunks(const Params& p) const { return min(kUC, p.n_ch - kUC * sc); }
+  __device__ __forceinline__ void next(const Params& p) {
+    if (++sc == p.n_sc) {
+      sc = 0;
+      ++rbg;
+      ++rb;
+      if (mi + 1 < p.n_mats && rbg >= p.mats[mi + 1].rb0) {
+        ++mi;
+        rb = 0;
+      }
+    }
+  }
+};
+
 // ---------------------------------------------------------------- x prep
-// Grid (block groups, tokens). Each CTA finds its token's max|x| (scale
-// s = 2^e puts it in [2^14, 2^15)), then converts 8 blocks of 32: positions
-// k%8 in {2,3,6,7} carry x*s/16 (their A values are 1024+16q). u is the value
-// the tensor core sees (hi + lo, times 16 at those positions).
-// sums[b][0][t] = Q4_0: sum (c+8) u, Q4_K: sum c u   (c = 1024 or 64)
-// sums[b][1][t] = sum u
-// CTAs with blockIdx.x == 0 also zero their token's outputs in the row-blocks
-// that several GEMV CTAs reduce into.
+// Grid (block groups of 8, token rows BP). For token row t < batch: the
+// token's max|x| sets s = 2^e (max|x|*s in [2^14, 2^15)); positions k%8 in
+// {2,3,6,7} carry x*s/16 (their A values are 1024+16q). u is the value the
+// tensor core sees (hi + lo, times 16 at those positions). Token rows
+// batch <= t < BT are written as zeros. Unit layout (XU bytes per 4 chunks):
+// 4 operand tiles [row 2*BP][128 B, 16-byte segment j of row r at
+// ((j ^ (r & 7)) << 4)], rows 0..BT-1 hi parts and BT..2BT-1 lo parts (rows
+// from 2*BT on are never read back: their product columns are ignored), then
+// per chunk
+// sums[blk 2][2][16]: [0] Q4_0: sum (c+8) u, Q4_K: sum c u (c = 1024 or
+// 64); [1] sum u.
+template <int BP, int BT>
 __global__ void __launch_bounds__(256) gemv_xprep_kernel(const float* __restrict__ x, int64_t ldx, int K, int n_blk,
-                                                         int q40, __half* __restrict__ xh, __half* __restrict__ xl,
-                                                         float* __restrict__ sums, float* __restrict__ inv,
-                                                         Params zp, int zero_split) {
+                                                         int q40, uint8_t* __restrict__ xunits,
+                                                         float* __restrict__ inv, Params zp, int zero_split) {
+  using C = Cfg<BP>;
   pdl_launch_dependents();
   pdl_wait();  // x may come from the previous kernel; scratch and y may still be in use by it
   __shared__ float red[8];
   const int t = blockIdx.y;
+  const bool live = t < zp.batch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* xr = x + (int64_t)t * ldx;
   float m = 0.f;
-  for (int k = threadIdx.x * 4; k < K; k += 1024) {
-    const float4 v = *reinterpret_cast<const float4*>(xr + k);
-    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-  }
+  if (live)
+    for (int k = threadIdx.x * 4; k < K; k += 1024) {
+      const float4 v = *reinterpret_cast<const float4*>(xr + k);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
 #pragma unroll
   for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) red[warp] = m;
@@ -142,20 +186,22 @@ __global__ void __launch_bounds__(256) gemv_xprep_kernel(const float* __restrict
     se = max(-126, min(127, 14 - e));
   }
   const float s = __int_as_float((127 + se) << 23);
-  if (blockIdx.x == 0 && threadIdx.x == 0) inv[t] = __int_as_float((127 - se) << 23);
+  if (live && blockIdx.x == 0 && threadIdx.x == 0) inv[t] = __int_as_float((127 - se) << 23);
   const bool scaled = (lane >> 1) & 1;  // k % 8 in {2,3,6,7}
   const float c = scaled ? 64.f : 1024.f;
   const int b = blockIdx.x * 8 + warp;
   if (b < n_blk) {
     const int k = 32 * b + lane;
-    const float v = k < K ? xr[k] : 0.f;
+    const float v = (live && k < K) ? xr[k] : 0.f;
     const float xs = scaled ? v * s * 0.0625f : v * s;
     const __half hi = __float2half_rn(xs);
     const __half lo = __float2half_rn(xs - __half2float(hi));
-    if (k < K) {
-      xh[(int64_t)t * K + k] = hi;
-      xl[(int64_t)t * K + k] = lo;
-    }
+    const int ch = b >> 1, kc = k & 63, j = kc >> 3;
+    uint8_t* unit = xunits + (int64_t)(ch / kUC) * C::XU;
+    uint8_t* tile = unit + (ch % kUC) * C::T;
+    const int rh = t, rl = BT + t;  // live hi rows, then live lo rows
+    *reinterpret_cast<__half*>(tile + rh * 128 + ((j ^ (rh & 7)) << 4) + (kc & 7) * 2) = hi;
+    *reinterpret_cast<__half*>(tile + rl * 128 + ((j ^ (rl & 7)) << 4) + (kc & 7) * 2) = lo;
     const float u = (__half2float(hi) + __half2float(lo)) * (scaled ? 16.f : 1.f);
     float a = (q40 ? c + 8.f : c) * u, su = u;
 #pragma unroll
@@ -164,11 +210,12 @@ __global__ void __launch_bounds__(256) gemv_xprep_kernel(const float* __restrict
       su += __shfl_xor_sync(0xffffffffu, su, o);
     }
     if (lane == 0) {
-      sums[(b * 2 + 0) * 16 + t] = a;
-      sums[(b * 2 + 1) * 16 + t] = su;
+      float* sums = reinterpret_cast<float*>(unit + kUC * C::T + (ch % kUC) * 256) + (b & 1) * 32;
+      sums[t] = a;
+      sums[16 + t] = su;
     }
   }
-  if (zero_split && blockIdx.x == 0) {
+  if (zero_split && live && blockIdx.x == 0) {
     for (int rbg = warp; rbg < zp.total_rb; rbg += 8) {
       if (!zp.zero_all && !((zp.split[rbg >> 5] >> (rbg & 31)) & 1u)) continue;
       const Mat& mt = zp.mats[find_mat(zp, rbg)];
@@ -180,60 +227,39 @@ __global__ void __launch_bounds__(256) gemv_xprep_kernel(const float* __restrict
 }
 
 // ---------------------------------------------------------------- GEMV
-// Chunk cursor: walks the CTA's iterations without divisions.
-struct Cursor {
-  int rbg, c, mi, rb;  // global row-block, chunk, matrix, row-block within the matrix
-  __device__ __forceinline__ void init(const Params& p, int64_t gi) {
-    rbg = (int)(gi / p.n_ch);
-    c = (int)(gi % p.n_ch);
-    mi = find_mat(p, rbg);
-    rb = rbg - p.mats[mi].rb0;
-  }
-  __device__ __forceinline__ void next(const Params& p) {
-    if (++c == p.n_ch) {
-      c = 0;
-      ++rbg;
-      ++rb;
-      if (mi + 1 < p.n_mats && rbg >= p.mats[mi + 1].rb0) {
-        ++mi;
-        rb = 0;
-      }
-    }
-  }
-};
-
-template <int DT, int BP>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(Params p) {
+// BT: live token columns rounded up to a power of two (<= BP)
+template <int DT, int BP, int BT>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
   using C = Cfg<BP>;
-  constexpr int SD = C::SD;
-  constexpr int SX = C::SX;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  // d_full[i % SD] completes when chunk i's MMAs are done: it also frees A
-  // slot i % kSA and activation slot i % SX (kSA, SX <= SD)
-  static_assert(kSA <= SD && SX <= SD, "ring sizes");
-  __shared__ __align__(8) uint64_t a_full[kSA], x_full[SX], sums_full[SD], d_full[SD], d_free[SD];
+  // per group g (CPG chunks): a_full[g % SG] -- its A tiles are in TMEM;
+  // d_full[g % SG] -- its MMAs completed; d_free[g % SG] -- its epilogue is
+  // done, so its A tiles, accumulators and row scales may be rewritten
+  __shared__ __align__(8) uint64_t w_full[kRW], w_empty[kRW], x_full[kRX], x_empty[kRX], a_full[C::SG],
+      d_full[C::SG], d_free[C::SG];
   __shared__ uint32_t tmem_base_sh;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
-  const int64_t i0 = (int64_t)blockIdx.x * p.total / G, i1 = (int64_t)(blockIdx.x + 1) * p.total / G;
-  const int n = (int)(i1 - i0);
+  const int64_t u0 = (int64_t)blockIdx.x * p.total / G, u1 = (int64_t)(blockIdx.x + 1) * p.total / G;
+  const int nu = (int)(u1 - u0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kSA; ++s) mbar_init(&a_full[s], 4);
-    for (int s = 0; s < SX; ++s) mbar_init(&x_full[s], 32);
-    for (int s = 0; s < SD; ++s) {
-      mbar_init(&sums_full[s], 32);
+    for (int r = 0; r < kRW; ++r) {
+      mbar_init(&w_full[r], 1);
+      mbar_init(&w_empty[r], 4);
+    }
+    for (int r = 0; r < kRX; ++r) {
+      mbar_init(&x_full[r], 1);
+      mbar_init(&x_empty[r], 4);
+    }
+    for (int s = 0; s < C::SG; ++s) {
+      mbar_init(&a_full[s], 4);
       mbar_init(&d_full[s], 1);
       mbar_init(&d_free[s], 4);
     }
     mbar_fence_init();
-  }
-  if (warp == 0) {
-    // activation rows >= batch are never written: zero every slot once
-    uint4* xz = reinterpret_cast<uint4*>(smem + C::OFF_X);
-    for (int i = lane; i < SX * C::X / 16; i += 32) xz[i] = make_uint4(0, 0, 0, 0);
   }
   if (warp == 1) sg_tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
   sg_tc_fence_before();
@@ -242,209 +268,218 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(Params p) {
   const uint32_t tmem = tmem_base_sh;
 
   if (warp == 0) {
-    // ======================================================= activation producer
-    // Per chunk: the BP hi + BP lo token rows (64 K each, 128-byte swizzle)
-    // and the block sums, copied with cp.async by the 32 lanes; a chunk is
-    // published (proxy fence + arrive) kXLag chunks after it was issued.
-    pdl_wait();  // activations and sums come from the prep kernel
-    Cursor xc;
-    xc.init(p, i0);
-    const int nrow = 2 * p.batch;  // real rows: hi of each token, then lo
-    bool ok = true;
-    auto publish = [&](int j) {
-      fence_proxy_async_smem();  // generic-proxy copies -> visible to the tensor core
-      mbar_arrive(&x_full[j % SX]);
-      mbar_arrive(&sums_full[j % SD]);
-    };
-    for (int i = 0; i < n; ++i) {
-      const int sx = i % SX, sd = i % SD;
-      bool w = true;
-      if (i >= SX) w = mbar_wait(&d_full[(i - SX) % SD], ((i - SX) / SD) & 1, 0x21);
-      if (w && i >= SD) w = mbar_wait(&d_free[sd], ((i / SD) & 1) ^ 1, 0x28);
-      if (!__all_sync(0xffffffffu, w)) {
-        ok = false;
-        break;
+    // ========================================================= weight producer
+    if (lane == 0) {
+      Cursor uc;
+      uc.init(p, u0);
+      int v = 0;
+      for (; v < nu; ++v) {
+        const int ws = v % kRW;
+        if (v >= kRW && !mbar_wait(&w_empty[ws], ((v / kRW) & 1) ^ 1, 0x21)) break;
+        const Mat& mt = p.mats[uc.mi];
+        const int cnt = uc.chunks(p);
+        uint8_t* dst = smem + C::OFF_W + ws * kWU;
+        mbar_arrive_expect_tx(&w_full[ws], cnt * SG_TILE_BYTES + (DT == SG_DTYPE_Q4_K ? 512 : 0));
+        bulk_g2s(dst, mt.tiles + ((int64_t)uc.rb * p.n_ch + kUC * uc.sc) * SG_TILE_BYTES, cnt * SG_TILE_BYTES,
+                 &w_full[ws]);
+        if (DT == SG_DTYPE_Q4_K)  // one Q4_K super-block per unit
+          bulk_g2s(dst + kUC * SG_TILE_BYTES, mt.dd + ((int64_t)uc.rb * mt.n_sb + uc.sc) * 128, 512, &w_full[ws]);
+        uc.next(p);
       }
-      uint8_t* xt = smem + C::OFF_X + sx * C::X;
-      const int k0 = 64 * xc.c;
-      for (int e = lane; e < nrow * 8; e += 32) {
-        const int rr = e >> 3, j = e & 7;            // rr: 0..batch-1 hi, batch.. lo
-        const int t = rr < p.batch ? rr : rr - p.batch;
-        const int srow = rr < p.batch ? t : BP + t;  // smem row
-        const __half* src = (rr < p.batch ? p.xh : p.xl) + (int64_t)t * p.K + k0 + 8 * j;
-        const int valid = p.K - (k0 + 8 * j) >= 8 ? 16 : 0;  // K is a multiple of 32
-        cp_async16(xt + srow * 128 + ((j ^ (srow & 7)) << 4), valid ? src : p.xh, valid);
-      }
-      if (lane < 16)
-        cp_async16(smem + C::OFF_SUM + sd * C::SUM + lane * 16, p.sums + (int64_t)xc.c * 64 + lane * 4, 16);
-      cp_async_commit();
-      xc.next(p);
-      if (i >= kXLag) {
-        cp_async_wait<kXLag>();
-        publish(i - kXLag);
-      }
+      if (*(volatile int*)&g_sg_error != 0)  // error path: no copy may land after the CTA exits
+        for (int j = max(0, v - kRW); j < v; ++j) mbar_wait_drain(&w_full[j % kRW], (j / kRW) & 1);
     }
-    cp_async_wait<0>();
-    if (ok)
-      for (int j = max(0, n - kXLag); j < n; ++j) publish(j);
+  } else if (warp == 10) {
+    // ===================================================== activation producer
+    if (lane == 0) {
+      pdl_wait();  // activations and sums come from the prep kernel
+      Cursor uc;
+      uc.init(p, u0);
+      int v = 0;
+      for (; v < nu; ++v) {
+        const int xs = v % kRX;
+        if (v >= kRX && !mbar_wait(&x_empty[xs], ((v / kRX) & 1) ^ 1, 0x22)) break;
+        mbar_arrive_expect_tx(&x_full[xs], C::XU);
+        bulk_g2s(smem + C::OFF_X + xs * C::XU, p.xunits + (int64_t)uc.sc * C::XU, C::XU, &x_full[xs]);
+        uc.next(p);
+      }
+      if (*(volatile int*)&g_sg_error != 0)
+        for (int j = max(0, v - kRX); j < v; ++j) mbar_wait_drain(&x_full[j % kRX], (j / kRX) & 1);
+    }
   } else if (warp == 1) {
     // ============================================================ MMA issuer
     if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < n; ++i) {
-        const int sa = i % kSA, sx = i % SX, sd = i % SD;
-        if (!mbar_wait(&a_full[sa], (i / kSA) & 1, 0x24) || !mbar_wait(&x_full[sx], (i / SX) & 1, 0x23)) break;
-        if (i >= SD && !mbar_wait(&d_free[sd], ((i / SD) & 1) ^ 1, 0x29)) break;
-        sg_tc_fence_after();
-        const uint64_t ad = sg_sdesc(smem_u32(smem + sa * kA), SG_SW128);
-        const uint64_t bd = sg_sdesc(smem_u32(smem + C::OFF_X + sx * C::X), SG_SW128);
-#pragma unroll
-        for (int blk = 0; blk < 2; ++blk) {
-          const uint32_t d = tmem + (uint32_t)((sd * 2 + blk) * C::N);
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const uint64_t o = (uint64_t)((2 * blk + j) * 2);  // 16 K = 32 bytes
-            sg_umma(d, ad + o, bd + o, C::IDESC, (uint32_t)j);
+      Cursor uc;
+      uc.init(p, u0);
+      int g = 0;
+      bool ok = true;
+      for (int v = 0; v < nu && ok; ++v) {
+        const int xs = v % kRX, cnt = uc.chunks(p);
+        if (!mbar_wait(&x_full[xs], (v / kRX) & 1, 0x23)) break;
+        for (int gi = 0; gi < C::GPU && gi * C::CPG < cnt; ++gi, ++g) {
+          const int sg = g % C::SG;
+          if (!mbar_wait(&a_full[sg], (g / C::SG) & 1, 0x24) ||
+              (g >= C::SG && !mbar_wait(&d_free[sg], ((g / C::SG) & 1) ^ 1, 0x29))) {
+            ok = false;
+            break;
           }
+          sg_tc_fence_after();
+          const int gc = min(C::CPG, cnt - gi * C::CPG);
+          for (int ci = 0; ci < gc; ++ci) {
+            const int cu = gi * C::CPG + ci;  // chunk within the unit
+            const uint32_t a0 = tmem + (uint32_t)(sg * C::A_COLS + ci * kACols);
+            const uint64_t bd = sg_sdesc(smem_u32(smem + C::OFF_X + xs * C::XU + cu * C::T), SG_SW128);
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+              const uint32_t d = tmem + C::D_COL0 + (uint32_t)(sg * C::D_COLS + (ci * 2 + blk) * C::N);
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                const int ks = 2 * blk + j;  // 16 K = 8 TMEM columns of A, 32 bytes of B
+                sg_umma_tmem_a(d, a0 + (uint32_t)(ks * 8), bd + (uint64_t)(ks * 2), C::IDESC, (uint32_t)j);
+              }
+            }
+          }
+          sg_umma_commit(&d_full[sg]);
         }
-        sg_umma_commit(&d_full[sd]);
-        issued = i + 1;
+        uc.next(p);
       }
       // every MMA issued must have completed before TMEM is freed (the last
       // commit covers all of them; on the normal path this returns at once)
-      if (issued > 0) mbar_wait_drain(&d_full[(issued - 1) % SD], ((issued - 1) / SD) & 1);
+      if (g > 0) mbar_wait_drain(&d_full[(g - 1) % C::SG], ((g - 1) / C::SG) & 1);
     }
   } else if (warp < 6) {
     // ====================================================== dequant warps
-    // One weight row per thread. The row's bytes of each chunk (2 x 16 B of
-    // nibbles, its scale word, Q4_K d|dmin) are loaded straight into
-    // registers kPD chunks ahead (coalesced: a warp's 32 rows are 512
-    // contiguous bytes), so the proxy fence before the tensor core reads the
-    // A tile covers only this thread's shared-memory stores.
-    const int row = (warp & 3) * 32 + lane;
-    const int x7 = row & 7;
-    Cursor rc;
-    rc.init(p, i0);
-    uint4 qa[kPD], qb[kPD];
-    uint32_t qs[kPD], qd[kPD];
-    auto load = [&](int slot) {
-      const Mat& mt = p.mats[rc.mi];
-      const uint8_t* tile = mt.tiles + ((int64_t)rc.rb * p.n_ch + rc.c) * SG_TILE_BYTES;
-      qa[slot] = __ldcs(reinterpret_cast<const uint4*>(tile + row * 16));
-      qb[slot] = __ldcs(reinterpret_cast<const uint4*>(tile + 2048 + row * 16));
-      qs[slot] = __ldcs(reinterpret_cast<const unsigned int*>(tile + SG_TILE_SC_OFF) + row);
-      if (DT == SG_DTYPE_Q4_K)
-        qd[slot] = __ldcs(reinterpret_cast<const unsigned int*>(mt.dd + ((int64_t)rc.rb * mt.n_sb + (rc.c >> 2)) * 128) + row);
-      rc.next(p);
-    };
-#pragma unroll
-    for (int j = 0; j < kPD; ++j)
-      if (j < n) load(j);
+    const int q = warp & 3;  // TMEM lane quadrant: rows 32q .. 32q+31
+    const int row = q * 32 + lane;
+    Cursor uc;
+    uc.init(p, u0);
+    int g = 0;
     bool ok = true;
-    for (int i0c = 0; i0c < n && ok; i0c += kPD) {
-#pragma unroll
-      for (int j = 0; j < kPD; ++j) {
-        const int i = i0c + j;
-        if (i >= n) break;
-        const int sa = i % kSA, sd = i % SD;
-        const uint4 n0 = qa[j], n1 = qb[j];
-        const uint32_t scw = qs[j], ddw = qd[j];
-        if (i + kPD < n) load(j);  // refill this register slot kPD chunks ahead
-        bool w = true;
-        if (i >= kSA) w = mbar_wait(&d_full[(i - kSA) % SD], ((i - kSA) / SD) & 1, 0x27);
-        if (w && i >= SD) w = mbar_wait(&d_free[sd], ((i / SD) & 1) ^ 1, 0x2A);
+    for (int v = 0; v < nu && ok; ++v) {
+      const int ws = v % kRW, cnt = uc.chunks(p);
+      if (!__all_sync(0xffffffffu, mbar_wait(&w_full[ws], (v / kRW) & 1, 0x26))) break;
+      const uint8_t* wu = smem + C::OFF_W + ws * kWU;
+      uint32_t ddw = 0;
+      if (DT == SG_DTYPE_Q4_K) ddw = *reinterpret_cast<const uint32_t*>(wu + kUC * SG_TILE_BYTES + row * 4);
+      for (int gi = 0; gi < C::GPU && gi * C::CPG < cnt; ++gi, ++g) {
+        const int sg = g % C::SG;
+        // the group's A tiles, accumulators and scale words were last used by
+        // group g - SG: wait until its epilogue has released them
+        const bool w = g < C::SG || mbar_wait(&d_free[sg], ((g / C::SG) & 1) ^ 1, 0x27);
         if (!__all_sync(0xffffffffu, w)) {
           ok = false;
           break;
         }
-        uint32_t* scal = reinterpret_cast<uint32_t*>(smem + C::OFF_SCAL + sd * C::SCAL);
-        scal[row] = scw;
-        if (DT == SG_DTYPE_Q4_K) scal[128 + row] = ddw;
-        uint8_t* arow = smem + sa * kA + row * 128;
-        const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+        sg_tc_fence_after();
+        uint32_t* scal = reinterpret_cast<uint32_t*>(smem + C::OFF_SCAL + sg * C::CPG * C::SCAL);
+        const int gc = min(C::CPG, cnt - gi * C::CPG);
+        for (int ci = 0; ci < gc; ++ci) {
+          const uint8_t* tile = wu + (gi * C::CPG + ci) * SG_TILE_BYTES;
+          const uint4 n0 = *reinterpret_cast<const uint4*>(tile + row * 16);
+          const uint4 n1 = *reinterpret_cast<const uint4*>(tile + 2048 + row * 16);
+          scal[ci * 256 + row] = *reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF + row * 4);
+          if (DT == SG_DTYPE_Q4_K) scal[ci * 256 + 128 + row] = ddw;
+          // this thread's row of the A tile: column c holds K pair (2c, 2c+1)
+          const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+          uint32_t av[32];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) *reinterpret_cast<uint4*>(arow + ((k ^ x7) << 4)) = sg_decode_word_f16(nw[k]);
-        fence_proxy_async_smem();
+          for (int j = 0; j < 8; ++j) {
+            const uint4 d = sg_decode_word_f16(nw[j]);
+            av[4 * j] = d.x;
+            av[4 * j + 1] = d.y;
+            av[4 * j + 2] = d.z;
+            av[4 * j + 3] = d.w;
+          }
+          sg_tmem_st32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(sg * C::A_COLS + ci * kACols), av);
+        }
+        sg_tmem_st_wait();
+        sg_tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[sa]);
+        if (lane == 0) mbar_arrive(&a_full[sg]);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&w_empty[ws]);  // this warp has read all of the unit's weights
+      uc.next(p);
     }
   } else {
     // ============================================================ epilogue warps
     const int q = warp & 3;  // TMEM lane quadrant
     const int row = q * 32 + lane;
-    float acc[BP];
+    float acc[BT];
 #pragma unroll
-    for (int t = 0; t < BP; ++t) acc[t] = 0.f;
+    for (int t = 0; t < BT; ++t) acc[t] = 0.f;
     bool waited_prev = false;
-    Cursor cur;
-    cur.init(p, i0);
-    bool seg_whole_start = cur.c == 0;
-    for (int i = 0; i < n; ++i) {
-      const int sd = i % SD;
-      const uint32_t ph = (i / SD) & 1;
-      bool w = mbar_wait(&sums_full[sd], ph, 0x2B);
-      if (w) w = mbar_wait(&d_full[sd], ph, 0x25);
-      if (!__all_sync(0xffffffffu, w)) break;
-      sg_tc_fence_after();
-      const float* sums = reinterpret_cast<const float*>(smem + C::OFF_SUM + sd * C::SUM);
-      const uint32_t* scal = reinterpret_cast<const uint32_t*>(smem + C::OFF_SCAL + sd * C::SCAL);
-      const uint32_t scw = scal[row];
-      float sc[2], of[2];
-      if (DT == SG_DTYPE_Q4_0) {
-        const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&scw));
-        sc[0] = d.x;
-        sc[1] = d.y;
-        of[0] = of[1] = 0.f;
-      } else {
-        const uint32_t ddw = scal[128 + row];
-        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddw));
-        sc[0] = dm.x * (float)(scw & 0xFFu);
-        sc[1] = dm.x * (float)((scw >> 8) & 0xFFu);
-        of[0] = dm.y * (float)((scw >> 16) & 0xFFu);
-        of[1] = dm.y * (float)(scw >> 24);
-      }
-#pragma unroll
-      for (int blk = 0; blk < 2; ++blk) {
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((sd * 2 + blk) * C::N);
-        float v[C::N];
-        if constexpr (C::N == 16) {
-          uint32_t rr[16];
-          sg_tmem_ld16(taddr, rr);
-          sg_tmem_ld_wait();
-#pragma unroll
-          for (int k = 0; k < 16; ++k) v[k] = __uint_as_float(rr[k]);
-        } else {
-          uint32_t rr[32];
-          sg_tmem_ld32(taddr, rr);
-          sg_tmem_ld_wait();
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(rr[k]);
+    Cursor uc;
+    uc.init(p, u0);
+    bool seg_whole_start = uc.sc == 0;
+    int g = 0;
+    bool ok = true;
+    for (int v = 0; v < nu && ok; ++v) {
+      const int xs = v % kRX, cnt = uc.chunks(p);
+      if (!__all_sync(0xffffffffu, mbar_wait(&x_full[xs], (v / kRX) & 1, 0x2B))) break;  // block sums
+      for (int gi = 0; gi < C::GPU && gi * C::CPG < cnt; ++gi, ++g) {
+        const int sg = g % C::SG;
+        if (!__all_sync(0xffffffffu, mbar_wait(&d_full[sg], (g / C::SG) & 1, 0x25))) {
+          ok = false;
+          break;
         }
-        const float* s0 = sums + blk * 32;
+        sg_tc_fence_after();
+        const uint32_t* scal = reinterpret_cast<const uint32_t*>(smem + C::OFF_SCAL + sg * C::CPG * C::SCAL);
+        const int gc = min(C::CPG, cnt - gi * C::CPG);
+        for (int ci = 0; ci < gc; ++ci) {
+          const int cu = gi * C::CPG + ci;
+          const float* sums = reinterpret_cast<const float*>(smem + C::OFF_X + xs * C::XU + kUC * C::T + cu * 256);
+          const uint32_t scw = scal[ci * 256 + row];
+          float sc[2], of[2];
+          if (DT == SG_DTYPE_Q4_0) {
+            const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&scw));
+            sc[0] = d.x;
+            sc[1] = d.y;
+            of[0] = of[1] = 0.f;
+          } else {
+            const uint32_t ddw = scal[ci * 256 + 128 + row];
+            const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddw));
+            sc[0] = dm.x * (float)(scw & 0xFFu);
+            sc[1] = dm.x * (float)((scw >> 8) & 0xFFu);
+            of[0] = dm.y * (float)((scw >> 16) & 0xFFu);
+            of[1] = dm.y * (float)(scw >> 24);
+          }
 #pragma unroll
-        for (int t = 0; t < BP; ++t) {
-          const float dot = (v[t] + v[BP + t]) - s0[t];
-          if (DT == SG_DTYPE_Q4_0) acc[t] = fmaf(sc[blk], dot, acc[t]);
-          else acc[t] = fmaf(sc[blk], dot, fmaf(-of[blk], s0[16 + t], acc[t]));
+          for (int blk = 0; blk < 2; ++blk) {
+            const uint32_t taddr =
+                tmem + ((uint32_t)(q * 32) << 16) + C::D_COL0 + (uint32_t)(sg * C::D_COLS + (ci * 2 + blk) * C::N);
+            uint32_t hl[2 * BT];  // hi-part columns [0, BT), lo-part columns [BT, 2 BT)
+            sg_tmem_ld_n<2 * BT>(taddr, hl);
+            sg_tmem_ld_wait();
+            const float* s0 = sums + blk * 32;
+#pragma unroll
+            for (int t = 0; t < BT; ++t) {
+              const float dot = (__uint_as_float(hl[t]) + __uint_as_float(hl[BT + t])) - s0[t];
+              if (DT == SG_DTYPE_Q4_0) acc[t] = fmaf(sc[blk], dot, acc[t]);
+              else acc[t] = fmaf(sc[blk], dot, fmaf(-of[blk], s0[16 + t], acc[t]));
+            }
+          }
         }
+        sg_tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&d_free[sg]);
       }
-      sg_tc_fence_before();
+      if (!ok) break;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&d_free[sd]);
+      if (lane == 0) mbar_arrive(&x_empty[xs]);  // this warp is done with the unit's block sums
       // row-block segment finished: store it whole, or reduce it
-      const bool rb_end = cur.c == p.n_ch - 1;
-      if (rb_end || i == n - 1) {
+      const bool rb_end = uc.sc == p.n_sc - 1;
+      if (rb_end || v == nu - 1) {
         if (!waited_prev) {
           pdl_wait();  // y: zeroing by the prep kernel, readers of the previous kernel
           waited_prev = true;
         }
-        const Mat& mt = p.mats[cur.mi];
-        const int grow = cur.rb * 128 + row;
+        const Mat& mt = p.mats[uc.mi];
+        const int grow = uc.rb * 128 + row;
         const bool whole = rb_end && seg_whole_start;
         if (grow < mt.n_rows) {
 #pragma unroll
-          for (int t = 0; t < BP; ++t) {
+          for (int t = 0; t < BT; ++t) {
             if (t < p.batch) {
               float* yp = mt.y + (int64_t)t * mt.ldy + grow;
               const float val = acc[t] * p.inv[t];
@@ -454,10 +489,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(Params p) {
           }
         }
 #pragma unroll
-        for (int t = 0; t < BP; ++t) acc[t] = 0.f;
-        seg_whole_start = true;  // the next segment starts at chunk 0 of its row-block
+        for (int t = 0; t < BT; ++t) acc[t] = 0.f;
+        seg_whole_start = true;  // the next segment starts at unit 0 of its row-block
       }
-      cur.next(p);
+      uc.next(p);
     }
   }
   pdl_launch_dependents();
@@ -471,47 +506,56 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(Params p) {
 
 // ------------------------------------------------------------ host side
 struct Layout {
-  __half* xh;
-  __half* xl;
-  float* sums;
+  uint8_t* xunits;
   float* inv;
   size_t bytes;
 };
 
+// scratch: activation units for the larger tile (BP = 16) + per-token scales
 Layout layout_of(void* base, int64_t K) {
-  auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
-  const int64_t n_ch = (K + 63) / 64;
+  auto up = [](size_t v) { return (v + 1023) & ~(size_t)1023; };
+  const int64_t n_sc = ((K + 63) / 64 + kUC - 1) / kUC;
   Layout l;
   uint8_t* b = static_cast<uint8_t*>(base);
-  const size_t xb = up((size_t)SG_GEMV_MAX_BATCH * K * 2);
-  const size_t sb = up((size_t)2 * n_ch * 2 * 16 * 4);
-  l.xh = reinterpret_cast<__half*>(b);
-  l.xl = reinterpret_cast<__half*>(b + xb);
-  l.sums = reinterpret_cast<float*>(b + 2 * xb);
-  l.inv = reinterpret_cast<float*>(b + 2 * xb + sb);
-  l.bytes = 2 * xb + sb + 256;
+  const size_t xb = up((size_t)n_sc * Cfg<16>::XU);
+  l.xunits = b;
+  l.inv = reinterpret_cast<float*>(b + xb);
+  l.bytes = xb + 1024;
   return l;
 }
 
-template <int DT, int BP>
-cudaError_t launch_gemv(int G, const Params& p, cudaStream_t st, cudaLaunchAttribute* attr) {
+template <int DT, int BP, int BT>
+cudaError_t launch(const Params& p, int G, const float* x, int64_t ldx, int K, bool zero_split, const Layout& l,
+                   cudaStream_t st) {
   using C = Cfg<BP>;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = sg_pdl_enabled() ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((2 * p.n_ch + 7) / 8), (unsigned)BT);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_xprep_kernel<BP, BT>, x, ldx, K, 2 * p.n_ch, DT == SG_DTYPE_Q4_0 ? 1 : 0,
+                                     l.xunits, l.inv, p, zero_split ? 1 : 0);
+  if (e != cudaSuccess) return e;
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<DT, BP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    e = cudaFuncSetAttribute(gemv_kernel<DT, BP, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_done[dev] = 1;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)G);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = C::SMEM;
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<DT, BP>, p);
+  cudaLaunchConfig_t g = {};
+  g.gridDim = dim3((unsigned)G);
+  g.blockDim = dim3(kThreads);
+  g.dynamicSmemBytes = C::SMEM;
+  g.stream = st;
+  g.attrs = attr;
+  g.numAttrs = 1;
+  return cudaLaunchKernelEx(&g, gemv_kernel<DT, BP, BT>, p);
 }
 
 }  // namespace gemv_tc
@@ -531,6 +575,7 @@ cudaError_t sg_gemv(const SgGemvMat* mats, int n_mats, const float* x, int64_t l
   p.n_mats = n_mats;
   p.batch = batch;
   p.n_ch = (int)w0->n_ch;
+  p.n_sc = (p.n_ch + kUC - 1) / kUC;
   p.accumulate = accumulate ? 1 : 0;
   int rb = 0;
   for (int i = 0; i < n_mats; ++i) {
@@ -539,42 +584,33 @@ cudaError_t sg_gemv(const SgGemvMat* mats, int n_mats, const float* x, int64_t l
     p.mats[i] = {w->tiles, w->dd, mats[i].y, mats[i].ldy, (int)w->n_rb, (int)w->n_rows, (int)w->n_sb, rb};
     rb += (int)w->n_rb;
   }
-  p.total = (int64_t)rb * p.n_ch;
+  p.total = (int64_t)rb * p.n_sc;
   const Layout l = layout_of(scratch, K);
-  p.sums = l.sums;
+  p.xunits = l.xunits;
   p.inv = l.inv;
-  p.xh = l.xh;
-  p.xl = l.xl;
-  p.K = (int)K;
-  // two CTAs per SM, at least two chunks each
-  const int G = (int)std::max<int64_t>(1, std::min<int64_t>(2LL * num_sms, p.total / 2));
+  // one CTA per SM
+  const int G = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms, p.total));
   p.total_rb = rb;
   p.zero_all = rb > kMaskWords * 32;
   bool split = false;
   for (int c = 1; c < G; ++c) {
-    const int64_t gi = (int64_t)c * p.total / G;
-    if (gi % p.n_ch == 0) continue;
+    const int64_t gu = (int64_t)c * p.total / G;
+    if (gu % p.n_sc == 0) continue;
     split = true;
-    const int64_t r = gi / p.n_ch;
+    const int64_t r = gu / p.n_sc;
     if (r < kMaskWords * 32) p.split[r >> 5] |= 1u << (r & 31);
   }
-
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = sg_pdl_enabled() ? 1 : 0;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((2 * p.n_ch + 7) / 8), (unsigned)batch);
-  cfg.blockDim = dim3(256);
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_xprep_kernel, x, ldx, (int)K, 2 * p.n_ch,
-                                     w0->dtype == SG_DTYPE_Q4_0 ? 1 : 0, l.xh, l.xl, l.sums, l.inv, p,
-                                     (split && !accumulate) ? 1 : 0);
-  if (e != cudaSuccess) return e;
-
-  const int BP = batch <= 8 ? 8 : 16;
-  if (w0->dtype == SG_DTYPE_Q4_0)
-    return BP == 8 ? launch_gemv<SG_DTYPE_Q4_0, 8>(G, p, st, attr) : launch_gemv<SG_DTYPE_Q4_0, 16>(G, p, st, attr);
-  return BP == 8 ? launch_gemv<SG_DTYPE_Q4_K, 8>(G, p, st, attr) : launch_gemv<SG_DTYPE_Q4_K, 16>(G, p, st, attr);
+  const bool zero_split = split && !accumulate;
+  const int K32 = (int)K;
+#define SG_GEMV_LAUNCH(DT)                                                                     \
+  switch (batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : batch <= 8 ? 8 : 16) {           \
+    case 1: return launch<DT, 8, 1>(p, G, x, ldx, K32, zero_split, l, st);                      \
+    case 2: return launch<DT, 8, 2>(p, G, x, ldx, K32, zero_split, l, st);                      \
+    case 4: return launch<DT, 8, 4>(p, G, x, ldx, K32, zero_split, l, st);                      \
+    case 8: return launch<DT, 8, 8>(p, G, x, ldx, K32, zero_split, l, st);                      \
+    default: return launch<DT, 16, 16>(p, G, x, ldx, K32, zero_split, l, st);                   \
+  }
+  if (w0->dtype == SG_DTYPE_Q4_0) SG_GEMV_LAUNCH(SG_DTYPE_Q4_0)
+  SG_GEMV_LAUNCH(SG_DTYPE_Q4_K)
+#undef SG_GEMV_LAUNCH
 }

@@ -44,6 +44,15 @@ __device__ __forceinline__ void sg_umma(uint32_t tmem_d, uint64_t adesc, uint64_
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// same, with the A operand in tensor memory (M lanes x K/2 columns of f16 pairs)
+__device__ __forceinline__ void sg_umma_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
 // arrive on bar once every tcgen05.mma this thread issued so far has completed
 __device__ __forceinline__ void sg_umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -82,7 +91,43 @@ __device__ __forceinline__ void sg_tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) 
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
 }
+// 32 lanes x N consecutive 32-bit columns, N in {1, 2, 4, 8, 16, 32}
+template <int N>
+__device__ __forceinline__ void sg_tmem_ld_n(uint32_t taddr, uint32_t (&v)[N]) {
+  if constexpr (N == 1) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v[0]) : "r"(taddr));
+  } else if constexpr (N == 2) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];" : "=r"(v[0]), "=r"(v[1]) : "r"(taddr));
+  } else if constexpr (N == 4) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(taddr));
+  } else if constexpr (N == 8) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+  } else if constexpr (N == 16) {
+    sg_tmem_ld16(taddr, v);
+  } else {
+    static_assert(N == 32, "tcgen05.ld width");
+    sg_tmem_ld32(taddr, v);
+  }
+}
+
 __device__ __forceinline__ void sg_tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive 32-bit columns from registers (lane quadrant = warp % 4)
+__device__ __forceinline__ void sg_tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void sg_tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ------------------------------------------------------- nibble decoding
 // f16 pairs from one layout word (nibble j at bit 16*(j&1) + 4*(j>>1)):
@@ -132,6 +177,25 @@ inline bool sg_make_map_16(CUtensorMap* map, const void* base, int64_t rows, int
   return fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
             dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The decode activations as a 4-D map: [chunk][part][row][64] over the
+// row-major part buffers (part 0 = hi, part 1 = lo, `part_stride` bytes
+// apart; rows `row_stride` bytes apart, each a multiple of 64 elements), so
+// one box of {64, box_rows, 2, chunks} brings, per chunk, box_rows hi rows
+// followed by box_rows lo rows: a K-major 128-byte-swizzled UMMA operand
+// tile of 2*box_rows rows. Rows >= rows and chunks >= n_chunks read as zero.
+inline bool sg_make_map_parts(CUtensorMap* map, const void* base, int64_t rows, int64_t row_stride,
+                              int64_t part_stride, int64_t n_chunks, int box_rows, int box_chunks) {
+  SgEncodeTiledFn fn = sg_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[4] = {64, (cuuint64_t)rows, 2, (cuuint64_t)n_chunks};
+  const cuuint64_t strides[3] = {(cuuint64_t)row_stride, (cuuint64_t)part_stride, 128};
+  const cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 2, (cuuint32_t)box_chunks};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 #endif
