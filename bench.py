@@ -317,26 +317,33 @@ def gpu_arm(args):
     l2 = torch.cuda.get_device_properties(local).L2_cache_size
     layer_b = sum(wbytes(k, n) for _, k, n in LAYER)
     copies = max(5, int(np.ceil(4.5 * l2 / (layer_b / world))) + 1, n_layers)
+    # one host tensor per layer linear, registered `copies` times: every copy
+    # is a separate device allocation, so rotating copies streams from HBM
+    host_w = {name: oracle.gen_weight(Q40, SEED, 1000 + i, n, k) for i, (name, k, n) in enumerate(LAYER)}
     model = []
     for c in range(copies):
         layer = {}
-        for i, (name, k, n) in enumerate(LAYER):
-            w = oracle.gen_weight(Q40, SEED, 1000 + 16 * c + i, n, k)
-            layer[name] = gpu.register(w, Q40, n, k, TP_MODE[name] if world > 1 else 0)
+        for name, k, n in LAYER:
+            layer[name] = gpu.register(host_w[name], Q40, n, k, TP_MODE[name] if world > 1 else 0)
         model.append(layer)
+    # K offset of each tensor's shard in x (row split takes a K slice)
+    col0 = {name: model[0][name].shard()[3] for name, _, _ in LAYER}
     xs = {b: torch.randn(b, 11008, device="cuda") for b in BATCHES}
     ys = {b: {name: torch.empty(b, 11008, device="cuda") for name, _, _ in LAYER} for b in BATCHES}
     LD = 11008
     kernels_per_call = 1  # the GEMV kernel
 
+    def xat(b, name):
+        return xs[b].data_ptr() + 4 * col0[name]
+
     def run_layer(layer, b, st):
-        x, y = xs[b].data_ptr(), ys[b]
-        gpu.linear_multi_device([layer["q"], layer["k"], layer["v"]], x, LD,
+        y = ys[b]
+        gpu.linear_multi_device([layer["q"], layer["k"], layer["v"]], xat(b, "q"), LD,
                                 [y["q"].data_ptr(), y["k"].data_ptr(), y["v"].data_ptr()], [LD] * 3, b, stream=st)
-        gpu.linear_device(layer["o"], x, LD, y["o"].data_ptr(), LD, b, stream=st)
-        gpu.linear_multi_device([layer["gate"], layer["up"]], x, LD, [y["gate"].data_ptr(), y["up"].data_ptr()],
-                                [LD] * 2, b, stream=st)
-        gpu.linear_device(layer["down"], x, LD, y["down"].data_ptr(), LD, b, stream=st)
+        gpu.linear_device(layer["o"], xat(b, "o"), LD, y["o"].data_ptr(), LD, b, stream=st)
+        gpu.linear_multi_device([layer["gate"], layer["up"]], xat(b, "gate"), LD,
+                                [y["gate"].data_ptr(), y["up"].data_ptr()], [LD] * 2, b, stream=st)
+        gpu.linear_device(layer["down"], xat(b, "down"), LD, y["down"].data_ptr(), LD, b, stream=st)
         return 4
 
     def step(j):
@@ -402,7 +409,7 @@ def gpu_arm(args):
             def one(name=name, b=b):
                 stp = torch.cuda.current_stream().cuda_stream
                 for c in range(copies):
-                    gpu.linear_device(model[c][name], xs[b].data_ptr(), LD, ys[b][name].data_ptr(), LD, b, stream=stp)
+                    gpu.linear_device(model[c][name], xat(b, name), LD, ys[b][name].data_ptr(), LD, b, stream=stp)
             g = graph_of(torch, one)
             g.replay()
             ms1 = time_graphs(torch, [g], reps, st)
@@ -420,15 +427,19 @@ def gpu_arm(args):
 
     # -------------------------------------------------------------- e2e
     # the public host-pointer C ABI: x copied in and y read back on every call
-    e2e = None
-    if world == 1:
-        xh = {b: np.ascontiguousarray(xs[b].cpu().numpy()) for b in BATCHES}
-        h2d = d2h = 0
-        e2e_steps = max(1, min(args.steps, args.e2e_steps))
-        t0 = time.perf_counter()
-        for j in range(e2e_steps):
-            for bi, b in enumerate(BATCHES):
-                layer = model[(j * len(BATCHES) + bi) % copies]
+    # every rank calls the host-buffer entry points for its shards (column
+    # split: its rows come back; row split: the all-reduced sum); whole-job
+    # bytes over the slowest rank's wall time
+    xh = {b: np.ascontiguousarray(xs[b].cpu().numpy()) for b in BATCHES}
+    h2d = d2h = 0
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for j in range(e2e_steps):
+        for bi, b in enumerate(BATCHES):
+            for li in range(n_layers):
+                layer = model[(j * len(BATCHES) * n_layers + bi * n_layers + li) % copies]
                 x4096 = np.ascontiguousarray(xh[b][:, :4096])
                 if b == 1:
                     gpu.linear_multi([layer["q"], layer["k"], layer["v"]], x4096[0])
@@ -440,11 +451,15 @@ def gpu_arm(args):
                 gpu.linear(layer["down"], xh[b])
                 h2d += b * 4096 * 4 * (2 if b == 1 else 6) + b * 11008 * 4
                 d2h += b * 4 * (5 * 4096 + 2 * 11008)
-        el = time.perf_counter() - t0
-        e2e = {"value": round(step_bytes(1) * e2e_steps / el / 1e9, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": h2d // e2e_steps, "d2h_bytes_per_step": d2h // e2e_steps,
-               "steps": e2e_steps,
-               "path": "sg_linear / sg_linear_multi, host buffers (copy in, launch, copy out, sync per call)"}
+    el = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([el], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el = float(t.item())
+    e2e = {"value": round(step_bytes(n_layers) * e2e_steps / el / 1e9, 3), "unit": "GB/s",
+           "h2d_bytes_per_step": h2d // e2e_steps, "d2h_bytes_per_step": d2h // e2e_steps,
+           "steps": e2e_steps,
+           "path": "sg_linear / sg_linear_multi, host buffers (copy in, launch, copy out, sync per call)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

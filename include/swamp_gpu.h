@@ -121,7 +121,8 @@ SG_API int sg_weight_shard(sg_weight_t w, int local_device, int64_t *n_rows, int
 
 /* forward_linear / forward_linear_batch: outs[b][r] = sum_k W[r][k] xs[b][k]
  * for b < batch. Host pointers (default): xs[b] has n_cols floats, outs[b]
- * n_rows floats (the whole tensor, whatever the TP split). With
+ * n_rows floats (the whole tensor, whatever the TP split; in one-process-per-
+ * GPU mode a column-split call fills only this rank's rows of outs[b]). With
  * SG_FLAG_DEVICE_PTRS (single-device or rank mode only) xs/outs point at
  * this rank's device and hold this rank's shard: x of n_cols_local, out of
  * n_rows_local (column split) or n_rows (replicate / row split, all-reduced).

@@ -80,6 +80,8 @@ struct DevState {
   size_t xbuf_bytes = 0;
   float* ybuf = nullptr;
   size_t ybuf_bytes = 0;
+  float* rbuf = nullptr;  // packed row-split partials of strided device outputs
+  size_t rbuf_bytes = 0;
   float* hbuf = nullptr;  // pinned host staging
   size_t hbuf_bytes = 0;
 };
@@ -240,6 +242,7 @@ void release_devices() {
     if (d.scratch) cudaFree(d.scratch);
     if (d.xbuf) cudaFree(d.xbuf);
     if (d.ybuf) cudaFree(d.ybuf);
+    if (d.rbuf) cudaFree(d.rbuf);
     if (d.hbuf) cudaFreeHost(d.hbuf);
     if (d.stream) cudaStreamDestroy(d.stream);
   }
@@ -668,21 +671,42 @@ int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x,
   // a NULL stream is CUDA's default stream (the CUDA convention), not the
   // library's internal stream, so callers on the default stream stay ordered
   cudaStream_t st = (cudaStream_t)stream;
-  int rc = run_linear(d, sw, n_weights, x, ldx, ys, ldys, batch, st, acc);
-  if (rc) return rc;
-  if (ws[0]->tp_mode == SG_TP_ROW && g_ctx.world > 1) {
-    if (!g_nccl.AllReduce) return fail(SG_ERR_NCCL, "NCCL not initialised");
+  if (ws[0]->tp_mode != SG_TP_ROW || g_ctx.world == 1) return run_linear(d, sw, n_weights, x, ldx, ys, ldys, batch, st, acc);
+  // Row split: every rank holds a partial sum of all n_rows outputs. They are
+  // written packed ([batch][n_rows] per tensor, back to back) so that one
+  // all-reduce covers the call, then copied into strided outputs if needed.
+  if (!g_nccl.AllReduce) return fail(SG_ERR_NCCL, "NCCL not initialised");
+  bool packed = true;
+  size_t count = 0;
+  for (int i = 0; i < n_weights; ++i) {
+    packed = packed && ldys[i] == ws[i]->n_rows && (i == 0 || ys[i] == ys[i - 1] + (size_t)batch * ws[i - 1]->n_rows);
+    count += (size_t)batch * ws[i]->n_rows;
+  }
+  float* yp[SG_GEMV_MAX_MATS];
+  int64_t lp[SG_GEMV_MAX_MATS];
+  if (packed) {
     for (int i = 0; i < n_weights; ++i) {
-      const int64_t nr = ws[i]->n_rows;
-      const int calls = ldys[i] == nr ? 1 : batch;
-      const size_t count = ldys[i] == nr ? (size_t)batch * nr : (size_t)nr;
-      for (int b = 0; b < calls; ++b) {
-        float* yb = ys[i] + (size_t)b * ldys[i];
-        ncclResult_t r = g_nccl.AllReduce(yb, yb, count, kNcclFloat, kNcclSum, d.comm, st);
-        if (r) return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
-      }
+      yp[i] = ys[i];
+      lp[i] = ldys[i];
+    }
+  } else {
+    int rc = ensure_buf((void**)&d.rbuf, &d.rbuf_bytes, count * sizeof(float));
+    if (rc) return rc;
+    size_t off = 0;
+    for (int i = 0; i < n_weights; ++i) {
+      yp[i] = d.rbuf + off;
+      lp[i] = ws[i]->n_rows;
+      off += (size_t)batch * ws[i]->n_rows;
     }
   }
+  int rc = run_linear(d, sw, n_weights, x, ldx, yp, lp, batch, st, false);
+  if (rc) return rc;
+  ncclResult_t r = g_nccl.AllReduce(yp[0], yp[0], count, kNcclFloat, kNcclSum, d.comm, st);
+  if (r) return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
+  if (!packed)
+    for (int i = 0; i < n_weights; ++i)
+      CUDA_TRY(cudaMemcpy2DAsync(ys[i], (size_t)ldys[i] * sizeof(float), yp[i], (size_t)lp[i] * sizeof(float),
+                                 (size_t)lp[i] * sizeof(float), batch, cudaMemcpyDeviceToDevice, st));
   return SG_OK;
 }
 
