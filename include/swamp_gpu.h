@@ -142,6 +142,22 @@ SG_API int sg_linear_device(sg_weight_t w, const float *x, int64_t ldx, float *y
 SG_API int sg_linear_multi_device(const sg_weight_t *ws, int n_weights, const float *x, int64_t ldx,
                            float *const *ys, const int64_t *ldys, int batch, void *stream, int flags);
 
+/* sg_linear_device for callers that must not trigger a device allocation --
+ * for example a serving loop with a fixed memory budget, where the implicit
+ * device-wide synchronisation of a first-use cudaMalloc would stall other
+ * streams. Same arguments and results as sg_linear_device for one tensor at
+ * decode batch 1..16, but the activation scratch is a fixed array inside the
+ * library (sized for n_cols <= 16384; larger tensors and batches are rejected
+ * with SG_ERR_UNSUPPORTED and a message naming the limit), so the call
+ * allocates nothing. The first call on a device looks up that array's address
+ * once; make it before any stream capture begins. Calls on one device share
+ * the array: calls whose work may overlap in time (different streams with no
+ * ordering between them) race, so order them. A row-split tensor in
+ * one-process-per-GPU mode needs ldy == n_rows and no SG_FLAG_ACCUMULATE.
+ * The reference has no counterpart: its CPU path allocates per call. */
+SG_API int sg_linear_device_noalloc(sg_weight_t w, const float *x, int64_t ldx, float *y, int64_t ldy, int batch,
+                                    void *stream, int flags);
+
 /* Dequantize the whole tensor to f32 [n_rows][n_cols] (host pointer, or this
  * rank's shard into device memory with SG_FLAG_DEVICE_PTRS). Bit-exact with
  * swamp-gguf's dequant. */

@@ -7,3 +7,4 @@
 #include "sg_gemv.cu"
 #include "sg_gemm.cu"
 #include "sg_api.cu"
+#include "sg_noalloc.cu"

@@ -34,7 +34,7 @@ BLOCK_BYTES = {SG_DTYPE_Q4_0: 18, SG_DTYPE_Q4_K: 144}
 EXPORTS = (
     "sg_init", "sg_get_unique_id", "sg_init_rank", "sg_shutdown", "sg_last_error", "sg_topology",
     "sg_weight_register", "sg_weight_free", "sg_tp_shard", "sg_weight_shard", "sg_linear", "sg_linear_multi",
-    "sg_linear_device", "sg_linear_multi_device", "sg_dequant_f32", "sg_fused_gemv_q4k",
+    "sg_linear_device", "sg_linear_multi_device", "sg_linear_device_noalloc", "sg_dequant_f32", "sg_fused_gemv_q4k",
     "sg_synchronize",
 )
 
@@ -64,6 +64,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     L.sg_linear_multi.argtypes = [P, i32, P, P, i32]
     L.sg_linear_device.argtypes = [P, P, i64, P, i64, i32, P, i32]
     L.sg_linear_multi_device.argtypes = [P, i32, P, i64, P, P, i32, P, i32]
+    L.sg_linear_device_noalloc.argtypes = [P, P, i64, P, i64, i32, P, i32]
     L.sg_dequant_f32.argtypes = [P, P, i32]
     L.sg_fused_gemv_q4k.argtypes = [P, P, P, i32, i32]
     L.sg_synchronize.argtypes = []
@@ -196,6 +197,11 @@ class SwampGpu:
                       stream: int = 0, flags: int = 0):
         """Stream-ordered device call (pointers are raw device addresses)."""
         self._check(self.L.sg_linear_device(w.handle, x_ptr, ldx, y_ptr, ldy, batch, stream or None, flags))
+
+    def linear_device_noalloc(self, w: Weight, x_ptr: int, ldx: int, y_ptr: int, ldy: int, batch: int,
+                              stream: int = 0, flags: int = 0):
+        """linear_device without any device allocation (decode batch 1..16, n_cols <= 16384)."""
+        self._check(self.L.sg_linear_device_noalloc(w.handle, x_ptr, ldx, y_ptr, ldy, batch, stream or None, flags))
 
     def linear_multi_device(self, ws: Sequence[Weight], x_ptr: int, ldx: int, y_ptrs: Sequence[int],
                             ldys: Sequence[int], batch: int, stream: int = 0, flags: int = 0):
