@@ -146,14 +146,18 @@ SG_API int sg_linear_multi_device(const sg_weight_t *ws, int n_weights, const fl
  * for example a serving loop with a fixed memory budget, where the implicit
  * device-wide synchronisation of a first-use cudaMalloc would stall other
  * streams. Same arguments and results as sg_linear_device for one tensor at
- * decode batch 1..16, but the activation scratch is a fixed array inside the
- * library (sized for n_cols <= 16384; larger tensors and batches are rejected
- * with SG_ERR_UNSUPPORTED and a message naming the limit), so the call
- * allocates nothing. The first call on a device looks up that array's address
- * once; make it before any stream capture begins. Calls on one device share
- * the array: calls whose work may overlap in time (different streams with no
- * ordering between them) race, so order them. A row-split tensor in
- * one-process-per-GPU mode needs ldy == n_rows and no SG_FLAG_ACCUMULATE.
+ * decode batch 1..16 (larger batches are rejected with SG_ERR_UNSUPPORTED:
+ * they run the prefill GEMM, whose activation scratch is allocated on first
+ * use). The decode kernel's workspace (cross-CTA flags and, from 3 tokens
+ * on, the converted activation operands) is a fixed per-device array inside
+ * the library, so the call allocates nothing: any n_cols at batch 1..2,
+ * n_cols up to 32768 at batch 16 (more at fewer tokens; wider tensors are
+ * rejected with SG_ERR_UNSUPPORTED and a message naming the limit). The first call on a
+ * device looks up that workspace's address once; make it before any stream
+ * capture begins. All decode calls on a device share the workspace: calls
+ * whose work may overlap in time (different streams with no ordering between
+ * them) race, so order them. A row-split tensor in one-process-per-GPU mode
+ * needs ldy == n_rows and no SG_FLAG_ACCUMULATE.
  * The reference has no counterpart: its CPU path allocates per call. */
 SG_API int sg_linear_device_noalloc(sg_weight_t w, const float *x, int64_t ldx, float *y, int64_t ldy, int batch,
                                     void *stream, int flags);

@@ -74,8 +74,10 @@ struct DevState {
   int num_sms = 0;
   cudaStream_t stream = nullptr;
   ncclComm_t comm = nullptr;
-  void* scratch = nullptr;  // activation scratch of the GEMV / GEMM kernels (grows on demand)
+  void* scratch = nullptr;  // activation scratch of the prefill GEMM (grows on demand)
   size_t scratch_bytes = 0;
+  void* gemv_ws = nullptr;  // decode workspace for tensors wider than the static one
+  size_t gemv_ws_bytes = 0;
   float* xbuf = nullptr;  // staging for host-pointer calls
   size_t xbuf_bytes = 0;
   float* ybuf = nullptr;
@@ -197,6 +199,33 @@ int ensure_host(DevState& d, size_t need) {
   return SG_OK;
 }
 
+// ------------------------------------------------------- GEMV workspace
+// The decode GEMV's workspace (sg_gemv.cuh): zeroing flags, then activation
+// images. Up to kStaticWsCols columns it is a fixed array per device inside
+// the library, so no decode call allocates; wider tensors use a buffer that
+// grows on demand (flags zeroed when it is allocated). Flags hold per-call
+// epochs, so no state carries over from one call (or a failed one) to the
+// next.
+constexpr int64_t kStaticWsCols = 32768;
+constexpr size_t kStaticWsBytes =
+    gemv_tc::kFlagsBytes + (size_t)((kStaticWsCols / 64 + gemv_tc::kUC - 1) / gemv_tc::kUC) * gemv_tc::Cfg<16>::XU;
+static __device__ __align__(256) uint8_t g_gemv_ws[kStaticWsBytes];
+std::mutex g_ws_mu;
+void* g_ws_ptr[64] = {nullptr};
+
+cudaError_t static_workspace(int device, void** out) {
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  if (!g_ws_ptr[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_ws);
+    if (e != cudaSuccess) return e;
+    g_ws_ptr[device] = p;
+  }
+  *out = g_ws_ptr[device];
+  return cudaSuccess;
+}
+
 int check_device_error(DevState& d) {
   int v = 0;
   CUDA_TRY(cudaSetDevice(d.device));
@@ -240,6 +269,7 @@ void release_devices() {
     cudaSetDevice(d.device);
     if (d.comm && g_nccl.CommDestroy) g_nccl.CommDestroy(d.comm);
     if (d.scratch) cudaFree(d.scratch);
+    if (d.gemv_ws) cudaFree(d.gemv_ws);
     if (d.xbuf) cudaFree(d.xbuf);
     if (d.ybuf) cudaFree(d.ybuf);
     if (d.rbuf) cudaFree(d.rbuf);
@@ -258,15 +288,33 @@ int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* 
   if (((uintptr_t)x & 15) || (ldx & 3))
     return fail(SG_ERR_INVALID_ARG, "x must be 16-byte aligned with a row stride that is a multiple of 4 floats");
   if (batch <= SG_GEMV_MAX_BATCH) {
-    int rc = ensure_buf(&d.scratch, &d.scratch_bytes, sg_gemv_scratch_bytes(K));
-    if (rc) return rc;
+    void* gws = nullptr;
+    size_t gws_bytes = sg_gemv_scratch_bytes(K, batch);
+    if (gws_bytes <= kStaticWsBytes) {
+      CUDA_TRY(static_workspace(d.device, &gws));
+      gws_bytes = kStaticWsBytes;
+    } else {
+      if (d.gemv_ws_bytes < gws_bytes) {
+        if (d.gemv_ws) cudaFree(d.gemv_ws);
+        d.gemv_ws = nullptr;
+        d.gemv_ws_bytes = 0;
+        if (cudaMalloc(&d.gemv_ws, gws_bytes) != cudaSuccess) {
+          cudaGetLastError();
+          return fail(SG_ERR_OOM, "cudaMalloc(%zu) failed", gws_bytes);
+        }
+        d.gemv_ws_bytes = gws_bytes;
+        CUDA_TRY(cudaMemsetAsync(d.gemv_ws, 0, gemv_tc::kFlagsBytes, st));
+      }
+      gws = d.gemv_ws;
+      gws_bytes = d.gemv_ws_bytes;
+    }
     // one launch per run of consecutive same-dtype matrices
     for (int i0 = 0; i0 < n_w;) {
       int i1 = i0 + 1;
       while (i1 < n_w && i1 - i0 < SG_GEMV_MAX_MATS && ws[i1]->dtype == ws[i0]->dtype) ++i1;
       SgGemvMat mats[SG_GEMV_MAX_MATS];
       for (int i = i0; i < i1; ++i) mats[i - i0] = {ws[i], ys[i], ldys[i]};
-      CUDA_TRY(sg_gemv(mats, i1 - i0, x, ldx, batch, accumulate, d.scratch, d.scratch_bytes, d.num_sms, st));
+      CUDA_TRY(sg_gemv(mats, i1 - i0, x, ldx, batch, accumulate, gws, gws_bytes, d.num_sms, st));
       i0 = i1;
     }
     return SG_OK;

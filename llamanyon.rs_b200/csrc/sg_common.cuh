@@ -98,18 +98,29 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Bounded wait: returns false (and records SG_DEVERR_WAIT_TIMEOUT | tag) if the
 // phase with the given parity has not completed after SG_WAIT_NS nanoseconds
 // of wall time (or after another thread already recorded an error).
+//
+// The poll loop touches nothing but the barrier and the SM's cycle counter:
+// the global error flag and the wall clock are read only once a wait has
+// lasted SG_WAIT_QUIET_CYCLES. A global load in the loop would take a
+// microsecond while HBM is saturated by the weight stream, and a barrier
+// that completes meanwhile would go unnoticed for that long.
 #ifndef SG_WAIT_NS
 #define SG_WAIT_NS 4000000000ull
 #endif
+#ifndef SG_WAIT_QUIET_CYCLES
+#define SG_WAIT_QUIET_CYCLES (1ll << 17)
+#endif
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int tag) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long c0 = clock64();
+  uint64_t t0 = 0;
   for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 16; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (*(volatile int*)&g_sg_error != 0) return false;
-    if (globaltimer_ns() - t0 > SG_WAIT_NS) break;
+    if (mbar_try_wait(bar, parity)) return true;
+    if (clock64() - c0 > SG_WAIT_QUIET_CYCLES) {  // a long wait: watch the error flag and the wall clock
+      if (t0 == 0) t0 = globaltimer_ns();
+      if (*(volatile int*)&g_sg_error != 0) return false;
+      if (globaltimer_ns() - t0 > SG_WAIT_NS) break;
+    }
   }
   sg_set_error(SG_DEVERR_WAIT_TIMEOUT | tag);
   return false;
@@ -219,6 +230,17 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint3
   uint32_t r;
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(orv));  // (a & b) | c
   return r;
+}
+
+// 64-bit flag store with release semantics at GPU scope, and a relaxed
+// (volatile) load of it; pair the load with __threadfence() to acquire.
+__device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void red_add_f32(float* addr, float v) {

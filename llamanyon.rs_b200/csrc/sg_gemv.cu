@@ -1,5 +1,5 @@
 // sg_gemv.cu -- decode GEMV (batch 1..16) for Q4_0 / Q4_K on B200 tensor
-// cores (tcgen05, accumulators in TMEM).
+// cores (tcgen05 kind::i8, operands and accumulators in TMEM).
 //
 // Replaces the engine's per-token GEMV routes: forward_linear's Q4_0 path
 // (swamp-engine/src/linear.rs:68-87: dequant + f32 row dots) and
@@ -9,88 +9,128 @@
 //
 // Arithmetic. Per 32-element block b of row r (Q4_0: w = d*(q-8); Q4_K:
 // w = sv*q - mv with sv = d*sc, mv = dmin*m):
-//   y[t][r] = sum_b ( sv_b * sum_{k in b} q_k u_k  -  mv_b * sum_{k in b} u_k )
-// The tensor core computes the integer part exactly: A holds f16 (1024+q) or
-// (1024+16q) (exact, straight from the nibbles), B holds the activation as
-// two f16 parts hi + lo per token (x scaled per token by a power of two so
-// the parts keep 22 significant bits; the x16 positions carry x/16). Each
-// block gets its own f32 accumulator in TMEM; the epilogue subtracts the
-// block's constant part (precomputed per token from the same hi + lo values,
-// so the 1024 offset cancels exactly) and applies the block scale in f32.
+//   y[t][r] = sum_b ( sv_b * sum_{k in b} q_k x_k  -  mv_b * sum_{k in b} x_k )
+// The integer part runs on the tensor core, exactly: A holds the raw nibbles
+// q as u8, B holds the activations as three signed 8-bit digits. Per unit of
+// 256 K and token, x is scaled by a power of two s (max |x| * s in [32, 64))
+// and rounded to V = rint(x * s * 2^14), |V| <= 2^20, which splits exactly
+// into V = d0 * 2^14 + d1 * 2^7 + d2 with every digit in [-64, 64].
+// D_i = sum_k q_k d_i,k per 32-block is exact in s32 (|D_i| < 2^15); the
+// epilogue rebuilds sum q u = D0 + D1/128 + D2/16384 (u = V / 2^14) exactly
+// before one rounding, subtracts the block's constant part (sum u, computed
+// from the same digits) and applies the block scales in f32; per unit the
+// sum is scaled back by 1/s.
 //
-// Data movement is built around one measured fact of the copy engine: each
-// issuing thread completes bulk copies one after another at a roughly fixed
-// cost per copy, so bandwidth comes from large copies. Work is therefore cut
-// in units of 4 chunks (128 rows x 256 K) -- 18 KB of packed weights,
-// contiguous in the tile layout -- and each unit's weights and activations
-// arrive in one bulk copy each.
+// Block-diagonal activation tiles. One MMA covers one 32-block (K = 32
+// bytes), and every block needs its own columns (its scales differ per
+// row). Instead of one accumulator per block, each chunk's activation tile
+// gives every (block, digit, token) its own row of B, holding that block's
+// digits in the block's half of K and zeros elsewhere; all MMAs of GC chunks
+// then accumulate into one accumulator of N = GC*6*BT columns (padded to
+// 16), each block landing in its own columns. At one token a whole 256-K
+// unit needs 32 TMEM columns instead of 8 x 16, so several groups fit in
+// flight.
 //
-// Kernels, chained with programmatic dependent launch:
-//  1. gemv_xprep_kernel: power-of-two scale per token, f16 hi/lo activation
-//     parts written directly in the swizzled UMMA operand layout, unit by
-//     unit, with each unit's per-block sums appended; zeroing of the output
-//     rows that several CTAs reduce into.
-//  2. gemv_kernel<dtype, BP>: one CTA per SM, balanced split -- CTA c takes
-//     units [c*T/G, (c+1)*T/G) of the T = row-blocks x units space, crossing
-//     row-block (and matrix) boundaries; a row-block seen whole is stored, a
-//     shared one is reduced with red.add.
-//       warp 0      weight producer: one cp.async.bulk per unit into a
-//                   4-slot ring (issued before the wait on the previous
-//                   kernel: weights do not depend on it).
-//       warp 10     activation producer: one cp.async.bulk per unit (4
-//                   operand tiles + block sums) into a 3-slot ring.
-//       warp 1      TMEM owner; one thread issues tcgen05.mma (A from TMEM,
-//                   M=128, N=2*BP: BP hi token rows + BP lo token rows,
-//                   K=16, f16 -> f32), two per 32-block, into a ring of TMEM
-//                   accumulator slots.
-//       warps 2-5   dequant: one weight row per thread, two 16-byte reads
-//                   and 8 lop3 + 2 shifts per 64 K, written with one
-//                   tcgen05.st into a tensor-memory A tile (lane = row), so
-//                   the dequantized operand never passes through shared
-//                   memory.
-//       warps 6-9   epilogue: per chunk, tcgen05.ld of the two block
-//                   accumulators of its TMEM lane quadrant (warp % 4), block
-//                   scales in f32, output rows stored or reduced.
-// Every mbarrier wait is bounded (sg_common.cuh).
+// Work split: the chunks (128 rows x 64 K, one 4608-byte tile each) of all
+// row-blocks of all matrices form one sequence, row-block major; CTA c of G
+// takes chunks [c*T/G, (c+1)*T/G). It walks them in pieces -- the part of
+// one unit (4 consecutive chunks = 256 K = one Q4_K super-block) inside its
+// range -- so each piece's weights arrive in one bulk copy (bandwidth comes
+// from large copies). A row-block covered by one CTA is stored directly;
+// one shared by several CTAs is reduced into y with red.add: the CTA holding
+// its first chunks zeroes its rows when the kernel starts and publishes the
+// call's epoch in a flag of the workspace after its first group; the other
+// CTAs confirm the flag (read early, checked at the end of their segment)
+// before their first red.add. With SG_FLAG_ACCUMULATE nothing is zeroed.
+//
+// One kernel per call, one CTA per SM, 12 warps:
+//   warp 0      weight producer: one cp.async.bulk per piece into a 6-slot
+//               ring (issued before the wait on the previous kernel: weights
+//               do not depend on it).
+//   warps 2-5   dequant: one weight row per thread: two 16-byte reads, two
+//               masks per 32-bit word, one tcgen05.st of the chunk's 64 u8
+//               nibbles into the row's TMEM lane (lane = row), and one
+//               tcgen05.st of the group's scale words; then the weight slot
+//               is released, so the ring never waits for the epilogue.
+//   warp 1      TMEM owner; one thread issues tcgen05.mma kind::i8 (A from
+//               TMEM, B = activation tile in shared memory, M=128, K=32,
+//               one instruction per 32-block) into a ring of TMEM groups.
+//   warps 6-9   epilogue: per group, tcgen05.ld of the accumulators and the
+//               scale words of its TMEM lane quadrant (warp % 4), block
+//               scales in f32, output rows stored or reduced.
+//   warps 10-11 activations: per piece, the unit's digits for each live
+//               token (one warp per token at a time) into a 3-slot ring of
+//               block-diagonal tiles; the next unit's x is loaded while
+//               waiting.
+// A TMEM group slot holds a group's A tiles, scale words and accumulators;
+// the dequant warps wait for its epilogue (d_free) before rewriting it, so
+// the MMA thread waits only for a_full. Every mbarrier wait is bounded
+// (sg_common.cuh).
 #include <algorithm>
+#include <atomic>
 
 #include "sg_gemv.cuh"
 #include "sg_tc.cuh"
 
 namespace gemv_tc {
 
-constexpr int kUC = 4;                     // chunks per unit
-constexpr int kRW = 4;                     // weight unit ring
-constexpr int kRX = 3;                     // activation unit ring
-constexpr int kACols = 32;                 // TMEM columns of one A tile: 128 lanes x 64 K f16
+constexpr int kUC = 4;                          // chunks per unit
+constexpr int kRW = 6;                          // weight piece ring
+constexpr int kACols = 16;                      // TMEM columns of one chunk's A tile: 64 K of u8 per lane
+constexpr int kScCols = 5;                      // TMEM columns of a group's scale words (chunks 0..3, Q4_K d|dmin at 4)
 constexpr int kWU = kUC * SG_TILE_BYTES + 512;  // packed weights of a unit + Q4_K d|dmin
-constexpr int kThreads = 352;
-constexpr int kMaskWords = 32;             // split row-block bitmask (row-blocks 0..1023)
+constexpr int kThreads = 384;
+constexpr int kXWarps = 2;                      // activation warps
+constexpr int kMaxCtas = SG_GEMV_MAX_CTAS;
+constexpr int kSumOff = 0;                      // within a unit's tail: block sums [chunk 4][blk 2][token 16] f32
+constexpr int kInvOff = 512;                    //                       1/s per token [16] f32
 
-template <int BP>
+template <int BT>
 struct Cfg {
-  static constexpr int N = 2 * BP;                   // MMA N: hi rows then lo rows
-  static constexpr int CPG = BP == 8 ? 4 : 2;        // chunks per group (one hand-off between roles)
-  static constexpr int GPU = kUC / CPG;              // groups per unit
-  static constexpr int SG = 2;                       // groups in flight: A tiles and accumulators in TMEM
-  static constexpr int T = N * 128;                  // activation tile bytes (one chunk)
-  static constexpr int XU = kUC * T + kUC * 256;     // activation unit: 4 tiles + 4 x block sums
-  static constexpr int SCAL = 1024;                  // per chunk: [2][128] u32 row scale words
+  static constexpr int GC = BT <= 2 ? 4 : BT == 16 ? 1 : 2;   // chunks per accumulator
+  // From 4 tokens on, the activation tiles are built once per call by
+  // gemv_xprep_kernel (an image in global memory, one bulk copy per piece):
+  // converting them in every CTA would repeat the work for each row-block.
+  // Work is then split on GC-chunk boundaries, so a chunk's accumulator
+  // position is always chunk % GC.
+  static constexpr bool XPRE = BT >= 4;
+  static constexpr int SPL = XPRE ? GC : 1;                  // work split granularity (chunks)
+  static constexpr int CPG = BT >= 8 ? 2 : 4;                // chunks per group (one hand-off between roles)
+  static constexpr int NACC = CPG / GC;                      // accumulators per group
+  static constexpr int ROWS = GC * 6 * BT;                   // B rows: (chunk, block, digit, token)
+  static constexpr int N = (ROWS + 15) / 16 * 16;            // MMA N
+  static constexpr int T = N * 64;                           // activation tile bytes (one chunk)
+  static constexpr int XU = kUC * T + 1024;                  // activation unit: 4 tiles + sums + scales
+  static constexpr int RX = BT == 1 ? 8 : BT == 2 ? 6 : 3;    // activation unit ring: deep where units are small
+  static constexpr int NTW = BT == 1 ? 1 : BT / kXWarps;     // tokens per activation job (one warp, one piece)
+  static constexpr int XS = XPRE ? 0 : 3;                    // staging slots per activation warp (x prefetch)
   static constexpr int OFF_X = 0;
-  static constexpr int OFF_W = OFF_X + kRX * XU;
-  static constexpr int OFF_SCAL = OFF_W + kRW * kWU;
-  // Each CTA takes all 512 TMEM columns, so two CTAs must never share an SM
-  // (the second would wait in tcgen05.alloc): ask for more than half of the
-  // SM's shared memory.
-  static constexpr int SMEM_USED = OFF_SCAL + SG * CPG * SCAL + 1024;
+  static constexpr int OFF_S = OFF_X + RX * XU;              // x staging: [warp][slot][token][256] f32
+  static constexpr int OFF_W = OFF_S + kXWarps * XS * NTW * 1024;
+  // One CTA per SM: two CTAs of consecutive calls sharing an SM under PDL
+  // would make the second wait in tcgen05.alloc; ask for more than half of
+  // the SM's shared memory.
+  static constexpr int SMEM_USED = OFF_W + kRW * kWU + 1024;
   static constexpr int SMEM = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
-  static constexpr uint32_t A_COLS = CPG * kACols;   // TMEM columns of a group's A tiles
-  static constexpr uint32_t D_COLS = CPG * 2 * N;    // TMEM columns of a group's block accumulators
-  static constexpr uint32_t D_COL0 = SG * A_COLS;    // A tiles first, then the accumulators
+  // TMEM: [SG accumulator blocks][SG A-tile blocks][SG x kScCols scale
+  // words]. Every multi-column access starts on a multiple of 16 columns;
+  // scale words are read and written one column at a time.
+  static constexpr uint32_t A_COLS = CPG * kACols;
+  static constexpr uint32_t D_COLS = NACC * N;
+  static constexpr uint32_t G_COLS = A_COLS + kScCols + D_COLS;  // one group slot
+  static constexpr int SG = (int)(512 / G_COLS) > 6 ? 6 : (int)(512 / G_COLS);  // group slots
+  static constexpr uint32_t A_COL0 = SG * D_COLS;
+  static constexpr uint32_t SC_COL0 = A_COL0 + SG * A_COLS;
+  __host__ __device__ static constexpr uint32_t d_col(int sg) { return (uint32_t)sg * D_COLS; }
+  __host__ __device__ static constexpr uint32_t a_col(int sg) { return A_COL0 + (uint32_t)sg * A_COLS; }
+  __host__ __device__ static constexpr uint32_t sc_col(int sg) { return SC_COL0 + (uint32_t)sg * kScCols; }
   static constexpr uint32_t TMEM_COLS = 512;
-  static_assert(D_COL0 + SG * D_COLS <= TMEM_COLS, "TMEM budget");
-  static constexpr uint32_t IDESC = sg_idesc_f16(128, N);
-  static_assert(XU % 1024 == 0, "activation units must keep 1024-byte tile alignment");
+  static constexpr uint32_t IDESC = sg_idesc_u8s8(128, N);
+  static_assert(SG >= 2 && SC_COL0 + SG * kScCols <= TMEM_COLS, "TMEM budget");
+  static_assert(D_COLS % 16 == 0 && A_COLS % 16 == 0, "TMEM alignment");
+  static_assert(N <= 256 && ROWS <= N, "MMA N");
+  static_assert(XU % 1024 == 0, "operand tiles keep 1024-byte alignment");
+  static_assert(SMEM_USED <= 227 * 1024, "shared memory budget");
 };
 
 struct Mat {
@@ -103,13 +143,16 @@ struct Mat {
 
 struct Params {
   Mat mats[SG_GEMV_MAX_MATS];
-  int n_mats, batch, n_ch, n_sc, accumulate;
-  int64_t total;          // row-blocks x units
-  const uint8_t* xunits;  // activation units (xprep layout)
-  const float* inv;       // [16] per-token 2^-e
-  int total_rb;
-  int zero_all;                  // more row-blocks than the mask holds: zero every split candidate
-  uint32_t split[kMaskWords];    // bit rbg: row-block reduced by more than one CTA (zeroed first)
+  int n_mats, batch, n_ch, accumulate;
+  int n_cp;        // chunks per row-block in the work index, n_ch rounded up to the split granularity
+  int spl;         // split granularity: CTA ranges start and end on multiples of it
+  int64_t total;   // work-index chunks over all row-blocks of all matrices (n_cp per row-block)
+  uint8_t* ximg;   // activation unit images (gemv_xprep_kernel), when the configuration uses them
+  const float* x;  // [batch][ldx]
+  int64_t ldx;
+  int K;
+  unsigned long long* zflags;  // [kMaxCtas][4]: epoch once CTA c zeroed the shared rows of lane quadrant q
+  unsigned long long epoch;    // this call's epoch (never 0, never repeated)
 };
 
 __device__ __forceinline__ int find_mat(const Params& p, int rbg) {
@@ -120,19 +163,43 @@ __device__ __forceinline__ int find_mat(const Params& p, int rbg) {
   return m;
 }
 
-// Unit cursor: walks the CTA's units without divisions.
+// CTA whose chunk range holds global chunk gc (range of c: [c*T/G, (c+1)*T/G))
+__device__ __forceinline__ int cta_of(const Params& p, int64_t gc) {
+  const int64_t ts = p.total / p.spl;
+  return (int)(((gc / p.spl + 1) * (int64_t)gridDim.x - 1) / ts);
+}
+// the work-index chunk range [g0, g1) of CTA b (multiples of spl)
+__device__ __forceinline__ void cta_range(const Params& p, int b, int64_t& g0, int64_t& g1) {
+  const int64_t ts = p.total / p.spl;
+  g0 = (int64_t)b * ts / gridDim.x * p.spl;
+  g1 = (int64_t)(b + 1) * ts / gridDim.x * p.spl;
+}
+
+// Piece cursor over the CTA's chunk range [g, g1).
 struct Cursor {
-  int rbg, sc, mi, rb;  // global row-block, unit within it, matrix, row-block within the matrix
-  __device__ __forceinline__ void init(const Params& p, int64_t gu) {
-    rbg = (int)(gu / p.n_sc);
-    sc = (int)(gu % p.n_sc);
+  int rbg, c, mi, rb;  // global row-block, chunk within it, matrix, row-block within the matrix
+  int64_t g, g1;
+  __device__ __forceinline__ void init(const Params& p, int64_t g0, int64_t gend) {
+    g = g0;
+    g1 = gend;
+    rbg = (int)(g0 / p.n_cp);
+    c = (int)(g0 - (int64_t)rbg * p.n_cp);  // range ends never fall in the padding
     mi = find_mat(p, rbg);
     rb = rbg - p.mats[mi].rb0;
   }
-  __device__ __forceinline__ int chunks(const Params& p) const { return min(kUC, p.n_ch - kUC * sc); }
+  __device__ __forceinline__ bool more() const { return g < g1; }
+  __device__ __forceinline__ int sc() const { return c >> 2; }
+  __device__ __forceinline__ int ci0() const { return c & 3; }
+  __device__ __forceinline__ int cnt(const Params& p) const {
+    return (int)min((int64_t)min(kUC - (c & 3), p.n_ch - c), g1 - g);
+  }
   __device__ __forceinline__ void next(const Params& p) {
-    if (++sc == p.n_sc) {
-      sc = 0;
+    const int n = cnt(p);
+    g += n;
+    c += n;
+    if (c == p.n_ch) {
+      g += p.n_cp - p.n_ch;  // skip the padding of the work index
+      c = 0;
       ++rbg;
       ++rb;
       if (mi + 1 < p.n_mats && rbg >= p.mats[mi + 1].rb0) {
@@ -143,115 +210,316 @@ struct Cursor {
   }
 };
 
-// ---------------------------------------------------------------- x prep
-// Grid (block groups of 8, token rows BP). For token row t < batch: the
-// token's max|x| sets s = 2^e (max|x|*s in [2^14, 2^15)); positions k%8 in
-// {2,3,6,7} carry x*s/16 (their A values are 1024+16q). u is the value the
-// tensor core sees (hi + lo, times 16 at those positions). Token rows
-// batch <= t < BT are written as zeros. Unit layout (XU bytes per 4 chunks):
-// 4 operand tiles [row 2*BP][128 B, 16-byte segment j of row r at
-// ((j ^ (r & 7)) << 4)], rows 0..BT-1 hi parts and BT..2BT-1 lo parts (rows
-// from 2*BT on are never read back: their product columns are ignored), then
-// per chunk
-// sums[blk 2][2][16]: [0] Q4_0: sum (c+8) u, Q4_K: sum c u (c = 1024 or
-// 64); [1] sum u.
-template <int BP, int BT>
-__global__ void __launch_bounds__(256) gemv_xprep_kernel(const float* __restrict__ x, int64_t ldx, int K, int n_blk,
-                                                         int q40, uint8_t* __restrict__ xunits,
-                                                         float* __restrict__ inv, Params zp, int zero_split) {
-  using C = Cfg<BP>;
-  pdl_launch_dependents();
-  pdl_wait();  // x may come from the previous kernel; scratch and y may still be in use by it
-  __shared__ float red[8];
-  const int t = blockIdx.y;
-  const bool live = t < zp.batch;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float* xr = x + (int64_t)t * ldx;
-  float m = 0.f;
-  if (live)
-    for (int k = threadIdx.x * 4; k < K; k += 1024) {
-      const float4 v = *reinterpret_cast<const float4*>(xr + k);
-      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
+
+// 16-byte segment j of row r of a K-major SWIZZLE_64B tile (64-byte rows)
+__device__ __forceinline__ int sw64_off(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
+
+// ------------------------------------------------------- activation digits
+// For unit sc and token t, lane l of a warp holds K = 256 sc + 8l + e,
+// e = 0..7: chunk l/8 of the unit, 32-block (l%8)/4 of the chunk, layout
+// word l%4 of the block. The unit's max |x| sets s = 2^se with max*s in
+// [32, 64); V = rint(x*s*2^14) = d0*2^14 + d1*2^7 + d2, every digit in
+// [-64, 64]. Digit i of the lane's 8 values is packed as two 32-bit words
+// whose bytes hold K offsets {0,4,1,5} and {2,6,3,7} -- the order in which a
+// layout word's low and high nibbles come out of one mask each. Per unit the
+// tail holds sums[chunk 4][blk 2][token 16] = sum_k V/2^14 over the 32-block
+// and inv[16] = 1/s (NaN when the unit holds a non-finite x, so the output
+// is non-finite too). K beyond the matrix reads as zero.
+struct UnitDigits {
+  uint32_t dig[3][2];
+  int vsum;    // sum of the lane's V
+  bool bad;    // the unit holds a non-finite x
+  int se;
+};
+
+__device__ __forceinline__ void load_x8(const Params& p, int sc, int t, int lane, float (&v)[8]) {
+  const int k0 = 256 * sc + 8 * lane;
+  if (t < p.batch && k0 < p.K) {
+    const float* xr = p.x + (int64_t)t * p.ldx + k0;
+    const float4 a = *reinterpret_cast<const float4*>(xr);
+    const float4 b = *reinterpret_cast<const float4*>(xr + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  } else {
 #pragma unroll
-  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0) red[warp] = m;
-  __syncthreads();
-  m = red[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
-  int se = 0;  // scale exponent
-  if (m > 0.f && m <= 3.0e38f) {
-    const int e = ((__float_as_int(m) >> 23) & 0xFF) - 127;  // m in [2^e, 2^(e+1)) for normal m
-    se = max(-126, min(127, 14 - e));
-  }
-  const float s = __int_as_float((127 + se) << 23);
-  if (live && blockIdx.x == 0 && threadIdx.x == 0) inv[t] = __int_as_float((127 - se) << 23);
-  const bool scaled = (lane >> 1) & 1;  // k % 8 in {2,3,6,7}
-  const float c = scaled ? 64.f : 1024.f;
-  const int b = blockIdx.x * 8 + warp;
-  if (b < n_blk) {
-    const int k = 32 * b + lane;
-    const float v = (live && k < K) ? xr[k] : 0.f;
-    const float xs = scaled ? v * s * 0.0625f : v * s;
-    const __half hi = __float2half_rn(xs);
-    const __half lo = __float2half_rn(xs - __half2float(hi));
-    const int ch = b >> 1, kc = k & 63, j = kc >> 3;
-    uint8_t* unit = xunits + (int64_t)(ch / kUC) * C::XU;
-    uint8_t* tile = unit + (ch % kUC) * C::T;
-    const int rh = t, rl = BT + t;  // live hi rows, then live lo rows
-    *reinterpret_cast<__half*>(tile + rh * 128 + ((j ^ (rh & 7)) << 4) + (kc & 7) * 2) = hi;
-    *reinterpret_cast<__half*>(tile + rl * 128 + ((j ^ (rl & 7)) << 4) + (kc & 7) * 2) = lo;
-    const float u = (__half2float(hi) + __half2float(lo)) * (scaled ? 16.f : 1.f);
-    float a = (q40 ? c + 8.f : c) * u, su = u;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      a += __shfl_xor_sync(0xffffffffu, a, o);
-      su += __shfl_xor_sync(0xffffffffu, su, o);
-    }
-    if (lane == 0) {
-      float* sums = reinterpret_cast<float*>(unit + kUC * C::T + (ch % kUC) * 256) + (b & 1) * 32;
-      sums[t] = a;
-      sums[16 + t] = su;
-    }
-  }
-  if (zero_split && live && blockIdx.x == 0) {
-    for (int rbg = warp; rbg < zp.total_rb; rbg += 8) {
-      if (!zp.zero_all && !((zp.split[rbg >> 5] >> (rbg & 31)) & 1u)) continue;
-      const Mat& mt = zp.mats[find_mat(zp, rbg)];
-      float* yr = mt.y + (int64_t)t * mt.ldy + (int64_t)(rbg - mt.rb0) * 128;
-      const int nr = min(128, mt.n_rows - (rbg - mt.rb0) * 128);
-      for (int r = lane; r < nr; r += 32) yr[r] = 0.f;
-    }
+    for (int e = 0; e < 8; ++e) v[e] = 0.f;
   }
 }
 
+// warp-collective: every lane of the warp calls it for the same token
+__device__ __forceinline__ UnitDigits unit_digits(const float (&v)[8]) {
+  UnitDigits u;
+  float m = 0.f;
+  bool bad = false;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    m = fmaxf(m, fabsf(v[e]));
+    bad |= !(fabsf(v[e]) <= 3.402823466e38f);  // inf or NaN
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  u.bad = __any_sync(0xffffffffu, bad);
+  u.se = 0;  // s = 2^se, with 1/s a normal float as well
+  if (m > 0.f && !u.bad) {
+    const int e = ((__float_as_int(m) >> 23) & 0xFF) - 127;  // m in [2^e, 2^(e+1)) for normal m
+    u.se = max(-126, min(126, 5 - e));
+  }
+  const float s = __int_as_float((127 + u.se) << 23);
+  int V[8];
+  u.vsum = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    V[e] = u.bad ? 0 : __float2int_rn((v[e] * s) * 16384.f);
+    u.vsum += V[e];
+  }
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+    for (int pb = 0; pb < 4; ++pb) {
+      const int e = (pb & 1) * 4 + (pb >> 1) + 2 * half;  // byte pb of the low / high word: K 0,4,1,5 | 2,6,3,7
+      const int d0 = (V[e] + 8192) >> 14;
+      const int r0 = V[e] - (d0 << 14);
+      const int d1 = (r0 + 64) >> 7;
+      const int d2 = r0 - (d1 << 7);
+      w0 |= (uint32_t)(d0 & 0xFF) << (8 * pb);
+      w1 |= (uint32_t)(d1 & 0xFF) << (8 * pb);
+      w2 |= (uint32_t)(d2 & 0xFF) << (8 * pb);
+    }
+    u.dig[0][half] = w0;
+    u.dig[1][half] = w1;
+    u.dig[2][half] = w2;
+  }
+  return u;
+}
+
+// the per-block sums and the token's 1/s into a unit's tail (warp-collective)
+__device__ __forceinline__ void store_tail(float* tail, const UnitDigits& u, int t, int lane) {
+  int vs = u.vsum;
+  vs += __shfl_xor_sync(0xffffffffu, vs, 1);
+  vs += __shfl_xor_sync(0xffffffffu, vs, 2);  // 4 lanes = one 32-block
+  if ((lane & 3) == 0) tail[kSumOff / 4 + ((lane >> 3) * 2 + ((lane >> 2) & 1)) * 16 + t] = (float)vs * (1.f / 16384.f);
+  if (lane == 0) tail[kInvOff / 4 + t] = u.bad ? __int_as_float(0x7fc00000) : __int_as_float((127 - u.se) << 23);
+}
+
+// B row of (position k of a chunk in its accumulator, block j, digit d,
+// token t) in the chunk's tile. A piece's chunk i (i = chunk - first chunk
+// of the piece) has position i % GC, so a position is a compile-time index
+// in the epilogue.
+template <int BT>
+__host__ __device__ constexpr int brow(int k, int j, int d, int t) {
+  return (k * 2 + j) * 3 * BT + d * BT + t;
+}
+
+// Block-diagonal tile of a chunk (K-major, 64-byte swizzle): row brow(k, j,
+// d, t) holds the digits in bytes 32j .. 32j+31, zeros elsewhere (the slots
+// are zeroed at kernel start and only digit bytes are written). Lanes of
+// chunks before ci0 (outside the piece) write nothing.
+template <int BT>
+__device__ __forceinline__ void store_digits(uint8_t* unit, const UnitDigits& u, int t, int lane, int ci0) {
+  using C = Cfg<BT>;
+  const int c = lane >> 3, j = (lane >> 2) & 1, w = lane & 3;
+  if (c >= ci0) {
+    uint8_t* tile = unit + c * C::T;
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      const int n = brow<BT>((c - ci0) % C::GC, j, d, t);
+      *reinterpret_cast<uint2*>(tile + sw64_off(n, 2 * j + (w >> 1)) + 8 * (w & 1)) = make_uint2(u.dig[d][0], u.dig[d][1]);
+    }
+  }
+  store_tail(reinterpret_cast<float*>(unit + kUC * C::T), u, t, lane);
+}
+
+// N consecutive TMEM columns of this warp's lane quadrant (N a multiple of 16)
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i + 32 <= N; i += 32) sg_tmem_ld_n<32>(taddr + i, *reinterpret_cast<uint32_t(*)[32]>(&v[i]));
+  if constexpr (N % 32 == 16) sg_tmem_ld_n<16>(taddr + (N - 16), *reinterpret_cast<uint32_t(*)[16]>(&v[N - 16]));
+}
+
+// sum_k q_k u_k = D0 + D1/128 + D2/16384, rounded once: D0*128 + D1
+// (|.| < 2^22) and D2 become floats exactly by adding them to the bits of
+// 1.5*2^23 and 1.5*2^9; the two 1.5 offsets cancel (-98304 - 768 + 768).
+__device__ __forceinline__ float digit_dot(uint32_t d0, uint32_t d1, uint32_t d2) {
+  const float f = __uint_as_float(d0 * 128u + d1 + 0x4B400000u);
+  const float u = fmaf(f, 0.0078125f, -99072.f);
+  const float g = __uint_as_float(d2 + 0x44400000u);
+  return u + g;
+}
+
+// ----------------------------------------------------- output row-blocks
+// A row-block segment (the rows a CTA accumulates between two stores) is
+// stored when the CTA ran the whole row-block, else reduced into y with
+// red.add. Before the first reduction into a shared row-block, its rows must
+// have been zeroed by the CTA holding the row-block's first chunk. Spare
+// lanes of warp 0 do that work off the critical path (shared_rows_role):
+// they zero this CTA's trailing row-block and publish the call's epoch in
+// the CTA's flag (then arrive on zero_own), and they poll the flag of the
+// CTA that zeroes this CTA's leading row-block (then arrive on zero_ok). The
+// epilogue only waits on those shared-memory barriers.
+__device__ __forceinline__ void shared_rows_role(const Params& p, int64_t g0, int64_t g1, int lane, uint64_t* zero_own,
+                                                 uint64_t* zero_ok) {
+  if (p.accumulate) return;
+  pdl_wait();  // y: the previous kernel may still use it
+  const int b = blockIdx.x;
+  const int64_t rl = (g1 - 1) / p.n_cp;  // row-block of the last chunk
+  if (rl * p.n_cp >= g0 && (rl + 1) * p.n_cp > g1) {
+    const Mat& mt = p.mats[find_mat(p, (int)rl)];
+    const int grow0 = ((int)rl - mt.rb0) * 128;
+    for (int r = lane - 1; r < 128; r += 31)
+      if (grow0 + r < mt.n_rows)
+        for (int t = 0; t < p.batch; ++t) mt.y[(int64_t)t * mt.ldy + grow0 + r] = 0.f;
+    __threadfence();
+    __syncwarp(0xfffffffeu);
+    if (lane == 1) {
+      st_release_u64(&p.zflags[b], p.epoch);
+      mbar_arrive(zero_own);
+    }
+  }
+  const int64_t rf = g0 / p.n_cp;  // row-block of the first chunk
+  if (rf * p.n_cp < g0 && lane == 1) {  // it started in an earlier CTA, which zeroes it
+    const unsigned long long* fl = &p.zflags[cta_of(p, rf * p.n_cp)];
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_volatile_u64(fl) != p.epoch) {
+      if (*(volatile int*)&g_sg_error != 0 || globaltimer_ns() - t0 > SG_WAIT_NS) {
+        sg_set_error(SG_DEVERR_WAIT_TIMEOUT | 0x2D);
+        break;
+      }
+    }
+    __threadfence();  // with the flag read: the zeroing happens before the adds
+    mbar_arrive(zero_ok);
+  }
+}
+
+// A segment shared with an earlier CTA (at most the CTA's first one) waits
+// for that CTA's zeroing; rather than stall the pipeline at its end, its sums
+// are held in registers and reduced after the CTA's last piece.
+template <int BT>
+struct HeldSegment {
+  float v[BT];
+  float* y = nullptr;
+  int64_t ldy = 0;
+  bool on = false;
+};
+
+// After the piece of cnt chunks at the cursor: if it ends a segment, write
+// acc (lanes with writer set), or hold it, and clear it. Warp-collective.
+template <int BT>
+__device__ __forceinline__ void end_segment(const Params& p, const Cursor& cur, int cnt, int64_t g0, int row, bool writer,
+                                            float (&acc)[BT], HeldSegment<BT>& held, uint64_t* zero_own) {
+  const bool rb_end = cur.c + cnt == p.n_ch;
+  if (!rb_end && cur.g + cnt != cur.g1) return;
+  const Mat& mt = p.mats[cur.mi];
+  const int grow = cur.rb * 128 + row;
+  const bool live = writer && grow < mt.n_rows;
+  const int64_t gr0 = (int64_t)cur.rbg * p.n_cp;
+  if (rb_end && gr0 >= g0) {  // this CTA ran the row-block from chunk 0
+    if (live) {
+#pragma unroll
+      for (int t = 0; t < BT; ++t) {
+        if (t < p.batch) {
+          float* yp = mt.y + (int64_t)t * mt.ldy + grow;
+          *yp = p.accumulate ? *yp + acc[t] : acc[t];
+        }
+      }
+    }
+  } else if (!p.accumulate && cta_of(p, gr0) != (int)blockIdx.x) {
+    held.on = true;
+    held.y = live ? mt.y + grow : nullptr;
+    held.ldy = mt.ldy;
+#pragma unroll
+    for (int t = 0; t < BT; ++t) held.v[t] = acc[t];
+  } else {
+    // accumulate, or this CTA's own trailing row-block: zeroed by warp 0
+    const bool ok = p.accumulate || __all_sync(0xffffffffu, mbar_wait(zero_own, 0, 0x2E));
+    if (live && ok) {
+#pragma unroll
+      for (int t = 0; t < BT; ++t)
+        if (t < p.batch) red_add_f32(mt.y + (int64_t)t * mt.ldy + grow, acc[t]);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < BT; ++t) acc[t] = 0.f;
+}
+
+// the held segment, once the earlier CTA has zeroed its rows. Warp-collective.
+template <int BT>
+__device__ __forceinline__ void flush_held(const Params& p, const HeldSegment<BT>& held, uint64_t* zero_ok) {
+  if (!held.on) return;
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(zero_ok, 0, 0x2F));
+  if (held.y && ok) {
+#pragma unroll
+    for (int t = 0; t < BT; ++t)
+      if (t < p.batch) red_add_f32(held.y + (int64_t)t * held.ldy, held.v[t]);
+  }
+}
+
+// ------------------------------------------------------ activation images
+// gemv_xprep_kernel: the activation units of one call, in the exact shared-
+// memory layout of a unit (block-diagonal tiles with position chunk % GC,
+// then sums and scales), written once to global memory for every CTA to
+// copy. One warp per (unit, token column t < BT); it writes every row of its
+// token in the unit's four tiles (digits in the (position, block) row's
+// half, zeros elsewhere), the token-0 warp also the padding rows, so no
+// byte of a previous call's image survives. Columns t >= batch are zero.
+template <int BT>
+__global__ void __launch_bounds__(128) gemv_xprep_kernel(Params p, int n_units) {
+  using C = Cfg<BT>;
+  pdl_launch_dependents();
+  pdl_wait();  // x may come from the previous kernel, which may also still read the images
+  const int lane = threadIdx.x & 31;
+  const int wg = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (wg >= n_units * BT) return;
+  const int u = wg / BT, t = wg - u * BT;
+  uint8_t* unit = p.ximg + (int64_t)u * C::XU;
+  float v[8];
+  load_x8(p, u, t, lane, v);  // zeros for t >= batch and K beyond the matrix
+  const UnitDigits ud = unit_digits(v);
+  const int c = lane >> 3, j = (lane >> 2) & 1, w = lane & 3;
+  uint8_t* tile = unit + c * C::T;
+  const int seg = 2 * j + (w >> 1), off = 8 * (w & 1);  // this lane's 8 bytes of a row: half j, word w
+#pragma unroll
+  for (int k = 0; k < C::GC; ++k)
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+      for (int d = 0; d < 3; ++d) {
+        const int n = brow<BT>(k, jj, d, t);
+        const bool mine = k == c % C::GC && jj == j;
+        *reinterpret_cast<uint2*>(tile + sw64_off(n, seg) + off) =
+            mine ? make_uint2(ud.dig[d][0], ud.dig[d][1]) : make_uint2(0u, 0u);
+      }
+  if (t == 0)
+    for (int n = C::ROWS; n < C::N; ++n) *reinterpret_cast<uint2*>(tile + sw64_off(n, seg) + off) = make_uint2(0u, 0u);
+  if (t < p.batch) store_tail(reinterpret_cast<float*>(unit + kUC * C::T), ud, t, lane);  // warp-uniform
+}
+
 // ---------------------------------------------------------------- GEMV
-// BT: live token columns rounded up to a power of two (<= BP)
-template <int DT, int BP, int BT>
+// BT: live token columns rounded up to a power of two
+template <int DT, int BT>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
-  using C = Cfg<BP>;
+  using C = Cfg<BT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  // per group g (CPG chunks): a_full[g % SG] -- its A tiles are in TMEM;
+  // per group g: a_full[g % SG] -- its A tiles and scale words are in TMEM;
   // d_full[g % SG] -- its MMAs completed; d_free[g % SG] -- its epilogue is
-  // done, so its A tiles, accumulators and row scales may be rewritten
-  __shared__ __align__(8) uint64_t w_full[kRW], w_empty[kRW], x_full[kRX], x_empty[kRX], a_full[C::SG],
-      d_full[C::SG], d_free[C::SG];
+  // done, so the whole slot may be rewritten
+  __shared__ __align__(8) uint64_t w_full[kRW], w_empty[kRW], x_full[C::RX], x_empty[C::RX], a_full[C::SG],
+      d_full[C::SG], d_free[C::SG], zero_own, zero_ok;
   __shared__ uint32_t tmem_base_sh;
 
+  pdl_launch_dependents();  // the next kernel may start its own prologue once SMs free up
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = gridDim.x;
-  const int64_t u0 = (int64_t)blockIdx.x * p.total / G, u1 = (int64_t)(blockIdx.x + 1) * p.total / G;
-  const int nu = (int)(u1 - u0);
+  int64_t g0, g1;
+  cta_range(p, blockIdx.x, g0, g1);
 
   if (threadIdx.x == 0) {
     for (int r = 0; r < kRW; ++r) {
       mbar_init(&w_full[r], 1);
       mbar_init(&w_empty[r], 4);
     }
-    for (int r = 0; r < kRX; ++r) {
-      mbar_init(&x_full[r], 1);
+    for (int r = 0; r < C::RX; ++r) {
+      mbar_init(&x_full[r], C::XPRE ? 1 : kXWarps);
       mbar_init(&x_empty[r], 4);
     }
     for (int s = 0; s < C::SG; ++s) {
@@ -259,8 +527,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
       mbar_init(&d_full[s], 1);
       mbar_init(&d_free[s], 4);
     }
+    mbar_init(&zero_own, 1);
+    mbar_init(&zero_ok, 1);
     mbar_fence_init();
   }
+  // activation tiles built here: zero once; afterwards only digit bytes are written
+  if (!C::XPRE)
+    for (int i = threadIdx.x; i < C::RX * C::XU / 16; i += kThreads)
+      reinterpret_cast<uint4*>(smem + C::OFF_X)[i] = make_uint4(0u, 0u, 0u, 0u);
   if (warp == 1) sg_tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
   sg_tc_fence_before();
   __syncthreads();
@@ -270,193 +544,292 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
   if (warp == 0) {
     // ========================================================= weight producer
     if (lane == 0) {
-      Cursor uc;
-      uc.init(p, u0);
+      Cursor cur;
+      cur.init(p, g0, g1);
       int v = 0;
-      for (; v < nu; ++v) {
+      for (; cur.more(); ++v, cur.next(p)) {
         const int ws = v % kRW;
         if (v >= kRW && !mbar_wait(&w_empty[ws], ((v / kRW) & 1) ^ 1, 0x21)) break;
-        const Mat& mt = p.mats[uc.mi];
-        const int cnt = uc.chunks(p);
+        const Mat& mt = p.mats[cur.mi];
+        const int cnt = cur.cnt(p);
         uint8_t* dst = smem + C::OFF_W + ws * kWU;
         mbar_arrive_expect_tx(&w_full[ws], cnt * SG_TILE_BYTES + (DT == SG_DTYPE_Q4_K ? 512 : 0));
-        bulk_g2s(dst, mt.tiles + ((int64_t)uc.rb * p.n_ch + kUC * uc.sc) * SG_TILE_BYTES, cnt * SG_TILE_BYTES,
-                 &w_full[ws]);
-        if (DT == SG_DTYPE_Q4_K)  // one Q4_K super-block per unit
-          bulk_g2s(dst + kUC * SG_TILE_BYTES, mt.dd + ((int64_t)uc.rb * mt.n_sb + uc.sc) * 128, 512, &w_full[ws]);
-        uc.next(p);
+        bulk_g2s(dst, mt.tiles + ((int64_t)cur.rb * p.n_ch + cur.c) * SG_TILE_BYTES, cnt * SG_TILE_BYTES, &w_full[ws]);
+        if (DT == SG_DTYPE_Q4_K)  // the unit's Q4_K super-block scales
+          bulk_g2s(dst + kUC * SG_TILE_BYTES, mt.dd + ((int64_t)cur.rb * mt.n_sb + cur.sc()) * 128, 512, &w_full[ws]);
       }
       if (*(volatile int*)&g_sg_error != 0)  // error path: no copy may land after the CTA exits
         for (int j = max(0, v - kRW); j < v; ++j) mbar_wait_drain(&w_full[j % kRW], (j / kRW) & 1);
-    }
-  } else if (warp == 10) {
-    // ===================================================== activation producer
-    if (lane == 0) {
-      pdl_wait();  // activations and sums come from the prep kernel
-      Cursor uc;
-      uc.init(p, u0);
-      int v = 0;
-      for (; v < nu; ++v) {
-        const int xs = v % kRX;
-        if (v >= kRX && !mbar_wait(&x_empty[xs], ((v / kRX) & 1) ^ 1, 0x22)) break;
-        mbar_arrive_expect_tx(&x_full[xs], C::XU);
-        bulk_g2s(smem + C::OFF_X + xs * C::XU, p.xunits + (int64_t)uc.sc * C::XU, C::XU, &x_full[xs]);
-        uc.next(p);
-      }
-      if (*(volatile int*)&g_sg_error != 0)
-        for (int j = max(0, v - kRX); j < v; ++j) mbar_wait_drain(&x_full[j % kRX], (j / kRX) & 1);
+    } else {
+      shared_rows_role(p, g0, g1, lane, &zero_own, &zero_ok);
     }
   } else if (warp == 1) {
     // ============================================================ MMA issuer
     if (lane == 0) {
-      Cursor uc;
-      uc.init(p, u0);
+      Cursor cur;
+      cur.init(p, g0, g1);
       int g = 0;
       bool ok = true;
-      for (int v = 0; v < nu && ok; ++v) {
-        const int xs = v % kRX, cnt = uc.chunks(p);
-        if (!mbar_wait(&x_full[xs], (v / kRX) & 1, 0x23)) break;
-        for (int gi = 0; gi < C::GPU && gi * C::CPG < cnt; ++gi, ++g) {
+      for (int v = 0; cur.more() && ok; ++v, cur.next(p)) {
+        const int xs = v % C::RX, cnt = cur.cnt(p), ci0 = cur.ci0();
+        if (!mbar_wait(&x_full[xs], (v / C::RX) & 1, 0x23)) break;
+        const uint32_t xbase = smem_u32(smem + C::OFF_X + xs * C::XU);
+        for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g) {
           const int sg = g % C::SG;
-          if (!mbar_wait(&a_full[sg], (g / C::SG) & 1, 0x24) ||
-              (g >= C::SG && !mbar_wait(&d_free[sg], ((g / C::SG) & 1) ^ 1, 0x29))) {
+          // the slot's previous epilogue finished before the dequant warps
+          // refilled it, so a_full alone makes the accumulators free too
+          if (!mbar_wait(&a_full[sg], (g / C::SG) & 1, 0x24)) {
             ok = false;
             break;
           }
           sg_tc_fence_after();
           const int gc = min(C::CPG, cnt - gi * C::CPG);
           for (int ci = 0; ci < gc; ++ci) {
-            const int cu = gi * C::CPG + ci;  // chunk within the unit
-            const uint32_t a0 = tmem + (uint32_t)(sg * C::A_COLS + ci * kACols);
-            const uint64_t bd = sg_sdesc(smem_u32(smem + C::OFF_X + xs * C::XU + cu * C::T), SG_SW128);
+            const int cu = ci0 + gi * C::CPG + ci;  // chunk within the unit: its activation tile
+            const uint32_t d = tmem + C::d_col(sg) + (uint32_t)((ci / C::GC) * C::N);
 #pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-              const uint32_t d = tmem + C::D_COL0 + (uint32_t)(sg * C::D_COLS + (ci * 2 + blk) * C::N);
-#pragma unroll
-              for (int j = 0; j < 2; ++j) {
-                const int ks = 2 * blk + j;  // 16 K = 8 TMEM columns of A, 32 bytes of B
-                sg_umma_tmem_a(d, a0 + (uint32_t)(ks * 8), bd + (uint64_t)(ks * 2), C::IDESC, (uint32_t)j);
-              }
-            }
+            for (int blk = 0; blk < 2; ++blk)  // one 32-block: 8 TMEM columns of A, 32 bytes of each B row
+              sg_umma_i8_tmem_a(d, tmem + C::a_col(sg) + (uint32_t)(ci * kACols + 8 * blk),
+                                sg_sdesc(xbase + cu * C::T + 32 * blk, SG_SW64), C::IDESC,
+                                (ci % C::GC == 0 && blk == 0) ? 0u : 1u);
           }
           sg_umma_commit(&d_full[sg]);
         }
-        uc.next(p);
       }
       // every MMA issued must have completed before TMEM is freed (the last
       // commit covers all of them; on the normal path this returns at once)
       if (g > 0) mbar_wait_drain(&d_full[(g - 1) % C::SG], ((g - 1) / C::SG) & 1);
     }
   } else if (warp < 6) {
-    // ====================================================== dequant warps
-    const int q = warp & 3;  // TMEM lane quadrant: rows 32q .. 32q+31
-    const int row = q * 32 + lane;
-    Cursor uc;
-    uc.init(p, u0);
+    // ======================================================== dequant warps
+    const int row = (warp & 3) * 32 + lane;  // TMEM lane quadrant = warp % 4
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    Cursor cur;
+    cur.init(p, g0, g1);
     int g = 0;
     bool ok = true;
-    for (int v = 0; v < nu && ok; ++v) {
-      const int ws = v % kRW, cnt = uc.chunks(p);
+    for (int v = 0; cur.more() && ok; ++v, cur.next(p)) {
+      const int ws = v % kRW, cnt = cur.cnt(p);
       if (!__all_sync(0xffffffffu, mbar_wait(&w_full[ws], (v / kRW) & 1, 0x26))) break;
       const uint8_t* wu = smem + C::OFF_W + ws * kWU;
-      uint32_t ddw = 0;
-      if (DT == SG_DTYPE_Q4_K) ddw = *reinterpret_cast<const uint32_t*>(wu + kUC * SG_TILE_BYTES + row * 4);
-      for (int gi = 0; gi < C::GPU && gi * C::CPG < cnt; ++gi, ++g) {
+      const uint32_t ddw = DT == SG_DTYPE_Q4_K ? *reinterpret_cast<const uint32_t*>(wu + kUC * SG_TILE_BYTES + row * 4) : 0u;
+      for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g) {
         const int sg = g % C::SG;
-        // the group's A tiles, accumulators and scale words were last used by
-        // group g - SG: wait until its epilogue has released them
+        // the slot was last used by group g - SG: wait for its epilogue
         const bool w = g < C::SG || mbar_wait(&d_free[sg], ((g / C::SG) & 1) ^ 1, 0x27);
         if (!__all_sync(0xffffffffu, w)) {
           ok = false;
           break;
         }
         sg_tc_fence_after();
-        uint32_t* scal = reinterpret_cast<uint32_t*>(smem + C::OFF_SCAL + sg * C::CPG * C::SCAL);
         const int gc = min(C::CPG, cnt - gi * C::CPG);
-        for (int ci = 0; ci < gc; ++ci) {
-          const uint8_t* tile = wu + (gi * C::CPG + ci) * SG_TILE_BYTES;
-          const uint4 n0 = *reinterpret_cast<const uint4*>(tile + row * 16);
-          const uint4 n1 = *reinterpret_cast<const uint4*>(tile + 2048 + row * 16);
-          scal[ci * 256 + row] = *reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF + row * 4);
-          if (DT == SG_DTYPE_Q4_K) scal[ci * 256 + 128 + row] = ddw;
-          // this thread's row of the A tile: column c holds K pair (2c, 2c+1)
-          const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-          uint32_t av[32];
+        uint32_t scw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint4 d = sg_decode_word_f16(nw[j]);
-            av[4 * j] = d.x;
-            av[4 * j + 1] = d.y;
-            av[4 * j + 2] = d.z;
-            av[4 * j + 3] = d.w;
+        for (int ci = 0; ci < C::CPG; ++ci) {
+          if (ci >= gc) break;  // warp-uniform
+          const uint8_t* tile = wu + (gi * C::CPG + ci) * SG_TILE_BYTES;
+          const uint4 n0 = *reinterpret_cast<const uint4*>(tile + row * 16);         // block 0: K 0..31
+          const uint4 n1 = *reinterpret_cast<const uint4*>(tile + 2048 + row * 16);  // block 1: K 32..63
+          scw[ci] = *reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF + row * 4);
+          const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+          // column 2w: the low nibbles of word w (K offsets 0,4,1,5 of its 8),
+          // column 2w+1: the high nibbles (2,6,3,7)
+          uint32_t av[16];
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            av[2 * jj] = nw[jj] & 0x0F0F0F0Fu;
+            av[2 * jj + 1] = (nw[jj] >> 4) & 0x0F0F0F0Fu;
           }
-          sg_tmem_st32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(sg * C::A_COLS + ci * kACols), av);
+          sg_tmem_st16(lane_base + C::a_col(sg) + (uint32_t)(ci * kACols), av);
         }
+        const uint32_t scc = lane_base + C::sc_col(sg);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t one[1] = {scw[i]};
+          sg_tmem_st_n<1>(scc + (uint32_t)i, one);
+        }
+        const uint32_t ddv[1] = {ddw};
+        sg_tmem_st_n<1>(scc + 4, ddv);
         sg_tmem_st_wait();
         sg_tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[sg]);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&w_empty[ws]);  // this warp has read all of the unit's weights
-      uc.next(p);
+      if (lane == 0) mbar_arrive(&w_empty[ws]);  // the piece's weights are all in TMEM now
+    }
+  } else if (warp >= 10) {
+    // ===================================================== activation warps
+    if constexpr (C::XPRE) {
+      // the call's unit images are ready once the prep kernel completes: one
+      // bulk copy per piece
+      if (warp == 10 && lane == 0) {
+        pdl_wait();
+        Cursor cur;
+        cur.init(p, g0, g1);
+        int v = 0;
+        for (; cur.more(); ++v, cur.next(p)) {
+          const int xs = v % C::RX;
+          if (v >= C::RX && !mbar_wait(&x_empty[xs], ((v / C::RX) & 1) ^ 1, 0x2A)) break;
+          mbar_arrive_expect_tx(&x_full[xs], C::XU);
+          bulk_g2s(smem + C::OFF_X + xs * C::XU, p.ximg + (int64_t)cur.sc() * C::XU, C::XU, &x_full[xs]);
+        }
+        if (*(volatile int*)&g_sg_error != 0)  // error path: no copy may land after the CTA exits
+          for (int j = max(0, v - C::RX); j < v; ++j) mbar_wait_drain(&x_full[j % C::RX], (j / C::RX) & 1);
+      }
+    } else {
+    // Jobs: at one token the two warps take alternate pieces, otherwise each
+    // takes half of the tokens of every piece. A job's x (NTW x 1 KB) is
+    // fetched with cp.async into this warp's staging slots XS - 1 jobs ahead,
+    // so the global latency overlaps the jobs in between.
+    const int xw = warp - 10;
+    constexpr int NTW = C::NTW, XS = C::XS;
+    constexpr int STEP = BT == 1 ? kXWarps : 1;  // pieces from one job of this warp to the next
+    float* stage = reinterpret_cast<float*>(smem + C::OFF_S) + xw * XS * NTW * 256;
+    pdl_wait();  // x may come from the previous kernel
+    Cursor cur;
+    cur.init(p, g0, g1);
+    Cursor pf = cur;  // next piece to stage for this warp
+    if (BT == 1)
+      for (int i = 0; i < xw && pf.more(); ++i) pf.next(p);
+    // stage the job at pf into slot sl (an empty group when pf is done), then
+    // step pf to this warp's next job
+    auto stage_next = [&](int sl) {
+      if (pf.more()) {
+        const int k0 = 256 * pf.sc() + 8 * lane;
+#pragma unroll
+        for (int i = 0; i < NTW; ++i) {
+          const int t = BT == 1 ? 0 : xw + kXWarps * i;
+          if (t < p.batch) {
+            const float* src = p.x + (int64_t)t * p.ldx + (k0 < p.K ? k0 : 0);
+            const uint32_t nb = k0 < p.K ? 16u : 0u;  // 0: zero-fill, nothing read
+            float* dst = stage + (sl * NTW + i) * 256 + 8 * lane;
+            cp_async16(dst, src, nb);
+            cp_async16(dst + 4, src + 4, nb);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < STEP; ++i)
+          if (pf.more()) pf.next(p);
+      }
+      cp_async_commit();
+    };
+#pragma unroll
+    for (int j = 0; j < XS - 1; ++j) stage_next(j);
+    const int shift0 = cur.ci0() % C::GC;  // only a CTA's first piece can start inside a unit
+    int job = 0;
+    for (int v = 0; cur.more(); ++v, cur.next(p)) {
+      const int xs = v % C::RX;
+      // the slot was last read by piece v - RX
+      if (v >= C::RX && !__all_sync(0xffffffffu, mbar_wait(&x_empty[xs], ((v / C::RX) & 1) ^ 1, 0x2A))) break;
+      uint8_t* xu = smem + C::OFF_X + xs * C::XU;
+      if (BT != 1 || v % kXWarps == xw) {
+        stage_next((job + XS - 1) % XS);
+        cp_async_wait<XS - 1>();  // this job's copies have landed (each lane reads only its own)
+        const float* sj = stage + (job % XS) * NTW * 256 + 8 * lane;
+        if (v == C::RX && shift0 != 0) {
+          // piece 0 placed its rows at shifted positions: clear every row of
+          // this job's tokens in the slot
+          for (int i = 0; i < NTW; ++i) {
+            const int t = BT == 1 ? 0 : xw + kXWarps * i;
+            if (t >= p.batch) break;
+            for (int e = lane; e < kUC * C::GC * 6 * 4; e += 32) {  // (tile, row of the token, 16-byte segment)
+              const int c = e / (C::GC * 6 * 4), r = (e / 4) % (C::GC * 6), sgm = e % 4;
+              const int n = brow<BT>(r / 6, (r / 3) % 2, r % 3, t);
+              reinterpret_cast<uint4*>(xu + c * C::T + n * 64)[sgm] = make_uint4(0u, 0u, 0u, 0u);
+            }
+          }
+          __syncwarp();
+        }
+#pragma unroll
+        for (int i = 0; i < NTW; ++i) {
+          const int t = BT == 1 ? 0 : xw + kXWarps * i;
+          if (t < p.batch) {  // warp-uniform
+            const float4 a = *reinterpret_cast<const float4*>(sj + i * 256);
+            const float4 b = *reinterpret_cast<const float4*>(sj + i * 256 + 4);
+            const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            store_digits<BT>(xu, unit_digits(xv), t, lane, cur.ci0());
+          }
+        }
+        ++job;
+      }
+      fence_proxy_async_smem();  // the tensor core reads the tiles through the async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&x_full[xs]);
+    }
+    cp_async_wait<0>();  // no copy may land after the CTA exits
     }
   } else {
     // ============================================================ epilogue warps
     const int q = warp & 3;  // TMEM lane quadrant
     const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    pdl_wait();  // y: the previous kernel may still use it
+    HeldSegment<BT> held;
     float acc[BT];
 #pragma unroll
     for (int t = 0; t < BT; ++t) acc[t] = 0.f;
-    bool waited_prev = false;
-    Cursor uc;
-    uc.init(p, u0);
-    bool seg_whole_start = uc.sc == 0;
+    Cursor cur;
+    cur.init(p, g0, g1);
     int g = 0;
     bool ok = true;
-    for (int v = 0; v < nu && ok; ++v) {
-      const int xs = v % kRX, cnt = uc.chunks(p);
-      if (!__all_sync(0xffffffffu, mbar_wait(&x_full[xs], (v / kRX) & 1, 0x2B))) break;  // block sums
-      for (int gi = 0; gi < C::GPU && gi * C::CPG < cnt; ++gi, ++g) {
+    for (int v = 0; cur.more() && ok; ++v, cur.next(p)) {
+      const int xs = v % C::RX, cnt = cur.cnt(p), ci0 = cur.ci0();
+      if (!__all_sync(0xffffffffu, mbar_wait(&x_full[xs], (v / C::RX) & 1, 0x2B))) break;
+      const float* tail = reinterpret_cast<const float*>(smem + C::OFF_X + xs * C::XU + kUC * C::T);
+      float accu[BT];
+#pragma unroll
+      for (int t = 0; t < BT; ++t) accu[t] = 0.f;
+      for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g) {
         const int sg = g % C::SG;
         if (!__all_sync(0xffffffffu, mbar_wait(&d_full[sg], (g / C::SG) & 1, 0x25))) {
           ok = false;
           break;
         }
         sg_tc_fence_after();
-        const uint32_t* scal = reinterpret_cast<const uint32_t*>(smem + C::OFF_SCAL + sg * C::CPG * C::SCAL);
         const int gc = min(C::CPG, cnt - gi * C::CPG);
-        for (int ci = 0; ci < gc; ++ci) {
-          const int cu = gi * C::CPG + ci;
-          const float* sums = reinterpret_cast<const float*>(smem + C::OFF_X + xs * C::XU + kUC * C::T + cu * 256);
-          const uint32_t scw = scal[ci * 256 + row];
-          float sc[2], of[2];
-          if (DT == SG_DTYPE_Q4_0) {
-            const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&scw));
-            sc[0] = d.x;
-            sc[1] = d.y;
-            of[0] = of[1] = 0.f;
-          } else {
-            const uint32_t ddw = scal[ci * 256 + 128 + row];
-            const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddw));
-            sc[0] = dm.x * (float)(scw & 0xFFu);
-            sc[1] = dm.x * (float)((scw >> 8) & 0xFFu);
-            of[0] = dm.y * (float)((scw >> 16) & 0xFFu);
-            of[1] = dm.y * (float)(scw >> 24);
+        uint32_t scw[4], ddv[1];
+        const uint32_t scc = lane_base + C::sc_col(sg);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sg_tmem_ld_n<1>(scc + (uint32_t)i, *reinterpret_cast<uint32_t(*)[1]>(&scw[i]));
+        sg_tmem_ld_n<1>(scc + 4, ddv);
+        float dmx = 0.f, dmy = 0.f;
+#pragma unroll
+        for (int a = 0; a < C::NACC; ++a) {
+          if (a * C::GC >= gc) break;  // warp-uniform
+          uint32_t dv[C::N];
+          tmem_ld_cols<C::N>(lane_base + C::d_col(sg) + (uint32_t)(a * C::N), dv);
+          sg_tmem_ld_wait();
+          if (DT == SG_DTYPE_Q4_K && a == 0) {
+            const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddv[0]));
+            dmx = dm.x;
+            dmy = dm.y;
           }
 #pragma unroll
-          for (int blk = 0; blk < 2; ++blk) {
-            const uint32_t taddr =
-                tmem + ((uint32_t)(q * 32) << 16) + C::D_COL0 + (uint32_t)(sg * C::D_COLS + (ci * 2 + blk) * C::N);
-            uint32_t hl[2 * BT];  // hi-part columns [0, BT), lo-part columns [BT, 2 BT)
-            sg_tmem_ld_n<2 * BT>(taddr, hl);
-            sg_tmem_ld_wait();
-            const float* s0 = sums + blk * 32;
+          for (int k = 0; k < C::GC; ++k) {
+            const int ci = a * C::GC + k;
+            if (ci < gc) {
+              const int cu = ci0 + gi * C::CPG + ci;  // chunk within the unit
+              const uint32_t w = scw[ci];
 #pragma unroll
-            for (int t = 0; t < BT; ++t) {
-              const float dot = (__uint_as_float(hl[t]) + __uint_as_float(hl[BT + t])) - s0[t];
-              if (DT == SG_DTYPE_Q4_0) acc[t] = fmaf(sc[blk], dot, acc[t]);
-              else acc[t] = fmaf(sc[blk], dot, fmaf(-of[blk], s0[16 + t], acc[t]));
+              for (int blk = 0; blk < 2; ++blk) {
+                float sc, of;
+                if (DT == SG_DTYPE_Q4_0) {
+                  sc = __half2float(__ushort_as_half((unsigned short)(w >> (16 * blk))));
+                  of = 0.f;
+                } else {
+                  sc = dmx * (float)((w >> (8 * blk)) & 0xFFu);
+                  of = dmy * (float)((w >> (16 + 8 * blk)) & 0xFFu);
+                }
+                const float* sv = tail + kSumOff / 4 + (cu * 2 + blk) * 16;
+                const int n0 = brow<BT>(k, blk, 0, 0);  // columns of (position k, block, digit, token)
+#pragma unroll
+                for (int t = 0; t < BT; ++t) {
+                  const float dot = digit_dot(dv[n0 + t], dv[n0 + BT + t], dv[n0 + 2 * BT + t]);
+                  if (DT == SG_DTYPE_Q4_0) accu[t] = fmaf(sc, fmaf(-8.f, sv[t], dot), accu[t]);
+                  else accu[t] = fmaf(sc, dot, fmaf(-of, sv[t], accu[t]));
+                }
+              }
             }
           }
         }
@@ -465,37 +838,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
         if (lane == 0) mbar_arrive(&d_free[sg]);
       }
       if (!ok) break;
+#pragma unroll
+      for (int t = 0; t < BT; ++t) acc[t] = fmaf(accu[t], tail[kInvOff / 4 + t], acc[t]);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&x_empty[xs]);  // this warp is done with the unit's block sums
-      // row-block segment finished: store it whole, or reduce it
-      const bool rb_end = uc.sc == p.n_sc - 1;
-      if (rb_end || v == nu - 1) {
-        if (!waited_prev) {
-          pdl_wait();  // y: zeroing by the prep kernel, readers of the previous kernel
-          waited_prev = true;
-        }
-        const Mat& mt = p.mats[uc.mi];
-        const int grow = uc.rb * 128 + row;
-        const bool whole = rb_end && seg_whole_start;
-        if (grow < mt.n_rows) {
-#pragma unroll
-          for (int t = 0; t < BT; ++t) {
-            if (t < p.batch) {
-              float* yp = mt.y + (int64_t)t * mt.ldy + grow;
-              const float val = acc[t] * p.inv[t];
-              if (!whole) red_add_f32(yp, val);
-              else *yp = p.accumulate ? *yp + val : val;
-            }
-          }
-        }
-#pragma unroll
-        for (int t = 0; t < BT; ++t) acc[t] = 0.f;
-        seg_whole_start = true;  // the next segment starts at unit 0 of its row-block
-      }
-      uc.next(p);
+      if (lane == 0) mbar_arrive(&x_empty[xs]);  // this warp is done with the unit's sums and scales
+      end_segment<BT>(p, cur, cnt, g0, row, true, acc, held, &zero_own);
     }
+    flush_held<BT>(p, held, &zero_ok);
   }
-  pdl_launch_dependents();
   sg_tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -505,48 +855,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
 }
 
 // ------------------------------------------------------------ host side
-struct Layout {
-  uint8_t* xunits;
-  float* inv;
-  size_t bytes;
-};
+constexpr size_t kFlagsBytes = (size_t)kMaxCtas * sizeof(unsigned long long);  // workspace: zeroing flags, then images
 
-// scratch: activation units for the larger tile (BP = 16) + per-token scales
-Layout layout_of(void* base, int64_t K) {
-  auto up = [](size_t v) { return (v + 1023) & ~(size_t)1023; };
-  const int64_t n_sc = ((K + 63) / 64 + kUC - 1) / kUC;
-  Layout l;
-  uint8_t* b = static_cast<uint8_t*>(base);
-  const size_t xb = up((size_t)n_sc * Cfg<16>::XU);
-  l.xunits = b;
-  l.inv = reinterpret_cast<float*>(b + xb);
-  l.bytes = xb + 1024;
-  return l;
-}
-
-template <int DT, int BP, int BT>
-cudaError_t launch(const Params& p, int G, const float* x, int64_t ldx, int K, bool zero_split, const Layout& l,
-                   cudaStream_t st) {
-  using C = Cfg<BP>;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = sg_pdl_enabled() ? 1 : 0;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((2 * p.n_ch + 7) / 8), (unsigned)BT);
-  cfg.blockDim = dim3(256);
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_xprep_kernel<BP, BT>, x, ldx, K, 2 * p.n_ch, DT == SG_DTYPE_Q4_0 ? 1 : 0,
-                                     l.xunits, l.inv, p, zero_split ? 1 : 0);
-  if (e != cudaSuccess) return e;
+template <int DT, int BT>
+cudaError_t launch(Params p, int rb_total, int num_sms, cudaStream_t st) {
+  using C = Cfg<BT>;
+  p.spl = C::SPL;
+  p.n_cp = (p.n_ch + C::SPL - 1) / C::SPL * C::SPL;
+  p.total = (int64_t)rb_total * p.n_cp;
+  const int64_t slots = p.total / p.spl;
+  const int G = (int)std::max<int64_t>(1, std::min<int64_t>(std::min(num_sms, kMaxCtas), slots));  // one CTA per SM
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    e = cudaFuncSetAttribute(gemv_kernel<DT, BP, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    const cudaError_t e = cudaFuncSetAttribute(gemv_kernel<DT, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_done[dev] = 1;
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = sg_pdl_enabled() ? 1 : 0;
+  if (C::XPRE) {
+    const int n_units = (p.n_ch + kUC - 1) / kUC;
+    cudaLaunchConfig_t x = {};
+    x.gridDim = dim3((unsigned)((n_units * BT + 3) / 4));
+    x.blockDim = dim3(128);
+    x.stream = st;
+    x.attrs = attr;
+    x.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&x, gemv_xprep_kernel<BT>, p, n_units);
+    if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t g = {};
   g.gridDim = dim3((unsigned)G);
@@ -555,12 +894,17 @@ cudaError_t launch(const Params& p, int G, const float* x, int64_t ldx, int K, b
   g.stream = st;
   g.attrs = attr;
   g.numAttrs = 1;
-  return cudaLaunchKernelEx(&g, gemv_kernel<DT, BP, BT>, p);
+  return cudaLaunchKernelEx(&g, gemv_kernel<DT, BT>, p);
 }
 
 }  // namespace gemv_tc
 
-size_t sg_gemv_scratch_bytes(int64_t n_cols) { return gemv_tc::layout_of(nullptr, n_cols).bytes; }
+size_t sg_gemv_scratch_bytes(int64_t n_cols, int batch) {
+  using namespace gemv_tc;
+  const int64_t n_units = ((n_cols + 63) / 64 + kUC - 1) / kUC;
+  const size_t xu = batch <= 2 ? 0 : batch <= 4 ? Cfg<4>::XU : batch <= 8 ? Cfg<8>::XU : Cfg<16>::XU;
+  return kFlagsBytes + (size_t)n_units * xu;
+}
 
 cudaError_t sg_gemv(const SgGemvMat* mats, int n_mats, const float* x, int64_t ldx, int batch, bool accumulate,
                     void* scratch, size_t scratch_bytes, int num_sms, cudaStream_t st) {
@@ -570,12 +914,11 @@ cudaError_t sg_gemv(const SgGemvMat* mats, int n_mats, const float* x, int64_t l
   const SgDevWeight* w0 = mats[0].w;
   const int64_t K = w0->n_cols;
   if ((K & 31) || K > (1 << 28) || ((uintptr_t)x & 15) || (ldx & 3) || ldx < K) return cudaErrorInvalidValue;
-  if (scratch_bytes < sg_gemv_scratch_bytes(K) || ((uintptr_t)scratch & 255)) return cudaErrorInvalidValue;
+  if (scratch_bytes < sg_gemv_scratch_bytes(K, batch) || ((uintptr_t)scratch & 255)) return cudaErrorInvalidValue;
   Params p = {};
   p.n_mats = n_mats;
   p.batch = batch;
   p.n_ch = (int)w0->n_ch;
-  p.n_sc = (p.n_ch + kUC - 1) / kUC;
   p.accumulate = accumulate ? 1 : 0;
   int rb = 0;
   for (int i = 0; i < n_mats; ++i) {
@@ -584,31 +927,20 @@ cudaError_t sg_gemv(const SgGemvMat* mats, int n_mats, const float* x, int64_t l
     p.mats[i] = {w->tiles, w->dd, mats[i].y, mats[i].ldy, (int)w->n_rb, (int)w->n_rows, (int)w->n_sb, rb};
     rb += (int)w->n_rb;
   }
-  p.total = (int64_t)rb * p.n_sc;
-  const Layout l = layout_of(scratch, K);
-  p.xunits = l.xunits;
-  p.inv = l.inv;
-  // one CTA per SM
-  const int G = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms, p.total));
-  p.total_rb = rb;
-  p.zero_all = rb > kMaskWords * 32;
-  bool split = false;
-  for (int c = 1; c < G; ++c) {
-    const int64_t gu = (int64_t)c * p.total / G;
-    if (gu % p.n_sc == 0) continue;
-    split = true;
-    const int64_t r = gu / p.n_sc;
-    if (r < kMaskWords * 32) p.split[r >> 5] |= 1u << (r & 31);
-  }
-  const bool zero_split = split && !accumulate;
-  const int K32 = (int)K;
-#define SG_GEMV_LAUNCH(DT)                                                                     \
-  switch (batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : batch <= 8 ? 8 : 16) {           \
-    case 1: return launch<DT, 8, 1>(p, G, x, ldx, K32, zero_split, l, st);                      \
-    case 2: return launch<DT, 8, 2>(p, G, x, ldx, K32, zero_split, l, st);                      \
-    case 4: return launch<DT, 8, 4>(p, G, x, ldx, K32, zero_split, l, st);                      \
-    case 8: return launch<DT, 8, 8>(p, G, x, ldx, K32, zero_split, l, st);                      \
-    default: return launch<DT, 16, 16>(p, G, x, ldx, K32, zero_split, l, st);                   \
+  p.x = x;
+  p.ldx = ldx;
+  p.K = (int)K;
+  p.zflags = static_cast<unsigned long long*>(scratch);
+  p.ximg = static_cast<uint8_t*>(scratch) + kFlagsBytes;
+  static std::atomic<unsigned long long> epochs{1};
+  p.epoch = epochs.fetch_add(1);
+#define SG_GEMV_LAUNCH(DT)                                                           \
+  switch (batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : batch <= 8 ? 8 : 16) { \
+    case 1: return launch<DT, 1>(p, rb, num_sms, st);                                \
+    case 2: return launch<DT, 2>(p, rb, num_sms, st);                                \
+    case 4: return launch<DT, 4>(p, rb, num_sms, st);                                \
+    case 8: return launch<DT, 8>(p, rb, num_sms, st);                                \
+    default: return launch<DT, 16>(p, rb, num_sms, st);                              \
   }
   if (w0->dtype == SG_DTYPE_Q4_0) SG_GEMV_LAUNCH(SG_DTYPE_Q4_0)
   SG_GEMV_LAUNCH(SG_DTYPE_Q4_K)

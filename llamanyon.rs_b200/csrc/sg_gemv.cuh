@@ -4,6 +4,7 @@
 
 #define SG_GEMV_MAX_MATS 4
 #define SG_GEMV_MAX_BATCH 16
+#define SG_GEMV_MAX_CTAS 256  // CTAs per launch (one per SM)
 
 // One matrix of a (multi-)GEMV call sharing the same activations.
 struct SgGemvMat {
@@ -12,11 +13,14 @@ struct SgGemvMat {
   int64_t ldy;
 };
 
-// Scratch bytes a decode call over n_cols needs (f16 activation parts and
-// per-32-block sums for up to 16 tokens).
-size_t sg_gemv_scratch_bytes(int64_t n_cols);
+// Bytes of the GEMV workspace for n_cols and batch: the flags through which
+// the CTA that zeroes a shared row-block's rows tells the other CTAs
+// (per-call epochs; zero them when the workspace is allocated, and keep it
+// across calls), then, from 3 tokens on, the activation unit images.
+size_t sg_gemv_scratch_bytes(int64_t n_cols, int batch);
 
 // y_m[b][r] = sum_k W_m[r][k] x[b][k] for all matrices m (same K and dtype),
-// batch 1..16; accumulate: y += W x. x must be 16-byte aligned with ldx % 4 == 0.
+// batch 1..16; accumulate: y += W x. x must be 16-byte aligned with ldx % 4
+// == 0. Calls sharing a workspace must not overlap in time.
 cudaError_t sg_gemv(const SgGemvMat* mats, int n_mats, const float* x, int64_t ldx, int batch, bool accumulate,
                     void* scratch, size_t scratch_bytes, int num_sms, cudaStream_t st);

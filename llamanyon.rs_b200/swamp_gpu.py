@@ -200,7 +200,7 @@ class SwampGpu:
 
     def linear_device_noalloc(self, w: Weight, x_ptr: int, ldx: int, y_ptr: int, ldy: int, batch: int,
                               stream: int = 0, flags: int = 0):
-        """linear_device without any device allocation (decode batch 1..16, n_cols <= 16384)."""
+        """linear_device without any device allocation (decode batch 1..16)."""
         self._check(self.L.sg_linear_device_noalloc(w.handle, x_ptr, ldx, y_ptr, ldy, batch, stream or None, flags))
 
     def linear_multi_device(self, ws: Sequence[Weight], x_ptr: int, ldx: int, y_ptrs: Sequence[int],

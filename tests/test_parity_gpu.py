@@ -159,6 +159,45 @@ def test_activation_ranges(gpu, oracle):
         W.free()
 
 
+@pytest.mark.parametrize("accumulate", [False, True])
+@pytest.mark.parametrize("batch", [1, 16])
+def test_gemv_shared_row_blocks(gpu, oracle, batch, accumulate):
+    """4096 x 4096 runs 2048 chunks on one CTA per SM, so most row-blocks are
+    shared by several CTAs (zeroed by the first, reduced into y by all);
+    repeated calls must agree and match the reference, also when adding into
+    a non-zero y."""
+    n = k = 4096
+    w = _weights(oracle, Q40, n, k, tid=30)
+    x = oracle.gen_x(SEED, 31, (batch, k))
+    W = gpu.register(w, Q40, n, k)
+    try:
+        ref, l2 = reference_outputs(oracle, Q40, w, x, n, k)
+        y0 = np.linspace(-3, 3, batch * n).astype(np.float32).reshape(batch, n)
+        for _ in range(3):
+            y = gpu.linear(W, x, accumulate_into=y0.copy()) - y0 if accumulate else gpu.linear(W, x)
+            reference_gate(y, ref, l2)
+    finally:
+        W.free()
+
+
+def test_gemv_nonfinite_activation(gpu, oracle):
+    """A non-finite x makes its token's outputs non-finite (as the reference's
+    f32 sums do) and leaves the other tokens exact."""
+    n, k = 200, 1024
+    w = _weights(oracle, Q4K, n, k, tid=32)
+    x = oracle.gen_x(SEED, 33, (3, k))
+    x[1, 300] = np.inf
+    x[2, 7] = np.nan
+    W = gpu.register(w, Q4K, n, k)
+    try:
+        y = gpu.linear(W, x)
+        assert not np.isfinite(y[1]).any() and not np.isfinite(y[2]).any()
+        ref, l2 = reference_outputs(oracle, Q4K, w, x[:1], n, k)
+        reference_gate(y[:1], ref, l2)
+    finally:
+        W.free()
+
+
 def test_multi_and_accumulate(gpu, oracle):
     k = 512
     ws = [_weights(oracle, Q40, n, k, tid=10 + i) for i, n in enumerate((256, 64, 64))]

@@ -1,6 +1,6 @@
 """sg_linear_device_noalloc through the C ABI: same results as
-sg_linear_device, two calls in a row, limits rejected with a clear error, and
-no device memory taken by the calls themselves.
+sg_linear_device, two calls in a row, prefill batches rejected with a clear
+error, and no device memory taken by the calls themselves.
 
 Collected last (file name) so it also runs after every other GPU test; it
 needs nothing from them and passes alone."""
@@ -16,7 +16,8 @@ SG_ERR_UNSUPPORTED = -5
 
 
 @pytest.mark.parametrize("dtype,n,k,batch", [(Q40, 300, 4096, 1), (Q40, 200, 11008, 4), (Q4K, 256, 4096, 16),
-                                             (Q4K, 130, 14336, 3), (Q40, 64, 16384, 8)])
+                                             (Q4K, 130, 14336, 3), (Q40, 64, 16384, 8),
+                                             (Q4K, 40, 32768 + 256, 2)])
 def test_noalloc_matches_device_entry(gpu, oracle, dtype, n, k, batch):
     torch = pytest.importorskip("torch")
     w = oracle.gen_weight(dtype, SEED, 90, n, k)
@@ -57,21 +58,37 @@ def test_noalloc_takes_no_device_memory(gpu, oracle):
         W.free()
 
 
-def test_noalloc_rejects_over_limit(gpu, oracle):
+def test_noalloc_rejects_wide_tensor_at_batch_16(gpu, oracle):
+    """From 3 tokens on the fixed workspace holds activation images (32768
+    columns at 16 tokens); a wider tensor is refused with the limit in the
+    message, while batch 2 (no images) still runs."""
     torch = pytest.importorskip("torch")
     import swamp_gpu as sg
-    k = 16384 + 256  # one Q4_K super-block past the fixed scratch
+    k = 32768 + 256
+    W = gpu.register(oracle.gen_weight(Q4K, SEED, 95, 8, k), Q4K, 8, k)
+    try:
+        x = torch.zeros(16, k, device="cuda")
+        y = torch.zeros(16, 8, device="cuda")
+        with pytest.raises(sg.SwampGpuError) as e:
+            gpu.linear_device_noalloc(W, x.data_ptr(), k, y.data_ptr(), 8, 16)
+        assert e.value.code == SG_ERR_UNSUPPORTED and "32768" in str(e.value)
+        gpu.linear_device_noalloc(W, x.data_ptr(), k, y.data_ptr(), 8, 2)
+        torch.cuda.synchronize()
+        assert torch.all(y[:2] == 0)
+    finally:
+        W.free()
+
+
+def test_noalloc_rejects_prefill_batch(gpu, oracle):
+    torch = pytest.importorskip("torch")
+    import swamp_gpu as sg
+    k = 4096
     W = gpu.register(oracle.gen_weight(Q4K, SEED, 94, 8, k), Q4K, 8, k)
     try:
-        x = torch.zeros(1, k, device="cuda")
-        y = torch.zeros(1, 8, device="cuda")
-        with pytest.raises(sg.SwampGpuError) as e:
-            gpu.linear_device_noalloc(W, x.data_ptr(), k, y.data_ptr(), 8, 1)
-        assert e.value.code == SG_ERR_UNSUPPORTED and "16384" in str(e.value)
         x17 = torch.zeros(17, k, device="cuda")
         y17 = torch.zeros(17, 8, device="cuda")
         with pytest.raises(sg.SwampGpuError) as e:
             gpu.linear_device_noalloc(W, x17.data_ptr(), k, y17.data_ptr(), 8, 17)
-        assert e.value.code == SG_ERR_UNSUPPORTED
+        assert e.value.code == SG_ERR_UNSUPPORTED and "1..16" in str(e.value)
     finally:
         W.free()
