@@ -573,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
       for (int v = 0; cur.more() && ok; ++v, cur.next(p)) {
         const int xs = v % C::RX, cnt = cur.cnt(p), ci0 = cur.ci0();
         if (!mbar_wait(&x_full[xs], (v / C::RX) & 1, 0x23)) break;
-        const uint32_t xbase = smem_u32(smem + C::OFF_X + xs * C::XU);
+        const uint64_t xdesc = sg_sdesc(smem_u32(smem + C::OFF_X + xs * C::XU), SG_SW64);
         for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g) {
           const int sg = g % C::SG;
           // the slot's previous epilogue finished before the dequant warps
@@ -583,15 +583,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
             break;
           }
           sg_tc_fence_after();
+          // The issuing thread is the pipeline's pacing resource: keep the
+          // work between MMAs to a few adds. A descriptor's start-address
+          // field is the byte address / 16, so a tile offset is added to it
+          // directly (shared memory addresses stay below 2^18: no carry).
           const int gc = min(C::CPG, cnt - gi * C::CPG);
-          for (int ci = 0; ci < gc; ++ci) {
-            const int cu = ci0 + gi * C::CPG + ci;  // chunk within the unit: its activation tile
-            const uint32_t d = tmem + C::d_col(sg) + (uint32_t)((ci / C::GC) * C::N);
+          const uint32_t dbase = tmem + C::d_col(sg), abase = tmem + C::a_col(sg);
+          const uint64_t bdesc = xdesc + (uint64_t)(((ci0 + gi * C::CPG) * C::T) >> 4);
 #pragma unroll
-            for (int blk = 0; blk < 2; ++blk)  // one 32-block: 8 TMEM columns of A, 32 bytes of each B row
-              sg_umma_i8_tmem_a(d, tmem + C::a_col(sg) + (uint32_t)(ci * kACols + 8 * blk),
-                                sg_sdesc(xbase + cu * C::T + 32 * blk, SG_SW64), C::IDESC,
-                                (ci % C::GC == 0 && blk == 0) ? 0u : 1u);
+          for (int ci = 0; ci < C::CPG; ++ci) {
+            if (ci < gc) {
+              const uint32_t d = dbase + (uint32_t)((ci / C::GC) * C::N);
+              const uint64_t bd = bdesc + (uint64_t)((ci * C::T) >> 4);
+              // one MMA per 32-block: 8 TMEM columns of A, 32 bytes of each B row
+              sg_umma_i8_tmem_a(d, abase + (uint32_t)(ci * kACols), bd, C::IDESC, ci % C::GC == 0 ? 0u : 1u);
+              sg_umma_i8_tmem_a(d, abase + (uint32_t)(ci * kACols + 8), bd + 2, C::IDESC, 1u);
+            }
           }
           sg_umma_commit(&d_full[sg]);
         }
