@@ -68,6 +68,7 @@
 // (sg_common.cuh).
 #include <algorithm>
 #include <atomic>
+#include <climits>
 
 #include "sg_gemv.cuh"
 #include "sg_tc.cuh"
@@ -178,21 +179,21 @@ __device__ __forceinline__ void cta_range(const Params& p, int b, int64_t& g0, i
 // Piece cursor over the CTA's chunk range [g, g1).
 struct Cursor {
   int rbg, c, mi, rb;  // global row-block, chunk within it, matrix, row-block within the matrix
-  int64_t g, g1;
+  int g, g1;           // work index (the host keeps the total below 2^31)
+  int nrb0;            // first global row-block of the next matrix
   __device__ __forceinline__ void init(const Params& p, int64_t g0, int64_t gend) {
-    g = g0;
-    g1 = gend;
-    rbg = (int)(g0 / p.n_cp);
-    c = (int)(g0 - (int64_t)rbg * p.n_cp);  // range ends never fall in the padding
+    g = (int)g0;
+    g1 = (int)gend;
+    rbg = g / p.n_cp;
+    c = g - rbg * p.n_cp;  // range ends never fall in the padding
     mi = find_mat(p, rbg);
     rb = rbg - p.mats[mi].rb0;
+    nrb0 = mi + 1 < p.n_mats ? p.mats[mi + 1].rb0 : INT_MAX;
   }
   __device__ __forceinline__ bool more() const { return g < g1; }
   __device__ __forceinline__ int sc() const { return c >> 2; }
   __device__ __forceinline__ int ci0() const { return c & 3; }
-  __device__ __forceinline__ int cnt(const Params& p) const {
-    return (int)min((int64_t)min(kUC - (c & 3), p.n_ch - c), g1 - g);
-  }
+  __device__ __forceinline__ int cnt(const Params& p) const { return min(min(kUC - (c & 3), p.n_ch - c), g1 - g); }
   __device__ __forceinline__ void next(const Params& p) {
     const int n = cnt(p);
     g += n;
@@ -202,14 +203,29 @@ struct Cursor {
       c = 0;
       ++rbg;
       ++rb;
-      if (mi + 1 < p.n_mats && rbg >= p.mats[mi + 1].rb0) {
+      if (rbg >= nrb0) {
         ++mi;
         rb = 0;
+        nrb0 = mi + 1 < p.n_mats ? p.mats[mi + 1].rb0 : INT_MAX;
       }
     }
   }
 };
 
+
+// Position in a ring of R mbarrier-guarded slots: the slot and the parity
+// of its current phase, stepped without division.
+template <int R>
+struct Ring {
+  int slot = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next() {
+    if (++slot == R) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
 
 // 16-byte segment j of row r of a K-major SWIZZLE_64B tile (64-byte rows)
 __device__ __forceinline__ int sw64_off(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
@@ -547,9 +563,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
       Cursor cur;
       cur.init(p, g0, g1);
       int v = 0;
-      for (; cur.more(); ++v, cur.next(p)) {
-        const int ws = v % kRW;
-        if (v >= kRW && !mbar_wait(&w_empty[ws], ((v / kRW) & 1) ^ 1, 0x21)) break;
+      Ring<kRW> wr;
+      for (; cur.more(); ++v, wr.next(), cur.next(p)) {
+        const int ws = wr.slot;
+        if (v >= kRW && !mbar_wait(&w_empty[ws], wr.phase ^ 1u, 0x21)) break;
         const Mat& mt = p.mats[cur.mi];
         const int cnt = cur.cnt(p);
         uint8_t* dst = smem + C::OFF_W + ws * kWU;
@@ -570,15 +587,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
       cur.init(p, g0, g1);
       int g = 0;
       bool ok = true;
-      for (int v = 0; cur.more() && ok; ++v, cur.next(p)) {
-        const int xs = v % C::RX, cnt = cur.cnt(p), ci0 = cur.ci0();
-        if (!mbar_wait(&x_full[xs], (v / C::RX) & 1, 0x23)) break;
+      Ring<C::RX> xr;
+      Ring<C::SG> gr;
+      for (; cur.more() && ok; xr.next(), cur.next(p)) {
+        const int xs = xr.slot, cnt = cur.cnt(p), ci0 = cur.ci0();
+        if (!mbar_wait(&x_full[xs], xr.phase, 0x23)) break;
         const uint64_t xdesc = sg_sdesc(smem_u32(smem + C::OFF_X + xs * C::XU), SG_SW64);
-        for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g) {
-          const int sg = g % C::SG;
+        for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g, gr.next()) {
+          const int sg = gr.slot;
           // the slot's previous epilogue finished before the dequant warps
           // refilled it, so a_full alone makes the accumulators free too
-          if (!mbar_wait(&a_full[sg], (g / C::SG) & 1, 0x24)) {
+          if (!mbar_wait(&a_full[sg], gr.phase, 0x24)) {
             ok = false;
             break;
           }
@@ -592,13 +611,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
           const uint64_t bdesc = xdesc + (uint64_t)(((ci0 + gi * C::CPG) * C::T) >> 4);
 #pragma unroll
           for (int ci = 0; ci < C::CPG; ++ci) {
-            if (ci < gc) {
-              const uint32_t d = dbase + (uint32_t)((ci / C::GC) * C::N);
-              const uint64_t bd = bdesc + (uint64_t)((ci * C::T) >> 4);
-              // one MMA per 32-block: 8 TMEM columns of A, 32 bytes of each B row
-              sg_umma_i8_tmem_a(d, abase + (uint32_t)(ci * kACols), bd, C::IDESC, ci % C::GC == 0 ? 0u : 1u);
-              sg_umma_i8_tmem_a(d, abase + (uint32_t)(ci * kACols + 8), bd + 2, C::IDESC, 1u);
-            }
+            const uint32_t d = dbase + (uint32_t)((ci / C::GC) * C::N);
+            const uint64_t bd = bdesc + (uint64_t)((ci * C::T) >> 4);
+            const uint32_t live = ci < gc;
+            // one MMA per 32-block: 8 TMEM columns of A, 32 bytes of each B row
+            sg_umma_i8_tmem_a_if(d, abase + (uint32_t)(ci * kACols), bd, C::IDESC, ci % C::GC == 0 ? 0u : 1u, live);
+            sg_umma_i8_tmem_a_if(d, abase + (uint32_t)(ci * kACols + 8), bd + 2, C::IDESC, 1u, live);
           }
           sg_umma_commit(&d_full[sg]);
         }
@@ -615,15 +633,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
     cur.init(p, g0, g1);
     int g = 0;
     bool ok = true;
-    for (int v = 0; cur.more() && ok; ++v, cur.next(p)) {
-      const int ws = v % kRW, cnt = cur.cnt(p);
-      if (!__all_sync(0xffffffffu, mbar_wait(&w_full[ws], (v / kRW) & 1, 0x26))) break;
+    Ring<kRW> wr;
+    Ring<C::SG> gr;
+    for (; cur.more() && ok; wr.next(), cur.next(p)) {
+      const int ws = wr.slot, cnt = cur.cnt(p);
+      if (!__all_sync(0xffffffffu, mbar_wait(&w_full[ws], wr.phase, 0x26))) break;
       const uint8_t* wu = smem + C::OFF_W + ws * kWU;
       const uint32_t ddw = DT == SG_DTYPE_Q4_K ? *reinterpret_cast<const uint32_t*>(wu + kUC * SG_TILE_BYTES + row * 4) : 0u;
-      for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g) {
-        const int sg = g % C::SG;
+      for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g, gr.next()) {
+        const int sg = gr.slot;
         // the slot was last used by group g - SG: wait for its epilogue
-        const bool w = g < C::SG || mbar_wait(&d_free[sg], ((g / C::SG) & 1) ^ 1, 0x27);
+        const bool w = g < C::SG || mbar_wait(&d_free[sg], gr.phase ^ 1u, 0x27);
         if (!__all_sync(0xffffffffu, w)) {
           ok = false;
           break;
@@ -675,9 +695,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
         Cursor cur;
         cur.init(p, g0, g1);
         int v = 0;
-        for (; cur.more(); ++v, cur.next(p)) {
-          const int xs = v % C::RX;
-          if (v >= C::RX && !mbar_wait(&x_empty[xs], ((v / C::RX) & 1) ^ 1, 0x2A)) break;
+        Ring<C::RX> xr;
+        for (; cur.more(); ++v, xr.next(), cur.next(p)) {
+          const int xs = xr.slot;
+          if (v >= C::RX && !mbar_wait(&x_empty[xs], xr.phase ^ 1u, 0x2A)) break;
           mbar_arrive_expect_tx(&x_full[xs], C::XU);
           bulk_g2s(smem + C::OFF_X + xs * C::XU, p.ximg + (int64_t)cur.sc() * C::XU, C::XU, &x_full[xs]);
         }
@@ -725,10 +746,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
     for (int j = 0; j < XS - 1; ++j) stage_next(j);
     const int shift0 = cur.ci0() % C::GC;  // only a CTA's first piece can start inside a unit
     int job = 0;
-    for (int v = 0; cur.more(); ++v, cur.next(p)) {
-      const int xs = v % C::RX;
+    Ring<C::RX> xr;
+    for (int v = 0; cur.more(); ++v, xr.next(), cur.next(p)) {
+      const int xs = xr.slot;
       // the slot was last read by piece v - RX
-      if (v >= C::RX && !__all_sync(0xffffffffu, mbar_wait(&x_empty[xs], ((v / C::RX) & 1) ^ 1, 0x2A))) break;
+      if (v >= C::RX && !__all_sync(0xffffffffu, mbar_wait(&x_empty[xs], xr.phase ^ 1u, 0x2A))) break;
       uint8_t* xu = smem + C::OFF_X + xs * C::XU;
       if (BT != 1 || v % kXWarps == xw) {
         stage_next((job + XS - 1) % XS);
@@ -778,18 +800,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
     for (int t = 0; t < BT; ++t) acc[t] = 0.f;
     Cursor cur;
     cur.init(p, g0, g1);
-    int g = 0;
     bool ok = true;
-    for (int v = 0; cur.more() && ok; ++v, cur.next(p)) {
-      const int xs = v % C::RX, cnt = cur.cnt(p), ci0 = cur.ci0();
-      if (!__all_sync(0xffffffffu, mbar_wait(&x_full[xs], (v / C::RX) & 1, 0x2B))) break;
+    Ring<C::RX> xr;
+    Ring<C::SG> gr;
+    for (; cur.more() && ok; xr.next(), cur.next(p)) {
+      const int xs = xr.slot, cnt = cur.cnt(p), ci0 = cur.ci0();
+      if (!__all_sync(0xffffffffu, mbar_wait(&x_full[xs], xr.phase, 0x2B))) break;
       const float* tail = reinterpret_cast<const float*>(smem + C::OFF_X + xs * C::XU + kUC * C::T);
       float accu[BT];
 #pragma unroll
       for (int t = 0; t < BT; ++t) accu[t] = 0.f;
-      for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g) {
-        const int sg = g % C::SG;
-        if (!__all_sync(0xffffffffu, mbar_wait(&d_full[sg], (g / C::SG) & 1, 0x25))) {
+      for (int gi = 0; gi * C::CPG < cnt; ++gi, gr.next()) {
+        const int sg = gr.slot;
+        if (!__all_sync(0xffffffffu, mbar_wait(&d_full[sg], gr.phase, 0x25))) {
           ok = false;
           break;
         }
@@ -870,6 +893,7 @@ cudaError_t launch(Params p, int rb_total, int num_sms, cudaStream_t st) {
   p.spl = C::SPL;
   p.n_cp = (p.n_ch + C::SPL - 1) / C::SPL * C::SPL;
   p.total = (int64_t)rb_total * p.n_cp;
+  if (p.total >= INT_MAX / 2) return cudaErrorInvalidValue;  // the device cursor counts chunks in 32 bits
   const int64_t slots = p.total / p.spl;
   const int G = (int)std::max<int64_t>(1, std::min<int64_t>(std::min(num_sms, kMaxCtas), slots));  // one CTA per SM
   static int attr_done[64] = {0};

@@ -51,6 +51,16 @@ __device__ __forceinline__ void sg_umma_i8_tmem_a(uint32_t tmem_d, uint32_t tmem
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// the same, issued only when `issue` is nonzero (a predicate instead of a
+// branch: the issuing thread runs straight-line code)
+__device__ __forceinline__ void sg_umma_i8_tmem_a_if(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                     uint32_t accumulate, uint32_t issue) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(issue));
+}
+
 __device__ __forceinline__ void sg_umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                              uint32_t accumulate) {
   asm volatile(
