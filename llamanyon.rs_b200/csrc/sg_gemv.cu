@@ -76,18 +76,21 @@
 namespace gemv_tc {
 
 constexpr int kUC = 4;                          // chunks per unit
-constexpr int kRW = 6;                          // weight piece ring
 constexpr int kACols = 16;                      // TMEM columns of one chunk's A tile: 64 K of u8 per lane
 constexpr int kScCols = 5;                      // TMEM columns of a group's scale words (chunks 0..3, Q4_K d|dmin at 4)
 constexpr int kWU = kUC * SG_TILE_BYTES + 512;  // packed weights of a unit + Q4_K d|dmin
-constexpr int kThreads = 384;
-constexpr int kXWarps = 2;                      // activation warps
 constexpr int kMaxCtas = SG_GEMV_MAX_CTAS;
 constexpr int kSumOff = 0;                      // within a unit's tail: block sums [chunk 4][blk 2][token 16] f32
 constexpr int kInvOff = 512;                    //                       1/s per token [16] f32
 
 template <int BT>
 struct Cfg {
+  // Every role's loop has a fixed cost per piece (waits, hand-offs) of the
+  // order of the time HBM takes to deliver the piece to one SM. At one token
+  // two CTAs share each SM (CPS), each with half the rings: two independent
+  // pipelines per SM. Wider batches need the registers of a whole SM.
+  static constexpr bool DUAL = BT == 1;
+  static constexpr int CPS = DUAL ? 2 : 1;                   // CTAs per SM
   static constexpr int GC = BT <= 2 ? 4 : BT == 16 ? 1 : 2;   // chunks per accumulator
   // From 4 tokens on, the activation tiles are built once per call by
   // gemv_xprep_kernel (an image in global memory, one bulk copy per piece):
@@ -102,36 +105,82 @@ struct Cfg {
   static constexpr int N = (ROWS + 15) / 16 * 16;            // MMA N
   static constexpr int T = N * 64;                           // activation tile bytes (one chunk)
   static constexpr int XU = kUC * T + 1024;                  // activation unit: 4 tiles + sums + scales
-  static constexpr int RX = BT == 1 ? 8 : BT == 2 ? 6 : 3;    // activation unit ring: deep where units are small
-  static constexpr int NTW = BT == 1 ? 1 : BT / kXWarps;     // tokens per activation job (one warp, one piece)
+  // activation unit ring: a slot is held from its conversion or copy until
+  // the epilogue has read the unit's sums, a loop of several microseconds
+  static constexpr int RX = DUAL ? 4 : BT <= 4 ? 6 : 4;
+  // Activations built in the kernel (1 or 2 tokens): NXW warps, XPP of them
+  // (one per token) on each piece, the pieces dealt round-robin to XL =
+  // NXW / XPP lanes of warps. Converting a unit is a chain of shuffles of
+  // about 0.8 us per warp, so several pieces must be in conversion at once.
+  static constexpr int NXW = XPRE ? 1 : DUAL ? 2 : 4;        // activation warps (with XPRE: the copy thread's)
+  static constexpr int XPP = XPRE ? 1 : BT;                  // warps (tokens) per piece
+  static constexpr int XL = NXW / XPP;                       // pieces converted side by side
   static constexpr int XS = XPRE ? 0 : 3;                    // staging slots per activation warp (x prefetch)
+  // One thread issues an MMA about every 50 cycles whatever its size, and
+  // issuers in different warps run side by side; a group's epilogue is a
+  // chain of waits and loads of similar latency. Up to 4 tokens a group is
+  // one piece, and two lanes -- an MMA issuer and a set of 4 epilogue warps
+  // each -- take alternate pieces: set s the pieces v with v % 2 == s.
+  static constexpr int NSET = !DUAL && BT <= 4 ? 2 : 1;
+  // Warps: 0 weights (lane 0) and shared output rows; 1 MMA issuer 0 and
+  // TMEM owner; 2-5 dequant; 6-9 epilogue set 0; 10 (and 11, 17, 18 when
+  // x is converted here) activations; 12-15 epilogue set 1; MMA issuer 1 at
+  // 16 (11 when x is prepared).
+  static constexpr int WARPS = DUAL ? 12 : BT == 2 ? 19 : BT == 4 ? 16 : 12;
+  static constexpr int THREADS = WARPS * 32;
+  // Registers per thread: a GEMV CTA leaves room for one CTA of the next
+  // call's activation prep kernel (128 threads x 32 registers), which under
+  // programmatic dependent launch must run on an SM next to it; at one token
+  // two GEMV CTAs share the SM.
+  static constexpr int MAXREG = DUAL ? 80 : ((65536 - 4096) / THREADS) / 8 * 8;
+  static constexpr int MMA1_WARP = BT <= 2 ? 16 : 11;
+  // activation warp index of `warp` (-1: not one)
+  __device__ static int x_warp(int warp) {
+    if (warp == 10) return 0;
+    if (!XPRE && warp == 11) return 1;
+    if (!XPRE && !DUAL && (warp == 17 || warp == 18)) return warp - 15;
+    return -1;
+  }
   static constexpr int OFF_X = 0;
-  static constexpr int OFF_S = OFF_X + RX * XU;              // x staging: [warp][slot][token][256] f32
-  static constexpr int OFF_W = OFF_S + kXWarps * XS * NTW * 1024;
+  static constexpr int OFF_S = OFF_X + RX * XU;              // x staging: [warp][slot][256] f32
+  static constexpr int OFF_W = OFF_S + NXW * XS * 1024;
   // One CTA per SM: two CTAs of consecutive calls sharing an SM under PDL
   // would make the second wait in tcgen05.alloc; ask for more than half of
   // the SM's shared memory.
-  static constexpr int SMEM_USED = OFF_W + kRW * kWU + 1024;
-  static constexpr int SMEM = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
-  // TMEM: [SG accumulator blocks][SG A-tile blocks][SG x kScCols scale
-  // words]. Every multi-column access starts on a multiple of 16 columns;
-  // scale words are read and written one column at a time.
+  // Weight ring: a slot holds a piece from its copy until the dequant warps
+  // have read it; at one CTA per SM the copies in flight must cover the HBM
+  // latency under load (about 2 us at 44 GB/s per SM), so the ring takes
+  // what shared memory leaves.
+  static constexpr int RW = DUAL ? 3 : BT <= 4 ? 7 : 6;
+  static constexpr int SMEM_USED = OFF_W + RW * kWU + 1024;
+  static constexpr int SMEM = DUAL || SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
+  // TMEM holds two rings. A-tile slots (SA) are free again once the MMAs
+  // that read them complete; accumulator slots (SD, each with the group's
+  // scale words) once the epilogue has read them. The dequant warps thus
+  // wait on the short dequant -> MMA loop for A, and the long loop through
+  // the epilogue is covered by the deeper accumulator ring. Layout:
+  // [SD accumulator blocks][SA A-tile blocks][SD x kScCols scale words];
+  // every multi-column access starts on a multiple of 16 columns, scale
+  // words are read and written one column at a time.
   static constexpr uint32_t A_COLS = CPG * kACols;
   static constexpr uint32_t D_COLS = NACC * N;
-  static constexpr uint32_t G_COLS = A_COLS + kScCols + D_COLS;  // one group slot
-  static constexpr int SG = (int)(512 / G_COLS) > 6 ? 6 : (int)(512 / G_COLS);  // group slots
-  static constexpr uint32_t A_COL0 = SG * D_COLS;
-  static constexpr uint32_t SC_COL0 = A_COL0 + SG * A_COLS;
-  __host__ __device__ static constexpr uint32_t d_col(int sg) { return (uint32_t)sg * D_COLS; }
-  __host__ __device__ static constexpr uint32_t a_col(int sg) { return A_COL0 + (uint32_t)sg * A_COLS; }
-  __host__ __device__ static constexpr uint32_t sc_col(int sg) { return SC_COL0 + (uint32_t)sg * kScCols; }
-  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t TMEM_COLS = DUAL ? 256 : 512;
+  static constexpr int SA = DUAL ? 2 : 3;
+  static constexpr int SD_FIT = (int)((TMEM_COLS - SA * A_COLS) / (D_COLS + kScCols));
+  static constexpr int SD = SD_FIT > 6 ? 6 : SD_FIT;
+  static constexpr uint32_t A_COL0 = SD * D_COLS;
+  static constexpr uint32_t SC_COL0 = A_COL0 + SA * A_COLS;
+  __host__ __device__ static constexpr uint32_t d_col(int sd) { return (uint32_t)sd * D_COLS; }
+  __host__ __device__ static constexpr uint32_t a_col(int sa) { return A_COL0 + (uint32_t)sa * A_COLS; }
+  __host__ __device__ static constexpr uint32_t sc_col(int sd) { return SC_COL0 + (uint32_t)sd * kScCols; }
   static constexpr uint32_t IDESC = sg_idesc_u8s8(128, N);
-  static_assert(SG >= 2 && SC_COL0 + SG * kScCols <= TMEM_COLS, "TMEM budget");
+  static_assert(SA >= 2 && SD >= 2 && SC_COL0 + SD * kScCols <= TMEM_COLS, "TMEM budget");
   static_assert(D_COLS % 16 == 0 && A_COLS % 16 == 0, "TMEM alignment");
   static_assert(N <= 256 && ROWS <= N, "MMA N");
   static_assert(XU % 1024 == 0, "operand tiles keep 1024-byte alignment");
-  static_assert(SMEM_USED <= 227 * 1024, "shared memory budget");
+  static_assert(SMEM_USED <= (DUAL ? 110 : 227) * 1024, "shared memory budget");
+  static_assert(NSET == 1 || (CPG == kUC && BT <= 4), "two lanes need one group per piece");
+  static_assert(XPRE || (BT <= 2 && XL * XPP == NXW && RX % XL == 0), "activation lanes");
 };
 
 struct Mat {
@@ -215,13 +264,15 @@ struct Cursor {
 
 // Position in a ring of R mbarrier-guarded slots: the slot and the parity
 // of its current phase, stepped without division.
-template <int R>
+template <int R, int S = 1>
 struct Ring {
-  int slot = 0;
-  uint32_t phase = 0;
-  __device__ __forceinline__ void next() {
-    if (++slot == R) {
-      slot = 0;
+  int slot;
+  uint32_t phase;
+  __device__ __forceinline__ explicit Ring(int start = 0) : slot(start), phase(0u) {}  // start < R
+  __device__ __forceinline__ void next() {  // S positions on (S <= R)
+    slot += S;
+    if (slot >= R) {
+      slot -= R;
       phase ^= 1u;
     }
   }
@@ -513,15 +564,19 @@ __global__ void __launch_bounds__(128) gemv_xprep_kernel(Params p, int n_units) 
 // ---------------------------------------------------------------- GEMV
 // BT: live token columns rounded up to a power of two
 template <int DT, int BT>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
+__global__ void __launch_bounds__(Cfg<BT>::THREADS) __maxnreg__(Cfg<BT>::MAXREG) gemv_kernel(Params p) {
   using C = Cfg<BT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  // per group g: a_full[g % SG] -- its A tiles and scale words are in TMEM;
-  // d_full[g % SG] -- its MMAs completed; d_free[g % SG] -- its epilogue is
-  // done, so the whole slot may be rewritten
-  __shared__ __align__(8) uint64_t w_full[kRW], w_empty[kRW], x_full[C::RX], x_empty[C::RX], a_full[C::SG],
-      d_full[C::SG], d_free[C::SG], zero_own, zero_ok;
+  // per group g: a_full[g % SA] -- its A tiles and scale words are in TMEM;
+  // a_free[g % SA] and d_full[g % SD] -- its MMAs completed; d_free[g % SD]
+  // -- its epilogue is done with the accumulators and scale words
+  __shared__ __align__(8) uint64_t w_full[C::RW], w_empty[C::RW], x_full[C::RX], x_empty[C::RX], a_full[C::SA],
+      a_free[C::SA], d_full[C::SD], d_free[C::SD], zero_own, zero_ok;
+  // two epilogue sets: at a segment end the set that did not run its last
+  // piece hands its sums over (seg_full), the other adds them (seg_empty)
+  __shared__ __align__(8) uint64_t seg_full, seg_empty;
+  __shared__ float seg_acc[C::NSET == 2 ? 128 * BT : 1];
   __shared__ uint32_t tmem_base_sh;
 
   pdl_launch_dependents();  // the next kernel may start its own prologue once SMs free up
@@ -530,26 +585,31 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
   cta_range(p, blockIdx.x, g0, g1);
 
   if (threadIdx.x == 0) {
-    for (int r = 0; r < kRW; ++r) {
+    for (int r = 0; r < C::RW; ++r) {
       mbar_init(&w_full[r], 1);
       mbar_init(&w_empty[r], 4);
     }
     for (int r = 0; r < C::RX; ++r) {
-      mbar_init(&x_full[r], C::XPRE ? 1 : kXWarps);
+      mbar_init(&x_full[r], C::XPP);
       mbar_init(&x_empty[r], 4);
     }
-    for (int s = 0; s < C::SG; ++s) {
+    for (int s = 0; s < C::SA; ++s) {
       mbar_init(&a_full[s], 4);
+      mbar_init(&a_free[s], 1);
+    }
+    for (int s = 0; s < C::SD; ++s) {
       mbar_init(&d_full[s], 1);
       mbar_init(&d_free[s], 4);
     }
     mbar_init(&zero_own, 1);
     mbar_init(&zero_ok, 1);
+    mbar_init(&seg_full, 4);
+    mbar_init(&seg_empty, 4);
     mbar_fence_init();
   }
   // activation tiles built here: zero once; afterwards only digit bytes are written
   if (!C::XPRE)
-    for (int i = threadIdx.x; i < C::RX * C::XU / 16; i += kThreads)
+    for (int i = threadIdx.x; i < C::RX * C::XU / 16; i += C::THREADS)
       reinterpret_cast<uint4*>(smem + C::OFF_X)[i] = make_uint4(0u, 0u, 0u, 0u);
   if (warp == 1) sg_tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
   sg_tc_fence_before();
@@ -563,10 +623,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
       Cursor cur;
       cur.init(p, g0, g1);
       int v = 0;
-      Ring<kRW> wr;
+      Ring<C::RW> wr;
       for (; cur.more(); ++v, wr.next(), cur.next(p)) {
         const int ws = wr.slot;
-        if (v >= kRW && !mbar_wait(&w_empty[ws], wr.phase ^ 1u, 0x21)) break;
+        if (v >= C::RW && !mbar_wait(&w_empty[ws], wr.phase ^ 1u, 0x21)) break;
         const Mat& mt = p.mats[cur.mi];
         const int cnt = cur.cnt(p);
         uint8_t* dst = smem + C::OFF_W + ws * kWU;
@@ -576,38 +636,42 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
           bulk_g2s(dst + kUC * SG_TILE_BYTES, mt.dd + ((int64_t)cur.rb * mt.n_sb + cur.sc()) * 128, 512, &w_full[ws]);
       }
       if (*(volatile int*)&g_sg_error != 0)  // error path: no copy may land after the CTA exits
-        for (int j = max(0, v - kRW); j < v; ++j) mbar_wait_drain(&w_full[j % kRW], (j / kRW) & 1);
+        for (int j = max(0, v - C::RW); j < v; ++j) mbar_wait_drain(&w_full[j % C::RW], (j / C::RW) & 1);
     } else {
       shared_rows_role(p, g0, g1, lane, &zero_own, &zero_ok);
     }
-  } else if (warp == 1) {
-    // ============================================================ MMA issuer
+  } else if (warp == 1 || (C::NSET == 2 && warp == C::MMA1_WARP)) {
+    // ============================================================ MMA issuers
     if (lane == 0) {
+      const int set = warp == 1 ? 0 : 1;
       Cursor cur;
       cur.init(p, g0, g1);
-      int g = 0;
+      if (set == 1 && cur.more()) cur.next(p);
+      int g = 0, last_sd = 0;
+      uint32_t last_ph = 0u;
       bool ok = true;
-      Ring<C::RX> xr;
-      Ring<C::SG> gr;
-      for (; cur.more() && ok; xr.next(), cur.next(p)) {
+      Ring<C::RX, C::NSET> xr(set);
+      Ring<C::SA, C::NSET> ar(set);
+      Ring<C::SD, C::NSET> dr(set);
+      while (cur.more() && ok) {
         const int xs = xr.slot, cnt = cur.cnt(p), ci0 = cur.ci0();
         if (!mbar_wait(&x_full[xs], xr.phase, 0x23)) break;
         const uint64_t xdesc = sg_sdesc(smem_u32(smem + C::OFF_X + xs * C::XU), SG_SW64);
-        for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g, gr.next()) {
-          const int sg = gr.slot;
-          // the slot's previous epilogue finished before the dequant warps
-          // refilled it, so a_full alone makes the accumulators free too
-          if (!mbar_wait(&a_full[sg], gr.phase, 0x24)) {
+        for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g, ar.next(), dr.next()) {
+          const int sa = ar.slot, sd = dr.slot;
+          // the dequant warps waited for the accumulator slot's previous
+          // epilogue before they signalled a_full: it makes both slots ready
+          if (!mbar_wait(&a_full[sa], ar.phase, 0x24)) {
             ok = false;
             break;
           }
           sg_tc_fence_after();
-          // The issuing thread is the pipeline's pacing resource: keep the
-          // work between MMAs to a few adds. A descriptor's start-address
-          // field is the byte address / 16, so a tile offset is added to it
-          // directly (shared memory addresses stay below 2^18: no carry).
+          // The issuing thread is a pacing resource: keep the work between
+          // MMAs to a few adds. A descriptor's start-address field is the
+          // byte address / 16, so a tile offset is added to it directly
+          // (shared memory addresses stay below 2^18: no carry).
           const int gc = min(C::CPG, cnt - gi * C::CPG);
-          const uint32_t dbase = tmem + C::d_col(sg), abase = tmem + C::a_col(sg);
+          const uint32_t dbase = tmem + C::d_col(sd), abase = tmem + C::a_col(sa);
           const uint64_t bdesc = xdesc + (uint64_t)(((ci0 + gi * C::CPG) * C::T) >> 4);
 #pragma unroll
           for (int ci = 0; ci < C::CPG; ++ci) {
@@ -618,12 +682,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
             sg_umma_i8_tmem_a_if(d, abase + (uint32_t)(ci * kACols), bd, C::IDESC, ci % C::GC == 0 ? 0u : 1u, live);
             sg_umma_i8_tmem_a_if(d, abase + (uint32_t)(ci * kACols + 8), bd + 2, C::IDESC, 1u, live);
           }
-          sg_umma_commit(&d_full[sg]);
+          sg_umma_commit(&d_full[sd]);
+          sg_umma_commit(&a_free[sa]);
+          last_sd = sd;
+          last_ph = dr.phase;
         }
+        xr.next();
+#pragma unroll
+        for (int i = 0; i < C::NSET; ++i)
+          if (cur.more()) cur.next(p);
       }
       // every MMA issued must have completed before TMEM is freed (the last
       // commit covers all of them; on the normal path this returns at once)
-      if (g > 0) mbar_wait_drain(&d_full[(g - 1) % C::SG], ((g - 1) / C::SG) & 1);
+      if (g > 0) mbar_wait_drain(&d_full[last_sd], last_ph);
     }
   } else if (warp < 6) {
     // ======================================================== dequant warps
@@ -633,32 +704,52 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
     cur.init(p, g0, g1);
     int g = 0;
     bool ok = true;
-    Ring<kRW> wr;
-    Ring<C::SG> gr;
+    Ring<C::RW> wr;
+    Ring<C::SA> ar;
+    Ring<C::SD> dr;
     for (; cur.more() && ok; wr.next(), cur.next(p)) {
       const int ws = wr.slot, cnt = cur.cnt(p);
       if (!__all_sync(0xffffffffu, mbar_wait(&w_full[ws], wr.phase, 0x26))) break;
       const uint8_t* wu = smem + C::OFF_W + ws * kWU;
       const uint32_t ddw = DT == SG_DTYPE_Q4_K ? *reinterpret_cast<const uint32_t*>(wu + kUC * SG_TILE_BYTES + row * 4) : 0u;
-      for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g, gr.next()) {
-        const int sg = gr.slot;
-        // the slot was last used by group g - SG: wait for its epilogue
-        const bool w = g < C::SG || mbar_wait(&d_free[sg], gr.phase ^ 1u, 0x27);
+      // A group's words of this row: every chunk slot of the group is read,
+      // live or not (a slot past the piece holds stale bytes of the ring and
+      // no MMA reads its columns), so the reads are straight-line code.
+      uint4 n0[C::CPG], n1[C::CPG];
+      uint32_t scw[4] = {0u, 0u, 0u, 0u};
+      auto load_group = [&](int gi) {
+#pragma unroll
+        for (int ci = 0; ci < C::CPG; ++ci) {
+          const uint8_t* tile = wu + (gi * C::CPG + ci) * SG_TILE_BYTES;
+          n0[ci] = *reinterpret_cast<const uint4*>(tile + row * 16);         // block 0: K 0..31
+          n1[ci] = *reinterpret_cast<const uint4*>(tile + 2048 + row * 16);  // block 1: K 32..63
+          scw[ci] = *reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF + row * 4);
+        }
+      };
+      // With one group per piece the words fit in registers: the weight slot
+      // is released before the waits for TMEM, so it holds only copies in
+      // flight and the ring keeps the HBM stream full.
+      constexpr bool kEarly = C::CPG == kUC;
+      if (kEarly) {
+        load_group(0);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&w_empty[ws]);
+      }
+      for (int gi = 0; gi * C::CPG < cnt; ++gi, ++g, ar.next(), dr.next()) {
+        const int sa = ar.slot, sd = dr.slot;
+        // the A slot was last read by the MMAs of group g - SA, the scale
+        // words and accumulators by the epilogue of group g - SD
+        const bool w = (g < C::SA || mbar_wait(&a_free[sa], ar.phase ^ 1u, 0x27)) &&
+                       (g < C::SD || mbar_wait(&d_free[sd], dr.phase ^ 1u, 0x28));
         if (!__all_sync(0xffffffffu, w)) {
           ok = false;
           break;
         }
         sg_tc_fence_after();
-        const int gc = min(C::CPG, cnt - gi * C::CPG);
-        uint32_t scw[4] = {0u, 0u, 0u, 0u};
+        if (!kEarly) load_group(gi);
 #pragma unroll
         for (int ci = 0; ci < C::CPG; ++ci) {
-          if (ci >= gc) break;  // warp-uniform
-          const uint8_t* tile = wu + (gi * C::CPG + ci) * SG_TILE_BYTES;
-          const uint4 n0 = *reinterpret_cast<const uint4*>(tile + row * 16);         // block 0: K 0..31
-          const uint4 n1 = *reinterpret_cast<const uint4*>(tile + 2048 + row * 16);  // block 1: K 32..63
-          scw[ci] = *reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF + row * 4);
-          const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+          const uint32_t nw[8] = {n0[ci].x, n0[ci].y, n0[ci].z, n0[ci].w, n1[ci].x, n1[ci].y, n1[ci].z, n1[ci].w};
           // column 2w: the low nibbles of word w (K offsets 0,4,1,5 of its 8),
           // column 2w+1: the high nibbles (2,6,3,7)
           uint32_t av[16];
@@ -667,9 +758,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
             av[2 * jj] = nw[jj] & 0x0F0F0F0Fu;
             av[2 * jj + 1] = (nw[jj] >> 4) & 0x0F0F0F0Fu;
           }
-          sg_tmem_st16(lane_base + C::a_col(sg) + (uint32_t)(ci * kACols), av);
+          sg_tmem_st16(lane_base + C::a_col(sa) + (uint32_t)(ci * kACols), av);
         }
-        const uint32_t scc = lane_base + C::sc_col(sg);
+        const uint32_t scc = lane_base + C::sc_col(sd);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const uint32_t one[1] = {scw[i]};
@@ -680,12 +771,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
         sg_tmem_st_wait();
         sg_tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[sg]);
+        if (lane == 0) mbar_arrive(&a_full[sa]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&w_empty[ws]);  // the piece's weights are all in TMEM now
+      if (!kEarly) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&w_empty[ws]);  // the piece's weights are all in TMEM now
+      }
     }
-  } else if (warp >= 10) {
+  } else if (C::x_warp(warp) >= 0) {
     // ===================================================== activation warps
     if constexpr (C::XPRE) {
       // the call's unit images are ready once the prep kernel completes: one
@@ -706,90 +799,84 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
           for (int j = max(0, v - C::RX); j < v; ++j) mbar_wait_drain(&x_full[j % C::RX], (j / C::RX) & 1);
       }
     } else {
-    // Jobs: at one token the two warps take alternate pieces, otherwise each
-    // takes half of the tokens of every piece. A job's x (NTW x 1 KB) is
-    // fetched with cp.async into this warp's staging slots XS - 1 jobs ahead,
-    // so the global latency overlaps the jobs in between.
-    const int xw = warp - 10;
-    constexpr int NTW = C::NTW, XS = C::XS;
-    constexpr int STEP = BT == 1 ? kXWarps : 1;  // pieces from one job of this warp to the next
-    float* stage = reinterpret_cast<float*>(smem + C::OFF_S) + xw * XS * NTW * 256;
+    // Warp xw converts token xw % XPP of the pieces v with v % XL == xw / XPP.
+    // A job's x (1 KB) is fetched with cp.async into the warp's staging
+    // slots XS - 1 jobs ahead, so the global latency overlaps the jobs in
+    // between.
+    const int xw = C::x_warp(warp);
+    constexpr int XS = C::XS, XL = C::XL;
+    const int xl = xw / C::XPP, t = xw % C::XPP;
+    const bool live = t < p.batch;  // warp-uniform
+    float* stage = reinterpret_cast<float*>(smem + C::OFF_S) + xw * XS * 256;
     pdl_wait();  // x may come from the previous kernel
     Cursor cur;
     cur.init(p, g0, g1);
+    const int shift0 = cur.ci0() % C::GC;  // only a CTA's first piece can start inside a unit
+    for (int i = 0; i < xl && cur.more(); ++i) cur.next(p);
     Cursor pf = cur;  // next piece to stage for this warp
-    if (BT == 1)
-      for (int i = 0; i < xw && pf.more(); ++i) pf.next(p);
     // stage the job at pf into slot sl (an empty group when pf is done), then
     // step pf to this warp's next job
     auto stage_next = [&](int sl) {
       if (pf.more()) {
         const int k0 = 256 * pf.sc() + 8 * lane;
-#pragma unroll
-        for (int i = 0; i < NTW; ++i) {
-          const int t = BT == 1 ? 0 : xw + kXWarps * i;
-          if (t < p.batch) {
-            const float* src = p.x + (int64_t)t * p.ldx + (k0 < p.K ? k0 : 0);
-            const uint32_t nb = k0 < p.K ? 16u : 0u;  // 0: zero-fill, nothing read
-            float* dst = stage + (sl * NTW + i) * 256 + 8 * lane;
-            cp_async16(dst, src, nb);
-            cp_async16(dst + 4, src + 4, nb);
-          }
+        if (live) {
+          const float* src = p.x + (int64_t)t * p.ldx + (k0 < p.K ? k0 : 0);
+          const uint32_t nb = k0 < p.K ? 16u : 0u;  // 0: zero-fill, nothing read
+          float* dst = stage + sl * 256 + 8 * lane;
+          cp_async16(dst, src, nb);
+          cp_async16(dst + 4, src + 4, nb);
         }
 #pragma unroll
-        for (int i = 0; i < STEP; ++i)
+        for (int i = 0; i < XL; ++i)
           if (pf.more()) pf.next(p);
       }
       cp_async_commit();
     };
 #pragma unroll
     for (int j = 0; j < XS - 1; ++j) stage_next(j);
-    const int shift0 = cur.ci0() % C::GC;  // only a CTA's first piece can start inside a unit
     int job = 0;
-    Ring<C::RX> xr;
-    for (int v = 0; cur.more(); ++v, xr.next(), cur.next(p)) {
+    Ring<C::RX, XL> xr(xl);
+    for (int v = xl; cur.more(); v += XL) {
       const int xs = xr.slot;
       // the slot was last read by piece v - RX
       if (v >= C::RX && !__all_sync(0xffffffffu, mbar_wait(&x_empty[xs], xr.phase ^ 1u, 0x2A))) break;
       uint8_t* xu = smem + C::OFF_X + xs * C::XU;
-      if (BT != 1 || v % kXWarps == xw) {
-        stage_next((job + XS - 1) % XS);
-        cp_async_wait<XS - 1>();  // this job's copies have landed (each lane reads only its own)
-        const float* sj = stage + (job % XS) * NTW * 256 + 8 * lane;
-        if (v == C::RX && shift0 != 0) {
-          // piece 0 placed its rows at shifted positions: clear every row of
-          // this job's tokens in the slot
-          for (int i = 0; i < NTW; ++i) {
-            const int t = BT == 1 ? 0 : xw + kXWarps * i;
-            if (t >= p.batch) break;
-            for (int e = lane; e < kUC * C::GC * 6 * 4; e += 32) {  // (tile, row of the token, 16-byte segment)
-              const int c = e / (C::GC * 6 * 4), r = (e / 4) % (C::GC * 6), sgm = e % 4;
-              const int n = brow<BT>(r / 6, (r / 3) % 2, r % 3, t);
-              reinterpret_cast<uint4*>(xu + c * C::T + n * 64)[sgm] = make_uint4(0u, 0u, 0u, 0u);
-            }
-          }
-          __syncwarp();
+      stage_next((job + XS - 1) % XS);
+      cp_async_wait<XS - 1>();  // this job's copies have landed (each lane reads only its own)
+      const float* sj = stage + (job % XS) * 256 + 8 * lane;
+      if (v == C::RX && shift0 != 0 && live) {
+        // piece 0 placed its rows at shifted positions: clear every row of
+        // this warp's token in the slot
+        for (int e = lane; e < kUC * C::GC * 6 * 4; e += 32) {  // (tile, row of the token, 16-byte segment)
+          const int c = e / (C::GC * 6 * 4), r = (e / 4) % (C::GC * 6), sgm = e % 4;
+          const int n = brow<BT>(r / 6, (r / 3) % 2, r % 3, t);
+          reinterpret_cast<uint4*>(xu + c * C::T + n * 64)[sgm] = make_uint4(0u, 0u, 0u, 0u);
         }
-#pragma unroll
-        for (int i = 0; i < NTW; ++i) {
-          const int t = BT == 1 ? 0 : xw + kXWarps * i;
-          if (t < p.batch) {  // warp-uniform
-            const float4 a = *reinterpret_cast<const float4*>(sj + i * 256);
-            const float4 b = *reinterpret_cast<const float4*>(sj + i * 256 + 4);
-            const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-            store_digits<BT>(xu, unit_digits(xv), t, lane, cur.ci0());
-          }
-        }
-        ++job;
+        __syncwarp();
       }
+      if (live) {
+        const float4 a = *reinterpret_cast<const float4*>(sj);
+        const float4 b = *reinterpret_cast<const float4*>(sj + 4);
+        const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        store_digits<BT>(xu, unit_digits(xv), t, lane, cur.ci0());
+      }
+      ++job;
       fence_proxy_async_smem();  // the tensor core reads the tiles through the async proxy
       __syncwarp();
       if (lane == 0) mbar_arrive(&x_full[xs]);
+      xr.next();
+#pragma unroll
+      for (int i = 0; i < XL; ++i)
+        if (cur.more()) cur.next(p);
     }
     cp_async_wait<0>();  // no copy may land after the CTA exits
     }
-  } else {
+  } else if ((warp >= 6 && warp < 10) || (C::NSET == 2 && warp >= 12 && warp < 16)) {
     // ============================================================ epilogue warps
+    // warps 6-9 (set 0) and, with two sets, 12-15 (set 1); set s runs the
+    // pieces v with v % NSET == s and sums them per row; at a segment end the
+    // other set's sums are added in before the store
+    const int set = warp >= 12 ? 1 : 0;
     const int q = warp & 3;  // TMEM lane quadrant
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
@@ -801,25 +888,42 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
     Cursor cur;
     cur.init(p, g0, g1);
     bool ok = true;
-    Ring<C::RX> xr;
-    Ring<C::SG> gr;
-    for (; cur.more() && ok; xr.next(), cur.next(p)) {
-      const int xs = xr.slot, cnt = cur.cnt(p), ci0 = cur.ci0();
+    Ring<C::RX, C::NSET> xr(set);
+    Ring<C::SD, C::NSET> dr(set);
+    int segs = 0;  // segment ends passed (both sets count every one)
+    for (int v = 0; cur.more() && ok; ++v, cur.next(p)) {
+      const int cnt = cur.cnt(p), ci0 = cur.ci0();
+      if (C::NSET == 2 && (v & 1) != set) {
+        if (cur.c + cnt == p.n_ch || cur.g + cnt == cur.g1) {
+          // the other set ends this segment: hand it this set's sums
+          if (segs > 0 && !__all_sync(0xffffffffu, mbar_wait(&seg_empty, (segs - 1) & 1, 0x30))) break;
+#pragma unroll
+          for (int t = 0; t < BT; ++t) {
+            seg_acc[row * BT + t] = acc[t];
+            acc[t] = 0.f;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&seg_full);
+          ++segs;
+        }
+        continue;
+      }
+      const int xs = xr.slot;
       if (!__all_sync(0xffffffffu, mbar_wait(&x_full[xs], xr.phase, 0x2B))) break;
       const float* tail = reinterpret_cast<const float*>(smem + C::OFF_X + xs * C::XU + kUC * C::T);
       float accu[BT];
 #pragma unroll
       for (int t = 0; t < BT; ++t) accu[t] = 0.f;
-      for (int gi = 0; gi * C::CPG < cnt; ++gi, gr.next()) {
-        const int sg = gr.slot;
-        if (!__all_sync(0xffffffffu, mbar_wait(&d_full[sg], gr.phase, 0x25))) {
+      for (int gi = 0; gi * C::CPG < cnt; ++gi, dr.next()) {
+        const int sd = dr.slot;
+        if (!__all_sync(0xffffffffu, mbar_wait(&d_full[sd], dr.phase, 0x25))) {
           ok = false;
           break;
         }
         sg_tc_fence_after();
         const int gc = min(C::CPG, cnt - gi * C::CPG);
         uint32_t scw[4], ddv[1];
-        const uint32_t scc = lane_base + C::sc_col(sg);
+        const uint32_t scc = lane_base + C::sc_col(sd);
 #pragma unroll
         for (int i = 0; i < 4; ++i) sg_tmem_ld_n<1>(scc + (uint32_t)i, *reinterpret_cast<uint32_t(*)[1]>(&scw[i]));
         sg_tmem_ld_n<1>(scc + 4, ddv);
@@ -828,7 +932,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
         for (int a = 0; a < C::NACC; ++a) {
           if (a * C::GC >= gc) break;  // warp-uniform
           uint32_t dv[C::N];
-          tmem_ld_cols<C::N>(lane_base + C::d_col(sg) + (uint32_t)(a * C::N), dv);
+          tmem_ld_cols<C::N>(lane_base + C::d_col(sd) + (uint32_t)(a * C::N), dv);
           sg_tmem_ld_wait();
           if (DT == SG_DTYPE_Q4_K && a == 0) {
             const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddv[0]));
@@ -837,41 +941,52 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(Params p) {
           }
 #pragma unroll
           for (int k = 0; k < C::GC; ++k) {
+            // every position is computed and the dead ones (past the piece:
+            // stale accumulator columns) are dropped by a select
             const int ci = a * C::GC + k;
-            if (ci < gc) {
-              const int cu = ci0 + gi * C::CPG + ci;  // chunk within the unit
-              const uint32_t w = scw[ci];
+            const bool live = ci < gc;
+            const int cu = (ci0 + gi * C::CPG + ci) & 3;  // chunk within the unit
+            const uint32_t w = scw[ci];
 #pragma unroll
-              for (int blk = 0; blk < 2; ++blk) {
-                float sc, of;
-                if (DT == SG_DTYPE_Q4_0) {
-                  sc = __half2float(__ushort_as_half((unsigned short)(w >> (16 * blk))));
-                  of = 0.f;
-                } else {
-                  sc = dmx * (float)((w >> (8 * blk)) & 0xFFu);
-                  of = dmy * (float)((w >> (16 + 8 * blk)) & 0xFFu);
-                }
-                const float* sv = tail + kSumOff / 4 + (cu * 2 + blk) * 16;
-                const int n0 = brow<BT>(k, blk, 0, 0);  // columns of (position k, block, digit, token)
+            for (int blk = 0; blk < 2; ++blk) {
+              float sc, of;
+              if (DT == SG_DTYPE_Q4_0) {
+                sc = __half2float(__ushort_as_half((unsigned short)(w >> (16 * blk))));
+                of = 0.f;
+              } else {
+                sc = dmx * (float)((w >> (8 * blk)) & 0xFFu);
+                of = dmy * (float)((w >> (16 + 8 * blk)) & 0xFFu);
+              }
+              const float* sv = tail + kSumOff / 4 + (cu * 2 + blk) * 16;
+              const int n0 = brow<BT>(k, blk, 0, 0);  // columns of (position k, block, digit, token)
 #pragma unroll
-                for (int t = 0; t < BT; ++t) {
-                  const float dot = digit_dot(dv[n0 + t], dv[n0 + BT + t], dv[n0 + 2 * BT + t]);
-                  if (DT == SG_DTYPE_Q4_0) accu[t] = fmaf(sc, fmaf(-8.f, sv[t], dot), accu[t]);
-                  else accu[t] = fmaf(sc, dot, fmaf(-of, sv[t], accu[t]));
-                }
+              for (int t = 0; t < BT; ++t) {
+                const float dot = digit_dot(dv[n0 + t], dv[n0 + BT + t], dv[n0 + 2 * BT + t]);
+                const float nv = DT == SG_DTYPE_Q4_0 ? fmaf(sc, fmaf(-8.f, sv[t], dot), accu[t])
+                                                     : fmaf(sc, dot, fmaf(-of, sv[t], accu[t]));
+                accu[t] = live ? nv : accu[t];
               }
             }
           }
         }
         sg_tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&d_free[sg]);
+        if (lane == 0) mbar_arrive(&d_free[sd]);
       }
       if (!ok) break;
 #pragma unroll
       for (int t = 0; t < BT; ++t) acc[t] = fmaf(accu[t], tail[kInvOff / 4 + t], acc[t]);
       __syncwarp();
       if (lane == 0) mbar_arrive(&x_empty[xs]);  // this warp is done with the unit's sums and scales
+      xr.next();
+      if (C::NSET == 2 && (cur.c + cnt == p.n_ch || cur.g + cnt == cur.g1)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&seg_full, segs & 1, 0x31))) break;
+#pragma unroll
+        for (int t = 0; t < BT; ++t) acc[t] += seg_acc[row * BT + t];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&seg_empty);
+        ++segs;
+      }
       end_segment<BT>(p, cur, cnt, g0, row, true, acc, held, &zero_own);
     }
     flush_held<BT>(p, held, &zero_ok);
@@ -895,7 +1010,7 @@ cudaError_t launch(Params p, int rb_total, int num_sms, cudaStream_t st) {
   p.total = (int64_t)rb_total * p.n_cp;
   if (p.total >= INT_MAX / 2) return cudaErrorInvalidValue;  // the device cursor counts chunks in 32 bits
   const int64_t slots = p.total / p.spl;
-  const int G = (int)std::max<int64_t>(1, std::min<int64_t>(std::min(num_sms, kMaxCtas), slots));  // one CTA per SM
+  const int G = (int)std::max<int64_t>(1, std::min<int64_t>(std::min(num_sms * C::CPS, kMaxCtas), slots));
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -920,7 +1035,7 @@ cudaError_t launch(Params p, int rb_total, int num_sms, cudaStream_t st) {
   }
   cudaLaunchConfig_t g = {};
   g.gridDim = dim3((unsigned)G);
-  g.blockDim = dim3(kThreads);
+  g.blockDim = dim3(C::THREADS);
   g.dynamicSmemBytes = C::SMEM;
   g.stream = st;
   g.attrs = attr;

@@ -4,7 +4,7 @@
 
 #define SG_GEMV_MAX_MATS 4
 #define SG_GEMV_MAX_BATCH 16
-#define SG_GEMV_MAX_CTAS 256  // CTAs per launch (one per SM)
+#define SG_GEMV_MAX_CTAS 512  // CTAs per launch (one or two per SM)
 
 // One matrix of a (multi-)GEMV call sharing the same activations.
 struct SgGemvMat {
