@@ -322,8 +322,9 @@ __device__ __forceinline__ UnitDigits unit_digits(const float (&v)[8]) {
     m = fmaxf(m, fabsf(v[e]));
     bad |= !(fabsf(v[e]) <= 3.402823466e38f);  // inf or NaN
   }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  // m >= 0 and not NaN (fmaxf drops NaN), so its bits order like its value:
+  // one warp reduction instead of a chain of shuffles
+  m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
   u.bad = __any_sync(0xffffffffu, bad);
   u.se = 0;  // s = 2^se, with 1/s a normal float as well
   if (m > 0.f && !u.bad) {
