@@ -125,10 +125,10 @@ def measured_peaks():
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch, from an ncu
-# capture of the current kernels (None where no capture exists yet):
-# decode GEMV 4096->11008 batch 1 (algorithmic 25,406,976 B); prefill GEMM
-# Q4_K 4096->14336 M=512 (algorithmic weight + activation bytes 41,418,752 B).
-NCU_TRAFFIC = {"gemv_4096x11008_b1": 25_406_976, "gemm_q4k_4096x14336_m512": 43_897_600}
+# capture of the current kernels (profiles/): decode GEMV 4096->11008 batch 1
+# (algorithmic 25,406,976 B); prefill GEMM Q4_K 4096->14336 M=512
+# (algorithmic weight + activation bytes 41,418,752 B).
+NCU_TRAFFIC = {"gemv_4096x11008_b1": 25_442_048, "gemm_q4k_4096x14336_m512": 54_764_032}
 
 
 def measured_tensor_peak():
@@ -331,7 +331,10 @@ def gpu_arm(args):
     xs = {b: torch.randn(b, 11008, device="cuda") for b in BATCHES}
     ys = {b: {name: torch.empty(b, 11008, device="cuda") for name, _, _ in LAYER} for b in BATCHES}
     LD = 11008
-    kernels_per_call = 1  # the GEMV kernel
+    # our kernels per call: the GEMV kernel, plus the activation prep kernel
+    # from 4 tokens on
+    def kernels_per_call(b):
+        return 1 if b <= 2 else 2
 
     def xat(b, name):
         return xs[b].data_ptr() + 4 * col0[name]
@@ -344,10 +347,11 @@ def gpu_arm(args):
         gpu.linear_multi_device([layer["gate"], layer["up"]], xat(b, "gate"), LD,
                                 [y["gate"].data_ptr(), y["up"].data_ptr()], [LD] * 2, b, stream=st)
         gpu.linear_device(layer["down"], xat(b, "down"), LD, y["down"].data_ptr(), LD, b, stream=st)
-        return 4
+        return 4 * kernels_per_call(b)
 
     def step(j):
-        """one step = batches 1, 4, 16 over n_layers layers; copies rotate with j"""
+        """one step = batches 1, 4, 16 over n_layers layers; copies rotate with
+        j. Returns the number of our kernel launches."""
         st = torch.cuda.current_stream().cuda_stream
         calls = 0
         for bi, b in enumerate(BATCHES):
@@ -359,7 +363,7 @@ def gpu_arm(args):
     for j in range(args.warmup):
         step(j)
     torch.cuda.synchronize()
-    calls_per_step = step(0)
+    launches_per_step = step(0)
     torch.cuda.synchronize()
     graphs = [graph_of(torch, lambda j=j: step(j)) for j in range(copies)] if not args.eager else None
     for j in range(args.warmup):
@@ -473,7 +477,8 @@ def gpu_arm(args):
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u4 weights, bf16 hi+lo activations, f32 accumulate",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "u4 weights x s8 activation digits (3 per value), s32 tensor-core accumulate, f32 epilogue",
             "data": "synthetic (seeded random-init Q4_0 blocks, N(0,1) activations)",
             "config": {"workload": "configs[1]: Llama-2-7B layer Q4_0 linears (4x 4096->4096, 2x 4096->11008, "
                                    "11008->4096) at decode batch 1, 4, 16",
@@ -485,12 +490,13 @@ def gpu_arm(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC["gemv_4096x11008_b1"],
                          "traffic_launch": "4096x11008 batch 1 (algorithmic 25,406,976 B)", "peak_kind": peak_kind,
+                         "traffic_note": "ncu dram bytes of one launch of that shape, per launch like achieved",
                          "kernel": "gemv_kernel (one launch per GEMV), back-to-back launches in a CUDA graph",
                          "per_shape_gbs": per_shape},
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clocks,
-            "gpu_launches": calls_per_step * kernels_per_call * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
@@ -553,7 +559,7 @@ def prefill_bench(torch, gpu, oracle, st, args):
                          "frac": round(achieved / burst, 4), "peak_kind": f"{kind} bf16 dense burst",
                          "tensor_pipe_frac": round(3 * achieved / burst, 4),
                          "traffic": NCU_TRAFFIC["gemm_q4k_4096x14336_m512"],
-                         "traffic_launch": "4096x14336 M=512 (weights 33.0 MB + bf16 hi/lo x 8.4 MB)",
+                         "traffic_launch": "4096x14336 M=512 (algorithmic: weights 33.0 MB + bf16 hi/lo x 8.4 MB)",
                          "kernel": "gemm_kernel (tcgen05 M128 N256 K16 bf16, 3 products per k-step) "
                                    "+ gemm_xprep_kernel"},
             "cpu_baseline": cpu,

@@ -43,29 +43,30 @@
 // CTAs confirm the flag (read early, checked at the end of their segment)
 // before their first red.add. With SG_FLAG_ACCUMULATE nothing is zeroed.
 //
-// One kernel per call, one CTA per SM, 12 warps:
-//   warp 0      weight producer: one cp.async.bulk per piece into a 6-slot
-//               ring (issued before the wait on the previous kernel: weights
-//               do not depend on it).
-//   warps 2-5   dequant: one weight row per thread: two 16-byte reads, two
-//               masks per 32-bit word, one tcgen05.st of the chunk's 64 u8
-//               nibbles into the row's TMEM lane (lane = row), and one
-//               tcgen05.st of the group's scale words; then the weight slot
-//               is released, so the ring never waits for the epilogue.
-//   warp 1      TMEM owner; one thread issues tcgen05.mma kind::i8 (A from
-//               TMEM, B = activation tile in shared memory, M=128, K=32,
-//               one instruction per 32-block) into a ring of TMEM groups.
-//   warps 6-9   epilogue: per group, tcgen05.ld of the accumulators and the
-//               scale words of its TMEM lane quadrant (warp % 4), block
-//               scales in f32, output rows stored or reduced.
-//   warps 10-11 activations: per piece, the unit's digits for each live
-//               token (one warp per token at a time) into a 3-slot ring of
-//               block-diagonal tiles; the next unit's x is loaded while
-//               waiting.
-// A TMEM group slot holds a group's A tiles, scale words and accumulators;
-// the dequant warps wait for its epilogue (d_free) before rewriting it, so
-// the MMA thread waits only for a_full. Every mbarrier wait is bounded
-// (sg_common.cuh).
+// One kernel per call (plus gemv_xprep_kernel from 4 tokens on). Roles, all
+// decoupled by mbarrier rings (the exact warp map and ring depths per batch
+// are in Cfg):
+//   weights     warp 0 lane 0: one cp.async.bulk per piece into a ring of
+//               weight slots, issued from CTA entry (weights do not depend on
+//               the previous kernel); spare lanes zero shared output rows.
+//   dequant     warps 2-5, one weight row per thread: two 16-byte reads and
+//               eight masks per 32-block, one tcgen05.st of the chunk's 64 u8
+//               into the row's TMEM lane, and the group's scale words.
+//   MMA         one thread per issuer: tcgen05.mma kind::i8 (M=128, K=32, A
+//               from TMEM, B = activation tile in shared memory), commits to
+//               the accumulator slot and to the A-tile slot.
+//   epilogue    4 warps per set (warp % 4 = TMEM lane quadrant): tcgen05.ld of
+//               the accumulators and scale words, block scales in f32, rows
+//               stored or reduced at segment ends.
+//   activations 1-2 tokens: warps convert x to digit tiles per piece; from 4
+//               tokens: one thread bulk-copies the prepared unit images.
+// One thread issues an MMA about every 50 cycles and every role's loop costs
+// about as much per piece as HBM takes to deliver it to one SM, so the
+// configurations multiply independent pipelines: two CTAs per SM at one
+// token, two MMA issuers and two epilogue sets taking alternate pieces at 2
+// and 4 tokens. TMEM holds two rings: A-tile slots (free once the MMAs that
+// read them complete) and accumulator slots with the scale words (free once
+// the epilogue read them). Every mbarrier wait is bounded (sg_common.cuh).
 #include <algorithm>
 #include <atomic>
 #include <climits>
