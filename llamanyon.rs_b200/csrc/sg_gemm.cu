@@ -28,9 +28,10 @@
 //     warp 1     allocates 512 TMEM columns (two 128 x 256 f32
 //                accumulators); one thread issues tcgen05.mma (M=128, N=256,
 //                K=16, bf16 -> f32) and tcgen05.commit.
-//     warps 2-5  dequantize: one weight row per thread, 32 K per stage,
-//                exact f32 via FMA from the f16 magic-number decode, split
-//                into bf16 hi/lo, 16-byte stores into the swizzled A tiles.
+//     warps 2-5, 10-13  dequantize, two sets taking the two K halves of each
+//                chunk: one weight row per thread, 32 K per stage, exact f32
+//                via FMA from the f16 magic-number decode, split into bf16
+//                hi/lo, 16-byte stores into the swizzled A tiles.
 //     warps 6-9  epilogue: tcgen05.ld of the finished accumulator (while the
 //                MMAs fill the other one), stores -- or red.add for a tile
 //                shared with another CTA.
@@ -51,7 +52,7 @@ constexpr int X_BYTES = BN * BK * 2;  // 16 KB
 constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * X_BYTES;
 constexpr int RAW_BYTES = SG_TILE_BYTES + 512;
 constexpr int SMEM_BYTES = kS * STAGE_BYTES + kR * RAW_BYTES + 1024;  // + alignment slack
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kIdesc = sg_idesc_bf16(BM, BN);
 
@@ -162,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int r = 0; r < kR; ++r) {
       mbar_init(&raw_full[r], 1);
-      mbar_init(&raw_empty[r], 4);
+      mbar_init(&raw_empty[r], 8);  // both dequant sets
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -264,8 +265,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ends with a commit, so the last one covers all (also on the error path)
       if (g > 0) mbar_wait_drain(&s_empty[(g - 1) % kS], ((g - 1) / kS) & 1);
     }
-  } else if (warp < 6) {
+  } else if (warp < 6 || warp >= 10) {
     // ====================================================== dequant warps
+    // two sets of four (warps 2-5 and 10-13); set s converts the K half h == s
+    // of every chunk, so two stages are converted at once
+    const int dset = warp < 6 ? 0 : 1;
     const int row = (warp & 3) * 32 + lane;
     int g = 0, rc = 0;
     bool ok = true;
@@ -276,9 +280,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = rc % kR;
         const uint8_t* rw = raw_ring + r * RAW_BYTES;
         for (int h = 0; h < 2; ++h) {
+          if (h != dset) {
+            ++g;
+            continue;
+          }
           const int s = g % kS;
-          bool w = true;
-          if (h == 0) w = mbar_wait(&raw_full[r], (rc / kR) & 1, 0x15);
+          bool w = mbar_wait(&raw_full[r], (rc / kR) & 1, 0x15);
           if (w && g >= kS) w = mbar_wait(&s_empty[s], ((g / kS) & 1) ^ 1, 0x16);
           if (!__all_sync(0xffffffffu, w)) {
             ok = false;
@@ -327,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) {
             mbar_arrive(&a_full[s]);
-            if (h == 1) mbar_arrive(&raw_empty[r]);
+            mbar_arrive(&raw_empty[r]);
           }
           ++g;
         }
