@@ -428,6 +428,7 @@ def gpu_arm(args):
 
     # ---------------------------------------------- prefill
     prefill = prefill_bench(torch, gpu, oracle, st, args) if world == 1 and not args.no_prefill else None
+    upload = gguf_upload_bench(torch, gpu, oracle) if world == 1 and not args.no_prefill else None
 
     # -------------------------------------------------------------- e2e
     # the public host-pointer C ABI: x copied in and y read back on every call
@@ -498,6 +499,7 @@ def gpu_arm(args):
             "clocks": clocks,
             "gpu_launches": launches_per_step * args.steps,
             "prefill": prefill,
+            "gguf_upload": upload,
         }
         print(json.dumps(line), flush=True)
     graphs = None
@@ -510,6 +512,39 @@ def gpu_arm(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def gguf_upload_bench(torch, gpu, oracle):
+    """The GGUF -> device path (sg_gguf_register): one Q4_K 4096->14336
+    tensor (33 MB of blocks) in a GGUF file under /tmp, mapped (page cache
+    warm) and uploaded with repack; host wall clock around register +
+    synchronize, median of 5."""
+    import tempfile
+    import numpy as np
+    import swamp_gpu as sg
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import gguf_writer
+    k, n = 4096, 14336
+    raw = oracle.gen_weight(Q4K, SEED, 4000, n, k)
+    img, _ = gguf_writer.model_file({"blk.0.ffn_up.weight": (Q4K, n, k, raw)})
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "upload.gguf")
+        with open(path, "wb") as f:
+            f.write(img)
+        g = sg.GgufFile(gpu, path=path)
+        t = g.tensor("blk.0.ffn_up.weight")
+        times = []
+        for _ in range(6):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            w = g.register(t)
+            gpu.synchronize()
+            times.append(time.perf_counter() - t0)
+            w.free()
+        g.close()
+    el = statistics.median(times[1:])
+    return {"value": round(t.nbytes / el / 1e9, 2), "unit": "GB/s", "bytes": t.nbytes,
+            "ms": round(el * 1e3, 3), "tensor": "Q4_K 4096->14336 from a mapped GGUF file (register + repack)"}
 
 
 def prefill_bench(torch, gpu, oracle, st, args):

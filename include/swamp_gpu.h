@@ -26,11 +26,13 @@
  *    zero-fill then accumulate, linear.rs:107,204-207, fused_gemv_q4k.rs:820)
  *    unless SG_FLAG_ACCUMULATE asks for the batched kernel's out += W x
  *    (fused_gemv_q4k.rs:696).
- *  - Numerics: dequantized weights are bit-identical to swamp-gguf's. GEMV /
- *    GEMM outputs accumulate in f32 with activations split into two 16-bit
- *    parts (the prefill GEMM splits the dequantized weights the same way);
- *    the tested bound is |y - y_ref| <= 1e-3 * max(|y_ref|, ||w.*x||_2)
- *    per element against the reference's f32 result.
+ *  - Numerics: dequantized weights are bit-identical to swamp-gguf's. The
+ *    decode GEMV multiplies the raw nibbles by the activations' exact 8-bit
+ *    digits in integer arithmetic and applies the block scales in f32; the
+ *    prefill GEMM accumulates in f32 with weights and activations split into
+ *    bf16 hi + lo parts. The tested bound is
+ *    |y - y_ref| <= 1e-3 * max(|y_ref|, ||w.*x||_2) per element against the
+ *    reference's f32 result.
  *  - Thread safety: calls are serialised on an internal mutex per library
  *    instance; each device has one stream. Calls may come from any host
  *    thread (the reference calls from rayon workers, linear.rs:35).
@@ -61,6 +63,8 @@ extern "C" {
 #define SG_ERR_UNSUPPORTED (-5)
 #define SG_ERR_NOT_INITIALIZED (-6)
 #define SG_ERR_DEVICE_FAULT (-7) /* a kernel's bounded wait gave up; see sg_last_error */
+#define SG_ERR_FORMAT (-8)       /* malformed GGUF file (swamp-gguf GgufError, error.rs) */
+#define SG_ERR_NOT_FOUND (-9)    /* no such GGUF tensor or metadata key */
 
 /* GgmlDType ids (swamp-gguf/src/dtype.rs:13,21) */
 #define SG_DTYPE_Q4_0 2
@@ -76,6 +80,7 @@ extern "C" {
 #define SG_FLAG_ACCUMULATE 0x2  /* out += W x instead of out = W x */
 
 typedef struct sg_weight_s *sg_weight_t;
+typedef struct sg_gguf_s *sg_gguf_t;
 
 /* ------------------------------------------------------------------ setup */
 
@@ -174,6 +179,48 @@ SG_API int sg_fused_gemv_q4k(const uint8_t *w_raw, const float *x, float *out, i
 
 /* Wait for this process's devices and surface any device-side error flag. */
 SG_API int sg_synchronize(void);
+
+/* ------------------------------------------------------------------ GGUF */
+
+/* GGUF reader and upload path, replacing swamp-gguf's GgufFile
+ * (swamp-gguf/src/mmap.rs:26-120, metadata.rs:118-236, tensor_info.rs:8-38).
+ * Host-only: these calls need no GPU and no sg_init, except
+ * sg_gguf_register. The format rules are the reference's: version 1..3;
+ * u32 counts and dimensions in version 1, u64 from 2; strings are a u64
+ * length and bytes decoded as UTF-8 with invalid sequences replaced by
+ * U+FFFD; a repeated metadata key keeps its last value; tensor data starts
+ * at the end of the tensor table rounded up to 32 bytes (general.alignment
+ * is not consulted, mmap.rs:13,78-89). Malformed files give SG_ERR_FORMAT.
+ * Returned strings stay valid until sg_gguf_close. */
+SG_API int sg_gguf_open(const char *path, sg_gguf_t *out);   /* mmap.rs:28-32 GgufFile::open */
+/* parse a file image the caller keeps alive until sg_gguf_close */
+SG_API int sg_gguf_open_memory(const void *data, size_t size, sg_gguf_t *out);
+SG_API int sg_gguf_close(sg_gguf_t g);
+SG_API int sg_gguf_header(sg_gguf_t g, uint32_t *version, int64_t *n_tensors, int64_t *n_kv, int64_t *data_offset,
+                          int64_t *file_size);
+/* first tensor with this name (mmap.rs:95-98 GgufFile::tensor); SG_ERR_NOT_FOUND otherwise */
+SG_API int sg_gguf_find_tensor(sg_gguf_t g, const char *name, int64_t *index);
+/* TensorInfo (tensor_info.rs:8-16): name, ggml type, dims (up to dims_cap of
+ * n_dims written; dims[0] is the contiguous one), absolute file offset and
+ * byte size (tensor_info.rs:24-26) */
+SG_API int sg_gguf_tensor_info(sg_gguf_t g, int64_t index, const char **name, int *dtype, int *n_dims, int64_t *dims,
+                               int dims_cap, int64_t *offset, int64_t *nbytes);
+/* the tensor's raw bytes in the mapped file, range-checked (mmap.rs:111-118) */
+SG_API int sg_gguf_tensor_data(sg_gguf_t g, int64_t index, const void **data, int64_t *nbytes);
+/* metadata: index of a key (its last occurrence), then its type (GGUF value
+ * type 0..12; 9 = array with elem_type and count elements) and values.
+ * Integer and bool types read as int64 (u64 as its bits), f32/f64 as double,
+ * strings as UTF-8 bytes; elem is 0 for a scalar. */
+SG_API int sg_gguf_find_kv(sg_gguf_t g, const char *key, int64_t *index);
+SG_API int sg_gguf_kv_info(sg_gguf_t g, int64_t index, const char **key, int *type, int *elem_type, int64_t *count);
+SG_API int sg_gguf_kv_int(sg_gguf_t g, int64_t index, int64_t elem, int64_t *value);
+SG_API int sg_gguf_kv_float(sg_gguf_t g, int64_t index, int64_t elem, double *value);
+SG_API int sg_gguf_kv_string(sg_gguf_t g, int64_t index, int64_t elem, const char **str, int64_t *len);
+/* Upload a Q4_0/Q4_K matrix of the file (shape[0] = n_cols K, shape[1] =
+ * n_rows N, as swamp-engine reads it, linear.rs:21-22) through
+ * sg_weight_register, straight from the mapped blocks; the handle is
+ * independent of the file afterwards. */
+SG_API int sg_gguf_register(sg_gguf_t g, int64_t index, int tp_mode, sg_weight_t *out);
 
 #ifdef __cplusplus
 }

@@ -86,6 +86,8 @@ struct DevState {
   size_t rbuf_bytes = 0;
   float* hbuf = nullptr;  // pinned host staging
   size_t hbuf_bytes = 0;
+  uint8_t* upbuf[2] = {nullptr, nullptr};  // pinned double buffer of weight uploads
+  cudaEvent_t upev[2] = {nullptr, nullptr};
 };
 
 struct Ctx {
@@ -274,6 +276,10 @@ void release_devices() {
     if (d.ybuf) cudaFree(d.ybuf);
     if (d.rbuf) cudaFree(d.rbuf);
     if (d.hbuf) cudaFreeHost(d.hbuf);
+    for (int i = 0; i < 2; ++i) {
+      if (d.upbuf[i]) cudaFreeHost(d.upbuf[i]);
+      if (d.upev[i]) cudaEventDestroy(d.upev[i]);
+    }
     if (d.stream) cudaStreamDestroy(d.stream);
   }
   g_ctx.devs.clear();
@@ -535,6 +541,46 @@ int sg_topology(int* rank, int* world, int* local_devices) {
   return SG_OK;
 }
 
+// Host blocks (any memory: a mapped GGUF file, pageable buffers) to the
+// device: rows of `lrow` bytes at a stride of `row_bytes` are gathered into
+// two pinned 8 MB buffers in turn, each copied asynchronously while the
+// other is filled, so the copy runs at pinned-memory speed and overlaps the
+// host gather.
+namespace {
+constexpr size_t kUploadChunk = 8u << 20;
+cudaError_t upload_rows(DevState& d, uint8_t* dst, const uint8_t* src, size_t row_bytes, size_t lrow, int64_t nr) {
+  for (int i = 0; i < 2; ++i) {
+    if (!d.upbuf[i]) {
+      cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&d.upbuf[i]), kUploadChunk, cudaHostAllocDefault);
+      if (e != cudaSuccess) return e;
+    }
+    if (!d.upev[i]) {
+      cudaError_t e = cudaEventCreateWithFlags(&d.upev[i], cudaEventDisableTiming);
+      if (e != cudaSuccess) return e;
+    }
+  }
+  if (lrow > kUploadChunk)  // a row wider than the staging buffer: one plain copy
+    return cudaMemcpy2DAsync(dst, lrow, src, row_bytes, lrow, (size_t)nr, cudaMemcpyHostToDevice, d.stream);
+  const int64_t rows_per = (int64_t)(kUploadChunk / lrow);
+  int b = 0;
+  for (int64_t r0 = 0; r0 < nr; r0 += rows_per, b ^= 1) {
+    const int64_t n = std::min(rows_per, nr - r0);
+    cudaError_t e = cudaEventSynchronize(d.upev[b]);  // this buffer's previous copy is done
+    if (e != cudaSuccess) return e;
+    uint8_t* buf = d.upbuf[b];
+    if (row_bytes == lrow) {
+      memcpy(buf, src + (size_t)r0 * row_bytes, (size_t)n * lrow);
+    } else {
+      for (int64_t r = 0; r < n; ++r) memcpy(buf + (size_t)r * lrow, src + (size_t)(r0 + r) * row_bytes, lrow);
+    }
+    e = cudaMemcpyAsync(dst + (size_t)r0 * lrow, buf, (size_t)n * lrow, cudaMemcpyHostToDevice, d.stream);
+    if (e == cudaSuccess) e = cudaEventRecord(d.upev[b], d.stream);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+}  // namespace
+
 int sg_weight_register(const void* host_blocks, int dtype, int64_t n_rows, int64_t n_cols, int tp_mode,
                        sg_weight_t* out) {
   std::lock_guard<std::mutex> lk(g_ctx.mu);
@@ -579,7 +625,7 @@ int sg_weight_register(const void* host_blocks, int dtype, int64_t n_rows, int64
     }
     const uint8_t* src = static_cast<const uint8_t*>(host_blocks) + (size_t)s.row0 * row_bytes +
                          (size_t)(s.col0 / bs) * bb;
-    cudaError_t e = cudaMemcpy2DAsync(raw, lrow, src, row_bytes, lrow, nr, cudaMemcpyHostToDevice, d.stream);
+    cudaError_t e = upload_rows(d, raw, src, row_bytes, lrow, nr);
     if (e == cudaSuccess) e = sg_layout_repack(&s.w, raw, d.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(d.stream);
     cudaFree(raw);

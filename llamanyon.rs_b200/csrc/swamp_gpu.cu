@@ -8,3 +8,4 @@
 #include "sg_gemm.cu"
 #include "sg_api.cu"
 #include "sg_noalloc.cu"
+#include "sg_gguf.cu"

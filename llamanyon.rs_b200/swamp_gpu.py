@@ -35,8 +35,11 @@ EXPORTS = (
     "sg_init", "sg_get_unique_id", "sg_init_rank", "sg_shutdown", "sg_last_error", "sg_topology",
     "sg_weight_register", "sg_weight_free", "sg_tp_shard", "sg_weight_shard", "sg_linear", "sg_linear_multi",
     "sg_linear_device", "sg_linear_multi_device", "sg_linear_device_noalloc", "sg_dequant_f32", "sg_fused_gemv_q4k",
-    "sg_synchronize",
+    "sg_synchronize", "sg_gguf_open", "sg_gguf_open_memory", "sg_gguf_close", "sg_gguf_header",
+    "sg_gguf_find_tensor", "sg_gguf_tensor_info", "sg_gguf_tensor_data", "sg_gguf_find_kv", "sg_gguf_kv_info",
+    "sg_gguf_kv_int", "sg_gguf_kv_float", "sg_gguf_kv_string", "sg_gguf_register",
 )
+SG_ERR_FORMAT, SG_ERR_NOT_FOUND = -8, -9
 
 
 class SwampGpuError(RuntimeError):
@@ -68,6 +71,19 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     L.sg_dequant_f32.argtypes = [P, P, i32]
     L.sg_fused_gemv_q4k.argtypes = [P, P, P, i32, i32]
     L.sg_synchronize.argtypes = []
+    L.sg_gguf_open.argtypes = [ctypes.c_char_p, P]
+    L.sg_gguf_open_memory.argtypes = [P, ctypes.c_size_t, P]
+    L.sg_gguf_close.argtypes = [P]
+    L.sg_gguf_header.argtypes = [P, P, P, P, P, P]
+    L.sg_gguf_find_tensor.argtypes = [P, ctypes.c_char_p, P]
+    L.sg_gguf_tensor_info.argtypes = [P, i64, P, P, P, P, i32, P, P]
+    L.sg_gguf_tensor_data.argtypes = [P, i64, P, P]
+    L.sg_gguf_find_kv.argtypes = [P, ctypes.c_char_p, P]
+    L.sg_gguf_kv_info.argtypes = [P, i64, P, P, P, P]
+    L.sg_gguf_kv_int.argtypes = [P, i64, i64, P]
+    L.sg_gguf_kv_float.argtypes = [P, i64, i64, P]
+    L.sg_gguf_kv_string.argtypes = [P, i64, i64, P, P]
+    L.sg_gguf_register.argtypes = [P, i64, i32, P]
     for name in EXPORTS:
         getattr(L, name).restype = ctypes.c_char_p if name == "sg_last_error" else ctypes.c_int
     return L
@@ -226,6 +242,114 @@ class SwampGpu:
         out = np.empty(n_rows, np.float32)
         self._check(self.L.sg_fused_gemv_q4k(w_raw.ctypes.data, x.ctypes.data, out.ctypes.data, n_rows, n_cols))
         return out
+
+
+# ---------------------------------------------------------------------------
+# swamp-gguf GgufFile (mmap.rs:26-120) over sg_gguf_*
+# ---------------------------------------------------------------------------
+
+@dataclass
+class GgufTensor:
+    """swamp-gguf TensorInfo (tensor_info.rs:10-16) with its index in the
+    file; offset is absolute in the file (mmap.rs:86-89)."""
+    index: int
+    name: str
+    shape: tuple
+    dtype: int
+    offset: int
+    nbytes: int
+
+
+class GgufFile:
+    """A GGUF file parsed by the library (host-only: no GPU or init needed,
+    except for ``register``). Errors raise SwampGpuError (SG_ERR_FORMAT for a
+    malformed file, SG_ERR_NOT_FOUND for a missing name or key)."""
+
+    def __init__(self, gpu: "SwampGpu | ctypes.CDLL", path: str | None = None, data: bytes | None = None):
+        self.L = gpu.L if isinstance(gpu, SwampGpu) else gpu
+        self._gpu = gpu if isinstance(gpu, SwampGpu) else None
+        self._data = data  # kept alive while the handle exists
+        h = ctypes.c_void_p()
+        if path is not None:
+            rc = self.L.sg_gguf_open(os.fsencode(path), ctypes.byref(h))
+        else:
+            self._buf = ctypes.create_string_buffer(bytes(data), len(data)) if data else None
+            rc = self.L.sg_gguf_open_memory(self._buf, len(data) if data else 0, ctypes.byref(h))
+        self._check(rc)
+        self.handle = h.value
+        v, nt, nk, do, fs = (ctypes.c_uint32(), ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64())
+        self._check(self.L.sg_gguf_header(self.handle, *[ctypes.byref(a) for a in (v, nt, nk, do, fs)]))
+        self.version, self.data_offset, self.file_size = v.value, do.value, fs.value
+        self.tensors = [self._tensor(i) for i in range(nt.value)]
+        self.n_kv = nk.value
+
+    def _check(self, rc: int):
+        if rc != SG_OK:
+            raise SwampGpuError(rc, self.L.sg_last_error().decode(errors="replace"))
+
+    def _tensor(self, i: int) -> GgufTensor:
+        name, dt, nd, off, nb = ctypes.c_char_p(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64()
+        dims = (ctypes.c_int64 * 64)()
+        self._check(self.L.sg_gguf_tensor_info(self.handle, i, ctypes.byref(name), ctypes.byref(dt), ctypes.byref(nd),
+                                               dims, 64, ctypes.byref(off), ctypes.byref(nb)))
+        shape = tuple(int(dims[d]) & 0xFFFFFFFFFFFFFFFF for d in range(min(nd.value, 64)))
+        return GgufTensor(i, name.value.decode(), shape, dt.value, off.value & 0xFFFFFFFFFFFFFFFF,
+                          nb.value & 0xFFFFFFFFFFFFFFFF)
+
+    def close(self):
+        if self.handle:
+            self._check(self.L.sg_gguf_close(self.handle))
+            self.handle = None
+
+    def tensor(self, name: str) -> GgufTensor:
+        """GgufFile::tensor_or_err (mmap.rs:100-104)."""
+        i = ctypes.c_int64()
+        self._check(self.L.sg_gguf_find_tensor(self.handle, name.encode(), ctypes.byref(i)))
+        return self.tensors[i.value]
+
+    def tensor_raw_bytes(self, t: GgufTensor) -> bytes:
+        """GgufFile::tensor_raw_bytes (mmap.rs:111-118)."""
+        p, n = ctypes.c_void_p(), ctypes.c_int64()
+        self._check(self.L.sg_gguf_tensor_data(self.handle, t.index, ctypes.byref(p), ctypes.byref(n)))
+        return ctypes.string_at(p.value, n.value) if n.value else b""
+
+    def kv(self, key: str):
+        """Metadata value of key (the last occurrence): int, float, str, bool
+        or a list of them for an array."""
+        i = ctypes.c_int64()
+        self._check(self.L.sg_gguf_find_kv(self.handle, key.encode(), ctypes.byref(i)))
+        return self.kv_at(i.value)[1]
+
+    def kv_at(self, index: int):
+        key, t, et, cnt = ctypes.c_char_p(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int64()
+        self._check(self.L.sg_gguf_kv_info(self.handle, index, ctypes.byref(key), ctypes.byref(t), ctypes.byref(et),
+                                           ctypes.byref(cnt)))
+        et_ = et.value if t.value == 9 else t.value
+        vals = [self._elem(index, e, et_) for e in range(cnt.value)]
+        return key.value.decode(), (vals if t.value == 9 else vals[0]), t.value, et.value
+
+    def _elem(self, index: int, e: int, t: int):
+        if t in (6, 12):
+            v = ctypes.c_double()
+            self._check(self.L.sg_gguf_kv_float(self.handle, index, e, ctypes.byref(v)))
+            return v.value
+        if t == 8:
+            p, n = ctypes.c_char_p(), ctypes.c_int64()
+            self._check(self.L.sg_gguf_kv_string(self.handle, index, e, ctypes.byref(p), ctypes.byref(n)))
+            return ctypes.string_at(p, n.value).decode()
+        v = ctypes.c_int64()
+        self._check(self.L.sg_gguf_kv_int(self.handle, index, e, ctypes.byref(v)))
+        if t == 7:
+            return bool(v.value)
+        return v.value & 0xFFFFFFFFFFFFFFFF if t == 10 else v.value
+
+    def register(self, t: GgufTensor, tp_mode: int = SG_TP_REPLICATE) -> Weight:
+        """Upload a Q4_0/Q4_K matrix straight from the mapped file."""
+        if self._gpu is None:
+            raise SwampGpuError(-6, "register needs an initialised SwampGpu")
+        h = ctypes.c_void_p()
+        self._check(self.L.sg_gguf_register(self.handle, t.index, tp_mode, ctypes.byref(h)))
+        return Weight(self._gpu, h.value, t.dtype, t.shape[1], t.shape[0], tp_mode)
 
 
 # ---------------------------------------------------------------------------
