@@ -181,6 +181,10 @@ struct Cfg {
   static_assert(XU % 1024 == 0, "operand tiles keep 1024-byte alignment");
   static_assert(SMEM_USED <= (DUAL ? 110 : 227) * 1024, "shared memory budget");
   static_assert(NSET == 1 || (CPG == kUC && BT <= 4), "two lanes need one group per piece");
+  // epilogue TMEM loads: LC columns at a time, whole (position, block) column
+  // groups of 3 x BT each (fewer live registers at 8 and 16 tokens)
+  static constexpr int LC = N < 48 ? N : 48;
+  static_assert(LC % 16 == 0 && (LC % (3 * BT) == 0 || 2 * GC * 3 * BT <= LC), "epilogue load split");
   static_assert(XPRE || (BT <= 2 && XL * XPP == NXW && RX % XL == 0), "activation lanes");
 };
 
@@ -933,41 +937,43 @@ __global__ void __launch_bounds__(Cfg<BT>::THREADS) __maxnreg__(Cfg<BT>::MAXREG)
 #pragma unroll
         for (int a = 0; a < C::NACC; ++a) {
           if (a * C::GC >= gc) break;  // warp-uniform
-          uint32_t dv[C::N];
-          tmem_ld_cols<C::N>(lane_base + C::d_col(sd) + (uint32_t)(a * C::N), dv);
-          sg_tmem_ld_wait();
-          if (DT == SG_DTYPE_Q4_K && a == 0) {
-            const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddv[0]));
-            dmx = dm.x;
-            dmy = dm.y;
-          }
+          const uint32_t abase = lane_base + C::d_col(sd) + (uint32_t)(a * C::N);
+          uint32_t dv[C::LC];
 #pragma unroll
-          for (int k = 0; k < C::GC; ++k) {
+          for (int kb = 0; kb < 2 * C::GC; ++kb) {
+            // (position k, block blk): columns brow(k, blk, d, t) = kb*3*BT + d*BT + t
+            const int k = kb >> 1, blk = kb & 1, col = kb * 3 * BT;
+            if (col % C::LC == 0) {
+              tmem_ld_cols<C::LC>(abase + (uint32_t)col, dv);
+              sg_tmem_ld_wait();
+            }
+            if (DT == SG_DTYPE_Q4_K && a == 0 && kb == 0) {
+              const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddv[0]));
+              dmx = dm.x;
+              dmy = dm.y;
+            }
             // every position is computed and the dead ones (past the piece:
             // stale accumulator columns) are dropped by a select
             const int ci = a * C::GC + k;
             const bool live = ci < gc;
             const int cu = (ci0 + gi * C::CPG + ci) & 3;  // chunk within the unit
             const uint32_t w = scw[ci];
+            float sc, of;
+            if (DT == SG_DTYPE_Q4_0) {
+              sc = __half2float(__ushort_as_half((unsigned short)(w >> (16 * blk))));
+              of = 0.f;
+            } else {
+              sc = dmx * (float)((w >> (8 * blk)) & 0xFFu);
+              of = dmy * (float)((w >> (16 + 8 * blk)) & 0xFFu);
+            }
+            const float* sv = tail + kSumOff / 4 + (cu * 2 + blk) * 16;
+            const int c0 = col % C::LC;
 #pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-              float sc, of;
-              if (DT == SG_DTYPE_Q4_0) {
-                sc = __half2float(__ushort_as_half((unsigned short)(w >> (16 * blk))));
-                of = 0.f;
-              } else {
-                sc = dmx * (float)((w >> (8 * blk)) & 0xFFu);
-                of = dmy * (float)((w >> (16 + 8 * blk)) & 0xFFu);
-              }
-              const float* sv = tail + kSumOff / 4 + (cu * 2 + blk) * 16;
-              const int n0 = brow<BT>(k, blk, 0, 0);  // columns of (position k, block, digit, token)
-#pragma unroll
-              for (int t = 0; t < BT; ++t) {
-                const float dot = digit_dot(dv[n0 + t], dv[n0 + BT + t], dv[n0 + 2 * BT + t]);
-                const float nv = DT == SG_DTYPE_Q4_0 ? fmaf(sc, fmaf(-8.f, sv[t], dot), accu[t])
-                                                     : fmaf(sc, dot, fmaf(-of, sv[t], accu[t]));
-                accu[t] = live ? nv : accu[t];
-              }
+            for (int t = 0; t < BT; ++t) {
+              const float dot = digit_dot(dv[c0 + t], dv[c0 + BT + t], dv[c0 + 2 * BT + t]);
+              const float nv = DT == SG_DTYPE_Q4_0 ? fmaf(sc, fmaf(-8.f, sv[t], dot), accu[t])
+                                                   : fmaf(sc, dot, fmaf(-of, sv[t], accu[t]));
+              accu[t] = live ? nv : accu[t];
             }
           }
         }
