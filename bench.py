@@ -429,6 +429,7 @@ def gpu_arm(args):
     # ---------------------------------------------- prefill
     prefill = prefill_bench(torch, gpu, oracle, st, args) if world == 1 and not args.no_prefill else None
     upload = gguf_upload_bench(torch, gpu, oracle) if world == 1 and not args.no_prefill else None
+    q6k = q6k_bench(torch, gpu, oracle, st) if world == 1 and not args.no_prefill else None
 
     # -------------------------------------------------------------- e2e
     # the public host-pointer C ABI: x copied in and y read back on every call
@@ -500,6 +501,7 @@ def gpu_arm(args):
             "gpu_launches": launches_per_step * args.steps,
             "prefill": prefill,
             "gguf_upload": upload,
+            "q6k": q6k,
         }
         print(json.dumps(line), flush=True)
     graphs = None
@@ -512,6 +514,42 @@ def gpu_arm(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def q6k_bench(torch, gpu, oracle, st):
+    """Q6_K, the dtype real Q4_K_M files keep for ffn_down and the output
+    head (Llama-3-8B shapes): decode GEMV GB/s at 1 and 16 tokens
+    (algorithmic bytes N*K*210/256 + activations) and prefill GEMM TFLOP/s at
+    M=512. Two rotating copies per shape (> L2), CUDA graphs of back-to-back
+    calls, device time per call."""
+    out = {}
+    Q6K = 14
+    for (k, n) in ((14336, 4096), (4096, 128256)):
+        ws = [gpu.register(oracle.gen_weight(Q6K, SEED, 5000 + c, n, k), Q6K, n, k) for c in range(2)]
+        for b in ((1, 16) if n < 100000 else (1,)) + ((PREFILL_M,) if n < 100000 else ()):
+            x = torch.randn(b, k, device="cuda")
+            y = torch.empty(b, n, device="cuda")
+
+            def one(b=b, x=x, y=y):
+                stp = torch.cuda.current_stream().cuda_stream
+                for w in ws:
+                    gpu.linear_device(w, x.data_ptr(), k, y.data_ptr(), n, b, stream=stp)
+            one()
+            g = graph_of(torch, one)
+            g.replay()
+            reps = 10
+            us = time_graphs(torch, [g], reps, st) * 1e3 / (reps * len(ws))
+            key = f"{k}x{n}_b{b}"
+            if b <= 16:
+                by = n * k * 210 // 256 + b * (k + n) * 4
+                out[key] = {"us": round(us, 2), "gbs": round(by / us / 1e3, 1)}
+            else:
+                out[key] = {"us": round(us, 2), "tflops": round(2 * b * n * k / us / 1e6, 1)}
+            del g
+        for w in ws:
+            w.free()
+    return {"kernels": "gemv_q6k_kernel (CUDA cores) at <= 16 tokens; gemm_kernel (tcgen05) above",
+            "per_shape": out}
 
 
 def gguf_upload_bench(torch, gpu, oracle):

@@ -69,6 +69,7 @@ extern "C" {
 /* GgmlDType ids (swamp-gguf/src/dtype.rs:13,21) */
 #define SG_DTYPE_Q4_0 2
 #define SG_DTYPE_Q4_K 12
+#define SG_DTYPE_Q6_K 14 /* swamp-gguf/src/quant/q6_k.rs: 210 B per 256 */
 
 /* tensor-parallel placement of a registered weight */
 #define SG_TP_REPLICATE 0 /* every rank holds the whole tensor */

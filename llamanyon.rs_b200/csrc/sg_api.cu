@@ -136,7 +136,7 @@ struct sg_weight_s {
 namespace {
 
 int64_t block_of(int dtype) { return dtype == SG_DTYPE_Q4_0 ? 32 : 256; }
-int64_t block_bytes(int dtype) { return dtype == SG_DTYPE_Q4_0 ? 18 : 144; }
+int64_t block_bytes(int dtype) { return dtype == SG_DTYPE_Q4_0 ? 18 : dtype == SG_DTYPE_Q4_K ? 144 : 210; }
 
 // The slice of an n_rows x n_cols tensor that rank R of W holds: column split
 // (SG_TP_COLUMN) takes rows [R*N/W, (R+1)*N/W); row split (SG_TP_ROW) takes
@@ -144,8 +144,8 @@ int64_t block_bytes(int dtype) { return dtype == SG_DTYPE_Q4_0 ? 18 : 144; }
 // Returns SG_OK or SG_ERR_INVALID_ARG / SG_ERR_UNSUPPORTED with a message.
 int shard_plan(int dtype, int64_t n_rows, int64_t n_cols, int tp_mode, int W, int R, int64_t* row0, int64_t* nr,
                int64_t* col0, int64_t* nc) {
-  if (dtype != SG_DTYPE_Q4_0 && dtype != SG_DTYPE_Q4_K)
-    return fail(SG_ERR_UNSUPPORTED, "dtype %d not supported (Q4_0=2, Q4_K=12)", dtype);
+  if (dtype != SG_DTYPE_Q4_0 && dtype != SG_DTYPE_Q4_K && dtype != SG_DTYPE_Q6_K)
+    return fail(SG_ERR_UNSUPPORTED, "dtype %d not supported (Q4_0=2, Q4_K=12, Q6_K=14)", dtype);
   if (n_rows <= 0 || n_cols <= 0)
     return fail(SG_ERR_INVALID_ARG, "empty tensor %lld x %lld", (long long)n_rows, (long long)n_cols);
   const int64_t bs = block_of(dtype);
@@ -314,8 +314,14 @@ int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* 
       gws = d.gemv_ws;
       gws_bytes = d.gemv_ws_bytes;
     }
-    // one launch per run of consecutive same-dtype matrices
+    // one launch per run of consecutive same-dtype matrices (Q6_K: one per
+    // matrix, on its own kernel)
     for (int i0 = 0; i0 < n_w;) {
+      if (ws[i0]->dtype == SG_DTYPE_Q6_K) {
+        CUDA_TRY(sg_gemv_q6k(ws[i0], x, ldx, ys[i0], ldys[i0], batch, accumulate, d.num_sms, st));
+        ++i0;
+        continue;
+      }
       int i1 = i0 + 1;
       while (i1 < n_w && i1 - i0 < SG_GEMV_MAX_MATS && ws[i1]->dtype == ws[i0]->dtype) ++i1;
       SgGemvMat mats[SG_GEMV_MAX_MATS];

@@ -15,6 +15,7 @@
 
 #define SG_DTYPE_Q4_0 2
 #define SG_DTYPE_Q4_K 12
+#define SG_DTYPE_Q6_K 14
 
 // Device layout geometry (see sg_layout.cuh).
 #define SG_RB_ROWS 128   // rows per row-block

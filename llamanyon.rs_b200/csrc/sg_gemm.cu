@@ -50,7 +50,7 @@ constexpr int kR = 3;  // raw weight chunk ring
 constexpr int A_BYTES = BM * BK * 2;  // 8 KB
 constexpr int X_BYTES = BN * BK * 2;  // 16 KB
 constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * X_BYTES;
-constexpr int RAW_BYTES = SG_TILE_BYTES + 512;
+constexpr int RAW_BYTES = SG_TILE6_BYTES + 512;  // the largest tile (Q6_K) + its d / d|dmin words
 constexpr int SMEM_BYTES = kS * STAGE_BYTES + kR * RAW_BYTES + 1024;  // + alignment slack
 constexpr int kThreads = 448;
 constexpr uint32_t kTmemCols = 512;
@@ -195,10 +195,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* rw = raw_ring + r * RAW_BYTES;
-          mbar_arrive_expect_tx(&raw_full[r], SG_TILE_BYTES + (p.dtype == SG_DTYPE_Q4_K ? 512 : 0));
-          bulk_g2s(rw, p.tiles + ((int64_t)rb * p.n_ch + ch) * SG_TILE_BYTES, SG_TILE_BYTES, &raw_full[r]);
-          if (p.dtype == SG_DTYPE_Q4_K)
-            bulk_g2s(rw + SG_TILE_BYTES, p.dd + ((int64_t)rb * p.n_sb + (ch >> 2)) * 128, 512, &raw_full[r]);
+          const int tb = sg_tile_bytes(p.dtype);
+          const bool has_dd = p.dtype != SG_DTYPE_Q4_0;
+          mbar_arrive_expect_tx(&raw_full[r], tb + (has_dd ? 512 : 0));
+          bulk_g2s(rw, p.tiles + ((int64_t)rb * p.n_ch + ch) * tb, tb, &raw_full[r]);
+          if (has_dd)
+            bulk_g2s(rw + tb, p.dd + ((int64_t)rb * p.n_sb + (ch >> 2)) * 128, 512, &raw_full[r]);
           ++rc;
           for (int h = 0; h < 2; ++h) {
             const int s = g % kS;
@@ -292,43 +294,79 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint4 nv = *reinterpret_cast<const uint4*>(rw + h * 2048 + row * 16);
-          const uint32_t scw = *reinterpret_cast<const uint32_t*>(rw + SG_TILE_SC_OFF + row * 4);
-          float sv, mv;  // w = sv*q - mv
-          if (p.dtype == SG_DTYPE_Q4_0) {
-            sv = __half2float(__ushort_as_half((unsigned short)(h ? (scw >> 16) : (scw & 0xFFFFu))));
-            mv = 8.f * sv;
-          } else {
-            const uint32_t ddw = *reinterpret_cast<const uint32_t*>(rw + SG_TILE_BYTES + row * 4);
-            const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddw));
-            sv = __fmul_rn(dm.x, (float)((scw >> (8 * h)) & 0xFFu));
-            mv = __fmul_rn(dm.y, (float)((scw >> (16 + 8 * h)) & 0xFFu));
-          }
-          // f = 1024+q (k%8 in {0,1,4,5}) or 1024+16q ({2,3,6,7}):
-          //   w = f*sv - (1024 sv + mv)   or   w = f*(sv/16) - (64 sv + mv)
-          const float mulA = sv, addA = -__fadd_rn(1024.f * sv, mv);
-          const float mulB = sv * 0.0625f, addB = -__fadd_rn(64.f * sv, mv);
           uint8_t* a_hi = smem + s * STAGE_BYTES;
           uint8_t* a_lo = a_hi + A_BYTES;
-          const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
+          if (p.dtype == SG_DTYPE_Q6_K) {
+            // w = (d * sc) * (q - 32), both products exact (q6_k.rs:37-46);
+            // q = low nibble | high 2 bits << 4, set side by side by masks
+            const uint2 hq = *reinterpret_cast<const uint2*>(rw + SG_TILE6_HI_OFF + (h * 128 + row) * 8);
+            const uint32_t scw6 = *reinterpret_cast<const uint32_t*>(rw + SG_TILE6_SC_OFF + row * 4);
+            const float d6 = __half2float(
+                __ushort_as_half((unsigned short)(*reinterpret_cast<const uint32_t*>(rw + SG_TILE6_BYTES + row * 4) & 0xFFFFu)));
+            const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 f16 = sg_decode_word_f16(nw[j]);
-            const uint32_t fp[4] = {f16.x, f16.y, f16.z, f16.w};
-            uint32_t hi[4], lo[4];
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t H = j < 2 ? hq.x : hq.y;
+              const uint32_t qa = (nw[j] & 0x0F0F0F0Fu) | (((j & 1) ? H : (H << 4)) & 0x30303030u);
+              const uint32_t qb = ((nw[j] >> 4) & 0x0F0F0F0Fu) | (((j & 1) ? (H >> 2) : (H << 2)) & 0x30303030u);
+              // K order 0..7: bytes (qa0, qa2, qb0, qb2, qa1, qa3, qb1, qb3)
+              const uint32_t sel[8] = {0x7650u, 0x7652u, 0x7650u, 0x7652u, 0x7651u, 0x7653u, 0x7651u, 0x7653u};
+              float qv[8];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&fp[e]));
-              const float mul = (e & 1) ? mulB : mulA, add = (e & 1) ? addB : addA;
-              const float w0 = fmaf(f.x, mul, add), w1 = fmaf(f.y, mul, add);
-              const uint32_t u0 = __float_as_uint(w0), u1 = __float_as_uint(w1);
-              hi[e] = __byte_perm(u0, u1, 0x7632);  // truncated bf16 pair (top halves)
-              const __nv_bfloat162 l = __floats2bfloat162_rn(w0 - __uint_as_float(u0 & 0xFFFF0000u),
-                                                             w1 - __uint_as_float(u1 & 0xFFFF0000u));
-              lo[e] = *reinterpret_cast<const uint32_t*>(&l);
+              for (int e = 0; e < 8; ++e)
+                qv[e] = __uint_as_float(__byte_perm((e & 2) ? qb : qa, 0x4B000000u, sel[e])) - 8388640.f;
+              const float sw = __fmul_rn(d6, (float)(int8_t)(scw6 >> (8 * (2 * h + (j >> 1)))));
+              uint32_t hi[4], lo[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float w0 = __fmul_rn(sw, qv[2 * e]), w1 = __fmul_rn(sw, qv[2 * e + 1]);
+                const uint32_t u0 = __float_as_uint(w0), u1 = __float_as_uint(w1);
+                hi[e] = __byte_perm(u0, u1, 0x7632);
+                const __nv_bfloat162 l = __floats2bfloat162_rn(w0 - __uint_as_float(u0 & 0xFFFF0000u),
+                                                               w1 - __uint_as_float(u1 & 0xFFFF0000u));
+                lo[e] = *reinterpret_cast<const uint32_t*>(&l);
+              }
+              const uint32_t off = sw64_chunk(row, j);
+              *reinterpret_cast<uint4*>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+              *reinterpret_cast<uint4*>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
-            const uint32_t off = sw64_chunk(row, j);
-            *reinterpret_cast<uint4*>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4*>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          } else {
+            const uint32_t scw = *reinterpret_cast<const uint32_t*>(rw + SG_TILE_SC_OFF + row * 4);
+            float sv, mv;  // w = sv*q - mv
+            if (p.dtype == SG_DTYPE_Q4_0) {
+              sv = __half2float(__ushort_as_half((unsigned short)(h ? (scw >> 16) : (scw & 0xFFFFu))));
+              mv = 8.f * sv;
+            } else {
+              const uint32_t ddw = *reinterpret_cast<const uint32_t*>(rw + SG_TILE_BYTES + row * 4);
+              const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&ddw));
+              sv = __fmul_rn(dm.x, (float)((scw >> (8 * h)) & 0xFFu));
+              mv = __fmul_rn(dm.y, (float)((scw >> (16 + 8 * h)) & 0xFFu));
+            }
+            // f = 1024+q (k%8 in {0,1,4,5}) or 1024+16q ({2,3,6,7}):
+            //   w = f*sv - (1024 sv + mv)   or   w = f*(sv/16) - (64 sv + mv)
+            const float mulA = sv, addA = -__fadd_rn(1024.f * sv, mv);
+            const float mulB = sv * 0.0625f, addB = -__fadd_rn(64.f * sv, mv);
+            const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
+  #pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 f16 = sg_decode_word_f16(nw[j]);
+              const uint32_t fp[4] = {f16.x, f16.y, f16.z, f16.w};
+              uint32_t hi[4], lo[4];
+  #pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&fp[e]));
+                const float mul = (e & 1) ? mulB : mulA, add = (e & 1) ? addB : addA;
+                const float w0 = fmaf(f.x, mul, add), w1 = fmaf(f.y, mul, add);
+                const uint32_t u0 = __float_as_uint(w0), u1 = __float_as_uint(w1);
+                hi[e] = __byte_perm(u0, u1, 0x7632);  // truncated bf16 pair (top halves)
+                const __nv_bfloat162 l = __floats2bfloat162_rn(w0 - __uint_as_float(u0 & 0xFFFF0000u),
+                                                               w1 - __uint_as_float(u1 & 0xFFFF0000u));
+                lo[e] = *reinterpret_cast<const uint32_t*>(&l);
+              }
+              const uint32_t off = sw64_chunk(row, j);
+              *reinterpret_cast<uint4*>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+              *reinterpret_cast<uint4*>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
           }
           fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
           __syncwarp();

@@ -405,8 +405,9 @@ int sg_gguf_register(sg_gguf_t g, int64_t index, int tp_mode, sg_weight_t* out) 
   if (!out) return fail(SG_ERR_INVALID_ARG, "null pointer");
   if (index < 0 || index >= (int64_t)g->tensors.size()) return fail(SG_ERR_INVALID_ARG, "gguf: tensor index %lld", (long long)index);
   const SgTensorInfo& t = g->tensors[(size_t)index];
-  if (t.dtype != SG_DTYPE_Q4_0 && t.dtype != SG_DTYPE_Q4_K)
-    return fail(SG_ERR_UNSUPPORTED, "gguf: %s has type %d; the device path takes Q4_0 (2) and Q4_K (12)", t.name.c_str(), t.dtype);
+  if (t.dtype != SG_DTYPE_Q4_0 && t.dtype != SG_DTYPE_Q4_K && t.dtype != SG_DTYPE_Q6_K)
+    return fail(SG_ERR_UNSUPPORTED, "gguf: %s has type %d; the device path takes Q4_0 (2), Q4_K (12) and Q6_K (14)",
+                t.name.c_str(), t.dtype);
   // a linear weight: shape[0] = n_cols (K, contiguous), shape[1] = n_rows (N);
   // trailing dimensions of 1 are allowed
   if (t.dims.size() < 2) return fail(SG_ERR_UNSUPPORTED, "gguf: %s is not a matrix", t.name.c_str());

@@ -18,6 +18,12 @@ __device__ __forceinline__ uint32_t raw_nibble(int dtype, const uint8_t* raw, in
     const int i = (int)(k & 31);
     const uint8_t byte = raw[(row * nb + b) * 18 + 2 + (i >> 1)];  // q4_0.rs:31
     return (i & 1) ? (byte >> 4) : (byte & 15u);                    // q4_0.rs:32
+  } else if (dtype == SG_DTYPE_Q6_K) {
+    // the low 4 bits of q (q6_k.rs:33-36): element 128h + 32m + l of a block
+    const int64_t nsb = n_cols / 256;
+    const int e = (int)(k & 255), h = e >> 7, m = (e >> 5) & 3, l = e & 31;
+    const uint8_t byte = raw[(row * nsb + (k >> 8)) * 210 + 64 * h + l + 32 * (m & 1)];
+    return (byte >> (4 * (m >> 1))) & 15u;
   } else {
     const int64_t nsb = n_cols / 256;
     const int64_t sb = k >> 8;
@@ -49,8 +55,32 @@ __global__ void repack_qs_kernel(int dtype, const uint8_t* __restrict__ raw, int
     }
     words[w] = v;
   }
-  *reinterpret_cast<uint4*>(tiles + tile * SG_TILE_BYTES + (h * 128 + r) * 16) =
+  *reinterpret_cast<uint4*>(tiles + tile * sg_tile_bytes(dtype) + (h * 128 + r) * 16) =
       make_uint4(words[0], words[1], words[2], words[3]);
+}
+
+// Q6_K high 2-bit plane: one thread per (tile, half, row), two words
+__global__ void repack_q6_hi_kernel(const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols, int64_t n_rb,
+                                    int64_t n_ch, uint8_t* __restrict__ tiles) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = n_rb * n_ch * 256;
+  if (tid >= total) return;
+  const int r = (int)(tid & 127), h = (int)((tid >> 7) & 1);
+  const int64_t tile = tid >> 8, rb = tile / n_ch, c = tile % n_ch;
+  const int64_t row = rb * 128 + r;
+  uint32_t words[2] = {0u, 0u};
+  if (row < n_rows) {
+    const int64_t nsb = n_cols / 256;
+#pragma unroll 4
+    for (int i = 0; i < 32; ++i) {
+      const int kk = 32 * h + i;
+      const int64_t k = c * 64 + kk;
+      const int e = (int)(k & 255), hb = e >> 7, m = (e >> 5) & 3, l = e & 31;
+      const uint8_t qh = raw[(row * nsb + (k >> 8)) * 210 + 128 + 32 * hb + l];  // q6_k.rs:33-36
+      words[sg_q6_hi_word(kk)] |= (uint32_t)((qh >> (2 * m)) & 3u) << sg_q6_hi_bit(kk);
+    }
+  }
+  reinterpret_cast<uint2*>(tiles + tile * SG_TILE6_BYTES + SG_TILE6_HI_OFF)[h * 128 + r] = make_uint2(words[0], words[1]);
 }
 
 // unpack_scales (swamp-gguf/src/quant/q4_k.rs:37-53)
@@ -74,7 +104,12 @@ __global__ void repack_scales_kernel(int dtype, const uint8_t* __restrict__ raw,
   const int64_t tile = tid >> 7, rb = tile / n_ch, c = tile % n_ch;
   const int64_t row = rb * 128 + r;
   uint32_t out = 0;
-  if (row < n_rows) {
+  if (row < n_rows && dtype == SG_DTYPE_Q6_K) {
+    // the int8 scales of the chunk's four 16-element sub-blocks (q6_k.rs:37-46:
+    // element e of a block uses sc[e / 16])
+    const uint8_t* blk = raw + (row * (n_cols / 256) + (c >> 2)) * 210 + 192 + 4 * (c & 3);
+    out = (uint32_t)blk[0] | ((uint32_t)blk[1] << 8) | ((uint32_t)blk[2] << 16) | ((uint32_t)blk[3] << 24);
+  } else if (row < n_rows) {
     if (dtype == SG_DTYPE_Q4_0) {
       const int64_t nb = n_cols / 32;
 #pragma unroll
@@ -95,12 +130,13 @@ __global__ void repack_scales_kernel(int dtype, const uint8_t* __restrict__ raw,
       out = sa | (sb << 8) | (ma << 16) | (mb << 24);
     }
   }
-  reinterpret_cast<uint32_t*>(tiles + tile * SG_TILE_BYTES + SG_TILE_SC_OFF)[r] = out;
+  if (dtype == SG_DTYPE_Q6_K) reinterpret_cast<uint32_t*>(tiles + tile * SG_TILE6_BYTES + SG_TILE6_SC_OFF)[r] = out;
+  else reinterpret_cast<uint32_t*>(tiles + tile * SG_TILE_BYTES + SG_TILE_SC_OFF)[r] = out;
 }
 
-// Q4_K dd: one thread per (rb, superblock, row).
+// Q4_K d|dmin, Q6_K d: one thread per (rb, superblock, row); bytes = block bytes.
 __global__ void repack_q4k_dd_kernel(const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_cols,
-                                     int64_t n_rb, int64_t n_sb, uint32_t* __restrict__ dd) {
+                                     int64_t n_rb, int64_t n_sb, uint32_t* __restrict__ dd, int bytes) {
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = n_rb * n_sb * 128;
   if (tid >= total) return;
@@ -108,9 +144,12 @@ __global__ void repack_q4k_dd_kernel(const uint8_t* __restrict__ raw, int64_t n_
   const int64_t tile = tid >> 7, rb = tile / n_sb, sb = tile % n_sb;
   const int64_t row = rb * 128 + r;
   uint32_t out = 0;
-  if (row < n_rows) {
+  if (row < n_rows && bytes == 144) {
     const uint8_t* blk = raw + (row * n_sb + sb) * 144;  // q4_k.rs:281-282
     out = (uint32_t)blk[0] | ((uint32_t)blk[1] << 8) | ((uint32_t)blk[2] << 16) | ((uint32_t)blk[3] << 24);
+  } else if (row < n_rows) {
+    const uint8_t* blk = raw + (row * n_sb + sb) * 210;  // q6_k.rs:28: d at 208
+    out = (uint32_t)blk[208] | ((uint32_t)blk[209] << 8);
   }
   dd[tid] = out;
 }
@@ -126,9 +165,28 @@ __global__ void dequant_kernel(SgDevWeight w, float* __restrict__ dst, int64_t l
   const int r = (int)(row & 127);
   const int64_t c = k0 >> 6;
   const int kk0 = (int)(k0 & 63);
-  const uint8_t* tile = w.tiles + (rb * w.n_ch + c) * SG_TILE_BYTES;
-  const uint32_t scw = reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF)[r];
+  const uint8_t* tile = w.tiles + (rb * w.n_ch + c) * sg_tile_bytes(w.dtype);
   float out[8];
+  if (w.dtype == SG_DTYPE_Q6_K) {
+    // q6_k.rs:37-46: w = d * (f32)sc * (f32)(q - 32), both products exact
+    const uint32_t scw = reinterpret_cast<const uint32_t*>(tile + SG_TILE6_SC_OFF)[r];
+    const uint32_t ddw = w.dd[(rb * w.n_sb + (c >> 2)) * 128 + r];
+    const float d = __half2float(__ushort_as_half((unsigned short)(ddw & 0xFFFFu)));
+    const uint2 hw = reinterpret_cast<const uint2*>(tile + SG_TILE6_HI_OFF)[(kk0 >> 5) * 128 + r];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int kk = kk0 + i;
+      const uint32_t hword = sg_q6_hi_word(kk) ? hw.y : hw.x;
+      const int q = (int)(tile_nibble(tile, r, kk) | (((hword >> sg_q6_hi_bit(kk)) & 3u) << 4));
+      const float sc = (float)(int8_t)(scw >> (8 * ((kk & 63) >> 4)));
+      out[i] = __fmul_rn(__fmul_rn(d, sc), (float)(q - 32));
+    }
+    float4* o = reinterpret_cast<float4*>(dst + row * ld + k0);
+    o[0] = make_float4(out[0], out[1], out[2], out[3]);
+    o[1] = make_float4(out[4], out[5], out[6], out[7]);
+    return;
+  }
+  const uint32_t scw = reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF)[r];
   if (w.dtype == SG_DTYPE_Q4_0) {
     const uint32_t dw = (kk0 >> 5) ? (scw >> 16) : (scw & 0xFFFFu);
     const float d = __half2float(__ushort_as_half((unsigned short)dw));
@@ -163,8 +221,8 @@ inline unsigned nblocks(int64_t n, int t) { return (unsigned)((n + t - 1) / t); 
 size_t sg_layout_bytes(int dtype, int64_t n_rows, int64_t n_cols) {
   const int64_t n_rb = (n_rows + 127) / 128;
   const int64_t n_ch = (n_cols + 63) / 64;
-  size_t b = (size_t)(n_rb * n_ch) * SG_TILE_BYTES;
-  if (dtype == SG_DTYPE_Q4_K) b += (size_t)(n_rb * (n_cols / 256)) * 512;
+  size_t b = (size_t)(n_rb * n_ch) * sg_tile_bytes(dtype);
+  if (dtype == SG_DTYPE_Q4_K || dtype == SG_DTYPE_Q6_K) b += (size_t)(n_rb * (n_cols / 256)) * 512;
   return b;
 }
 
@@ -174,10 +232,10 @@ int sg_layout_alloc(SgDevWeight* w, int dtype, int64_t n_rows, int64_t n_cols) {
   w->n_cols = n_cols;
   w->n_rb = (n_rows + 127) / 128;
   w->n_ch = (n_cols + 63) / 64;
-  w->n_sb = dtype == SG_DTYPE_Q4_K ? n_cols / 256 : 0;
+  w->n_sb = dtype == SG_DTYPE_Q4_K || dtype == SG_DTYPE_Q6_K ? n_cols / 256 : 0;
   w->tiles = nullptr;
   w->dd = nullptr;
-  const size_t tile_bytes = (size_t)(w->n_rb * w->n_ch) * SG_TILE_BYTES;
+  const size_t tile_bytes = (size_t)(w->n_rb * w->n_ch) * sg_tile_bytes(dtype);
   const size_t dd_bytes = (size_t)(w->n_rb * w->n_sb) * 512;
   if (cudaMalloc(&w->tiles, tile_bytes) != cudaSuccess) return -1;
   if (dd_bytes && cudaMalloc(&w->dd, dd_bytes) != cudaSuccess) {
@@ -202,9 +260,12 @@ cudaError_t sg_layout_repack(const SgDevWeight* w, const uint8_t* raw_dev, cudaS
   const int64_t ns = w->n_rb * w->n_ch * 128;
   repack_scales_kernel<<<nblocks(ns, T), T, 0, st>>>(w->dtype, raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch,
                                                      w->tiles);
-  if (w->dtype == SG_DTYPE_Q4_K) {
+  if (w->dtype == SG_DTYPE_Q6_K)
+    repack_q6_hi_kernel<<<nblocks(nq, T), T, 0, st>>>(raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_ch, w->tiles);
+  if (w->dtype == SG_DTYPE_Q4_K || w->dtype == SG_DTYPE_Q6_K) {
     const int64_t nd = w->n_rb * w->n_sb * 128;
-    repack_q4k_dd_kernel<<<nblocks(nd, T), T, 0, st>>>(raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_sb, w->dd);
+    repack_q4k_dd_kernel<<<nblocks(nd, T), T, 0, st>>>(raw_dev, w->n_rows, w->n_cols, w->n_rb, w->n_sb, w->dd,
+                                                         w->dtype == SG_DTYPE_Q4_K ? 144 : 210);
   }
   return cudaGetLastError();
 }

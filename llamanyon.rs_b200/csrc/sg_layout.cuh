@@ -27,22 +27,49 @@
 // Q4_0 keeps exactly 18 B per 32 weights. Q4_K stores 148 B per 256 weights
 // instead of 144 (the 6-bit scale/min pairs are kept one byte each so the
 // kernels skip the unpack); roofline bytes are still counted at 144.
+//
+// Q6_K (6-bit q, 16-element sub-blocks with int8 scales, f16 d per 256;
+// swamp-gguf/src/quant/q6_k.rs) uses 6656-byte tiles:
+//   [0, 4096)    the low 4 bits of q, exactly as the Q4 nibble words
+//   [4096, 6144) the high 2 bits: [half 2][row 128][word 2]; word i covers
+//                nibble words 2i and 2i+1; its byte b holds, for the bytes b
+//                that one mask makes of each nibble word (K offsets {0,4,1,5}
+//                of the low nibbles, {2,6,3,7} of the high ones), the high
+//                bits of word 2i's low / high nibble at bits 0-1 / 2-3 and of
+//                word 2i+1's at bits 4-5 / 6-7 -- two masks and a shift put
+//                them next to the nibbles
+//   [6144, 6656) one word per row: the int8 scales of the chunk's four
+//                16-element sub-blocks
+//   dd [rb][superblock][row 128] uint32: the f16 d (low half)
+// 208 B per 256 weights instead of 210.
 #pragma once
 #include "sg_common.cuh"
 
 #define SG_TILE_BYTES 4608
 #define SG_TILE_SC_OFF 4096
+#define SG_TILE6_BYTES 6656
+#define SG_TILE6_HI_OFF 4096
+#define SG_TILE6_SC_OFF 6144
+
+__host__ __device__ constexpr int sg_tile_bytes(int dtype) { return dtype == SG_DTYPE_Q6_K ? SG_TILE6_BYTES : SG_TILE_BYTES; }
 
 struct SgDevWeight {
   int dtype;
   int64_t n_rows, n_cols;  // logical sizes of this shard (N, K)
   int64_t n_rb, n_ch, n_sb;
-  uint8_t* tiles;  // n_rb * n_ch * SG_TILE_BYTES
-  uint32_t* dd;    // Q4_K: uint32[n_rb*n_sb*128]; Q4_0: nullptr
+  uint8_t* tiles;  // n_rb * n_ch * sg_tile_bytes(dtype)
+  uint32_t* dd;    // Q4_K, Q6_K: uint32[n_rb*n_sb*128]; Q4_0: nullptr
 };
 
 // Bit position of nibble j (0..7) inside its 32-bit word.
 __host__ __device__ constexpr int sg_nib_pos(int j) { return 16 * (j & 1) + 4 * (j >> 1); }
+
+// Q6_K: position of the high 2 bits of (k-in-chunk kk) in the high plane:
+// word index (of the row's two per half) and bit offset
+__host__ __device__ constexpr int sg_q6_hi_word(int kk) { return (kk & 31) >> 4; }
+__host__ __device__ constexpr int sg_q6_hi_bit(int kk) {
+  return 8 * (((kk & 1) << 1) | ((kk >> 2) & 1)) + 2 * ((kk >> 1) & 1) + 4 * ((kk >> 3) & 1);
+}
 
 // Nibble at (row-in-block r, k-in-chunk kk) inside one tile.
 __device__ __forceinline__ uint32_t tile_nibble(const uint8_t* tile, int r, int kk) {

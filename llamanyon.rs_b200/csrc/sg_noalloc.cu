@@ -20,7 +20,7 @@ int sg_linear_device_noalloc(sg_weight_t w, const float* x, int64_t ldx, float* 
     return fail(SG_ERR_UNSUPPORTED, "sg_linear_device_noalloc: batch %d outside the decode range 1..%d", batch,
                 SG_GEMV_MAX_BATCH);
   const SgDevWeight* sw = &w->shards[0].w;
-  if (sg_gemv_scratch_bytes(sw->n_cols, batch) > kStaticWsBytes)
+  if (sw->dtype != SG_DTYPE_Q6_K && sg_gemv_scratch_bytes(sw->n_cols, batch) > kStaticWsBytes)
     return fail(SG_ERR_UNSUPPORTED, "sg_linear_device_noalloc: n_cols %lld above %lld at batch %d (the fixed workspace)",
                 (long long)sw->n_cols, (long long)kStaticWsCols, batch);
   const bool acc = (flags & SG_FLAG_ACCUMULATE) != 0;
@@ -38,8 +38,12 @@ int sg_linear_device_noalloc(sg_weight_t w, const float* x, int64_t ldx, float* 
   void* ws = nullptr;
   CUDA_TRY(static_workspace(d.device, &ws));
   cudaStream_t st = (cudaStream_t)stream;
-  SgGemvMat m = {sw, y, ldy};
-  CUDA_TRY(sg_gemv(&m, 1, x, ldx, batch, acc, ws, kStaticWsBytes, d.num_sms, st));
+  if (sw->dtype == SG_DTYPE_Q6_K) {  // no workspace: zeroes y and reduces K ranges in place
+    CUDA_TRY(sg_gemv_q6k(sw, x, ldx, y, ldy, batch, acc, d.num_sms, st));
+  } else {
+    SgGemvMat m = {sw, y, ldy};
+    CUDA_TRY(sg_gemv(&m, 1, x, ldx, batch, acc, ws, kStaticWsBytes, d.num_sms, st));
+  }
   if (row_split) {
     if (!g_nccl.AllReduce) return fail(SG_ERR_NCCL, "NCCL not initialised");
     const ncclResult_t r = g_nccl.AllReduce(y, y, (size_t)batch * w->n_rows, kNcclFloat, kNcclSum, d.comm, st);

@@ -5,6 +5,7 @@
 // device code.
 #include "sg_layout.cu"
 #include "sg_gemv.cu"
+#include "sg_gemv_q6k.cu"
 #include "sg_gemm.cu"
 #include "sg_api.cu"
 #include "sg_noalloc.cu"

@@ -23,12 +23,13 @@ LIB_PATH = os.path.join(HERE, "libswamp_gpu.so")
 SG_OK = 0
 SG_DTYPE_Q4_0 = 2
 SG_DTYPE_Q4_K = 12
+SG_DTYPE_Q6_K = 14
 SG_TP_REPLICATE, SG_TP_COLUMN, SG_TP_ROW = 0, 1, 2
 SG_FLAG_DEVICE_PTRS = 0x1
 SG_FLAG_ACCUMULATE = 0x2
 
-BLOCK = {SG_DTYPE_Q4_0: 32, SG_DTYPE_Q4_K: 256}
-BLOCK_BYTES = {SG_DTYPE_Q4_0: 18, SG_DTYPE_Q4_K: 144}
+BLOCK = {SG_DTYPE_Q4_0: 32, SG_DTYPE_Q4_K: 256, SG_DTYPE_Q6_K: 256}
+BLOCK_BYTES = {SG_DTYPE_Q4_0: 18, SG_DTYPE_Q4_K: 144, SG_DTYPE_Q6_K: 210}
 
 # every symbol include/swamp_gpu.h declares
 EXPORTS = (

@@ -157,11 +157,84 @@ int orc_q4k_dequant(const uint8_t *raw, size_t raw_len, float *dst, size_t n) {
     return 0;
 }
 
-/* swamp-gguf/src/quant/mod.rs:18-33 (the two dtypes in scope) */
+/* swamp-gguf/src/quant/q6_k.rs:8-57. Per 256-block: ql[128] low nibbles,
+ * qh[64] high 2-bit pairs, 16 int8 scales, f16 d. Half h (128 elements),
+ * l in 0..32, m in 0..4: element 128h + 32m + l has
+ *   q = ((ql[64h + l + 32(m&1)] >> 4(m>>1)) & 0xF) | (((qh[32h + l] >> 2m) & 3) << 4)
+ * and w = d * (f32)sc[8h + 2m + l/16] * (f32)(q - 32), left to right (:37-46).
+ * Both products are exact in f32 (d: 11 significant bits, sc: at most 7,
+ * q - 32: at most 5), as in the reference. */
+int orc_q6k_dequant(const uint8_t *raw, size_t raw_len, float *dst, size_t n) {
+    size_t n_blocks = (n + ORC_Q6_K_BLOCK - 1) / ORC_Q6_K_BLOCK;
+    if (raw_len < n_blocks * ORC_Q6_K_BYTES) return -1; /* :12-17 */
+    for (size_t b = 0; b < n_blocks; b++) {
+        const uint8_t *blk = raw + b * ORC_Q6_K_BYTES;
+        const uint8_t *ql = blk, *qh = blk + 128, *sc = blk + 192;
+        float d = ld_f16(blk + 208); /* :28 */
+        float y[256];
+        for (int h = 0; h < 2; h++) {
+            for (int l = 0; l < 32; l++) {
+                int is = l / 16;
+                int q1 = (int)(int8_t)((ql[l] & 0xF) | ((qh[l] & 3) << 4)) - 32;
+                int q2 = (int)(int8_t)((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                int q3 = (int)(int8_t)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                int q4 = (int)(int8_t)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+                y[128 * h + l] = d * (float)(int8_t)sc[is] * (float)q1;
+                y[128 * h + l + 32] = d * (float)(int8_t)sc[is + 2] * (float)q2;
+                y[128 * h + l + 64] = d * (float)(int8_t)sc[is + 4] * (float)q3;
+                y[128 * h + l + 96] = d * (float)(int8_t)sc[is + 6] * (float)q4;
+            }
+            ql += 64;
+            qh += 32;
+            sc += 8;
+        }
+        size_t out_start = b * ORC_Q6_K_BLOCK;
+        size_t cnt = n - out_start < 256 ? n - out_start : 256;
+        memcpy(dst + out_start, y, cnt * sizeof(float));
+    }
+    return 0;
+}
+
+/* swamp-gguf/src/quant/mod.rs:18-33 (the dtypes in scope) */
 int orc_dequantize(int dtype, const uint8_t *raw, size_t raw_len, float *dst, size_t n) {
     if (dtype == ORC_DTYPE_Q4_0) return orc_q4_0_dequant(raw, raw_len, dst, n);
     if (dtype == ORC_DTYPE_Q4_K) return orc_q4k_dequant(raw, raw_len, dst, n);
+    if (dtype == ORC_DTYPE_Q6_K) return orc_q6k_dequant(raw, raw_len, dst, n);
     return -2;
+}
+
+/* swamp-kernels/src/fused_gemv_q6k.rs:248-291, the scalar path of the engine's
+ * Q6_K route (swamp-engine/src/linear.rs:48-67): acc += d*sc*q*x in f32, left
+ * to right, blocks, halves, then l with the four elements l, l+32, l+64,
+ * l+96. d is decoded exactly (the kernel's own f16 decode, :11-20, breaks on
+ * subnormal d; the dequantizer's exact one, q6_k.rs:28, is the parity
+ * target); for normal d both agree. */
+void orc_gemv_q6k_scalar(const uint8_t *w, const float *x, float *out, int64_t n_rows, int64_t n_cols) {
+    int64_t n_blocks = n_cols / ORC_Q6_K_BLOCK;
+    for (int64_t row = 0; row < n_rows; row++) {
+        float acc = 0.0f;
+        for (int64_t blk = 0; blk < n_blocks; blk++) {
+            const uint8_t *b = w + (size_t)(row * n_blocks + blk) * ORC_Q6_K_BYTES;
+            float d = ld_f16(b + 208);
+            const float *x_blk = x + blk * ORC_Q6_K_BLOCK;
+            for (int half = 0; half < 2; half++) {
+                const uint8_t *ql = b + 64 * half, *qh = b + 128 + 32 * half, *sc = b + 192 + 8 * half;
+                const float *xh = x_blk + 128 * half;
+                for (int l = 0; l < 32; l++) {
+                    int is = l / 16;
+                    float q1 = (float)((int)((ql[l] & 0x0F) | ((qh[l] & 3) << 4)) - 32);
+                    float q2 = (float)((int)((ql[l + 32] & 0x0F) | (((qh[l] >> 2) & 3) << 4)) - 32);
+                    float q3 = (float)((int)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32);
+                    float q4 = (float)((int)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32);
+                    acc += d * (float)(int8_t)sc[is] * q1 * xh[l];
+                    acc += d * (float)(int8_t)sc[is + 2] * q2 * xh[l + 32];
+                    acc += d * (float)(int8_t)sc[is + 4] * q3 * xh[l + 64];
+                    acc += d * (float)(int8_t)sc[is + 6] * q4 * xh[l + 96];
+                }
+            }
+        }
+        out[row] = acc;
+    }
 }
 
 /* ------------------------------------------------------------------------- */
@@ -288,7 +361,7 @@ int orc_linear_q4_0(const uint8_t *w, const float *x, float *out,
 }
 
 typedef struct {
-    int kind; /* 0 q4k gemv, 1 dot rows, 2 q4k batched */
+    int kind; /* 0 q4k gemv, 1 dot rows, 2 q4k batched, 3 q6k gemv */
     const uint8_t *w;
     const float *x;
     const float *const *xs;
@@ -308,6 +381,9 @@ static void *orc_worker(void *arg) {
     } else if (t->kind == 1) {
         for (int64_t b = 0; b < t->batch; b++)
             dot_rows(t->deq, t->xs[b], t->outs[b], t->r0, t->r1, t->nc);
+    } else if (t->kind == 3) {
+        size_t row_bytes = (size_t)(t->nc / ORC_Q6_K_BLOCK) * ORC_Q6_K_BYTES;
+        orc_gemv_q6k_scalar(t->w + (size_t)t->r0 * row_bytes, t->x, t->out + t->r0, rc, t->nc);
     } else {
         size_t row_bytes = (size_t)(t->nc / ORC_Q4_K_BLOCK) * ORC_Q4_K_BYTES;
         float *local_outs[1024];
@@ -351,6 +427,12 @@ int orc_forward_linear(int dtype, const uint8_t *w, const float *x, float *out,
     if (dtype == ORC_DTYPE_Q4_K) {
         if (n_cols % ORC_Q4_K_BLOCK) return -1;
         proto.kind = 0;
+        run_partitioned(proto, n_rows, n_threads);
+        return 0;
+    }
+    if (dtype == ORC_DTYPE_Q6_K) {  /* linear.rs:48-67 */
+        if (n_cols % ORC_Q6_K_BLOCK) return -1;
+        proto.kind = 3;
         run_partitioned(proto, n_rows, n_threads);
         return 0;
     }
@@ -536,10 +618,41 @@ static void gen_q4k_blocks(uint64_t seed, uint64_t id, int64_t b0, int64_t b1, u
     }
 }
 
+/* Q6_K: d as the other types; 16 int8 scales uniform over -128..127; 256
+ * 6-bit values uniform over 0..63, packed as q6_k.rs reads them (:33-46). */
+static void gen_q6k_blocks(uint64_t seed, uint64_t id, int64_t b0, int64_t b1, uint8_t *out) {
+    for (int64_t b = b0; b < b1; b++) {
+        uint8_t *blk = out + (size_t)b * ORC_Q6_K_BYTES;
+        uint64_t base = 40 * (uint64_t)b;
+        uint64_t r0 = hh(seed, id, base), r1 = hh(seed, id, base + 1), r2 = hh(seed, id, base + 2);
+        uint16_t d = gen_scale(r0 >> 40);
+        for (int j = 0; j < 8; j++) {
+            blk[192 + j] = (uint8_t)(r1 >> (8 * j));
+            blk[200 + j] = (uint8_t)(r2 >> (8 * j));
+        }
+        blk[208] = (uint8_t)(d & 0xFF);
+        blk[209] = (uint8_t)(d >> 8);
+        uint8_t q[256];
+        for (int g = 0; g < 32; g++) {  /* 8 values of 6 bits per draw */
+            uint64_t r = hh(seed, id, base + 3 + (uint64_t)g);
+            for (int i = 0; i < 8; i++) q[8 * g + i] = (uint8_t)((r >> (6 * i)) & 63);
+        }
+        memset(blk, 0, 192);
+        for (int h = 0; h < 2; h++)
+            for (int m = 0; m < 4; m++)
+                for (int l = 0; l < 32; l++) {
+                    uint8_t v = q[128 * h + 32 * m + l];
+                    blk[64 * h + l + 32 * (m & 1)] |= (uint8_t)((v & 0xF) << (4 * (m >> 1)));
+                    blk[128 + 32 * h + l] |= (uint8_t)((v >> 4) << (2 * m));
+                }
+    }
+}
+
 static void *gen_worker(void *arg) {
     gen_task *t = (gen_task *)arg;
     if (t->kind == 0) gen_q4_0_blocks(t->seed, t->id, t->b0, t->b1, t->out);
-    else gen_q4k_blocks(t->seed, t->id, t->b0, t->b1, t->out);
+    else if (t->kind == 1) gen_q4k_blocks(t->seed, t->id, t->b0, t->b1, t->out);
+    else gen_q6k_blocks(t->seed, t->id, t->b0, t->b1, t->out);
     return NULL;
 }
 
@@ -576,6 +689,11 @@ void orc_gen_q4k(uint64_t seed, uint64_t tensor_id, int64_t n_rows,
     gen_parallel(1, seed, tensor_id, n_rows * (n_cols / ORC_Q4_K_BLOCK), out, n_threads);
 }
 
+void orc_gen_q6k(uint64_t seed, uint64_t tensor_id, int64_t n_rows,
+                 int64_t n_cols, uint8_t *out, int n_threads) {
+    gen_parallel(2, seed, tensor_id, n_rows * (n_cols / ORC_Q6_K_BLOCK), out, n_threads);
+}
+
 /* N(0,1) by Box-Muller in double, rounded once to f32. */
 void orc_gen_x(uint64_t seed, uint64_t tensor_id, int64_t n, float *out) {
     const double two_pi = 6.283185307179586476925286766559;
@@ -599,6 +717,7 @@ int orc_gemv_f64(int dtype, const uint8_t *w, const float *x, int64_t n_rows,
     size_t row_bytes;
     if (dtype == ORC_DTYPE_Q4_0) row_bytes = (size_t)(n_cols / ORC_Q4_0_BLOCK) * ORC_Q4_0_BYTES;
     else if (dtype == ORC_DTYPE_Q4_K) row_bytes = (size_t)(n_cols / ORC_Q4_K_BLOCK) * ORC_Q4_K_BYTES;
+    else if (dtype == ORC_DTYPE_Q6_K) row_bytes = (size_t)(n_cols / ORC_Q6_K_BLOCK) * ORC_Q6_K_BYTES;
     else return -2;
     float *row = (float *)malloc((size_t)n_cols * sizeof(float));
     if (!row) return -3;

@@ -29,6 +29,9 @@ extern "C" {
 #define ORC_Q4_0_BYTES 18
 #define ORC_Q4_K_BLOCK 256
 #define ORC_Q4_K_BYTES 144
+#define ORC_DTYPE_Q6_K 14
+#define ORC_Q6_K_BLOCK 256
+#define ORC_Q6_K_BYTES 210
 
 /* IEEE binary16 <-> binary32 (crate `half` 2.7.1, Cargo.lock:607-608;
  * call sites q4_0.rs:24, q4_k.rs:281-282, fused_gemv_q4k.rs:708-710). */
@@ -43,6 +46,10 @@ void orc_q4k_unpack_scales(const uint8_t sc[12], uint8_t scales[8], uint8_t mins
 
 /* swamp-gguf/src/quant/q4_k.rs:21-33,278-322 (the dispatched scalar path). */
 int orc_q4k_dequant(const uint8_t *raw, size_t raw_len, float *dst, size_t n);
+/* swamp-gguf/src/quant/q6_k.rs:8-57 */
+int orc_q6k_dequant(const uint8_t *raw, size_t raw_len, float *dst, size_t n);
+/* swamp-kernels/src/fused_gemv_q6k.rs:248-291 (exact f16 d) */
+void orc_gemv_q6k_scalar(const uint8_t *w, const float *x, float *out, int64_t n_rows, int64_t n_cols);
 
 /* Dispatch like swamp-gguf/src/quant/mod.rs:18-33 for the two dtypes. */
 int orc_dequantize(int dtype, const uint8_t *raw, size_t raw_len, float *dst, size_t n);
@@ -106,6 +113,7 @@ void orc_make_x(int64_t n_cols, float *out);
 uint64_t orc_splitmix64(uint64_t z);
 void orc_gen_q4_0(uint64_t seed, uint64_t tensor_id, int64_t n_rows,
                   int64_t n_cols, uint8_t *out, int n_threads);
+void orc_gen_q6k(uint64_t seed, uint64_t tensor_id, int64_t n_rows, int64_t n_cols, uint8_t *out, int n_threads);
 void orc_gen_q4k(uint64_t seed, uint64_t tensor_id, int64_t n_rows,
                  int64_t n_cols, uint8_t *out, int n_threads);
 void orc_gen_x(uint64_t seed, uint64_t tensor_id, int64_t n, float *out);

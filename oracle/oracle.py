@@ -21,8 +21,9 @@ LIB_PATH = os.path.join(HERE, "liboracle.so")
 
 DTYPE_Q4_0 = 2
 DTYPE_Q4_K = 12
-BLOCK = {DTYPE_Q4_0: 32, DTYPE_Q4_K: 256}
-BLOCK_BYTES = {DTYPE_Q4_0: 18, DTYPE_Q4_K: 144}
+DTYPE_Q6_K = 14
+BLOCK = {DTYPE_Q4_0: 32, DTYPE_Q4_K: 256, DTYPE_Q6_K: 256}
+BLOCK_BYTES = {DTYPE_Q4_0: 18, DTYPE_Q4_K: 144, DTYPE_Q6_K: 210}
 
 _lib = None
 
@@ -66,6 +67,8 @@ def lib() -> ctypes.CDLL:
     L.orc_splitmix64.restype = ctypes.c_uint64
     L.orc_gen_q4_0.argtypes = [ctypes.c_uint64, ctypes.c_uint64, i64, i64, P, ctypes.c_int]
     L.orc_gen_q4k.argtypes = [ctypes.c_uint64, ctypes.c_uint64, i64, i64, P, ctypes.c_int]
+    L.orc_gen_q6k.argtypes = [ctypes.c_uint64, ctypes.c_uint64, i64, i64, P, ctypes.c_int]
+    L.orc_gemv_q6k_scalar.argtypes = [P, P, P, i64, i64]
     L.orc_gen_x.argtypes = [ctypes.c_uint64, ctypes.c_uint64, i64, P]
     L.orc_gemv_f64.argtypes = [ctypes.c_int, P, P, i64, i64, P, P, P]
     L.orc_gemv_f64.restype = ctypes.c_int
@@ -91,7 +94,8 @@ def f32_to_f16(f: float) -> int:
 
 
 def dequantize(dtype: int, raw: np.ndarray, n: int) -> np.ndarray:
-    """swamp-gguf quant::dequantize for Q4_0 (q4_0.rs) / Q4_K (q4_k.rs scalar)."""
+    """swamp-gguf quant::dequantize for Q4_0 (q4_0.rs), Q4_K (q4_k.rs scalar)
+    and Q6_K (q6_k.rs)."""
     raw = np.ascontiguousarray(raw, dtype=np.uint8)
     out = np.empty(n, dtype=np.float32)
     rc = lib().orc_dequantize(dtype, _p(raw), raw.size, _p(out), n)
@@ -126,6 +130,15 @@ def gemv_q4k_batched_scalar(w, xs: np.ndarray, outs: np.ndarray, n_rows, n_cols)
     return outs
 
 
+def gemv_q6k_scalar(w: np.ndarray, x: np.ndarray, n_rows: int, n_cols: int) -> np.ndarray:
+    """fused_gemv_q6k_scalar (swamp-kernels/src/fused_gemv_q6k.rs:248-291),
+    the engine's Q6_K route (linear.rs:48-67), with the exact f16 decode."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(n_rows, np.float32)
+    lib().orc_gemv_q6k_scalar(_p(w), _p(x), _p(out), n_rows, n_cols)
+    return out
+
+
 def linear_q4_0(w, x, n_rows, n_cols) -> np.ndarray:
     """Engine Q4_0 route (swamp-engine/src/linear.rs:68-87)."""
     x = np.ascontiguousarray(x, np.float32)
@@ -146,6 +159,8 @@ def reference_linear(dtype: int, w, x: np.ndarray, n_rows: int, n_cols: int) -> 
     for b in range(x.shape[0]):
         if dtype == DTYPE_Q4_K:
             out[b] = gemv_q4k_scalar(w, x[b], n_rows, n_cols)
+        elif dtype == DTYPE_Q6_K:
+            out[b] = gemv_q6k_scalar(w, x[b], n_rows, n_cols)
         else:
             out[b] = linear_q4_0(w, x[b], n_rows, n_cols)
     return out
@@ -204,6 +219,8 @@ def gen_weight(dtype: int, seed: int, tensor_id: int, n_rows: int, n_cols: int,
     out = np.empty(n_rows * row_bytes(dtype, n_cols), np.uint8)
     if dtype == DTYPE_Q4_0:
         lib().orc_gen_q4_0(seed, tensor_id, n_rows, n_cols, _p(out), n_threads)
+    elif dtype == DTYPE_Q6_K:
+        lib().orc_gen_q6k(seed, tensor_id, n_rows, n_cols, _p(out), n_threads)
     else:
         lib().orc_gen_q4k(seed, tensor_id, n_rows, n_cols, _p(out), n_threads)
     return out

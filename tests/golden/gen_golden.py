@@ -82,6 +82,42 @@ def np_dequant_q4k(raw: np.ndarray, n: int) -> np.ndarray:
     return (prod - mv[:, :, None]).astype(np.float32).reshape(-1)
 
 
+def np_dequant_q6k(raw: np.ndarray, n: int) -> np.ndarray:
+    """q6_k.rs:22-57, vectorised: element 128h + 32m + l of a block takes the
+    low nibble of ql[64h + l + 32(m&1)] (>> 4(m>>1)), the 2 bits
+    (qh[32h + l] >> 2m) & 3, and w = d * sc[e/16] * (q - 32)."""
+    blocks = raw[: (n // 256) * 210].reshape(-1, 210).astype(np.int32)
+    d = np_f16(np.ascontiguousarray(raw[: (n // 256) * 210].reshape(-1, 210)[:, 208:210]))[:, 0]
+    q = np.empty((blocks.shape[0], 256), np.int32)
+    for h in range(2):
+        for m in range(4):
+            lo = (blocks[:, 64 * h + 32 * (m & 1): 64 * h + 32 * (m & 1) + 32] >> (4 * (m >> 1))) & 0xF
+            hi = (blocks[:, 128 + 32 * h: 128 + 32 * h + 32] >> (2 * m)) & 3
+            q[:, 128 * h + 32 * m: 128 * h + 32 * m + 32] = lo | (hi << 4)
+    sc = blocks[:, 192:208].astype(np.uint8).view(np.int8).astype(np.float32)
+    s16 = (d[:, None] * sc).astype(np.float32)                    # d * sc, exact
+    w = (np.repeat(s16, 16, axis=1) * (q - 32).astype(np.float32)).astype(np.float32)
+    return w.reshape(-1)
+
+
+def np_gemv_q6k_scalar_order(w: np.ndarray, x: np.ndarray, n_rows: int, n_cols: int) -> np.ndarray:
+    """fused_gemv_q6k_scalar (fused_gemv_q6k.rs:248-291): acc += w*x in f32,
+    per block and half over l with the elements l, l+32, l+64, l+96."""
+    deq = np_dequant_q6k(w, n_rows * n_cols).reshape(n_rows, n_cols)
+    out = np.zeros(n_rows, np.float32)
+    for r in range(n_rows):
+        acc = F32(0.0)
+        for blk in range(n_cols // 256):
+            for h in range(2):
+                base = blk * 256 + 128 * h
+                for l in range(32):
+                    for m in range(4):
+                        k = base + l + 32 * m
+                        acc = F32(acc + F32(deq[r, k] * x[k]))
+        out[r] = acc
+    return out
+
+
 def np_seq_dot(w_row: np.ndarray, x: np.ndarray) -> np.float32:
     """acc += w*x in float32, left to right, products rounded before adding."""
     acc = F32(0.0)
@@ -253,8 +289,69 @@ def random_fixtures():
     return out
 
 
+def q6k_create_test_data(n_rows: int, n_blocks: int) -> np.ndarray:
+    """create_test_data (swamp-kernels/src/fused_gemv_q6k.rs:331-356)."""
+    raw = np.zeros(n_rows * n_blocks * 210, np.uint8)
+    for row in range(n_rows):
+        for blk in range(n_blocks):
+            b = (row * n_blocks + blk) * 210
+            for i in range(128):
+                raw[b + i] = (i & 0x0F) | ((((i + 128) & 0xFF) & 0x0F) << 4)
+            for i in range(64):
+                b0 = (i >> 4) & 3
+                b1 = ((i + 64) >> 4) & 3
+                b2 = (((i + 128) & 0xFF) >> 4) & 3
+                b3 = (((i + 192) & 0xFF) >> 4) & 3
+                raw[b + 128 + i] = b0 | (b1 << 2) | (b2 << 4) | (b3 << 6)
+            for i in range(16):
+                raw[b + 192 + i] = (row * 16 + i + 1) & 0x7F
+            raw[b + 208] = 0x00
+            raw[b + 209] = 0x38  # d = f16 0x3800 = 0.5
+    return raw
+
+
+def kat_q6k_reference_tests():
+    """The reference's Q6_K test (fused_gemv_q6k.rs:358-376): create_test_data
+    with 2 rows x 2 blocks, x[i] = sin(0.01 i) in f32 (here numpy's float32
+    sin; Rust's may differ by an ulp, and the test's bound is loose), the
+    scalar kernel against the dequantized dot."""
+    n_rows, n_blocks = 2, 2
+    n_cols = 256 * n_blocks
+    raw = q6k_create_test_data(n_rows, n_blocks)
+    x = np.sin(np.arange(n_cols, dtype=np.float32) * F32(0.01)).astype(np.float32)
+    deq_np = np_dequant_q6k(raw, n_rows * n_cols).reshape(n_rows, n_cols)
+    deq_c = oracle.dequantize(oracle.DTYPE_Q6_K, raw, n_rows * n_cols).reshape(n_rows, n_cols)
+    assert np.array_equal(deq_np, deq_c)
+    fused_np = np_gemv_q6k_scalar_order(raw, x, n_rows, n_cols)
+    fused_c = oracle.gemv_q6k_scalar(raw, x, n_rows, n_cols)
+    assert np.array_equal(fused_np, fused_c)
+    dot_ref = [float(np.sum((deq_np[r] * x).astype(np.float32), dtype=np.float32)) for r in range(n_rows)]
+    for r in range(n_rows):  # the reference test's own relation (:371-374)
+        diff = abs(float(fused_np[r]) - dot_ref[r])
+        assert diff < 1.0 or diff / max(abs(dot_ref[r]), 1.0) < 1e-4
+    return {"n_rows": n_rows, "n_cols": n_cols, "weight_hex": raw.tobytes().hex(), "x": x.tolist(),
+            "dequant_row0_first16": deq_np[0, :16].tolist(),
+            "expect_f32_scalar_kernel": fused_np.tolist(), "dequant_dot_f32": dot_ref,
+            "source": "swamp-kernels/src/fused_gemv_q6k.rs:331-376 (create_test_data, test_q6k_bitexact_vs_dequant_scalar)"}
+
+
+def q6k_random_fixtures():
+    n_rows, n_cols, B = 24, 512, 2
+    w = oracle.gen_weight(oracle.DTYPE_Q6_K, SEED, 7, n_rows, n_cols)
+    x = oracle.gen_x(SEED, 8, (B, n_cols))
+    deq_np = np_dequant_q6k(w, n_rows * n_cols)
+    assert np.array_equal(deq_np, oracle.dequantize(oracle.DTYPE_Q6_K, w, n_rows * n_cols))
+    ref_np = np.stack([np_gemv_q6k_scalar_order(w, x[b], n_rows, n_cols) for b in range(B)])
+    assert np.array_equal(ref_np, oracle.reference_linear(oracle.DTYPE_Q6_K, w, x, n_rows, n_cols))
+    return {"q6k_w": w, "q6k_x": x, "q6k_deq": deq_np.reshape(n_rows, n_cols), "q6k_ref": ref_np,
+            "q6k_shape": np.array([n_rows, n_cols, B], np.int64)}
+
+
 def main():
     oracle.build()
+    with open(os.path.join(HERE, "q6k_reference_tests.json"), "w") as f:
+        json.dump(kat_q6k_reference_tests(), f, indent=1)
+    np.savez_compressed(os.path.join(HERE, "q6k_small.npz"), seed=np.uint64(SEED), **q6k_random_fixtures())
     with open(os.path.join(HERE, "q4k_reference_tests.json"), "w") as f:
         json.dump(kat_reference_tests(), f, indent=1)
     with open(os.path.join(HERE, "q4_0_known_answers.json"), "w") as f:

@@ -248,8 +248,9 @@ def test_random_files_agree(lib):
 
 
 def test_register_needs_the_device_path_types(lib):
-    """sg_gguf_register takes Q4_0/Q4_K matrices only; without sg_init it
-    reports that first for a supported tensor."""
+    """sg_gguf_register takes Q4_0, Q4_K and Q6_K matrices only; a supported
+    tensor goes on to sg_weight_register, which without sg_init reports
+    SG_ERR_NOT_INITIALIZED."""
     with open(os.path.join(GOLDEN, "gguf_all_types_v3.gguf"), "rb") as f:
         img = f.read()
     f = sg.GgufFile(lib, data=img)
@@ -257,7 +258,7 @@ def test_register_needs_the_device_path_types(lib):
         import ctypes
         h = ctypes.c_void_p()
         rc = lib.sg_gguf_register(f.handle, f.tensor("w.q6_k").index, 0, ctypes.byref(h))
-        assert rc == -5  # SG_ERR_UNSUPPORTED: Q6_K is not on the device path
+        assert rc == -6  # supported type: sg_weight_register, not initialised
         rc = lib.sg_gguf_register(f.handle, f.tensor("t.f32.3d").index, 0, ctypes.byref(h))
         assert rc == -5
     finally:
