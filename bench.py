@@ -310,21 +310,19 @@ def time_graphs(torch, graphs, reps, st):
 def gpu_arm(args):
     import numpy as np
     torch, gpu, dist, rank, world, local = setup_gpu(args)
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle  # host-side synthetic weight generator only
 
     n_layers = world  # weak scaling: per-GPU bytes fixed
     l2 = torch.cuda.get_device_properties(local).L2_cache_size
     layer_b = sum(wbytes(k, n) for _, k, n in LAYER)
     copies = max(5, int(np.ceil(4.5 * l2 / (layer_b / world))) + 1, n_layers)
-    # one host tensor per layer linear, registered `copies` times: every copy
-    # is a separate device allocation, so rotating copies streams from HBM
-    host_w = {name: oracle.gen_weight(Q40, SEED, 1000 + i, n, k) for i, (name, k, n) in enumerate(LAYER)}
+    # one seeded tensor per layer linear, generated on the device `copies`
+    # times: every copy is a separate allocation, so rotating copies streams
+    # from HBM
     model = []
     for c in range(copies):
         layer = {}
-        for name, k, n in LAYER:
-            layer[name] = gpu.register(host_w[name], Q40, n, k, TP_MODE[name] if world > 1 else 0)
+        for i, (name, k, n) in enumerate(LAYER):
+            layer[name] = gpu.synth_weight(Q40, SEED, 1000 + i, n, k, TP_MODE[name] if world > 1 else 0)
         model.append(layer)
     # K offset of each tensor's shard in x (row split takes a K slice)
     col0 = {name: model[0][name].shard()[3] for name, _, _ in LAYER}
@@ -427,9 +425,10 @@ def gpu_arm(args):
     peak, peak_kind = measured_peaks()
 
     # ---------------------------------------------- prefill
-    prefill = prefill_bench(torch, gpu, oracle, st, args) if world == 1 and not args.no_prefill else None
-    upload = gguf_upload_bench(torch, gpu, oracle) if world == 1 and not args.no_prefill else None
-    q6k = q6k_bench(torch, gpu, oracle, st) if world == 1 and not args.no_prefill else None
+    prefill = prefill_bench(torch, gpu, st, args) if world == 1 and not args.no_prefill else None
+    upload = gguf_upload_bench(torch, gpu) if world == 1 and not args.no_prefill else None
+    q6k = q6k_bench(torch, gpu, st) if world == 1 and not args.no_prefill else None
+    decode = model_decode_bench(torch, gpu, args) if world == 1 and not args.no_model else None
 
     # -------------------------------------------------------------- e2e
     # the public host-pointer C ABI: x copied in and y read back on every call
@@ -502,7 +501,15 @@ def gpu_arm(args):
             "prefill": prefill,
             "gguf_upload": upload,
             "q6k": q6k,
+            "model_decode": decode,
         }
+        if decode and cpu:
+            # the CPU engine streams the same weight bytes per token at the
+            # GEMV route's measured rate (a full 32-layer CPU run would take
+            # minutes per token)
+            for key, run in decode["runs"].items():
+                run["cpu_extrapolated_tok_s"] = round(
+                    int(key[1:]) * cpu["value"] * 1e9 / decode["weight_bytes_per_step"], 4)
         print(json.dumps(line), flush=True)
     graphs = None
     torch.cuda.synchronize()
@@ -516,7 +523,106 @@ def gpu_arm(args):
     return 0
 
 
-def q6k_bench(torch, gpu, oracle, st):
+def model_decode_bench(torch, gpu, args):
+    """a random-init Llama-3-8B-architecture model in Q4_K (32
+    layers, d 4096, 32 query / 8 KV heads, FFN 14336, vocab 128256, Q4_K
+    output head) on the device through llamanyon.rs_b200/decoder.py: a
+    512-token prompt prefilled in one pass (prefill GEMMs, causal attention
+    rows), then greedy decoding, at batch 1 and 8 (independent sequences with
+    their own KV-cache slots). Each decode step is one CUDA graph (every
+    layer's linears, RMSNorms, RoPE + cache store, attention, SiLU-mul, the
+    output head, argmax, the device-side token advance and the D2H copy of
+    the step's tokens to pinned host memory); 3 warm-up steps, then the
+    position is reset and model_new - 1 steps are timed with CUDA events
+    (the first new token comes from the prefill). Weights are generated on
+    the device; prompt tokens are seeded uniform over the vocabulary."""
+    import numpy as np
+    import decoder as dec
+    P, NEW = 512, args.model_new
+    cfg = dec.DecoderConfig(n_layers=args.model_layers, d=4096, n_heads=32, n_kv_heads=8, ffn=14336,
+                            vocab=128256, dtype=Q4K, context_len=2048, max_seq=2048)
+    model = dec.SynthModel(gpu, cfg, SEED)
+    wbytes_step = model.weight_bytes()
+    peak, peak_kind = measured_peaks()
+    runs = {}
+    for B in (1, 8):
+        D = dec.Decoder(gpu, model, n_seqs=B, max_rows=B * P)
+        rng = np.random.default_rng(SEED + B)
+        prompts = rng.integers(0, cfg.vocab, size=(B, P))
+        st = torch.cuda.Stream()
+        ev = lambda: torch.cuda.Event(enable_timing=True)
+        host_tok = torch.empty(B, dtype=torch.int32, pin_memory=True)
+        with torch.cuda.stream(st):
+            # rows in (position, sequence) order: the last position's rows are
+            # the last B, whose logits the prefill computes
+            def prefill_rows():
+                return D.set_rows(prompts.T.reshape(-1), np.repeat(np.arange(P), B), np.tile(np.arange(B), P))
+            rows = prefill_rows()
+            D.forward(rows, stream=st.cuda_stream, logits_rows=slice(rows - B, rows))  # first use: workspaces
+            st.synchronize()
+            e0, e1 = ev(), ev()
+            e0.record(st)
+            rows = prefill_rows()  # H2D of the prompt inside the timed region
+            D.forward(rows, stream=st.cuda_stream, logits_rows=slice(rows - B, rows))
+            host_tok.copy_(D.next[:B], non_blocking=True)
+            e1.record(st)
+            st.synchronize()
+            prefill_ms = e0.elapsed_time(e1)
+            first = D.next[:B].clone()
+            seqs = torch.arange(B, dtype=torch.int32, device="cuda")
+
+            def start():
+                D.tokens[:B].copy_(first)
+                D.pos[:B].fill_(P)
+                D.seq[:B].copy_(seqs)
+            start()
+            D.forward(B, stream=st.cuda_stream)  # first use of the decode shapes
+            start()
+            st.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                D.forward(B, stream=st.cuda_stream)
+                D.advance(B)
+                host_tok.copy_(D.tokens[:B], non_blocking=True)
+            for _ in range(3):
+                g.replay()
+            start()
+            st.synchronize()
+            steps = NEW - 1
+            e2, e3 = ev(), ev()
+            e2.record(st)
+            for _ in range(steps):
+                g.replay()
+            e3.record(st)
+            st.synchronize()
+            dec_ms = e2.elapsed_time(e3)
+            del g
+        step_ms = dec_ms / steps
+        # algorithmic bytes of a step: every weight once plus the K and V rows
+        # attention reads (mean position of the timed steps)
+        mean_len = P + 1 + (steps - 1) / 2
+        kv_bytes = 2 * B * cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 4 * mean_len
+        by = wbytes_step + kv_bytes
+        gbs = by / (step_ms * 1e-3) / 1e9
+        runs[f"b{B}"] = {
+            "prefill_ms": round(prefill_ms, 2), "prefill_tok_s": round(B * P / (prefill_ms * 1e-3), 1),
+            "decode_ms_per_step": round(step_ms, 4), "decode_tok_s": round(B / (step_ms * 1e-3), 1),
+            "e2e_tok_s": round(B * NEW / ((prefill_ms + dec_ms) * 1e-3), 1),
+            "decode_bytes_per_step": int(by),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_kind": peak_kind},
+            "h2d_bytes": B * P * 12, "d2h_bytes_per_step": B * 4}
+        D.free()
+    model.free()
+    return {"workload": f"configs[3]: random-init Llama-3-8B-architecture Q4_K, {cfg.n_layers} layers, prompt {P}, "
+                        f"{NEW} new tokens, greedy, batch 1 and 8",
+            "weight_bytes_per_step": wbytes_step, "runs": runs,
+            "execution": "prefill: one eager pass; decode: one CUDA graph per token",
+            "ops": "sg_embed / sg_rmsnorm / sg_linear_multi (QKV, gate+up) / sg_rope_kv / sg_attention / "
+                   "sg_linear + accumulate (O, down) / sg_silu_mul / sg_argmax"}
+
+
+def q6k_bench(torch, gpu, st):
     """Q6_K, the dtype real Q4_K_M files keep for ffn_down and the output
     head (Llama-3-8B shapes): decode GEMV GB/s at 1 and 16 tokens
     (algorithmic bytes N*K*210/256 + activations) and prefill GEMM TFLOP/s at
@@ -525,7 +631,7 @@ def q6k_bench(torch, gpu, oracle, st):
     out = {}
     Q6K = 14
     for (k, n) in ((14336, 4096), (4096, 128256)):
-        ws = [gpu.register(oracle.gen_weight(Q6K, SEED, 5000 + c, n, k), Q6K, n, k) for c in range(2)]
+        ws = [gpu.synth_weight(Q6K, SEED, 5000 + c, n, k) for c in range(2)]
         for b in ((1, 16) if n < 100000 else (1,)) + ((PREFILL_M,) if n < 100000 else ()):
             x = torch.randn(b, k, device="cuda")
             y = torch.empty(b, n, device="cuda")
@@ -552,7 +658,7 @@ def q6k_bench(torch, gpu, oracle, st):
             "per_shape": out}
 
 
-def gguf_upload_bench(torch, gpu, oracle):
+def gguf_upload_bench(torch, gpu):
     """The GGUF -> device path (sg_gguf_register): one Q4_K 4096->14336
     tensor (33 MB of blocks) in a GGUF file under /tmp, mapped (page cache
     warm) and uploaded with repack; host wall clock around register +
@@ -563,7 +669,7 @@ def gguf_upload_bench(torch, gpu, oracle):
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import gguf_writer
     k, n = 4096, 14336
-    raw = oracle.gen_weight(Q4K, SEED, 4000, n, k)
+    raw = gpu.synth_blocks(Q4K, SEED, 4000, n, k)
     img, _ = gguf_writer.model_file({"blk.0.ffn_up.weight": (Q4K, n, k, raw)})
     with tempfile.TemporaryDirectory() as d:
         path = os.path.join(d, "upload.gguf")
@@ -585,7 +691,7 @@ def gguf_upload_bench(torch, gpu, oracle):
             "ms": round(el * 1e3, 3), "tensor": "Q4_K 4096->14336 from a mapped GGUF file (register + repack)"}
 
 
-def prefill_bench(torch, gpu, oracle, st, args):
+def prefill_bench(torch, gpu, st, args):
     """Q4_K prefill GEMM, M=512, the four Llama-3-8B shapes. Two
     rotating weight copies per shape (156 MB > L2); each shape timed as a CUDA
     graph of back-to-back calls. TFLOP/s counts 2*M*N*K (one product); the
@@ -594,8 +700,8 @@ def prefill_bench(torch, gpu, oracle, st, args):
     import numpy as np
     copies = 2
     M = PREFILL_M
-    ws = {(k, n): [gpu.register(oracle.gen_weight(Q4K, SEED, 2000 + 8 * c + i, n, k), Q4K, n, k)
-                   for c in range(copies)] for i, (k, n) in enumerate(PREFILL_SHAPES)}
+    ws = {(k, n): [gpu.synth_weight(Q4K, SEED, 2000 + 8 * c + i, n, k) for c in range(copies)]
+          for i, (k, n) in enumerate(PREFILL_SHAPES)}
     x = torch.randn(M, 14336, device="cuda")
     y = torch.empty(M, 14336, device="cuda")
     reps = max(3, min(50, args.prefill_reps))
@@ -643,12 +749,10 @@ def profile_arm(args):
     """One tensor shape, eager back-to-back launches (for ncu; not a bench line)."""
     import numpy as np
     torch, gpu, dist, rank, world, local = setup_gpu(args)
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
     k, n, b = (int(v) for v in args.profile.split(","))
     dtype = Q4K if args.dtype == "q4k" else Q40
     copies = 4
-    ws = [gpu.register(oracle.gen_weight(dtype, SEED, 3000 + c, n, k), dtype, n, k) for c in range(copies)]
+    ws = [gpu.synth_weight(dtype, SEED, 3000 + c, n, k) for c in range(copies)]
     x = torch.randn(b, k, device="cuda")
     y = torch.empty(b, n, device="cuda")
     st = torch.cuda.current_stream()
@@ -685,6 +789,9 @@ def main():
     ap.add_argument("--dtype", default="q4_0", choices=["q4_0", "q4k"])
     ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] prefill measurement")
     ap.add_argument("--prefill-reps", type=int, default=20)
+    ap.add_argument("--no-model", action="store_true", help="skip the configs[3] model decode measurement")
+    ap.add_argument("--model-layers", type=int, default=32, help="configs[3] layers (32 = the named model)")
+    ap.add_argument("--model-new", type=int, default=256, help="configs[3] generated tokens")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -223,6 +223,102 @@ SG_API int sg_gguf_kv_string(sg_gguf_t g, int64_t index, int64_t elem, const cha
  * independent of the file afterwards. */
 SG_API int sg_gguf_register(sg_gguf_t g, int64_t index, int tp_mode, sg_weight_t *out);
 
+/* ------------------------------------------------------- synthetic inputs */
+
+/* Seeded random-init tensors of the benchmark configurations, generated on
+ * the device: Q4_0 d uniform in [0.001, 0.01) (f16), nibbles uniform 0..15;
+ * Q4_K d and dmin likewise, 6-bit scales and mins uniform, packed as
+ * make_q4k_block (swamp-kernels/src/fused_gemv_q4k.rs:708-724); Q6_K int8
+ * scales and 6-bit values uniform. Each block's bytes are a function of
+ * (seed, tensor_id, block index) through splitmix64, so a tensor-parallel
+ * shard generates only its own blocks. sg_synth_weight registers such a
+ * tensor like sg_weight_register would; sg_synth_blocks writes its GGUF
+ * bytes (host memory, or device memory with SG_FLAG_DEVICE_PTRS). */
+SG_API int sg_synth_weight(int dtype, uint64_t seed, uint64_t tensor_id, int64_t n_rows, int64_t n_cols,
+                           int tp_mode, sg_weight_t *out);
+SG_API int sg_synth_blocks(int dtype, uint64_t seed, uint64_t tensor_id, int64_t n_rows, int64_t n_cols,
+                           void *dst, int flags);
+/* N(0,1) activations (Box-Muller in double, one f32 rounding), host memory;
+ * needs no GPU. */
+SG_API int sg_synth_x(uint64_t seed, uint64_t tensor_id, int64_t n, float *dst);
+
+/* ------------------------------------------------------------- layer ops */
+
+/* The non-matmul operations of a decoder layer on device-resident
+ * activations, so that an engine keeps x between the linears on the GPU
+ * (swamp-engine/src/executor.rs:403-550 decode, :48-190 prefill). All are
+ * stream-ordered on the caller's stream (NULL = CUDA's default stream), take
+ * device pointers, need one device per process, and return once the work is
+ * enqueued. Per-row int32 arrays (pos, seq_len, seq, tokens) live in device
+ * memory so that a captured CUDA graph can be replayed with new positions.
+ * A device-side index out of range (position outside the cache, token
+ * outside the table, sequence outside the cache) skips that row's work and
+ * makes the next sg_synchronize return SG_ERR_DEVICE_FAULT. */
+typedef struct sg_rope_s *sg_rope_t;
+typedef struct sg_kv_cache_s *sg_kv_cache_t;
+
+/* init_rope_lut (swamp-engine/src/ops.rs:20-38): the f32 (cos, sin) table of
+ * theta = 10000 for head_dim and positions 0..max_context-1, computed with
+ * the host libm as the reference does and kept on the device.
+ * sg_rope_table copies it to host memory ([max_context][head_dim/2][2]). */
+SG_API int sg_rope_create(int head_dim, int max_context, sg_rope_t *out);
+SG_API int sg_rope_free(sg_rope_t rope);
+SG_API int sg_rope_table(sg_rope_t rope, float *dst);
+
+/* PagedKVCache::new (swamp-engine/src/cache.rs:55-100): K and V of n_seqs
+ * independent sequences, zero-filled, laid out
+ * [seq][layer][kv_head][max_seq][head_dim] f32 (the reference's pages of 32
+ * positions exist to move them to NVMe; here the cache stays resident).
+ * sg_kv_cache_ptr gives the device address of position 0 of one
+ * (seq, layer, kv_head); position p is p * head_dim floats further
+ * (get_k_unchecked / k_page_ptr, cache.rs:373-410). */
+SG_API int sg_kv_cache_create(int n_layers, int n_kv_heads, int head_dim, int max_seq, int n_seqs,
+                              sg_kv_cache_t *out);
+SG_API int sg_kv_cache_free(sg_kv_cache_t cache);
+SG_API int sg_kv_cache_ptr(sg_kv_cache_t cache, int seq, int layer, int kv_head, float **k, float **v);
+
+/* rmsnorm (ops.rs:188-201) of `rows` rows of n: out = x / sqrt(mean(x^2) + eps) * weight.
+ * out may equal x. */
+SG_API int sg_rmsnorm_device(const float *x, int64_t ldx, const float *weight, float *out, int64_t ldo, int n,
+                             int rows, float eps, void *stream);
+
+/* apply_rope_ufc (ops.rs:42-80) on q (n_q_heads heads) and k (the cache's
+ * n_kv_heads) of each row at position pos[r] (table row min(pos,
+ * max_context - 1)), in place, then PagedKVCache::save_at (cache.rs:412-434):
+ * k and v of row r go to position pos[r] of sequence seq[r] (seq NULL: 0) in
+ * `layer`. rope NULL stores k and v without rotating (q unused). */
+SG_API int sg_rope_kv_device(sg_rope_t rope, sg_kv_cache_t cache, int layer, float *q, int64_t ldq, float *k,
+                             int64_t ldk, const float *v, int64_t ldv, const int32_t *pos, const int32_t *seq,
+                             int rows, int n_q_heads, void *stream);
+
+/* attention (ops.rs:82-186): row r's n_heads query heads (q [rows][ldq],
+ * head h at h*head_dim) attend positions 0..min(pos[r], seq_len[r]-1) of
+ * sequence seq[r] (seq_len NULL: pos+1; seq NULL: 0), query head h reading
+ * KV head h / (n_heads / n_kv_heads); softmax of q.k / sqrt(head_dim);
+ * out [rows][ldo] gets the weighted sum of V. head_dim 64, 128 or 256, at
+ * most 8 query heads per KV head. The split partials live in a per-device
+ * workspace that grows on first use (make one call with the largest `rows`
+ * before capturing a graph) and is shared by all attention calls, so calls
+ * on different streams must be ordered. */
+SG_API int sg_attention_device(sg_kv_cache_t cache, int layer, const float *q, int64_t ldq, float *out, int64_t ldo,
+                               const int32_t *pos, const int32_t *seq_len, const int32_t *seq, int rows, int n_heads,
+                               void *stream);
+
+/* silu then mul_in_place (ops.rs:203-214): g = g / (1 + exp(-g)) * u. */
+SG_API int sg_silu_mul_device(float *g, int64_t ldg, const float *u, int64_t ldu, int n, int rows, void *stream);
+/* add_in_place (ops.rs:216-220): x += y. (A linear's SG_FLAG_ACCUMULATE
+ * adds its result into the residual stream in the same kernel.) */
+SG_API int sg_add_device(float *x, int64_t ldx, const float *y, int64_t ldy, int n, int rows, void *stream);
+/* Greedy decoding: out[r] = index of the largest logit of row r, the last
+ * of equal maxima (the sampler's max_by fallback, sampler.rs:94-95); -1 for
+ * a row holding a NaN (where the reference panics). */
+SG_API int sg_argmax_device(const float *logits, int64_t ld, int n, int rows, int32_t *out, void *stream);
+/* Embedding lookup (executor.rs:416-418): out[r] = row tokens[r] of the
+ * registered (replicated) table, dequantized bit-exactly; out 16-byte
+ * aligned, ldo % 4 == 0. */
+SG_API int sg_embed_device(sg_weight_t table, const int32_t *tokens, int rows, float *out, int64_t ldo,
+                           void *stream);
+
 #ifdef __cplusplus
 }
 #endif

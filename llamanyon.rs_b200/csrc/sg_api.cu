@@ -84,6 +84,8 @@ struct DevState {
   size_t ybuf_bytes = 0;
   float* rbuf = nullptr;  // packed row-split partials of strided device outputs
   size_t rbuf_bytes = 0;
+  float* attn_ws = nullptr;  // attention split partials (sg_attention_device)
+  size_t attn_ws_bytes = 0;
   float* hbuf = nullptr;  // pinned host staging
   size_t hbuf_bytes = 0;
   uint8_t* upbuf[2] = {nullptr, nullptr};  // pinned double buffer of weight uploads
@@ -235,7 +237,9 @@ int check_device_error(DevState& d) {
   if (v != 0) {
     int z = 0;
     cudaMemcpyToSymbol(g_sg_error, &z, sizeof(int));
-    return fail(SG_ERR_DEVICE_FAULT, "device %d: kernel wait gave up (code 0x%x)", d.device, v);
+    return fail(SG_ERR_DEVICE_FAULT, "device %d: %s (code 0x%x)", d.device,
+                v == 0x300 ? "a kernel read a position, token or sequence index out of range"
+                           : v == 0x200 ? "a kernel was launched with bad arguments" : "a kernel wait gave up", v);
   }
   return SG_OK;
 }
@@ -275,6 +279,7 @@ void release_devices() {
     if (d.xbuf) cudaFree(d.xbuf);
     if (d.ybuf) cudaFree(d.ybuf);
     if (d.rbuf) cudaFree(d.rbuf);
+    if (d.attn_ws) cudaFree(d.attn_ws);
     if (d.hbuf) cudaFreeHost(d.hbuf);
     for (int i = 0; i < 2; ++i) {
       if (d.upbuf[i]) cudaFreeHost(d.upbuf[i]);
@@ -585,13 +590,28 @@ cudaError_t upload_rows(DevState& d, uint8_t* dst, const uint8_t* src, size_t ro
   }
   return cudaSuccess;
 }
-}  // namespace
 
-int sg_weight_register(const void* host_blocks, int dtype, int64_t n_rows, int64_t n_cols, int tp_mode,
-                       sg_weight_t* out) {
-  std::lock_guard<std::mutex> lk(g_ctx.mu);
+// Fills a rank's raw GGUF block buffer on its device: rows [row0, row0+nr)
+// and blocks [cb0, cb0+ncb) of every row, row-major with ncb*block_bytes per
+// row. Host uploads and the on-device synthetic generator implement it.
+struct RawFill {
+  virtual cudaError_t fill(DevState& d, uint8_t* raw, int64_t row0, int64_t nr, int64_t cb0, int64_t ncb) = 0;
+  virtual ~RawFill() {}
+};
+
+struct HostFill : RawFill {
+  const uint8_t* blocks;
+  size_t row_bytes, bb;
+  cudaError_t fill(DevState& d, uint8_t* raw, int64_t row0, int64_t nr, int64_t cb0, int64_t ncb) override {
+    return upload_rows(d, raw, blocks + (size_t)row0 * row_bytes + (size_t)cb0 * bb, row_bytes, (size_t)ncb * bb, nr);
+  }
+};
+
+// Validate, shard, fill the raw blocks of each local shard on its device and
+// repack them into the tile layout. Called with g_ctx.mu held.
+int register_weight(RawFill& src, int dtype, int64_t n_rows, int64_t n_cols, int tp_mode, sg_weight_t* out) {
   if (!g_ctx.inited) return fail(SG_ERR_NOT_INITIALIZED, "sg_init not called");
-  if (!host_blocks || !out) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (!out) return fail(SG_ERR_INVALID_ARG, "null pointer");
   const int W = g_ctx.world;
   for (int R = 0; R < W; ++R) {  // validates the arguments for every rank's slice
     int64_t r0, nr, c0, nc;
@@ -599,8 +619,6 @@ int sg_weight_register(const void* host_blocks, int dtype, int64_t n_rows, int64
     if (rc != SG_OK) return rc;
   }
   const int64_t bs = block_of(dtype), bb = block_bytes(dtype);
-  const int64_t nblk = n_cols / bs;
-  const size_t row_bytes = (size_t)nblk * bb;
   auto* w = new sg_weight_s();
   w->dtype = dtype;
   w->n_rows = n_rows;
@@ -629,9 +647,7 @@ int sg_weight_register(const void* host_blocks, int dtype, int64_t n_rows, int64
       rc = fail(SG_ERR_OOM, "device %d: cannot allocate upload staging", d.device);
       break;
     }
-    const uint8_t* src = static_cast<const uint8_t*>(host_blocks) + (size_t)s.row0 * row_bytes +
-                         (size_t)(s.col0 / bs) * bb;
-    cudaError_t e = upload_rows(d, raw, src, row_bytes, lrow, nr);
+    cudaError_t e = src.fill(d, raw, s.row0, nr, s.col0 / bs, nc / bs);
     if (e == cudaSuccess) e = sg_layout_repack(&s.w, raw, d.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(d.stream);
     cudaFree(raw);
@@ -652,6 +668,18 @@ int sg_weight_register(const void* host_blocks, int dtype, int64_t n_rows, int64
   }
   *out = w;
   return SG_OK;
+}
+}  // namespace
+
+int sg_weight_register(const void* host_blocks, int dtype, int64_t n_rows, int64_t n_cols, int tp_mode,
+                       sg_weight_t* out) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!host_blocks) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  HostFill f;
+  f.blocks = static_cast<const uint8_t*>(host_blocks);
+  f.bb = (size_t)block_bytes(dtype);
+  f.row_bytes = (size_t)(n_cols / std::max<int64_t>(1, block_of(dtype))) * f.bb;
+  return register_weight(f, dtype, n_rows, n_cols, tp_mode, out);
 }
 
 int sg_weight_free(sg_weight_t w) {

@@ -154,19 +154,13 @@ __global__ void repack_q4k_dd_kernel(const uint8_t* __restrict__ raw, int64_t n_
   dd[tid] = out;
 }
 
-// Dequantize 8 consecutive k of one row per thread.
-__global__ void dequant_kernel(SgDevWeight w, float* __restrict__ dst, int64_t ld) {
-  const int64_t kq = w.n_cols / 8;
-  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (tid >= w.n_rows * kq) return;
-  const int64_t row = tid / kq;
-  const int64_t k0 = (tid % kq) * 8;
+// The 8 weights k0 .. k0+7 (k0 % 8 == 0) of one row, bit-exact.
+__device__ __forceinline__ void dequant8(const SgDevWeight& w, int64_t row, int64_t k0, float out[8]) {
   const int64_t rb = row >> 7;
   const int r = (int)(row & 127);
   const int64_t c = k0 >> 6;
   const int kk0 = (int)(k0 & 63);
   const uint8_t* tile = w.tiles + (rb * w.n_ch + c) * sg_tile_bytes(w.dtype);
-  float out[8];
   if (w.dtype == SG_DTYPE_Q6_K) {
     // q6_k.rs:37-46: w = d * (f32)sc * (f32)(q - 32), both products exact
     const uint32_t scw = reinterpret_cast<const uint32_t*>(tile + SG_TILE6_SC_OFF)[r];
@@ -181,9 +175,6 @@ __global__ void dequant_kernel(SgDevWeight w, float* __restrict__ dst, int64_t l
       const float sc = (float)(int8_t)(scw >> (8 * ((kk & 63) >> 4)));
       out[i] = __fmul_rn(__fmul_rn(d, sc), (float)(q - 32));
     }
-    float4* o = reinterpret_cast<float4*>(dst + row * ld + k0);
-    o[0] = make_float4(out[0], out[1], out[2], out[3]);
-    o[1] = make_float4(out[4], out[5], out[6], out[7]);
     return;
   }
   const uint32_t scw = reinterpret_cast<const uint32_t*>(tile + SG_TILE_SC_OFF)[r];
@@ -209,6 +200,17 @@ __global__ void dequant_kernel(SgDevWeight w, float* __restrict__ dst, int64_t l
       out[i] = __fsub_rn(__fmul_rn(sv, (float)q), mv);
     }
   }
+}
+
+// Dequantize 8 consecutive k of one row per thread.
+__global__ void dequant_kernel(SgDevWeight w, float* __restrict__ dst, int64_t ld) {
+  const int64_t kq = w.n_cols / 8;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (tid >= w.n_rows * kq) return;
+  const int64_t row = tid / kq;
+  const int64_t k0 = (tid % kq) * 8;
+  float out[8];
+  dequant8(w, row, k0, out);
   float4* o = reinterpret_cast<float4*>(dst + row * ld + k0);
   o[0] = make_float4(out[0], out[1], out[2], out[3]);
   o[1] = make_float4(out[4], out[5], out[6], out[7]);

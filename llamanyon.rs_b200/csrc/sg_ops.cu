@@ -1,0 +1,722 @@
+// sg_ops.cu -- the non-matmul layer operations of a decoder layer on the GPU,
+// so that an engine keeps its activations in device memory between the
+// quantized linears (swamp-engine/src/executor.rs:403-550 decode step,
+// :48-190 batched prefill).
+//
+//   sg_rmsnorm_device    ops.rs:188-201   rmsnorm
+//   sg_rope_create       ops.rs:20-38     init_rope_lut (f32 table, same libm)
+//   sg_rope_kv_device    ops.rs:42-80     apply_rope_ufc, then
+//                        cache.rs:348-371,412-434  PagedKVCache::save / save_at
+//   sg_attention_device  ops.rs:82-186    attention (GQA, causal, softmax)
+//   sg_silu_mul_device   ops.rs:203-214   silu, mul_in_place
+//   sg_add_device        ops.rs:216-220   add_in_place
+//   sg_argmax_device     sampler.rs:94-95 greedy pick (the sampler's fallback)
+//   sg_embed_device      executor.rs:416-418 embedding row copy, dequantized
+//                        from the GGUF tensor on the device
+//
+// Numerics. RoPE applies the reference's f32 table with the reference's
+// operation order and no FMA contraction: bit-exact. Residual add, SiLU-mul's
+// multiply and the embedding rows are exact or single IEEE operations
+// (SiLU's exp is CUDA's expf, within 2 ulp of the host libm). RMSNorm and
+// attention sum in a different order than the reference's sequential loops:
+// tolerance-bound.
+//
+// KV cache layout. The reference pages its cache in blocks of 32 positions
+// with [layer][kv_head][slot][head_dim] per page so that pages can move to
+// NVMe. On a 180 GB GPU the cache stays resident, so it is one array per K
+// and V: [seq][layer][kv_head][max_seq][head_dim] f32. The positions of one
+// (seq, layer, head) are contiguous, and so is any run of them that an
+// attention split reads.
+#include <cmath>
+
+struct sg_rope_s {
+  int head_dim = 0, max_context = 0, device = -1;
+  float2* lut = nullptr;  // [max_context][head_dim/2] (cos, sin)
+};
+
+struct sg_kv_cache_s {
+  int n_layers = 0, n_kv_heads = 0, head_dim = 0, max_seq = 0, n_seqs = 0, device = -1;
+  float* k = nullptr;
+  float* v = nullptr;
+  __host__ __device__ size_t head_off(int seq, int layer, int kvh) const {
+    return (((size_t)seq * n_layers + layer) * n_kv_heads + kvh) * (size_t)max_seq * head_dim;
+  }
+};
+
+namespace ops {
+
+#define SG_DEVERR_BAD_INPUT 0x300  // a device-side index (position, token, sequence) out of range
+
+struct KvView {  // the cache geometry passed by value to kernels
+  int n_layers, n_kv_heads, head_dim, max_seq, n_seqs;
+  float* k;
+  float* v;
+  __device__ size_t head_off(int seq, int layer, int kvh) const {
+    return (((size_t)seq * n_layers + layer) * n_kv_heads + kvh) * (size_t)max_seq * head_dim;
+  }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ------------------------------------------------------------------ rmsnorm
+// One CTA per row: ss = sum x^2, ss /= n, ss += eps, inv = 1 / sqrt(ss),
+// out = (x * inv) * w, each step one IEEE operation as in ops.rs:190-199;
+// only the summation order of ss differs (a tree instead of a running sum).
+constexpr int kNormThreads = 256;
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* x, int64_t ldx, const float* __restrict__ w,
+                                                              float* out, int64_t ldo, int n, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  const float* xr = x + (int64_t)blockIdx.x * ldx;
+  float* orow = out + (int64_t)blockIdx.x * ldo;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += kNormThreads) ss = __fmaf_rn(xr[i], xr[i], ss);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) ss += red[i];
+  ss = __fdiv_rn(ss, (float)n);
+  ss = __fadd_rn(ss, eps);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ss));
+  for (int i = threadIdx.x; i < n; i += kNormThreads) orow[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+}
+
+// -------------------------------------------------------- RoPE + cache store
+// One CTA per row. Pair k of every head: (x, y) -> (x cos - y sin, x sin + y cos)
+// with each product rounded before the add (ops.rs:77-78). The table row is
+// min(pos, max_context - 1) (ops.rs:54). Rotated k and the row's v are then
+// stored at position pos of sequence seq in layer `layer` (cache.rs:348-371).
+// lut == nullptr stores without rotating.
+__global__ void rope_kv_kernel(const float2* __restrict__ lut, int max_context, KvView kv, int layer, float* q,
+                               int64_t ldq, float* k, int64_t ldk, const float* v, int64_t ldv, const int32_t* pos,
+                               const int32_t* seq, int n_q_heads) {
+  const int r = blockIdx.x;
+  const int p = pos[r];
+  const int s = seq ? seq[r] : 0;
+  const int hd = kv.head_dim, half = hd >> 1;
+  const bool store_ok = p >= 0 && p < kv.max_seq && s >= 0 && s < kv.n_seqs;
+  if (!store_ok || (lut && p < 0)) {
+    if (threadIdx.x == 0) sg_set_error(SG_DEVERR_BAD_INPUT);
+    return;
+  }
+  if (lut) {
+    const float2* row = lut + (int64_t)min(p, max_context - 1) * half;
+    float* qr = q + (int64_t)r * ldq;
+    for (int i = threadIdx.x; i < n_q_heads * half; i += blockDim.x) {
+      const int h = i / half, j = i - h * half;
+      float* e = qr + h * hd + 2 * j;
+      const float x0 = e[0], y0 = e[1];
+      const float2 cs = row[j];
+      e[0] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(y0, cs.y));
+      e[1] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(y0, cs.x));
+    }
+    float* kr = k + (int64_t)r * ldk;
+    for (int i = threadIdx.x; i < kv.n_kv_heads * half; i += blockDim.x) {
+      const int h = i / half, j = i - h * half;
+      float* e = kr + h * hd + 2 * j;
+      const float x0 = e[0], y0 = e[1];
+      const float2 cs = row[j];
+      const float a = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(y0, cs.y));
+      const float b = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(y0, cs.x));
+      e[0] = a;
+      e[1] = b;
+      float* c = kv.k + kv.head_off(s, layer, h) + (size_t)p * hd + 2 * j;
+      c[0] = a;
+      c[1] = b;
+    }
+  } else {
+    const float* kr = k + (int64_t)r * ldk;
+    for (int i = threadIdx.x; i < kv.n_kv_heads * hd; i += blockDim.x) {
+      const int h = i / hd, j = i - h * hd;
+      kv.k[kv.head_off(s, layer, h) + (size_t)p * hd + j] = kr[i];
+    }
+  }
+  const float* vr = v + (int64_t)r * ldv;
+  for (int i = threadIdx.x; i < kv.n_kv_heads * hd; i += blockDim.x) {
+    const int h = i / hd, j = i - h * hd;
+    kv.v[kv.head_off(s, layer, h) + (size_t)p * hd + j] = vr[i];
+  }
+}
+
+// ---------------------------------------------------------------- attention
+// Row r (one query token: sequence seq[r], position pos[r]) attends positions
+// 0 .. valid_end = min(pos, seq_len - 1) of its sequence (ops.rs:95), with
+// query head h reading KV head h / n_rep (ops.rs:94,105). Scores are
+// dot(q, k) * scale, softmax over them, out = sum p v (ops.rs:135-180).
+//
+// Split: CTAs of 128 threads take 128 positions of one (row, KV head) and all
+// n_rep query heads of that head, so each K and V row is read once per
+// query token. A thread scores one position against the n_rep queries
+// (queries in shared memory); each warp then sums p v over its 32 positions
+// with lanes owning head_dim/32 components. A CTA writes (max m, sum l of
+// exp(s - m), sum exp(s - m) v) per query head; the combine kernel rescales
+// the splits to the global max and divides by the global sum.
+constexpr int kAttnP = 128;  // positions per split (= threads per CTA)
+constexpr int kMaxRep = 8;   // query heads per KV head
+
+struct AttnArgs {
+  KvView kv;
+  int layer;
+  const float* q;
+  int64_t ldq;
+  const int32_t* pos;
+  const int32_t* seq_len;
+  const int32_t* seq;
+  int n_heads, n_rep, n_split;
+  float scale;
+  float* ws;  // [row][head][split][HD + 2]
+};
+
+__device__ __forceinline__ int attn_valid_end(const AttnArgs& a, int r) {
+  const int p = a.pos[r];
+  int e = p;
+  if (a.seq_len) e = min(e, a.seq_len[r] - 1);
+  return min(e, a.kv.max_seq - 1);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnP) attn_split_kernel(AttnArgs a) {
+  constexpr int DL = HD / 32;  // components per lane
+  __shared__ __align__(16) float qs[kMaxRep][HD];
+  __shared__ float sc[kMaxRep][kAttnP];
+  __shared__ __align__(16) float red[kAttnP / 32][kMaxRep][HD];
+  __shared__ float mls[kMaxRep][2];
+  const int sp = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int valid_end = attn_valid_end(a, r);
+  const int t0 = sp * kAttnP;
+  if (valid_end < 0 || t0 > valid_end) return;  // the combine reads splits 0 .. valid_end / 128 only
+  const int s = a.seq ? a.seq[r] : 0;
+  if (s < 0 || s >= a.kv.n_seqs) {
+    if (tid == 0) sg_set_error(SG_DEVERR_BAD_INPUT);
+    return;
+  }
+  const int n_rep = a.n_rep;
+  const float* qrow = a.q + (int64_t)r * a.ldq + (int64_t)g * n_rep * HD;
+  for (int i = tid; i < n_rep * HD; i += kAttnP) qs[i / HD][i % HD] = qrow[i];
+  __syncthreads();
+  const size_t hoff = a.kv.head_off(s, a.layer, g);
+  const float* kb = a.kv.k + hoff;
+  const float* vb = a.kv.v + hoff;
+  // scores: this thread's position against every query head of the group
+  {
+    const int t = t0 + tid;
+    float acc[kMaxRep];
+#pragma unroll
+    for (int j = 0; j < kMaxRep; ++j) acc[j] = 0.f;
+    if (t <= valid_end) {
+      const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)t * HD);
+#pragma unroll 4
+      for (int d4 = 0; d4 < HD / 4; ++d4) {
+        const float4 kv4 = kr[d4];
+#pragma unroll
+        for (int j = 0; j < kMaxRep; ++j) {
+          if (j < n_rep) {
+            const float4 q4 = *reinterpret_cast<const float4*>(&qs[j][4 * d4]);
+            acc[j] = fmaf(q4.x, kv4.x, acc[j]);
+            acc[j] = fmaf(q4.y, kv4.y, acc[j]);
+            acc[j] = fmaf(q4.z, kv4.z, acc[j]);
+            acc[j] = fmaf(q4.w, kv4.w, acc[j]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxRep; ++j)
+      if (j < n_rep) sc[j][tid] = t <= valid_end ? acc[j] * a.scale : -INFINITY;
+  }
+  __syncthreads();
+  // split max and exp per query head (one warp per head)
+  for (int j = warp; j < n_rep; j += kAttnP / 32) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kAttnP / 32; ++i) m = fmaxf(m, sc[j][lane + 32 * i]);
+    m = warp_max(m);
+    float l = 0.f;
+#pragma unroll
+    for (int i = 0; i < kAttnP / 32; ++i) {
+      const float e = expf(sc[j][lane + 32 * i] - m);  // exp(-inf) = 0 past valid_end
+      sc[j][lane + 32 * i] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      mls[j][0] = m;
+      mls[j][1] = l;
+    }
+  }
+  __syncthreads();
+  // sum p v over this warp's 32 positions, lanes owning DL components each
+  {
+    float acc[kMaxRep][DL];
+#pragma unroll
+    for (int j = 0; j < kMaxRep; ++j)
+#pragma unroll
+      for (int c = 0; c < DL; ++c) acc[j][c] = 0.f;
+    const int tw = t0 + warp * 32;
+    const int nt = min(32, valid_end - tw + 1);
+    for (int i = 0; i < nt; ++i) {
+      const float* vr = vb + (size_t)(tw + i) * HD + lane * DL;
+      float vv[DL];
+      if constexpr (DL == 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(vr);
+        vv[0] = v4.x;
+        vv[1] = v4.y;
+        vv[2] = v4.z;
+        vv[3] = v4.w;
+      } else if constexpr (DL == 2) {
+        const float2 v2 = *reinterpret_cast<const float2*>(vr);
+        vv[0] = v2.x;
+        vv[1] = v2.y;
+      } else {
+#pragma unroll
+        for (int c = 0; c < DL; ++c) vv[c] = vr[c];
+      }
+#pragma unroll
+      for (int j = 0; j < kMaxRep; ++j) {
+        if (j < n_rep) {
+          const float pj = sc[j][warp * 32 + i];
+#pragma unroll
+          for (int c = 0; c < DL; ++c) acc[j][c] = fmaf(pj, vv[c], acc[j][c]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxRep; ++j)
+      if (j < n_rep)
+#pragma unroll
+        for (int c = 0; c < DL; ++c) red[warp][j][lane * DL + c] = acc[j][c];
+  }
+  __syncthreads();
+  for (int i = tid; i < n_rep * HD; i += kAttnP) {
+    const int j = i / HD, d = i - j * HD;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnP / 32; ++w) v += red[w][j][d];
+    float* rec = a.ws + (((int64_t)r * a.n_heads + g * n_rep + j) * a.n_split + sp) * (HD + 2);
+    rec[2 + d] = v;
+    if (d == 0) {
+      rec[0] = mls[j][0];
+      rec[1] = mls[j][1];
+    }
+  }
+}
+
+// One CTA of HD threads per (query head, row): out[d] = sum_s e_s acc_s[d] / L
+// with e_s = exp(m_s - M), M = max m_s, L = sum e_s l_s.
+template <int HD>
+__global__ void __launch_bounds__(HD) attn_combine_kernel(AttnArgs a, float* out, int64_t ldo) {
+  const int h = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
+  const int valid_end = attn_valid_end(a, r);
+  float* o = out + (int64_t)r * ldo + (int64_t)h * HD;
+  if (valid_end < 0) {
+    o[d] = 0.f;
+    return;
+  }
+  const int ns = valid_end / kAttnP + 1;
+  const float* rec = a.ws + ((int64_t)r * a.n_heads + h) * a.n_split * (HD + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, rec[s * (HD + 2)]);
+  float L = 0.f, acc = 0.f;
+  for (int s = 0; s < ns; ++s) {
+    const float e = expf(rec[s * (HD + 2)] - M);
+    L = fmaf(e, rec[s * (HD + 2) + 1], L);
+    acc = fmaf(e, rec[s * (HD + 2) + 2 + d], acc);
+  }
+  o[d] = acc / L;
+}
+
+// ------------------------------------------------------------- elementwise
+// g = silu(g) * u with silu(v) = v / (1 + exp(-v)) (ops.rs:203-214).
+__global__ void silu_mul_kernel(float* g, int64_t ldg, const float* u, int64_t ldu, int n, int64_t total) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / n, c = i - row * n;
+    float* gp = g + row * ldg + c;
+    const float v = *gp;
+    const float sv = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+    *gp = __fmul_rn(sv, u[row * ldu + c]);
+  }
+}
+
+// x += y (ops.rs:216-220).
+__global__ void add_kernel(float* x, int64_t ldx, const float* y, int64_t ldy, int n, int64_t total) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / n, c = i - row * n;
+    x[row * ldx + c] = __fadd_rn(x[row * ldx + c], y[row * ldy + c]);
+  }
+}
+
+// ------------------------------------------------------------------- argmax
+// Greedy pick: the index of the largest logit, the LAST one among equals
+// (Iterator::max_by keeps the last maximum, sampler.rs:95; -0.0 == +0.0).
+// A row holding a NaN, where the reference's partial_cmp().unwrap() panics,
+// gives -1.
+constexpr int kArgThreads = 1024;
+__device__ __forceinline__ void arg_better(float& bv, int& bi, float v, int i) {
+  if (v > bv || (v == bv && i > bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+__global__ void __launch_bounds__(kArgThreads) argmax_kernel(const float* logits, int64_t ld, int n, int32_t* out) {
+  __shared__ float sv[kArgThreads / 32];
+  __shared__ int si[kArgThreads / 32];
+  __shared__ int nan_seen;
+  if (threadIdx.x == 0) nan_seen = 0;
+  __syncthreads();
+  const float* row = logits + (int64_t)blockIdx.x * ld;
+  float bv = -INFINITY;
+  int bi = -1;
+  bool nan = false;
+  for (int i = threadIdx.x; i < n; i += kArgThreads) {
+    const float v = row[i];
+    nan |= v != v;
+    arg_better(bv, bi, v, i);
+  }
+  if (nan) nan_seen = 1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (oi >= 0) arg_better(bv, bi, ov, oi);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = bv;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = sv[0];
+    int idx = si[0];
+    for (int w = 1; w < kArgThreads / 32; ++w)
+      if (si[w] >= 0) arg_better(v, idx, sv[w], si[w]);
+    if (idx < 0) idx = n - 1;  // every logit is -inf: the last one
+    out[blockIdx.x] = nan_seen ? -1 : idx;
+  }
+}
+
+// ---------------------------------------------------------------- embedding
+// out[r] = row tokens[r] of the dequantized table (bit-exact with swamp-gguf's
+// dequant, which the reference applies to the whole table at load,
+// executor.rs:212).
+__global__ void embed_kernel(SgDevWeight w, const int32_t* tokens, float* out, int64_t ldo) {
+  const int r = blockIdx.y;
+  const int64_t k0 = 8 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+  if (k0 >= w.n_cols) return;
+  const int tok = tokens[r];
+  float* o = out + (int64_t)r * ldo + k0;
+  if (tok < 0 || tok >= w.n_rows) {
+    if (k0 == 0) sg_set_error(SG_DEVERR_BAD_INPUT);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = 0.f;
+    return;
+  }
+  float v[8];
+  dequant8(w, tok, k0, v);
+  reinterpret_cast<float4*>(o)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(o)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+unsigned ew_grid(int64_t total, int num_sms) {
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)num_sms * 8));
+}
+
+}  // namespace ops
+
+namespace {
+// The single device that the op entry points run on.
+int op_device(DevState** out) {
+  if (!g_ctx.inited) return fail(SG_ERR_NOT_INITIALIZED, "sg_init not called");
+  if (g_ctx.devs.size() != 1) return fail(SG_ERR_INVALID_ARG, "device entry points need one device per process");
+  *out = &g_ctx.devs[0];
+  CUDA_TRY(cudaSetDevice((*out)->device));
+  return SG_OK;
+}
+
+ops::KvView kv_view(const sg_kv_cache_s* c) {
+  return ops::KvView{c->n_layers, c->n_kv_heads, c->head_dim, c->max_seq, c->n_seqs, c->k, c->v};
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+}  // namespace
+
+extern "C" {
+
+int sg_rope_create(int head_dim, int max_context, sg_rope_t* out) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  if (!out) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (head_dim < 2 || (head_dim & 1) || max_context < 1)
+    return fail(SG_ERR_INVALID_ARG, "head_dim %d must be even and >= 2, max_context %d >= 1", head_dim, max_context);
+  // init_rope_lut (ops.rs:27-36) in f32 with the host libm the reference
+  // calls (powf, cosf, sinf), so the table is the reference's bit for bit
+  const int half = head_dim / 2;
+  std::vector<float2> lut((size_t)max_context * half);
+  const float theta = 10000.0f;
+  for (int k = 0; k < half; ++k) {
+    const float e = (float)(2 * k) / (float)head_dim;
+    const float freq = 1.0f / powf(theta, e);
+    for (int m = 0; m < max_context; ++m) {
+      const float angle = (float)m * freq;
+      lut[(size_t)m * half + k] = make_float2(cosf(angle), sinf(angle));
+    }
+  }
+  auto* r = new sg_rope_s();
+  r->head_dim = head_dim;
+  r->max_context = max_context;
+  r->device = d->device;
+  if (cudaMalloc(&r->lut, lut.size() * sizeof(float2)) != cudaSuccess) {
+    cudaGetLastError();
+    delete r;
+    return fail(SG_ERR_OOM, "cannot allocate the RoPE table");
+  }
+  cudaError_t e = cudaMemcpy(r->lut, lut.data(), lut.size() * sizeof(float2), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(r->lut);
+    delete r;
+    return fail(SG_ERR_CUDA, "RoPE table upload: %s", cudaGetErrorString(e));
+  }
+  *out = r;
+  return SG_OK;
+}
+
+int sg_rope_free(sg_rope_t r) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!r) return fail(SG_ERR_INVALID_ARG, "null handle");
+  cudaSetDevice(r->device);
+  cudaFree(r->lut);
+  delete r;
+  return SG_OK;
+}
+
+int sg_rope_table(sg_rope_t r, float* dst) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!r || !dst) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  CUDA_TRY(cudaSetDevice(r->device));
+  CUDA_TRY(cudaMemcpy(dst, r->lut, (size_t)r->max_context * (r->head_dim / 2) * sizeof(float2), cudaMemcpyDeviceToHost));
+  return SG_OK;
+}
+
+int sg_kv_cache_create(int n_layers, int n_kv_heads, int head_dim, int max_seq, int n_seqs, sg_kv_cache_t* out) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  if (!out) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (n_layers < 1 || n_kv_heads < 1 || head_dim < 1 || max_seq < 1 || n_seqs < 1 || (head_dim & 3))
+    return fail(SG_ERR_INVALID_ARG, "bad cache geometry (layers %d, kv heads %d, head_dim %d (multiple of 4), max_seq %d, seqs %d)",
+                n_layers, n_kv_heads, head_dim, max_seq, n_seqs);
+  auto* c = new sg_kv_cache_s();
+  c->n_layers = n_layers;
+  c->n_kv_heads = n_kv_heads;
+  c->head_dim = head_dim;
+  c->max_seq = max_seq;
+  c->n_seqs = n_seqs;
+  c->device = d->device;
+  const size_t bytes = c->head_off(n_seqs, 0, 0) * sizeof(float);
+  if (cudaMalloc(&c->k, bytes) != cudaSuccess || cudaMalloc(&c->v, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(c->k);
+    delete c;
+    return fail(SG_ERR_OOM, "cannot allocate 2 x %zu bytes of KV cache", bytes);
+  }
+  // pages start zeroed like the reference's alloc_zeroed pages (cache.rs:136)
+  cudaError_t e = cudaMemset(c->k, 0, bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->v, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(c->k);
+    cudaFree(c->v);
+    delete c;
+    return fail(SG_ERR_CUDA, "KV cache clear: %s", cudaGetErrorString(e));
+  }
+  *out = c;
+  return SG_OK;
+}
+
+int sg_kv_cache_free(sg_kv_cache_t c) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!c) return fail(SG_ERR_INVALID_ARG, "null handle");
+  cudaSetDevice(c->device);
+  cudaFree(c->k);
+  cudaFree(c->v);
+  delete c;
+  return SG_OK;
+}
+
+int sg_kv_cache_ptr(sg_kv_cache_t c, int seq, int layer, int kv_head, float** k, float** v) {
+  if (!c || !k || !v) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (seq < 0 || seq >= c->n_seqs || layer < 0 || layer >= c->n_layers || kv_head < 0 || kv_head >= c->n_kv_heads)
+    return fail(SG_ERR_INVALID_ARG, "seq %d / layer %d / kv head %d out of range", seq, layer, kv_head);
+  *k = c->k + c->head_off(seq, layer, kv_head);
+  *v = c->v + c->head_off(seq, layer, kv_head);
+  return SG_OK;
+}
+
+int sg_rmsnorm_device(const float* x, int64_t ldx, const float* weight, float* out, int64_t ldo, int n, int rows,
+                      float eps, void* stream) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  if (rows < 0 || n < 1 || ldx < n || ldo < n) return fail(SG_ERR_INVALID_ARG, "bad sizes (n %d, rows %d)", n, rows);
+  if (!x || !weight || !out) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (rows == 0) return SG_OK;
+  ops::rmsnorm_kernel<<<rows, ops::kNormThreads, 0, (cudaStream_t)stream>>>(x, ldx, weight, out, ldo, n, eps);
+  CUDA_TRY(cudaGetLastError());
+  return SG_OK;
+}
+
+int sg_rope_kv_device(sg_rope_t rope, sg_kv_cache_t cache, int layer, float* q, int64_t ldq, float* k, int64_t ldk,
+                      const float* v, int64_t ldv, const int32_t* pos, const int32_t* seq, int rows, int n_q_heads,
+                      void* stream) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  if (!cache || !k || !v || !pos || (rope && !q)) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (layer < 0 || layer >= cache->n_layers) return fail(SG_ERR_INVALID_ARG, "layer %d out of range", layer);
+  if (rows < 0) return fail(SG_ERR_INVALID_ARG, "negative rows");
+  const int hd = cache->head_dim, nkv = cache->n_kv_heads;
+  if (ldk < (int64_t)nkv * hd || ldv < (int64_t)nkv * hd)
+    return fail(SG_ERR_INVALID_ARG, "k/v row stride below n_kv_heads * head_dim");
+  if (rope) {
+    if (rope->head_dim != hd) return fail(SG_ERR_INVALID_ARG, "RoPE head_dim %d != cache head_dim %d", rope->head_dim, hd);
+    if (n_q_heads < 1 || ldq < (int64_t)n_q_heads * hd) return fail(SG_ERR_INVALID_ARG, "bad q heads / stride");
+  }
+  if (rows == 0) return SG_OK;
+  ops::rope_kv_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(rope ? rope->lut : nullptr, rope ? rope->max_context : 1,
+                                                              kv_view(cache), layer, q, ldq, k, ldk, v, ldv, pos, seq,
+                                                              n_q_heads);
+  CUDA_TRY(cudaGetLastError());
+  return SG_OK;
+}
+
+int sg_attention_device(sg_kv_cache_t cache, int layer, const float* q, int64_t ldq, float* out, int64_t ldo,
+                        const int32_t* pos, const int32_t* seq_len, const int32_t* seq, int rows, int n_heads,
+                        void* stream) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  if (!cache || !q || !out || !pos) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (layer < 0 || layer >= cache->n_layers) return fail(SG_ERR_INVALID_ARG, "layer %d out of range", layer);
+  const int hd = cache->head_dim, nkv = cache->n_kv_heads;
+  if (hd != 64 && hd != 128 && hd != 256) return fail(SG_ERR_UNSUPPORTED, "head_dim %d (64, 128 or 256)", hd);
+  if (n_heads < nkv || n_heads % nkv || n_heads / nkv > ops::kMaxRep)
+    return fail(SG_ERR_UNSUPPORTED, "n_heads %d over %d KV heads (a multiple, at most %d per KV head)", n_heads, nkv,
+                ops::kMaxRep);
+  if (rows < 0 || ldq < (int64_t)n_heads * hd || ldo < (int64_t)n_heads * hd)
+    return fail(SG_ERR_INVALID_ARG, "bad rows or strides");
+  if (!aligned16(q) || (ldq & 3)) return fail(SG_ERR_INVALID_ARG, "q must be 16-byte aligned with ldq % 4 == 0");
+  if (rows == 0) return SG_OK;
+  ops::AttnArgs a;
+  a.kv = kv_view(cache);
+  a.layer = layer;
+  a.q = q;
+  a.ldq = ldq;
+  a.pos = pos;
+  a.seq_len = seq_len;
+  a.seq = seq;
+  a.n_heads = n_heads;
+  a.n_rep = n_heads / nkv;
+  a.n_split = (cache->max_seq + ops::kAttnP - 1) / ops::kAttnP;
+  a.scale = 1.0f / sqrtf((float)hd);  // ops.rs:93
+  const size_t ws_bytes = (size_t)rows * n_heads * a.n_split * (hd + 2) * sizeof(float);
+  rc = ensure_buf((void**)&d->attn_ws, &d->attn_ws_bytes, ws_bytes);
+  if (rc) return rc;
+  a.ws = d->attn_ws;
+  cudaStream_t st = (cudaStream_t)stream;
+  const dim3 g1(a.n_split, nkv, rows), g2(n_heads, rows);
+  switch (hd) {
+    case 64:
+      ops::attn_split_kernel<64><<<g1, ops::kAttnP, 0, st>>>(a);
+      ops::attn_combine_kernel<64><<<g2, 64, 0, st>>>(a, out, ldo);
+      break;
+    case 128:
+      ops::attn_split_kernel<128><<<g1, ops::kAttnP, 0, st>>>(a);
+      ops::attn_combine_kernel<128><<<g2, 128, 0, st>>>(a, out, ldo);
+      break;
+    default:
+      ops::attn_split_kernel<256><<<g1, ops::kAttnP, 0, st>>>(a);
+      ops::attn_combine_kernel<256><<<g2, 256, 0, st>>>(a, out, ldo);
+  }
+  CUDA_TRY(cudaGetLastError());
+  return SG_OK;
+}
+
+int sg_silu_mul_device(float* g, int64_t ldg, const float* u, int64_t ldu, int n, int rows, void* stream) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  if (!g || !u) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (n < 1 || rows < 0 || ldg < n || ldu < n) return fail(SG_ERR_INVALID_ARG, "bad sizes");
+  const int64_t total = (int64_t)n * rows;
+  if (total == 0) return SG_OK;
+  ops::silu_mul_kernel<<<ops::ew_grid(total, d->num_sms), 256, 0, (cudaStream_t)stream>>>(g, ldg, u, ldu, n, total);
+  CUDA_TRY(cudaGetLastError());
+  return SG_OK;
+}
+
+int sg_add_device(float* x, int64_t ldx, const float* y, int64_t ldy, int n, int rows, void* stream) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  if (!x || !y) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (n < 1 || rows < 0 || ldx < n || ldy < n) return fail(SG_ERR_INVALID_ARG, "bad sizes");
+  const int64_t total = (int64_t)n * rows;
+  if (total == 0) return SG_OK;
+  ops::add_kernel<<<ops::ew_grid(total, d->num_sms), 256, 0, (cudaStream_t)stream>>>(x, ldx, y, ldy, n, total);
+  CUDA_TRY(cudaGetLastError());
+  return SG_OK;
+}
+
+int sg_argmax_device(const float* logits, int64_t ld, int n, int rows, int32_t* out, void* stream) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  if (!logits || !out) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (n < 1 || rows < 0 || ld < n) return fail(SG_ERR_INVALID_ARG, "bad sizes");
+  if (rows == 0) return SG_OK;
+  ops::argmax_kernel<<<rows, ops::kArgThreads, 0, (cudaStream_t)stream>>>(logits, ld, n, out);
+  CUDA_TRY(cudaGetLastError());
+  return SG_OK;
+}
+
+int sg_embed_device(sg_weight_t table, const int32_t* tokens, int rows, float* out, int64_t ldo, void* stream) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  rc = validate_weight(table);
+  if (rc) return rc;
+  if (table->tp_mode != SG_TP_REPLICATE && g_ctx.world > 1)
+    return fail(SG_ERR_INVALID_ARG, "the embedding table must be replicated");
+  if (!tokens || !out) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  const SgDevWeight& w = table->shards[0].w;
+  if (rows < 0 || ldo < w.n_cols) return fail(SG_ERR_INVALID_ARG, "bad rows or ldo");
+  if (!aligned16(out) || (ldo & 3)) return fail(SG_ERR_INVALID_ARG, "out must be 16-byte aligned with ldo % 4 == 0");
+  if (rows == 0) return SG_OK;
+  const int64_t per_row = w.n_cols / 8;
+  const dim3 grid((unsigned)((per_row + 127) / 128), (unsigned)rows);
+  ops::embed_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(w, tokens, out, ldo);
+  CUDA_TRY(cudaGetLastError());
+  return SG_OK;
+}
+
+}  // extern "C"

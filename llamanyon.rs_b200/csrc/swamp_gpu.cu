@@ -8,5 +8,7 @@
 #include "sg_gemv_q6k.cu"
 #include "sg_gemm.cu"
 #include "sg_api.cu"
+#include "sg_synth.cu"
+#include "sg_ops.cu"
 #include "sg_noalloc.cu"
 #include "sg_gguf.cu"

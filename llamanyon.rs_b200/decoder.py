@@ -1,0 +1,179 @@
+"""A device-resident decoder forward over the C ABI of libswamp_gpu.so.
+
+Host-side mirror of swamp-engine's inference loop (executor.rs:403-550 for
+one decode step, executor.rs:48-190 for the batched prompt prefill) in which
+every tensor stays in GPU memory: the embedding row, RMSNorm, the quantized
+Q/K/V, O, gate/up and down linears, RoPE with the KV-cache store, attention,
+SiLU-mul, the residual adds (folded into the O and down linears with
+SG_FLAG_ACCUMULATE), the final norm, the output head and the greedy pick.
+A Rust engine makes the same calls through the FFI; torch here only owns
+device buffers and streams.
+
+Rows are query tokens: one per sequence in a decode step, all prompt
+positions in a prefill. Each row carries (token, position, sequence) in
+device int32 arrays, so a step captured in a CUDA graph replays with new
+positions. Several sequences share the batch (the benchmark's batch 8) with
+their own KV-cache slots.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+import swamp_gpu as sg
+
+ROLES = ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down")
+
+
+@dataclass
+class DecoderConfig:
+    """Llama-style architecture (swamp-engine/src/model.rs config fields)."""
+    n_layers: int
+    d: int
+    n_heads: int
+    n_kv_heads: int
+    ffn: int
+    vocab: int
+    dtype: int = sg.SG_DTYPE_Q4_K
+    eps: float = 1e-5          # executor.rs:272
+    context_len: int = 2048    # RoPE table length (ops.rs:20, executor.rs:207)
+    max_seq: int = 2048        # KV-cache positions (executor.rs:320)
+
+    @property
+    def head_dim(self) -> int:
+        return self.d // self.n_heads
+
+    def shape(self, role: str):
+        """(n_rows N, n_cols K) of a linear (shape[1], shape[0] in GGUF)."""
+        kv = self.n_kv_heads * self.head_dim
+        return {"attn_q": (self.d, self.d), "attn_k": (kv, self.d), "attn_v": (kv, self.d),
+                "attn_output": (self.d, self.d), "ffn_gate": (self.ffn, self.d), "ffn_up": (self.ffn, self.d),
+                "ffn_down": (self.d, self.ffn), "output": (self.vocab, self.d),
+                "token_embd": (self.vocab, self.d)}[role]
+
+
+def tensor_id(role: str, layer: int = -1) -> int:
+    """Synthetic-generator id of a model tensor (weights and norm vectors)."""
+    if layer < 0:
+        return {"token_embd": 1, "output": 2, "output_norm": 3}[role]
+    names = ROLES + ("attn_norm", "ffn_norm")
+    return 1000 * (layer + 1) + names.index(role)
+
+
+def norm_vector(gpu: sg.SwampGpu, seed: int, tid: int, n: int) -> np.ndarray:
+    """Synthetic RMSNorm weight: 1 + 0.1 * N(0,1), rounded to f32."""
+    return (1.0 + 0.1 * gpu.synth_x(seed, tid, (n,)).astype(np.float64)).astype(np.float32)
+
+
+class SynthModel:
+    """Random-init weights of the architecture, generated on the device."""
+
+    def __init__(self, gpu: sg.SwampGpu, cfg: DecoderConfig, seed: int):
+        import torch
+        self.cfg, self.seed = cfg, seed
+        self.layers = []
+        for l in range(cfg.n_layers):
+            self.layers.append({r: gpu.synth_weight(cfg.dtype, seed, tensor_id(r, l), *cfg.shape(r)) for r in ROLES})
+        self.token_embd = gpu.synth_weight(cfg.dtype, seed, tensor_id("token_embd"), *cfg.shape("token_embd"))
+        self.output = gpu.synth_weight(cfg.dtype, seed, tensor_id("output"), *cfg.shape("output"))
+        dev = torch.device("cuda")
+        self.attn_norm = torch.from_numpy(np.stack(
+            [norm_vector(gpu, seed, tensor_id("attn_norm", l), cfg.d) for l in range(cfg.n_layers)])).to(dev)
+        self.ffn_norm = torch.from_numpy(np.stack(
+            [norm_vector(gpu, seed, tensor_id("ffn_norm", l), cfg.d) for l in range(cfg.n_layers)])).to(dev)
+        self.output_norm = torch.from_numpy(norm_vector(gpu, seed, tensor_id("output_norm"), cfg.d)).to(dev)
+
+    def weight_bytes(self) -> int:
+        """GGUF bytes of every quantized tensor one decode step reads (the
+        embedding table contributes one row per token, not counted)."""
+        c = self.cfg
+        tot = sum(sg.row_bytes(c.dtype, c.shape(r)[1]) * c.shape(r)[0] for r in ROLES) * c.n_layers
+        return tot + sg.row_bytes(c.dtype, c.d) * c.vocab
+
+    def free(self):
+        for lw in self.layers:
+            for w in lw.values():
+                w.free()
+        self.token_embd.free()
+        self.output.free()
+
+
+class Decoder:
+    """Buffers and the forward pass for up to max_rows query rows."""
+
+    def __init__(self, gpu: sg.SwampGpu, model: SynthModel, n_seqs: int, max_rows: int):
+        import torch
+        self.torch = torch
+        self.gpu, self.m, self.cfg = gpu, model, model.cfg
+        self.ops = sg.LayerOps(gpu)
+        c = self.cfg
+        self.rope = sg.Rope(gpu, c.head_dim, c.context_len)
+        self.cache = sg.KvCache(gpu, c.n_layers, c.n_kv_heads, c.head_dim, c.max_seq, n_seqs)
+        self.max_rows = max_rows
+        dev = torch.device("cuda")
+        f = dict(device=dev, dtype=torch.float32)
+        kv = c.n_kv_heads * c.head_dim
+        self.x = torch.zeros(max_rows, c.d, **f)
+        self.xn = torch.zeros(max_rows, c.d, **f)
+        self.q = torch.zeros(max_rows, c.d, **f)
+        self.k = torch.zeros(max_rows, kv, **f)
+        self.v = torch.zeros(max_rows, kv, **f)
+        self.att = torch.zeros(max_rows, c.d, **f)
+        self.gate = torch.zeros(max_rows, c.ffn, **f)
+        self.up = torch.zeros(max_rows, c.ffn, **f)
+        self.logits = torch.zeros(max_rows, c.vocab, **f)
+        i32 = dict(device=dev, dtype=torch.int32)
+        self.tokens = torch.zeros(max_rows, **i32)
+        self.pos = torch.zeros(max_rows, **i32)
+        self.seq = torch.zeros(max_rows, **i32)
+        self.next = torch.zeros(max_rows, **i32)
+
+    def set_rows(self, tokens, pos, seq):
+        """Copy a batch's (token, position, sequence) rows to the device."""
+        n = len(tokens)
+        assert n <= self.max_rows
+        t = self.torch
+        self.tokens[:n].copy_(t.as_tensor(np.asarray(tokens, np.int32)))
+        self.pos[:n].copy_(t.as_tensor(np.asarray(pos, np.int32)))
+        self.seq[:n].copy_(t.as_tensor(np.asarray(seq, np.int32)))
+        return n
+
+    def forward(self, rows: int, stream: int | None = None, logits_rows: slice | None = None):
+        """One forward pass of `rows` rows: logits (and the greedy pick in
+        `next`) for the rows in logits_rows (default: all)."""
+        c, o, g = self.cfg, self.ops, self.gpu
+        p = lambda t: t.data_ptr()
+        D, KV = c.d, c.n_kv_heads * c.head_dim
+        ACC = sg.SG_FLAG_ACCUMULATE
+        o.embed(self.m.token_embd, p(self.tokens), rows, p(self.x), D, stream)
+        for l, lw in enumerate(self.m.layers):
+            o.rmsnorm(p(self.x), D, p(self.m.attn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
+            g.linear_multi_device([lw["attn_q"], lw["attn_k"], lw["attn_v"]], p(self.xn), D,
+                                  [p(self.q), p(self.k), p(self.v)], [D, KV, KV], rows, stream=stream)
+            o.rope_kv(self.rope, self.cache, l, p(self.q), D, p(self.k), KV, p(self.v), KV, p(self.pos),
+                      p(self.seq), rows, c.n_heads, stream)
+            o.attention(self.cache, l, p(self.q), D, p(self.att), D, p(self.pos), None, p(self.seq), rows,
+                        c.n_heads, stream)
+            g.linear_device(lw["attn_output"], p(self.att), D, p(self.x), D, rows, stream=stream, flags=ACC)
+            o.rmsnorm(p(self.x), D, p(self.m.ffn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
+            g.linear_multi_device([lw["ffn_gate"], lw["ffn_up"]], p(self.xn), D, [p(self.gate), p(self.up)],
+                                  [c.ffn, c.ffn], rows, stream=stream)
+            o.silu_mul(p(self.gate), c.ffn, p(self.up), c.ffn, c.ffn, rows, stream)
+            g.linear_device(lw["ffn_down"], p(self.gate), c.ffn, p(self.x), D, rows, stream=stream, flags=ACC)
+        r0, r1 = (0, rows) if logits_rows is None else (logits_rows.start, logits_rows.stop)
+        n = r1 - r0
+        o.rmsnorm(p(self.x[r0]), D, p(self.m.output_norm), p(self.xn), D, D, n, c.eps, stream)
+        g.linear_device(self.m.output, p(self.xn), D, p(self.logits), c.vocab, n, stream=stream)
+        o.argmax(p(self.logits), c.vocab, c.vocab, n, p(self.next), stream)
+        return n
+
+    def advance(self, rows: int):
+        """Greedy decoding: the next step's token is this step's pick, one
+        position further (torch ops on the current stream)."""
+        self.tokens[:rows].copy_(self.next[:rows])
+        self.pos[:rows].add_(1)
+
+    def free(self):
+        self.rope.free()
+        self.cache.free()

@@ -39,6 +39,10 @@ EXPORTS = (
     "sg_synchronize", "sg_gguf_open", "sg_gguf_open_memory", "sg_gguf_close", "sg_gguf_header",
     "sg_gguf_find_tensor", "sg_gguf_tensor_info", "sg_gguf_tensor_data", "sg_gguf_find_kv", "sg_gguf_kv_info",
     "sg_gguf_kv_int", "sg_gguf_kv_float", "sg_gguf_kv_string", "sg_gguf_register",
+    "sg_synth_weight", "sg_synth_blocks", "sg_synth_x",
+    "sg_rope_create", "sg_rope_free", "sg_rope_table", "sg_kv_cache_create", "sg_kv_cache_free", "sg_kv_cache_ptr",
+    "sg_rmsnorm_device", "sg_rope_kv_device", "sg_attention_device", "sg_silu_mul_device", "sg_add_device",
+    "sg_argmax_device", "sg_embed_device",
 )
 SG_ERR_FORMAT, SG_ERR_NOT_FOUND = -8, -9
 
@@ -85,6 +89,23 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     L.sg_gguf_kv_float.argtypes = [P, i64, i64, P]
     L.sg_gguf_kv_string.argtypes = [P, i64, i64, P, P]
     L.sg_gguf_register.argtypes = [P, i64, i32, P]
+    u64, f32 = ctypes.c_uint64, ctypes.c_float
+    L.sg_synth_weight.argtypes = [i32, u64, u64, i64, i64, i32, P]
+    L.sg_synth_blocks.argtypes = [i32, u64, u64, i64, i64, P, i32]
+    L.sg_synth_x.argtypes = [u64, u64, i64, P]
+    L.sg_rope_create.argtypes = [i32, i32, P]
+    L.sg_rope_free.argtypes = [P]
+    L.sg_rope_table.argtypes = [P, P]
+    L.sg_kv_cache_create.argtypes = [i32, i32, i32, i32, i32, P]
+    L.sg_kv_cache_free.argtypes = [P]
+    L.sg_kv_cache_ptr.argtypes = [P, i32, i32, i32, P, P]
+    L.sg_rmsnorm_device.argtypes = [P, i64, P, P, i64, i32, i32, f32, P]
+    L.sg_rope_kv_device.argtypes = [P, P, i32, P, i64, P, i64, P, i64, P, P, i32, i32, P]
+    L.sg_attention_device.argtypes = [P, i32, P, i64, P, i64, P, P, P, i32, i32, P]
+    L.sg_silu_mul_device.argtypes = [P, i64, P, i64, i32, i32, P]
+    L.sg_add_device.argtypes = [P, i64, P, i64, i32, i32, P]
+    L.sg_argmax_device.argtypes = [P, i64, i32, i32, P, P]
+    L.sg_embed_device.argtypes = [P, P, i32, P, i64, P]
     for name in EXPORTS:
         getattr(L, name).restype = ctypes.c_char_p if name == "sg_last_error" else ctypes.c_int
     return L
@@ -243,6 +264,106 @@ class SwampGpu:
         out = np.empty(n_rows, np.float32)
         self._check(self.L.sg_fused_gemv_q4k(w_raw.ctypes.data, x.ctypes.data, out.ctypes.data, n_rows, n_cols))
         return out
+
+
+    # ------------------------------------------------------- synthetic inputs
+    def synth_weight(self, dtype: int, seed: int, tensor_id: int, n_rows: int, n_cols: int,
+                     tp_mode: int = SG_TP_REPLICATE) -> Weight:
+        """A seeded random-init tensor generated and registered on the device."""
+        h = ctypes.c_void_p()
+        self._check(self.L.sg_synth_weight(dtype, seed, tensor_id, n_rows, n_cols, tp_mode, ctypes.byref(h)))
+        return Weight(self, h.value, dtype, n_rows, n_cols, tp_mode)
+
+    def synth_blocks(self, dtype: int, seed: int, tensor_id: int, n_rows: int, n_cols: int) -> np.ndarray:
+        """The GGUF bytes of that tensor (row-major), copied to the host."""
+        out = np.empty(n_rows * row_bytes(dtype, n_cols), np.uint8)
+        self._check(self.L.sg_synth_blocks(dtype, seed, tensor_id, n_rows, n_cols, out.ctypes.data, 0))
+        return out
+
+    def synth_x(self, seed: int, tensor_id: int, shape) -> np.ndarray:
+        n = int(np.prod(shape))
+        out = np.empty(n, np.float32)
+        self._check(self.L.sg_synth_x(seed, tensor_id, n, out.ctypes.data))
+        return out.reshape(shape)
+
+
+class Rope:
+    """init_rope_lut (swamp-engine/src/ops.rs:20-38), kept on the device."""
+
+    def __init__(self, lib: SwampGpu, head_dim: int, max_context: int):
+        self.lib, self.head_dim, self.max_context = lib, head_dim, max_context
+        h = ctypes.c_void_p()
+        lib._check(lib.L.sg_rope_create(head_dim, max_context, ctypes.byref(h)))
+        self.handle = h.value
+
+    def table(self) -> np.ndarray:
+        out = np.empty((self.max_context, self.head_dim // 2, 2), np.float32)
+        self.lib._check(self.lib.L.sg_rope_table(self.handle, out.ctypes.data))
+        return out
+
+    def free(self):
+        if self.handle:
+            self.lib._check(self.lib.L.sg_rope_free(self.handle))
+            self.handle = None
+
+
+class KvCache:
+    """PagedKVCache (swamp-engine/src/cache.rs) of n_seqs sequences resident
+    on the device: [seq][layer][kv_head][max_seq][head_dim] f32."""
+
+    def __init__(self, lib: SwampGpu, n_layers: int, n_kv_heads: int, head_dim: int, max_seq: int, n_seqs: int = 1):
+        self.lib = lib
+        self.n_layers, self.n_kv_heads, self.head_dim, self.max_seq, self.n_seqs = (
+            n_layers, n_kv_heads, head_dim, max_seq, n_seqs)
+        h = ctypes.c_void_p()
+        lib._check(lib.L.sg_kv_cache_create(n_layers, n_kv_heads, head_dim, max_seq, n_seqs, ctypes.byref(h)))
+        self.handle = h.value
+
+    def ptrs(self, seq: int, layer: int, kv_head: int):
+        """Device addresses of position 0 of (seq, layer, kv_head) in K and V."""
+        k, v = ctypes.c_void_p(), ctypes.c_void_p()
+        self.lib._check(self.lib.L.sg_kv_cache_ptr(self.handle, seq, layer, kv_head, ctypes.byref(k), ctypes.byref(v)))
+        return k.value, v.value
+
+    def free(self):
+        if self.handle:
+            self.lib._check(self.lib.L.sg_kv_cache_free(self.handle))
+            self.handle = None
+
+
+class LayerOps:
+    """The decoder layer's non-matmul operations (ops.rs, sampler.rs) on
+    device pointers (ints: data_ptr() of CUDA tensors), stream-ordered;
+    stream is a cudaStream_t as an int, 0/None for the default stream."""
+
+    def __init__(self, lib: SwampGpu):
+        self.lib, self.L = lib, lib.L
+
+    def rmsnorm(self, x: int, ldx: int, weight: int, out: int, ldo: int, n: int, rows: int, eps: float,
+                stream: int | None = None):
+        self.lib._check(self.L.sg_rmsnorm_device(x, ldx, weight, out, ldo, n, rows, eps, stream or None))
+
+    def rope_kv(self, rope: Rope | None, cache: KvCache, layer: int, q: int, ldq: int, k: int, ldk: int, v: int,
+                ldv: int, pos: int, seq: int | None, rows: int, n_q_heads: int, stream: int | None = None):
+        self.lib._check(self.L.sg_rope_kv_device(rope.handle if rope else None, cache.handle, layer, q or None, ldq,
+                                                 k, ldk, v, ldv, pos, seq or None, rows, n_q_heads, stream or None))
+
+    def attention(self, cache: KvCache, layer: int, q: int, ldq: int, out: int, ldo: int, pos: int,
+                  seq_len: int | None, seq: int | None, rows: int, n_heads: int, stream: int | None = None):
+        self.lib._check(self.L.sg_attention_device(cache.handle, layer, q, ldq, out, ldo, pos, seq_len or None,
+                                                   seq or None, rows, n_heads, stream or None))
+
+    def silu_mul(self, g: int, ldg: int, u: int, ldu: int, n: int, rows: int, stream: int | None = None):
+        self.lib._check(self.L.sg_silu_mul_device(g, ldg, u, ldu, n, rows, stream or None))
+
+    def add(self, x: int, ldx: int, y: int, ldy: int, n: int, rows: int, stream: int | None = None):
+        self.lib._check(self.L.sg_add_device(x, ldx, y, ldy, n, rows, stream or None))
+
+    def argmax(self, logits: int, ld: int, n: int, rows: int, out: int, stream: int | None = None):
+        self.lib._check(self.L.sg_argmax_device(logits, ld, n, rows, out, stream or None))
+
+    def embed(self, table: Weight, tokens: int, rows: int, out: int, ldo: int, stream: int | None = None):
+        self.lib._check(self.L.sg_embed_device(table.handle, tokens, rows, out, ldo, stream or None))
 
 
 # ---------------------------------------------------------------------------

@@ -741,3 +741,118 @@ int orc_gemv_f64(int dtype, const uint8_t *w, const float *x, int64_t n_rows,
     free(row);
     return 0;
 }
+
+/* ------------------------------------------------------------------------- */
+/* Decoder-layer operations (swamp-engine/src/ops.rs, sampler.rs)            */
+/* ------------------------------------------------------------------------- */
+
+/* rmsnorm, ops.rs:188-201: a running f32 sum of x*x, then mean, + eps,
+ * 1 / sqrt, and out = x * inv * w left to right. */
+void orc_rmsnorm(const float *x, const float *w, float *out, int64_t n, float eps) {
+    float ss = 0.0f;
+    for (int64_t i = 0; i < n; i++) ss += x[i] * x[i];
+    ss /= (float)n;
+    ss += eps;
+    float inv = 1.0f / sqrtf(ss);
+    for (int64_t i = 0; i < n; i++) out[i] = x[i] * inv * w[i];
+}
+
+/* init_rope_lut, ops.rs:20-38 (theta = 10000, ops.rs:11): lut[m][k] =
+ * (cos, sin) of m * (1 / 10000^(2k / head_dim)), all f32 with the libm
+ * powf / cosf / sinf that Rust's f32::powf / cos / sin call. */
+void orc_rope_lut(int head_dim, int64_t max_seq_len, float *lut) {
+    int half = head_dim / 2;
+    for (int64_t m = 0; m < max_seq_len; m++)
+        for (int k = 0; k < half; k++) {
+            float freq = 1.0f / powf(10000.0f, (float)(2 * k) / (float)head_dim);
+            float angle = (float)m * freq;
+            lut[2 * (m * half + k)] = cosf(angle);
+            lut[2 * (m * half + k) + 1] = sinf(angle);
+        }
+}
+
+/* apply_rope_ufc + apply_rotation_pair, ops.rs:42-80. */
+void orc_rope_apply(float *q, float *k, int64_t pos, int n_q_heads, int n_kv_heads, int head_dim,
+                    int64_t max_context, const float *lut) {
+    int half = head_dim / 2;
+    if (pos > max_context - 1) pos = max_context - 1;
+    const float *cs = lut + 2 * pos * half;
+    for (int pass = 0; pass < 2; pass++) {
+        float *v = pass ? k : q;
+        int nh = pass ? n_kv_heads : n_q_heads;
+        for (int h = 0; h < nh; h++)
+            for (int j = 0; j < half; j++) {
+                float *e = v + (int64_t)h * head_dim + 2 * j;
+                float x = e[0], y = e[1], c = cs[2 * j], s = cs[2 * j + 1];
+                e[0] = x * c - y * s;
+                e[1] = x * s + y * c;
+            }
+    }
+}
+
+/* attention, ops.rs:82-186 with the scalar dot_product_raw / weighted_sum_raw
+ * (swamp-kernels/src/simd.rs:155-161,175-179): per query head h, KV head
+ * h / n_rep; scores dot * scale over 0..=valid_end (valid_end = min(q_pos,
+ * seq_len - 1)), -inf past it; softmax with a running max; out = sum p v.
+ * k_cache / v_cache hold this sequence and layer as [kv_head][head_stride],
+ * position t at t * head_dim (the reference's pages only change addressing). */
+void orc_attention(float *out, const float *q, const float *k_cache, const float *v_cache, int64_t head_stride,
+                   int64_t seq_len, int64_t q_pos, int n_heads, int n_kv_heads, int head_dim) {
+    float scale = 1.0f / sqrtf((float)head_dim);
+    int n_rep = n_heads / n_kv_heads;
+    int64_t valid_end = q_pos < seq_len - 1 ? q_pos : seq_len - 1;
+    float *scores = (float *)malloc((size_t)seq_len * sizeof(float));
+    for (int h = 0; h < n_heads; h++) {
+        const float *qh = q + (int64_t)h * head_dim;
+        const float *kb = k_cache + (int64_t)(h / n_rep) * head_stride;
+        const float *vb = v_cache + (int64_t)(h / n_rep) * head_stride;
+        float max_score = -INFINITY;
+        for (int64_t t = 0; t <= valid_end; t++) {
+            float sum = 0.0f;
+            for (int d = 0; d < head_dim; d++) sum += qh[d] * kb[t * head_dim + d];
+            float score = sum * scale;
+            scores[t] = score;
+            if (score > max_score) max_score = score;
+        }
+        for (int64_t t = valid_end + 1; t < seq_len; t++) scores[t] = -INFINITY;
+        float sum_exp = 0.0f;
+        for (int64_t t = 0; t < seq_len; t++) {
+            float e = expf(scores[t] - max_score);
+            scores[t] = e;
+            sum_exp += e;
+        }
+        float inv_sum = 1.0f / sum_exp;
+        for (int64_t t = 0; t < seq_len; t++) scores[t] *= inv_sum;
+        float *o = out + (int64_t)h * head_dim;
+        for (int d = 0; d < head_dim; d++) o[d] = 0.0f;
+        for (int64_t t = 0; t <= valid_end; t++)
+            for (int d = 0; d < head_dim; d++) o[d] += scores[t] * vb[t * head_dim + d];
+    }
+    free(scores);
+}
+
+/* silu then mul_in_place, ops.rs:203-214 */
+void orc_silu_mul(float *g, const float *u, int64_t n) {
+    for (int64_t i = 0; i < n; i++) {
+        float val = g[i];
+        g[i] = val / (1.0f + expf(-val));
+    }
+    for (int64_t i = 0; i < n; i++) g[i] *= u[i];
+}
+
+/* add_in_place, ops.rs:216-220 */
+void orc_add(float *a, const float *b, int64_t n) {
+    for (int64_t i = 0; i < n; i++) a[i] += b[i];
+}
+
+/* Greedy pick, sampler.rs:94-95: Iterator::max_by over partial_cmp keeps the
+ * last of equal maxima; a NaN makes partial_cmp return None and the unwrap
+ * panic, reported here as -1. */
+int64_t orc_argmax(const float *logits, int64_t n) {
+    int64_t best = 0;
+    for (int64_t i = 0; i < n; i++)
+        if (logits[i] != logits[i]) return -1;
+    for (int64_t i = 1; i < n; i++)
+        if (!(logits[i] < logits[best])) best = i;
+    return best;
+}

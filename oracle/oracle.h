@@ -124,6 +124,17 @@ void orc_gen_x(uint64_t seed, uint64_t tensor_id, int64_t n, float *out);
 int orc_gemv_f64(int dtype, const uint8_t *w, const float *x, int64_t n_rows,
                  int64_t n_cols, double *out64, double *absdot, double *l2dot);
 
+/* decoder-layer operations (swamp-engine/src/ops.rs, sampler.rs) */
+void orc_rmsnorm(const float *x, const float *w, float *out, int64_t n, float eps);
+void orc_rope_lut(int head_dim, int64_t max_seq_len, float *lut);
+void orc_rope_apply(float *q, float *k, int64_t pos, int n_q_heads, int n_kv_heads, int head_dim,
+                    int64_t max_context, const float *lut);
+void orc_attention(float *out, const float *q, const float *k_cache, const float *v_cache, int64_t head_stride,
+                   int64_t seq_len, int64_t q_pos, int n_heads, int n_kv_heads, int head_dim);
+void orc_silu_mul(float *g, const float *u, int64_t n);
+void orc_add(float *a, const float *b, int64_t n);
+int64_t orc_argmax(const float *logits, int64_t n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -72,6 +72,15 @@ def lib() -> ctypes.CDLL:
     L.orc_gen_x.argtypes = [ctypes.c_uint64, ctypes.c_uint64, i64, P]
     L.orc_gemv_f64.argtypes = [ctypes.c_int, P, P, i64, i64, P, P, P]
     L.orc_gemv_f64.restype = ctypes.c_int
+    f32 = ctypes.c_float
+    L.orc_rmsnorm.argtypes = [P, P, P, i64, f32]
+    L.orc_rope_lut.argtypes = [ctypes.c_int, i64, P]
+    L.orc_rope_apply.argtypes = [P, P, i64, ctypes.c_int, ctypes.c_int, ctypes.c_int, i64, P]
+    L.orc_attention.argtypes = [P, P, P, P, i64, i64, i64, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.orc_silu_mul.argtypes = [P, P, i64]
+    L.orc_add.argtypes = [P, P, i64]
+    L.orc_argmax.argtypes = [P, i64]
+    L.orc_argmax.restype = i64
     _lib = L
     return L
 
@@ -243,3 +252,64 @@ def gemv_f64(dtype, w, x, n_rows, n_cols):
     if rc:
         raise ValueError(rc)
     return o, a, l2
+
+
+# ------------------------------------------------------------ decoder-layer ops
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, np.float32)
+
+
+def rmsnorm(x, w, eps: float) -> np.ndarray:
+    """swamp-engine ops::rmsnorm (ops.rs:188-201) of one row."""
+    x, w = _f32(x), _f32(w)
+    out = np.empty_like(x)
+    lib().orc_rmsnorm(_p(x), _p(w), _p(out), x.size, eps)
+    return out
+
+
+def rope_lut(head_dim: int, max_seq_len: int) -> np.ndarray:
+    """ops::init_rope_lut (ops.rs:20-38): [max_seq_len][head_dim/2][cos, sin]."""
+    out = np.empty((max_seq_len, head_dim // 2, 2), np.float32)
+    lib().orc_rope_lut(head_dim, max_seq_len, _p(out))
+    return out
+
+
+def rope_apply(q, k, pos, n_q_heads, n_kv_heads, head_dim, max_context, lut):
+    """ops::apply_rope_ufc (ops.rs:42-80) of one token; returns rotated copies."""
+    q, k, lut = _f32(q).copy(), _f32(k).copy(), _f32(lut)
+    lib().orc_rope_apply(_p(q), _p(k), pos, n_q_heads, n_kv_heads, head_dim, max_context, _p(lut))
+    return q, k
+
+
+def attention(q, k_cache, v_cache, seq_len, q_pos, n_heads, n_kv_heads, head_dim) -> np.ndarray:
+    """ops::attention (ops.rs:82-186) of one token. k_cache / v_cache:
+    [n_kv_heads][positions][head_dim] of this sequence and layer."""
+    q, kc, vc = _f32(q), _f32(k_cache), _f32(v_cache)
+    assert kc.shape == vc.shape and kc.shape[0] == n_kv_heads and kc.shape[2] == head_dim
+    assert min(q_pos, seq_len - 1) < kc.shape[1]
+    out = np.empty(n_heads * head_dim, np.float32)
+    lib().orc_attention(_p(out), _p(q), _p(kc), _p(vc), kc.shape[1] * head_dim, seq_len, q_pos,
+                        n_heads, n_kv_heads, head_dim)
+    return out
+
+
+def silu_mul(g, u) -> np.ndarray:
+    """ops::silu then ops::mul_in_place (ops.rs:203-214)."""
+    g, u = _f32(g).copy(), _f32(u)
+    lib().orc_silu_mul(_p(g), _p(u), g.size)
+    return g
+
+
+def add(a, b) -> np.ndarray:
+    """ops::add_in_place (ops.rs:216-220)."""
+    a, b = _f32(a).copy(), _f32(b)
+    lib().orc_add(_p(a), _p(b), a.size)
+    return a
+
+
+def argmax(logits) -> int:
+    """Greedy pick: the sampler's max_by fallback (sampler.rs:94-95), the last
+    of equal maxima; -1 for a row with a NaN (the reference panics)."""
+    l = _f32(logits)
+    return int(lib().orc_argmax(_p(l), l.size))
