@@ -86,6 +86,9 @@ struct DevState {
   size_t rbuf_bytes = 0;
   float* attn_ws = nullptr;  // attention split partials (sg_attention_device)
   size_t attn_ws_bytes = 0;
+  void* argmax_ws = nullptr;  // argmax chunk keys, row counters and NaN flags
+  size_t argmax_ws_bytes = 0;
+  int argmax_rows = 0;  // rows the argmax counters and flags cover
   float* hbuf = nullptr;  // pinned host staging
   size_t hbuf_bytes = 0;
   uint8_t* upbuf[2] = {nullptr, nullptr};  // pinned double buffer of weight uploads
@@ -280,6 +283,7 @@ void release_devices() {
     if (d.ybuf) cudaFree(d.ybuf);
     if (d.rbuf) cudaFree(d.rbuf);
     if (d.attn_ws) cudaFree(d.attn_ws);
+    if (d.argmax_ws) cudaFree(d.argmax_ws);
     if (d.hbuf) cudaFreeHost(d.hbuf);
     for (int i = 0; i < 2; ++i) {
       if (d.upbuf[i]) cudaFreeHost(d.upbuf[i]);

@@ -67,14 +67,39 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Every op kernel is launched with programmatic dependent launch, like the
+// linears: it lets the next kernel start its prologue at once and waits for
+// the previous kernel's results before its first global access, so a GEMV
+// that follows streams its weights while the op still runs.
+__device__ __forceinline__ void pdl_enter() {
+  pdl_launch_dependents();
+  pdl_wait();
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = sg_pdl_enabled() ? 1 : 0;
+  cudaLaunchConfig_t c = {};
+  c.gridDim = grid;
+  c.blockDim = block;
+  c.dynamicSmemBytes = smem;
+  c.stream = st;
+  c.attrs = attr;
+  c.numAttrs = 1;
+  return cudaLaunchKernelEx(&c, kernel, args...);
+}
+
 // ------------------------------------------------------------------ rmsnorm
 // One CTA per row: ss = sum x^2, ss /= n, ss += eps, inv = 1 / sqrt(ss),
 // out = (x * inv) * w, each step one IEEE operation as in ops.rs:190-199;
 // only the summation order of ss differs (a tree instead of a running sum).
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = 512;
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* x, int64_t ldx, const float* __restrict__ w,
                                                               float* out, int64_t ldo, int n, float eps) {
   __shared__ float red[kNormThreads / 32];
+  pdl_enter();
   const float* xr = x + (int64_t)blockIdx.x * ldx;
   float* orow = out + (int64_t)blockIdx.x * ldo;
   float ss = 0.f;
@@ -100,6 +125,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* x, i
 __global__ void rope_kv_kernel(const float2* __restrict__ lut, int max_context, KvView kv, int layer, float* q,
                                int64_t ldq, float* k, int64_t ldk, const float* v, int64_t ldv, const int32_t* pos,
                                const int32_t* seq, int n_q_heads) {
+  pdl_enter();
   const int r = blockIdx.x;
   const int p = pos[r];
   const int s = seq ? seq[r] : 0;
@@ -154,15 +180,19 @@ __global__ void rope_kv_kernel(const float2* __restrict__ lut, int max_context, 
 // query head h reading KV head h / n_rep (ops.rs:94,105). Scores are
 // dot(q, k) * scale, softmax over them, out = sum p v (ops.rs:135-180).
 //
-// Split: CTAs of 128 threads take 128 positions of one (row, KV head) and all
-// n_rep query heads of that head, so each K and V row is read once per
-// query token. A thread scores one position against the n_rep queries
-// (queries in shared memory); each warp then sums p v over its 32 positions
-// with lanes owning head_dim/32 components. A CTA writes (max m, sum l of
-// exp(s - m), sum exp(s - m) v) per query head; the combine kernel rescales
-// the splits to the global max and divides by the global sum.
-constexpr int kAttnP = 128;  // positions per split (= threads per CTA)
-constexpr int kMaxRep = 8;   // query heads per KV head
+// Split: a CTA of 64 threads takes 64 positions of one (row, KV head) and all
+// n_rep query heads of that head, so each K and V row is read once per query
+// token. One thread copies the split's K and V rows (contiguous in the cache)
+// into shared memory with two bulk copies, so a whole split is in flight at
+// once. A thread then scores one position against the n_rep queries,
+// starting its walk over head_dim at its own offset so that the 8 threads of
+// a shared-memory phase touch 8 different banks; each warp sums p v over its
+// 32 positions with lanes owning head_dim/32 components. A CTA writes (max m,
+// sum l of exp(s - m), sum exp(s - m) v) per query head; the combine kernel
+// rescales the splits to the global max and divides by the global sum.
+constexpr int kAttnP = 64;        // positions per split
+constexpr int kAttnThreads = 64;  // one per position
+constexpr int kMaxRep = 8;        // query heads per KV head
 
 struct AttnArgs {
   KvView kv;
@@ -177,6 +207,17 @@ struct AttnArgs {
   float* ws;  // [row][head][split][HD + 2]
 };
 
+template <int HD>
+struct AttnSmem {
+  static constexpr size_t kTile = (size_t)kAttnP * HD * 4;
+  static constexpr size_t kQ = 2 * kTile;
+  static constexpr size_t kSc = kQ + (size_t)kMaxRep * HD * 4;
+  static constexpr size_t kRed = kSc + (size_t)kMaxRep * kAttnP * 4;
+  static constexpr size_t kMl = kRed + (size_t)(kAttnThreads / 32) * kMaxRep * HD * 4;
+  static constexpr size_t kBar = kMl + (size_t)kMaxRep * 2 * 4;
+  static constexpr size_t kBytes = kBar + 16;
+};
+
 __device__ __forceinline__ int attn_valid_end(const AttnArgs& a, int r) {
   const int p = a.pos[r];
   int e = p;
@@ -185,74 +226,93 @@ __device__ __forceinline__ int attn_valid_end(const AttnArgs& a, int r) {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kAttnP) attn_split_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
+  using L = AttnSmem<HD>;
   constexpr int DL = HD / 32;  // components per lane
-  __shared__ __align__(16) float qs[kMaxRep][HD];
-  __shared__ float sc[kMaxRep][kAttnP];
-  __shared__ __align__(16) float red[kAttnP / 32][kMaxRep][HD];
-  __shared__ float mls[kMaxRep][2];
+  constexpr int NC = HD / 4;   // float4 columns per row
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* ks = reinterpret_cast<float*>(smem);
+  float* vs = ks + kAttnP * HD;
+  float* qs = reinterpret_cast<float*>(smem + L::kQ);
+  float* sc = reinterpret_cast<float*>(smem + L::kSc);
+  float* red = reinterpret_cast<float*>(smem + L::kRed);
+  float* mls = reinterpret_cast<float*>(smem + L::kMl);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  __shared__ int ok_flag;
+  pdl_launch_dependents();
+  pdl_wait();  // q and the cache rows come from the previous kernels
   const int sp = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int valid_end = attn_valid_end(a, r);
   const int t0 = sp * kAttnP;
-  if (valid_end < 0 || t0 > valid_end) return;  // the combine reads splits 0 .. valid_end / 128 only
+  if (valid_end < 0 || t0 > valid_end) return;  // the combine reads splits 0 .. valid_end / 64 only
   const int s = a.seq ? a.seq[r] : 0;
   if (s < 0 || s >= a.kv.n_seqs) {
     if (tid == 0) sg_set_error(SG_DEVERR_BAD_INPUT);
     return;
   }
+  const int nv = min(kAttnP, valid_end - t0 + 1);
+  const size_t hoff = a.kv.head_off(s, a.layer, g) + (size_t)t0 * HD;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const uint32_t bytes = (uint32_t)nv * HD * 4;  // whole rows: a multiple of 16
+    mbar_arrive_expect_tx(bar, 2 * bytes);
+    bulk_g2s(ks, a.kv.k + hoff, bytes, bar);
+    bulk_g2s(vs, a.kv.v + hoff, bytes, bar);
+  }
   const int n_rep = a.n_rep;
   const float* qrow = a.q + (int64_t)r * a.ldq + (int64_t)g * n_rep * HD;
-  for (int i = tid; i < n_rep * HD; i += kAttnP) qs[i / HD][i % HD] = qrow[i];
+  for (int i = tid; i < n_rep * HD; i += kAttnThreads) qs[i] = qrow[i];
+  if (tid == 0) ok_flag = mbar_wait(bar, 0, 0x40) ? 1 : 0;
   __syncthreads();
-  const size_t hoff = a.kv.head_off(s, a.layer, g);
-  const float* kb = a.kv.k + hoff;
-  const float* vb = a.kv.v + hoff;
+  if (!ok_flag) {  // the bounded wait gave up (error recorded): let the copies land, then leave
+    if (tid == 0) mbar_wait_drain(bar, 0);
+    return;
+  }
+  mbar_test(bar, 0);  // completed: acquire the copied rows in this thread
   // scores: this thread's position against every query head of the group
   {
-    const int t = t0 + tid;
     float acc[kMaxRep];
 #pragma unroll
     for (int j = 0; j < kMaxRep; ++j) acc[j] = 0.f;
-    if (t <= valid_end) {
-      const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)t * HD);
-#pragma unroll 4
-      for (int d4 = 0; d4 < HD / 4; ++d4) {
-        const float4 kv4 = kr[d4];
+    if (tid < nv) {
+      const float4* kr = reinterpret_cast<const float4*>(ks + tid * HD);
+#pragma unroll 8
+      for (int i = 0; i < NC; ++i) {
+        const int c = (i + tid) & (NC - 1);
+        const float4 k4 = kr[c];
 #pragma unroll
         for (int j = 0; j < kMaxRep; ++j) {
           if (j < n_rep) {
-            const float4 q4 = *reinterpret_cast<const float4*>(&qs[j][4 * d4]);
-            acc[j] = fmaf(q4.x, kv4.x, acc[j]);
-            acc[j] = fmaf(q4.y, kv4.y, acc[j]);
-            acc[j] = fmaf(q4.z, kv4.z, acc[j]);
-            acc[j] = fmaf(q4.w, kv4.w, acc[j]);
+            const float4 q4 = reinterpret_cast<const float4*>(qs + j * HD)[c];
+            acc[j] = fmaf(q4.x, k4.x, acc[j]);
+            acc[j] = fmaf(q4.y, k4.y, acc[j]);
+            acc[j] = fmaf(q4.z, k4.z, acc[j]);
+            acc[j] = fmaf(q4.w, k4.w, acc[j]);
           }
         }
       }
     }
 #pragma unroll
     for (int j = 0; j < kMaxRep; ++j)
-      if (j < n_rep) sc[j][tid] = t <= valid_end ? acc[j] * a.scale : -INFINITY;
+      if (j < n_rep) sc[j * kAttnP + tid] = tid < nv ? acc[j] * a.scale : -INFINITY;
   }
   __syncthreads();
   // split max and exp per query head (one warp per head)
-  for (int j = warp; j < n_rep; j += kAttnP / 32) {
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < kAttnP / 32; ++i) m = fmaxf(m, sc[j][lane + 32 * i]);
-    m = warp_max(m);
-    float l = 0.f;
-#pragma unroll
-    for (int i = 0; i < kAttnP / 32; ++i) {
-      const float e = expf(sc[j][lane + 32 * i] - m);  // exp(-inf) = 0 past valid_end
-      sc[j][lane + 32 * i] = e;
-      l += e;
-    }
-    l = warp_sum(l);
+  for (int j = warp; j < n_rep; j += kAttnThreads / 32) {
+    float* sj = sc + j * kAttnP;
+    const float m = warp_max(fmaxf(sj[lane], sj[lane + 32]));
+    const float e0 = expf(sj[lane] - m), e1 = expf(sj[lane + 32] - m);  // exp(-inf) = 0 past nv
+    sj[lane] = e0;
+    sj[lane + 32] = e1;
+    const float l = warp_sum(e0 + e1);
     if (lane == 0) {
-      mls[j][0] = m;
-      mls[j][1] = l;
+      mls[2 * j] = m;
+      mls[2 * j + 1] = l;
     }
   }
   __syncthreads();
@@ -263,29 +323,29 @@ __global__ void __launch_bounds__(kAttnP) attn_split_kernel(AttnArgs a) {
     for (int j = 0; j < kMaxRep; ++j)
 #pragma unroll
       for (int c = 0; c < DL; ++c) acc[j][c] = 0.f;
-    const int tw = t0 + warp * 32;
-    const int nt = min(32, valid_end - tw + 1);
-    for (int i = 0; i < nt; ++i) {
-      const float* vr = vb + (size_t)(tw + i) * HD + lane * DL;
+    const int pb = warp * 32, pe = min(pb + 32, nv);
+#pragma unroll 4
+    for (int t = pb; t < pe; ++t) {
+      const float* vr = vs + t * HD + lane * DL;
       float vv[DL];
-      if constexpr (DL == 4) {
-        const float4 v4 = *reinterpret_cast<const float4*>(vr);
-        vv[0] = v4.x;
-        vv[1] = v4.y;
-        vv[2] = v4.z;
-        vv[3] = v4.w;
-      } else if constexpr (DL == 2) {
+      if constexpr (DL % 4 == 0) {
+#pragma unroll
+        for (int c = 0; c < DL; c += 4) {
+          const float4 v4 = *reinterpret_cast<const float4*>(vr + c);
+          vv[c] = v4.x;
+          vv[c + 1] = v4.y;
+          vv[c + 2] = v4.z;
+          vv[c + 3] = v4.w;
+        }
+      } else {
         const float2 v2 = *reinterpret_cast<const float2*>(vr);
         vv[0] = v2.x;
         vv[1] = v2.y;
-      } else {
-#pragma unroll
-        for (int c = 0; c < DL; ++c) vv[c] = vr[c];
       }
 #pragma unroll
       for (int j = 0; j < kMaxRep; ++j) {
         if (j < n_rep) {
-          const float pj = sc[j][warp * 32 + i];
+          const float pj = sc[j * kAttnP + t];
 #pragma unroll
           for (int c = 0; c < DL; ++c) acc[j][c] = fmaf(pj, vv[c], acc[j][c]);
         }
@@ -295,19 +355,19 @@ __global__ void __launch_bounds__(kAttnP) attn_split_kernel(AttnArgs a) {
     for (int j = 0; j < kMaxRep; ++j)
       if (j < n_rep)
 #pragma unroll
-        for (int c = 0; c < DL; ++c) red[warp][j][lane * DL + c] = acc[j][c];
+        for (int c = 0; c < DL; ++c) red[(warp * kMaxRep + j) * HD + lane * DL + c] = acc[j][c];
   }
   __syncthreads();
-  for (int i = tid; i < n_rep * HD; i += kAttnP) {
+  for (int i = tid; i < n_rep * HD; i += kAttnThreads) {
     const int j = i / HD, d = i - j * HD;
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kAttnP / 32; ++w) v += red[w][j][d];
+    for (int w = 0; w < kAttnThreads / 32; ++w) v += red[(w * kMaxRep + j) * HD + d];
     float* rec = a.ws + (((int64_t)r * a.n_heads + g * n_rep + j) * a.n_split + sp) * (HD + 2);
     rec[2 + d] = v;
     if (d == 0) {
-      rec[0] = mls[j][0];
-      rec[1] = mls[j][1];
+      rec[0] = mls[2 * j];
+      rec[1] = mls[2 * j + 1];
     }
   }
 }
@@ -316,6 +376,7 @@ __global__ void __launch_bounds__(kAttnP) attn_split_kernel(AttnArgs a) {
 // with e_s = exp(m_s - M), M = max m_s, L = sum e_s l_s.
 template <int HD>
 __global__ void __launch_bounds__(HD) attn_combine_kernel(AttnArgs a, float* out, int64_t ldo) {
+  pdl_enter();
   const int h = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
   const int valid_end = attn_valid_end(a, r);
   float* o = out + (int64_t)r * ldo + (int64_t)h * HD;
@@ -339,6 +400,7 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(AttnArgs a, float* out
 // ------------------------------------------------------------- elementwise
 // g = silu(g) * u with silu(v) = v / (1 + exp(-v)) (ops.rs:203-214).
 __global__ void silu_mul_kernel(float* g, int64_t ldg, const float* u, int64_t ldu, int n, int64_t total) {
+  pdl_enter();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t row = i / n, c = i - row * n;
     float* gp = g + row * ldg + c;
@@ -350,6 +412,7 @@ __global__ void silu_mul_kernel(float* g, int64_t ldg, const float* u, int64_t l
 
 // x += y (ops.rs:216-220).
 __global__ void add_kernel(float* x, int64_t ldx, const float* y, int64_t ldy, int n, int64_t total) {
+  pdl_enter();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t row = i / n, c = i - row * n;
     x[row * ldx + c] = __fadd_rn(x[row * ldx + c], y[row * ldy + c]);
@@ -361,47 +424,72 @@ __global__ void add_kernel(float* x, int64_t ldx, const float* y, int64_t ldy, i
 // (Iterator::max_by keeps the last maximum, sampler.rs:95; -0.0 == +0.0).
 // A row holding a NaN, where the reference's partial_cmp().unwrap() panics,
 // gives -1.
-constexpr int kArgThreads = 1024;
-__device__ __forceinline__ void arg_better(float& bv, int& bi, float v, int i) {
-  if (v > bv || (v == bv && i > bi)) {
-    bv = v;
-    bi = i;
-  }
+//
+// Each (value, index) becomes one 64-bit key whose unsigned order is the
+// pick's order: the float's bits mapped to an order-preserving integer in
+// the high half (-0.0 folded onto +0.0), the index in the low half, so the
+// largest key is the largest value and, among equal values, the last index.
+// CTAs of 256 threads reduce 4096 logits each to one key; the last CTA of a
+// row to finish (counted with an atomic) reduces the row's keys, writes the
+// pick and resets the row's counter and NaN flag for the next call.
+constexpr int kArgThreads = 256;
+constexpr int kArgChunk = 4096;
+
+__device__ __forceinline__ unsigned long long arg_key(float v, int i) {
+  if (v == 0.f) v = 0.f;  // -0.0 -> +0.0
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)o << 32) | (uint32_t)i;
 }
-__global__ void __launch_bounds__(kArgThreads) argmax_kernel(const float* logits, int64_t ld, int n, int32_t* out) {
-  __shared__ float sv[kArgThreads / 32];
-  __shared__ int si[kArgThreads / 32];
-  __shared__ int nan_seen;
-  if (threadIdx.x == 0) nan_seen = 0;
+
+__device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) { return a > b ? a : b; }
+
+__device__ __forceinline__ unsigned long long block_max_key(unsigned long long k, unsigned long long* sk) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) k = umax64(k, __shfl_xor_sync(0xffffffffu, k, o));
+  if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = k;
   __syncthreads();
-  const float* row = logits + (int64_t)blockIdx.x * ld;
-  float bv = -INFINITY;
-  int bi = -1;
+  k = 0;
+#pragma unroll
+  for (int w = 0; w < kArgThreads / 32; ++w) k = umax64(k, sk[w]);
+  return k;
+}
+
+__global__ void __launch_bounds__(kArgThreads) argmax_kernel(const float* logits, int64_t ld, int n, int n_chunks,
+                                                          unsigned long long* keys, unsigned int* counters,
+                                                          unsigned int* nan_flags, int32_t* out) {
+  __shared__ unsigned long long sk[kArgThreads / 32];
+  __shared__ bool last;
+  pdl_enter();
+  const int cb = blockIdx.x, r = blockIdx.y;
+  const float* row = logits + (int64_t)r * ld;
+  const int i0 = cb * kArgChunk, i1 = min(n, i0 + kArgChunk);
+  unsigned long long k = 0;
   bool nan = false;
-  for (int i = threadIdx.x; i < n; i += kArgThreads) {
+  for (int i = i0 + threadIdx.x; i < i1; i += kArgThreads) {
     const float v = row[i];
     nan |= v != v;
-    arg_better(bv, bi, v, i);
+    if (v == v) k = umax64(k, arg_key(v, i));
   }
-  if (nan) nan_seen = 1;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (oi >= 0) arg_better(bv, bi, ov, oi);
-  }
-  if ((threadIdx.x & 31) == 0) {
-    sv[threadIdx.x >> 5] = bv;
-    si[threadIdx.x >> 5] = bi;
+  if (__syncthreads_or(nan) && threadIdx.x == 0) atomicOr(&nan_flags[r], 1u);
+  k = block_max_key(k, sk);
+  if (threadIdx.x == 0) {
+    keys[(int64_t)r * n_chunks + cb] = k;
+    __threadfence();
+    last = atomicAdd(&counters[r], 1u) == (unsigned)(n_chunks - 1);
   }
   __syncthreads();
+  if (!last) return;
+  __threadfence();
+  k = 0;
+  for (int c = threadIdx.x; c < n_chunks; c += kArgThreads)
+    k = umax64(k, __ldcg(&keys[(int64_t)r * n_chunks + c]));
+  k = block_max_key(k, sk);
   if (threadIdx.x == 0) {
-    float v = sv[0];
-    int idx = si[0];
-    for (int w = 1; w < kArgThreads / 32; ++w)
-      if (si[w] >= 0) arg_better(v, idx, sv[w], si[w]);
-    if (idx < 0) idx = n - 1;  // every logit is -inf: the last one
-    out[blockIdx.x] = nan_seen ? -1 : idx;
+    const bool any_nan = __ldcg(&nan_flags[r]) != 0;
+    out[r] = any_nan ? -1 : (k == 0 ? n - 1 : (int32_t)(k & 0xFFFFFFFFu));
+    counters[r] = 0;
+    nan_flags[r] = 0;
   }
 }
 
@@ -410,6 +498,7 @@ __global__ void __launch_bounds__(kArgThreads) argmax_kernel(const float* logits
 // dequant, which the reference applies to the whole table at load,
 // executor.rs:212).
 __global__ void embed_kernel(SgDevWeight w, const int32_t* tokens, float* out, int64_t ldo) {
+  pdl_enter();
   const int r = blockIdx.y;
   const int64_t k0 = 8 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
   if (k0 >= w.n_cols) return;
@@ -448,6 +537,21 @@ ops::KvView kv_view(const sg_kv_cache_s* c) {
 }
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+template <int HD>
+int attention_launch(const ops::AttnArgs& a, dim3 g1, dim3 g2, float* out, int64_t ldo, cudaStream_t st) {
+  static int attr_done[64] = {0};
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 64 && !attr_done[dev]) {
+    CUDA_TRY(cudaFuncSetAttribute(ops::attn_split_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)ops::AttnSmem<HD>::kBytes));
+    attr_done[dev] = 1;
+  }
+  CUDA_TRY(ops::launch(ops::attn_split_kernel<HD>, g1, dim3(ops::kAttnThreads), ops::AttnSmem<HD>::kBytes, st, a));
+  CUDA_TRY(ops::launch(ops::attn_combine_kernel<HD>, g2, dim3(HD), 0, st, a, out, ldo));
+  return SG_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -574,8 +678,8 @@ int sg_rmsnorm_device(const float* x, int64_t ldx, const float* weight, float* o
   if (rows < 0 || n < 1 || ldx < n || ldo < n) return fail(SG_ERR_INVALID_ARG, "bad sizes (n %d, rows %d)", n, rows);
   if (!x || !weight || !out) return fail(SG_ERR_INVALID_ARG, "null pointer");
   if (rows == 0) return SG_OK;
-  ops::rmsnorm_kernel<<<rows, ops::kNormThreads, 0, (cudaStream_t)stream>>>(x, ldx, weight, out, ldo, n, eps);
-  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(ops::launch(ops::rmsnorm_kernel, dim3(rows), dim3(ops::kNormThreads), 0, (cudaStream_t)stream, x, ldx, weight,
+                       out, ldo, n, eps));
   return SG_OK;
 }
 
@@ -597,10 +701,9 @@ int sg_rope_kv_device(sg_rope_t rope, sg_kv_cache_t cache, int layer, float* q, 
     if (n_q_heads < 1 || ldq < (int64_t)n_q_heads * hd) return fail(SG_ERR_INVALID_ARG, "bad q heads / stride");
   }
   if (rows == 0) return SG_OK;
-  ops::rope_kv_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(rope ? rope->lut : nullptr, rope ? rope->max_context : 1,
-                                                              kv_view(cache), layer, q, ldq, k, ldk, v, ldv, pos, seq,
-                                                              n_q_heads);
-  CUDA_TRY(cudaGetLastError());
+  const float2* lut = rope ? rope->lut : nullptr;
+  CUDA_TRY(ops::launch(ops::rope_kv_kernel, dim3(rows), dim3(256), 0, (cudaStream_t)stream, lut,
+                       rope ? rope->max_context : 1, kv_view(cache), layer, q, ldq, k, ldk, v, ldv, pos, seq, n_q_heads));
   return SG_OK;
 }
 
@@ -642,19 +745,15 @@ int sg_attention_device(sg_kv_cache_t cache, int layer, const float* q, int64_t 
   const dim3 g1(a.n_split, nkv, rows), g2(n_heads, rows);
   switch (hd) {
     case 64:
-      ops::attn_split_kernel<64><<<g1, ops::kAttnP, 0, st>>>(a);
-      ops::attn_combine_kernel<64><<<g2, 64, 0, st>>>(a, out, ldo);
+      rc = attention_launch<64>(a, g1, g2, out, ldo, st);
       break;
     case 128:
-      ops::attn_split_kernel<128><<<g1, ops::kAttnP, 0, st>>>(a);
-      ops::attn_combine_kernel<128><<<g2, 128, 0, st>>>(a, out, ldo);
+      rc = attention_launch<128>(a, g1, g2, out, ldo, st);
       break;
     default:
-      ops::attn_split_kernel<256><<<g1, ops::kAttnP, 0, st>>>(a);
-      ops::attn_combine_kernel<256><<<g2, 256, 0, st>>>(a, out, ldo);
+      rc = attention_launch<256>(a, g1, g2, out, ldo, st);
   }
-  CUDA_TRY(cudaGetLastError());
-  return SG_OK;
+  return rc;
 }
 
 int sg_silu_mul_device(float* g, int64_t ldg, const float* u, int64_t ldu, int n, int rows, void* stream) {
@@ -666,8 +765,8 @@ int sg_silu_mul_device(float* g, int64_t ldg, const float* u, int64_t ldu, int n
   if (n < 1 || rows < 0 || ldg < n || ldu < n) return fail(SG_ERR_INVALID_ARG, "bad sizes");
   const int64_t total = (int64_t)n * rows;
   if (total == 0) return SG_OK;
-  ops::silu_mul_kernel<<<ops::ew_grid(total, d->num_sms), 256, 0, (cudaStream_t)stream>>>(g, ldg, u, ldu, n, total);
-  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(ops::launch(ops::silu_mul_kernel, dim3(ops::ew_grid(total, d->num_sms)), dim3(256), 0, (cudaStream_t)stream, g,
+                       ldg, u, ldu, n, total));
   return SG_OK;
 }
 
@@ -680,8 +779,8 @@ int sg_add_device(float* x, int64_t ldx, const float* y, int64_t ldy, int n, int
   if (n < 1 || rows < 0 || ldx < n || ldy < n) return fail(SG_ERR_INVALID_ARG, "bad sizes");
   const int64_t total = (int64_t)n * rows;
   if (total == 0) return SG_OK;
-  ops::add_kernel<<<ops::ew_grid(total, d->num_sms), 256, 0, (cudaStream_t)stream>>>(x, ldx, y, ldy, n, total);
-  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(ops::launch(ops::add_kernel, dim3(ops::ew_grid(total, d->num_sms)), dim3(256), 0, (cudaStream_t)stream, x, ldx,
+                       y, ldy, n, total));
   return SG_OK;
 }
 
@@ -693,8 +792,25 @@ int sg_argmax_device(const float* logits, int64_t ld, int n, int rows, int32_t* 
   if (!logits || !out) return fail(SG_ERR_INVALID_ARG, "null pointer");
   if (n < 1 || rows < 0 || ld < n) return fail(SG_ERR_INVALID_ARG, "bad sizes");
   if (rows == 0) return SG_OK;
-  ops::argmax_kernel<<<rows, ops::kArgThreads, 0, (cudaStream_t)stream>>>(logits, ld, n, out);
-  CUDA_TRY(cudaGetLastError());
+  // row counters and NaN flags first (zero between calls: the last CTA of a
+  // row resets them; their place depends only on the row), then chunk keys
+  const int n_chunks = (n + ops::kArgChunk - 1) / ops::kArgChunk;
+  const int cap = std::max(rows, d->argmax_rows);
+  const size_t need = (size_t)cap * 8 + (size_t)rows * n_chunks * 8;
+  if (d->argmax_ws_bytes < need || rows > d->argmax_rows) {
+    size_t have = d->argmax_ws_bytes;
+    if (rows > d->argmax_rows) have = 0;  // the flags region grows: start over
+    rc = ensure_buf(&d->argmax_ws, &have, need);
+    if (rc) return rc;
+    d->argmax_ws_bytes = have;
+    d->argmax_rows = cap;
+    CUDA_TRY(cudaMemset(d->argmax_ws, 0, d->argmax_ws_bytes));
+  }
+  auto* counters = static_cast<unsigned int*>(d->argmax_ws);
+  auto* nan_flags = counters + d->argmax_rows;
+  auto* keys = reinterpret_cast<unsigned long long*>(counters + 2 * (size_t)d->argmax_rows);
+  CUDA_TRY(ops::launch(ops::argmax_kernel, dim3(n_chunks, rows), dim3(ops::kArgThreads), 0, (cudaStream_t)stream, logits,
+                       ld, n, n_chunks, keys, counters, nan_flags, out));
   return SG_OK;
 }
 
@@ -714,8 +830,7 @@ int sg_embed_device(sg_weight_t table, const int32_t* tokens, int rows, float* o
   if (rows == 0) return SG_OK;
   const int64_t per_row = w.n_cols / 8;
   const dim3 grid((unsigned)((per_row + 127) / 128), (unsigned)rows);
-  ops::embed_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(w, tokens, out, ldo);
-  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(ops::launch(ops::embed_kernel, grid, dim3(128), 0, (cudaStream_t)stream, w, tokens, out, ldo));
   return SG_OK;
 }
 

@@ -346,6 +346,13 @@ def test_argmax_device(gpu, oracle, ops):
     ops.argmax(_t(L).data_ptr(), V, V, len(rows), out.data_ptr())
     assert out.cpu().tolist() == [oracle.argmax(r) for r in rows]
     assert out.cpu().tolist()[1] == 128255 and out.cpu().tolist()[-1] == -1
+    # calls of other shapes reuse the per-row state: results stay exact
+    for shape in ((1, 5000), (2, 4096), (3, 1), (8, 128256), (1, 128256)):
+        R, n = shape
+        L2 = oracle.gen_x(SEED, 520 + n, (R, n))
+        o2 = torch.full((R,), -7, dtype=torch.int32, device="cuda")
+        ops.argmax(_t(L2).data_ptr(), n, n, R, o2.data_ptr())
+        assert o2.cpu().tolist() == [oracle.argmax(r) for r in L2], shape
 
 
 @pytest.mark.gpu
