@@ -20,6 +20,7 @@
 #include "../../include/swamp_gpu.h"
 #include "sg_gemm.cuh"
 #include "sg_gemv.cuh"
+#include "sg_peer.cuh"
 
 // ---------------------------------------------------------------- NCCL shim
 namespace {
@@ -28,7 +29,7 @@ typedef struct {
   char internal[128];
 } ncclUniqueId;
 typedef int ncclResult_t;
-enum { kNcclFloat = 7, kNcclSum = 0 };
+enum { kNcclUint8 = 1, kNcclInt32 = 2, kNcclFloat = 7, kNcclSum = 0, kNcclMin = 3 };
 
 struct NcclApi {
   void* h = nullptr;
@@ -36,6 +37,7 @@ struct NcclApi {
   ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*CommInitAll)(ncclComm_t*, int, const int*) = nullptr;
   ncclResult_t (*AllReduce)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
@@ -58,6 +60,7 @@ struct NcclApi {
     SG_SYM(CommInitRank, "ncclCommInitRank");
     SG_SYM(CommInitAll, "ncclCommInitAll");
     SG_SYM(AllReduce, "ncclAllReduce");
+    SG_SYM(AllGather, "ncclAllGather");
     SG_SYM(GroupStart, "ncclGroupStart");
     SG_SYM(GroupEnd, "ncclGroupEnd");
     SG_SYM(CommDestroy, "ncclCommDestroy");
@@ -93,6 +96,14 @@ struct DevState {
   size_t hbuf_bytes = 0;
   uint8_t* upbuf[2] = {nullptr, nullptr};  // pinned double buffer of weight uploads
   cudaEvent_t upev[2] = {nullptr, nullptr};
+  // peer all-reduce (one process per GPU, sg_peer.cuh): this rank's receive
+  // buffer and flags (one allocation, exported by CUDA IPC), the mappings of
+  // every rank's, and the per-chunk epoch counters
+  bool peer_on = false;
+  void* peer_base = nullptr;
+  uint32_t* peer_ctr = nullptr;
+  SgPeerPtrs peer = {};
+  void* peer_mapped[SG_PEER_MAX] = {};
 };
 
 struct Ctx {
@@ -289,6 +300,10 @@ void release_devices() {
       if (d.upbuf[i]) cudaFreeHost(d.upbuf[i]);
       if (d.upev[i]) cudaEventDestroy(d.upev[i]);
     }
+    for (int p = 0; p < SG_PEER_MAX; ++p)
+      if (d.peer_mapped[p]) cudaIpcCloseMemHandle(d.peer_mapped[p]);
+    if (d.peer_base) cudaFree(d.peer_base);
+    if (d.peer_ctr) cudaFree(d.peer_ctr);
     if (d.stream) cudaStreamDestroy(d.stream);
   }
   g_ctx.devs.clear();
@@ -350,8 +365,92 @@ int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* 
   return SG_OK;
 }
 
+constexpr int64_t kPeerCap = (int64_t)kArChunk * kArMaxChunks;  // floats per slot
+
+// Sum all-reduce of `count` floats in place on this rank's device: the peer
+// kernel when it is set up and the vector fits a slot, else NCCL.
+int allreduce_rank(DevState& d, float* buf, size_t count, cudaStream_t st) {
+  if (g_ctx.world <= 1 || count == 0) return SG_OK;
+  if (d.peer_on && (int64_t)count <= kPeerCap) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = sg_pdl_enabled() ? 1 : 0;
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3((unsigned)((count + kArChunk - 1) / kArChunk));
+    c.blockDim = dim3(kArThreads);
+    c.stream = st;
+    c.attrs = attr;
+    c.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&c, peer_allreduce_kernel, (const float*)buf, buf, (int64_t)count, g_ctx.world,
+                                g_ctx.rank_base, d.peer, d.peer_ctr, kPeerCap));
+    return SG_OK;
+  }
+  if (!g_nccl.AllReduce) return fail(SG_ERR_NCCL, "NCCL not initialised");
+  ncclResult_t r = g_nccl.AllReduce(buf, buf, count, kNcclFloat, kNcclSum, d.comm, st);
+  if (r) return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
+  return SG_OK;
+}
+
+// Set up the peer all-reduce of a rank (collective: every rank calls it
+// from sg_init_rank). Each rank allocates and zeroes its receive buffer,
+// exports it, gathers every rank's handle over NCCL and maps the others;
+// the ranks then agree (NCCL min) whether all of them succeeded, so that
+// either every rank uses the peer kernel or every rank uses NCCL.
+int peer_setup(DevState& d) {
+  const int W = g_ctx.world, R = g_ctx.rank_base;
+  int ok = W <= SG_PEER_MAX;
+  const char* env = std::getenv("SG_PEER_ALLREDUCE");
+  if (!env || env[0] != '1') ok = 0;  // opt-in until validated on a multi-GPU box
+  const size_t buf_bytes = (size_t)2 * W * kPeerCap * sizeof(float);
+  const size_t flag_bytes = (size_t)2 * W * kArMaxChunks * sizeof(uint32_t);
+  cudaIpcMemHandle_t mine = {};
+  if (ok && (cudaMalloc(&d.peer_base, buf_bytes + flag_bytes) != cudaSuccess ||
+             cudaMalloc((void**)&d.peer_ctr, kArMaxChunks * sizeof(uint32_t)) != cudaSuccess ||
+             cudaMemset(d.peer_base, 0, buf_bytes + flag_bytes) != cudaSuccess ||
+             cudaMemset(d.peer_ctr, 0, kArMaxChunks * sizeof(uint32_t)) != cudaSuccess ||
+             cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&mine, d.peer_base) != cudaSuccess)) {
+    cudaGetLastError();
+    ok = 0;
+  }
+  // gather the handles (64 bytes each) through a device buffer
+  uint8_t* dev = nullptr;
+  CUDA_TRY(cudaMalloc(&dev, (size_t)(W + 1) * sizeof(cudaIpcMemHandle_t)));
+  std::vector<cudaIpcMemHandle_t> all(W);
+  CUDA_TRY(cudaMemcpy(dev + (size_t)W * sizeof mine, &mine, sizeof mine, cudaMemcpyHostToDevice));
+  ncclResult_t r = g_nccl.AllGather(dev + (size_t)W * sizeof mine, dev, sizeof mine, kNcclUint8, d.comm, d.stream);
+  if (r) {
+    cudaFree(dev);
+    return fail(SG_ERR_NCCL, "ncclAllGather: %s", g_nccl.GetErrorString(r));
+  }
+  CUDA_TRY(cudaStreamSynchronize(d.stream));
+  CUDA_TRY(cudaMemcpy(all.data(), dev, (size_t)W * sizeof mine, cudaMemcpyDeviceToHost));
+  for (int p = 0; p < W && ok; ++p) {
+    if (p == R) {
+      d.peer.buf[p] = static_cast<float*>(d.peer_base);
+    } else if (cudaIpcOpenMemHandle(&d.peer_mapped[p], all[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = 0;
+      break;
+    } else {
+      d.peer.buf[p] = static_cast<float*>(d.peer_mapped[p]);
+    }
+    d.peer.flags[p] = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(d.peer.buf[p]) + buf_bytes);
+  }
+  // every rank must take the same path
+  int* dok = reinterpret_cast<int*>(dev);
+  CUDA_TRY(cudaMemcpy(dok, &ok, sizeof ok, cudaMemcpyHostToDevice));
+  r = g_nccl.AllReduce(dok, dok, 1, kNcclInt32, kNcclMin, d.comm, d.stream);
+  CUDA_TRY(cudaStreamSynchronize(d.stream));
+  CUDA_TRY(cudaMemcpy(&ok, dok, sizeof ok, cudaMemcpyDeviceToHost));
+  cudaFree(dev);
+  if (r) return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
+  d.peer_on = ok != 0;
+  return SG_OK;
+}
+
 int allreduce_local(const std::vector<float*>& bufs, size_t count) {
   if (g_ctx.world <= 1) return SG_OK;
+  if (g_ctx.devs.size() == 1) return allreduce_rank(g_ctx.devs[0], bufs[0], count, g_ctx.devs[0].stream);
   if (!g_nccl.AllReduce) return fail(SG_ERR_NCCL, "NCCL not initialised");
   ncclResult_t r = g_nccl.GroupStart();
   for (size_t i = 0; i < g_ctx.devs.size() && r == 0; ++i) {
@@ -531,6 +630,13 @@ int sg_init_rank(int rank, int world, const void* id128, int device) {
     if (r) {
       release_devices();
       return fail(SG_ERR_NCCL, "ncclCommInitRank: %s", g_nccl.GetErrorString(r));
+    }
+    g_ctx.world = world;
+    g_ctx.rank_base = rank;
+    rc = peer_setup(g_ctx.devs[0]);
+    if (rc) {
+      release_devices();
+      return rc;
     }
   }
   g_ctx.inited = true;
@@ -833,8 +939,8 @@ int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x,
   }
   int rc = run_linear(d, sw, n_weights, x, ldx, yp, lp, batch, st, false);
   if (rc) return rc;
-  ncclResult_t r = g_nccl.AllReduce(yp[0], yp[0], count, kNcclFloat, kNcclSum, d.comm, st);
-  if (r) return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
+  rc = allreduce_rank(d, yp[0], count, st);
+  if (rc) return rc;
   if (!packed)
     for (int i = 0; i < n_weights; ++i)
       CUDA_TRY(cudaMemcpy2DAsync(ys[i], (size_t)ldys[i] * sizeof(float), yp[i], (size_t)lp[i] * sizeof(float),
@@ -885,6 +991,24 @@ int sg_fused_gemv_q4k(const uint8_t* w_raw, const float* x, float* out, int n_ro
   rc = sg_linear(w, xs, outs, 1, 0);
   int rc2 = sg_weight_free(w);
   return rc ? rc : rc2;
+}
+
+int sg_allreduce_device(float* buf, int64_t count, void* stream) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!g_ctx.inited) return fail(SG_ERR_NOT_INITIALIZED, "sg_init not called");
+  if (g_ctx.devs.size() != 1) return fail(SG_ERR_INVALID_ARG, "device entry points need one device per process");
+  if (count < 0 || (!buf && count)) return fail(SG_ERR_INVALID_ARG, "bad buffer");
+  DevState& d = g_ctx.devs[0];
+  CUDA_TRY(cudaSetDevice(d.device));
+  return allreduce_rank(d, buf, (size_t)count, (cudaStream_t)stream);
+}
+
+int sg_allreduce_path(int* peer) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!g_ctx.inited) return fail(SG_ERR_NOT_INITIALIZED, "sg_init not called");
+  if (!peer) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  *peer = g_ctx.devs.size() == 1 && g_ctx.devs[0].peer_on ? 1 : 0;
+  return SG_OK;
 }
 
 int sg_synchronize(void) {

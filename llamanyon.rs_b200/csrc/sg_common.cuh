@@ -181,7 +181,7 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// 2-D tiled TMA load (no multicast), completion on an mbarrier.
+// 2-D tiled TMA load into this CTA only, completion on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* map, int c0, int c1,
                                             uint64_t* bar) {
   asm volatile(
@@ -191,7 +191,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* m
       : "memory");
 }
 
-// 4-D tiled TMA load (no multicast), completion on an mbarrier.
+// 4-D tiled TMA load into this CTA only, completion on an mbarrier.
 __device__ __forceinline__ void tma_load_4d(void* dst_smem, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint64_t* bar) {
   asm volatile(

@@ -42,7 +42,7 @@ EXPORTS = (
     "sg_synth_weight", "sg_synth_blocks", "sg_synth_x",
     "sg_rope_create", "sg_rope_free", "sg_rope_table", "sg_kv_cache_create", "sg_kv_cache_free", "sg_kv_cache_ptr",
     "sg_rmsnorm_device", "sg_rope_kv_device", "sg_attention_device", "sg_silu_mul_device", "sg_add_device",
-    "sg_argmax_device", "sg_embed_device",
+    "sg_argmax_device", "sg_embed_device", "sg_allreduce_device", "sg_allreduce_path",
 )
 SG_ERR_FORMAT, SG_ERR_NOT_FOUND = -8, -9
 
@@ -106,6 +106,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     L.sg_add_device.argtypes = [P, i64, P, i64, i32, i32, P]
     L.sg_argmax_device.argtypes = [P, i64, i32, i32, P, P]
     L.sg_embed_device.argtypes = [P, P, i32, P, i64, P]
+    L.sg_allreduce_device.argtypes = [P, i64, P]
+    L.sg_allreduce_path.argtypes = [P]
     for name in EXPORTS:
         getattr(L, name).restype = ctypes.c_char_p if name == "sg_last_error" else ctypes.c_int
     return L
@@ -265,6 +267,15 @@ class SwampGpu:
         self._check(self.L.sg_fused_gemv_q4k(w_raw.ctypes.data, x.ctypes.data, out.ctypes.data, n_rows, n_cols))
         return out
 
+
+    def allreduce_device(self, buf_ptr: int, count: int, stream: int = 0):
+        """In-place sum across the job's ranks (stream-ordered)."""
+        self._check(self.L.sg_allreduce_device(buf_ptr, count, stream or None))
+
+    def allreduce_path(self) -> str:
+        v = ctypes.c_int()
+        self._check(self.L.sg_allreduce_path(ctypes.byref(v)))
+        return "peer" if v.value else "nccl"
 
     # ------------------------------------------------------- synthetic inputs
     def synth_weight(self, dtype: int, seed: int, tensor_id: int, n_rows: int, n_cols: int,
