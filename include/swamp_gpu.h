@@ -186,8 +186,9 @@ SG_API int sg_fused_gemv_q4k(const uint8_t *w_raw, const float *x, float *out, i
  * sg_init_rank), raises a flag there, waits (bounded) for the peers' flags
  * and sums in rank order, so every rank gets the same bits. Larger vectors,
  * or jobs where any rank could not map its peers, use ncclAllReduce.
- * Stream-ordered and graph-capturable. SG_PEER_ALLREDUCE=0 in the
- * environment at sg_init_rank selects NCCL for every call.
+ * Stream-ordered and graph-capturable. The peer kernel is enabled by
+ * SG_PEER_ALLREDUCE=1 in the environment at sg_init_rank; otherwise every
+ * call uses NCCL.
  * sg_allreduce_path reports which one this job uses (1: peer kernel). */
 SG_API int sg_allreduce_device(float *buf, int64_t count, void *stream);
 SG_API int sg_allreduce_path(int *peer);
