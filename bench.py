@@ -576,12 +576,12 @@ def model_decode_bench(torch, gpu, args):
                 D.pos[:B].fill_(P)
                 D.seq[:B].copy_(seqs)
             start()
-            D.forward(B, stream=st.cuda_stream)  # first use of the decode shapes
+            D.forward(B, stream=st.cuda_stream, decode=True)  # first use of the decode shapes
             start()
             st.synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=st):
-                D.forward(B, stream=st.cuda_stream)
+                D.forward(B, stream=st.cuda_stream, decode=True)
                 D.advance(B)
                 host_tok.copy_(D.tokens[:B], non_blocking=True)
             for _ in range(3):

@@ -319,6 +319,19 @@ SG_API int sg_attention_device(sg_kv_cache_t cache, int layer, const float *q, i
                                const int32_t *pos, const int32_t *seq_len, const int32_t *seq, int rows, int n_heads,
                                void *stream);
 
+/* The decode form of sg_rope_kv_device followed by sg_attention_device, in
+ * one kernel: row r is the next token of sequence seq[r] (one row per
+ * sequence, so rows <= the cache's n_seqs) at position pos[r]; it rotates
+ * q and k with the table row, stores k and v at pos[r], and attends
+ * positions 0..pos[r]. q, k and v are read and left unchanged; out gets the
+ * attention output. The results are the same bits as the two-call form. The
+ * per-(row, KV head) split counters live in a per-device array that grows
+ * on first use, like the attention workspace. */
+SG_API int sg_rope_attention_device(sg_rope_t rope, sg_kv_cache_t cache, int layer, const float *q, int64_t ldq,
+                                    const float *k, int64_t ldk, const float *v, int64_t ldv, float *out,
+                                    int64_t ldo, const int32_t *pos, const int32_t *seq, int rows, int n_heads,
+                                    void *stream);
+
 /* silu then mul_in_place (ops.rs:203-214): g = g / (1 + exp(-g)) * u. */
 SG_API int sg_silu_mul_device(float *g, int64_t ldg, const float *u, int64_t ldu, int n, int rows, void *stream);
 /* add_in_place (ops.rs:216-220): x += y. (A linear's SG_FLAG_ACCUMULATE

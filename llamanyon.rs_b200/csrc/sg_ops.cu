@@ -205,6 +205,18 @@ struct AttnArgs {
   int n_heads, n_rep, n_split;
   float scale;
   float* ws;  // [row][head][split][HD + 2]
+  // decode form only (one row per sequence): RoPE and the cache store of
+  // the row's own k and v happen in the split that holds its position, and
+  // the last split of a (row, KV head) to finish combines
+  const float2* lut;
+  int max_context;
+  const float* k_new;
+  int64_t ldk;
+  const float* v_new;
+  int64_t ldv;
+  unsigned int* counters;  // [row][kv head], zero between calls
+  float* out;
+  int64_t ldo;
 };
 
 template <int HD>
@@ -225,7 +237,7 @@ __device__ __forceinline__ int attn_valid_end(const AttnArgs& a, int r) {
   return min(e, a.kv.max_seq - 1);
 }
 
-template <int HD>
+template <int HD, bool DECODE>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
   using L = AttnSmem<HD>;
   constexpr int DL = HD / 32;  // components per lane
@@ -238,11 +250,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
   float* red = reinterpret_cast<float*>(smem + L::kRed);
   float* mls = reinterpret_cast<float*>(smem + L::kMl);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  __shared__ int ok_flag;
+  __shared__ int ok_flag, last_flag;
   pdl_launch_dependents();
   pdl_wait();  // q and the cache rows come from the previous kernels
   const int sp = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int p = a.pos[r];
+  if (DECODE && (p < 0 || p >= a.kv.max_seq)) {  // the row's k and v have no cache slot
+    if (tid == 0 && sp == 0) sg_set_error(SG_DEVERR_BAD_INPUT);
+    return;
+  }
   const int valid_end = attn_valid_end(a, r);
   const int t0 = sp * kAttnP;
   if (valid_end < 0 || t0 > valid_end) return;  // the combine reads splits 0 .. valid_end / 64 only
@@ -252,6 +269,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
     return;
   }
   const int nv = min(kAttnP, valid_end - t0 + 1);
+  // decode: the split holding position p (= valid_end) makes row p itself
+  const bool own = DECODE && t0 + nv - 1 == p;
+  const int ncopy = own ? nv - 1 : nv;
   const size_t hoff = a.kv.head_off(s, a.layer, g) + (size_t)t0 * HD;
   if (tid == 0) {
     mbar_init(bar, 1);
@@ -259,14 +279,51 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
   }
   __syncthreads();
   if (tid == 0) {
-    const uint32_t bytes = (uint32_t)nv * HD * 4;  // whole rows: a multiple of 16
+    const uint32_t bytes = (uint32_t)ncopy * HD * 4;  // whole rows: a multiple of 16
     mbar_arrive_expect_tx(bar, 2 * bytes);
-    bulk_g2s(ks, a.kv.k + hoff, bytes, bar);
-    bulk_g2s(vs, a.kv.v + hoff, bytes, bar);
+    if (bytes) {
+      bulk_g2s(ks, a.kv.k + hoff, bytes, bar);
+      bulk_g2s(vs, a.kv.v + hoff, bytes, bar);
+    }
   }
   const int n_rep = a.n_rep;
   const float* qrow = a.q + (int64_t)r * a.ldq + (int64_t)g * n_rep * HD;
-  for (int i = tid; i < n_rep * HD; i += kAttnThreads) qs[i] = qrow[i];
+  if constexpr (DECODE) {
+    // apply_rope_ufc on this group's query heads (ops.rs:57-60,77-78)
+    const float2* cs = a.lut + (int64_t)min(p, a.max_context - 1) * (HD / 2);
+    for (int i = tid; i < n_rep * HD / 2; i += kAttnThreads) {
+      const int h = i / (HD / 2), j = i - h * (HD / 2);
+      const float x0 = qrow[h * HD + 2 * j], y0 = qrow[h * HD + 2 * j + 1];
+      const float2 c = cs[j];
+      qs[h * HD + 2 * j] = __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(y0, c.y));
+      qs[h * HD + 2 * j + 1] = __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(y0, c.x));
+    }
+    if (own) {
+      // this KV head's k (rotated, ops.rs:62-65) and v of position p: to the
+      // cache (cache.rs:354-368) and to the tile's last row
+      const float* kr = a.k_new + (int64_t)r * a.ldk + (int64_t)g * HD;
+      const float* vr = a.v_new + (int64_t)r * a.ldv + (int64_t)g * HD;
+      float* kc = a.kv.k + hoff + (size_t)(nv - 1) * HD;
+      float* vc = a.kv.v + hoff + (size_t)(nv - 1) * HD;
+      for (int j = tid; j < HD / 2; j += kAttnThreads) {
+        const float x0 = kr[2 * j], y0 = kr[2 * j + 1];
+        const float2 c = cs[j];
+        const float k0 = __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(y0, c.y));
+        const float k1 = __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(y0, c.x));
+        kc[2 * j] = k0;
+        kc[2 * j + 1] = k1;
+        ks[(nv - 1) * HD + 2 * j] = k0;
+        ks[(nv - 1) * HD + 2 * j + 1] = k1;
+      }
+      for (int i = tid; i < HD; i += kAttnThreads) {
+        const float v0 = vr[i];
+        vc[i] = v0;
+        vs[(nv - 1) * HD + i] = v0;
+      }
+    }
+  } else {
+    for (int i = tid; i < n_rep * HD; i += kAttnThreads) qs[i] = qrow[i];
+  }
   if (tid == 0) ok_flag = mbar_wait(bar, 0, 0x40) ? 1 : 0;
   __syncthreads();
   if (!ok_flag) {  // the bounded wait gave up (error recorded): let the copies land, then leave
@@ -369,6 +426,32 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
       rec[0] = mls[2 * j];
       rec[1] = mls[2 * j + 1];
     }
+  }
+  if constexpr (DECODE) {
+    // the last split of this (row, KV head) to finish combines its heads:
+    // out = sum_s e_s acc_s / sum_s e_s l_s, e_s = exp(m_s - max_s m_s)
+    const int ns = valid_end / kAttnP + 1;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_flag = atomicAdd(&a.counters[r * a.kv.n_kv_heads + g], 1u) == (unsigned)(ns - 1);
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+    for (int i = tid; i < n_rep * HD; i += kAttnThreads) {
+      const int j = i / HD, d = i - j * HD;
+      const int h = g * n_rep + j;
+      const float* rec = a.ws + ((int64_t)r * a.n_heads + h) * a.n_split * (HD + 2);
+      float M = -INFINITY;
+      for (int q = 0; q < ns; ++q) M = fmaxf(M, __ldcg(rec + q * (HD + 2)));
+      float L = 0.f, acc = 0.f;
+      for (int q = 0; q < ns; ++q) {
+        const float e = expf(__ldcg(rec + q * (HD + 2)) - M);
+        L = fmaf(e, __ldcg(rec + q * (HD + 2) + 1), L);
+        acc = fmaf(e, __ldcg(rec + q * (HD + 2) + 2 + d), acc);
+      }
+      a.out[(int64_t)r * a.ldo + (int64_t)h * HD + d] = acc / L;
+    }
+    if (tid == 0) a.counters[r * a.kv.n_kv_heads + g] = 0;
   }
 }
 
@@ -544,11 +627,19 @@ int attention_launch(const ops::AttnArgs& a, dim3 g1, dim3 g2, float* out, int64
   int dev = 0;
   CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 64 && !attr_done[dev]) {
-    CUDA_TRY(cudaFuncSetAttribute(ops::attn_split_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    CUDA_TRY(cudaFuncSetAttribute(ops::attn_split_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)ops::AttnSmem<HD>::kBytes));
+    CUDA_TRY(cudaFuncSetAttribute(ops::attn_split_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)ops::AttnSmem<HD>::kBytes));
     attr_done[dev] = 1;
   }
-  CUDA_TRY(ops::launch(ops::attn_split_kernel<HD>, g1, dim3(ops::kAttnThreads), ops::AttnSmem<HD>::kBytes, st, a));
+  if (a.counters) {  // decode form: RoPE, cache store and combine inside the split kernel
+    CUDA_TRY(ops::launch(ops::attn_split_kernel<HD, true>, g1, dim3(ops::kAttnThreads), ops::AttnSmem<HD>::kBytes, st,
+                         a));
+    return SG_OK;
+  }
+  CUDA_TRY(ops::launch(ops::attn_split_kernel<HD, false>, g1, dim3(ops::kAttnThreads), ops::AttnSmem<HD>::kBytes, st,
+                       a));
   CUDA_TRY(ops::launch(ops::attn_combine_kernel<HD>, g2, dim3(HD), 0, st, a, out, ldo));
   return SG_OK;
 }
@@ -725,7 +816,7 @@ int sg_attention_device(sg_kv_cache_t cache, int layer, const float* q, int64_t 
     return fail(SG_ERR_INVALID_ARG, "bad rows or strides");
   if (!aligned16(q) || (ldq & 3)) return fail(SG_ERR_INVALID_ARG, "q must be 16-byte aligned with ldq % 4 == 0");
   if (rows == 0) return SG_OK;
-  ops::AttnArgs a;
+  ops::AttnArgs a = {};
   a.kv = kv_view(cache);
   a.layer = layer;
   a.q = q;
@@ -754,6 +845,72 @@ int sg_attention_device(sg_kv_cache_t cache, int layer, const float* q, int64_t 
       rc = attention_launch<256>(a, g1, g2, out, ldo, st);
   }
   return rc;
+}
+
+int sg_rope_attention_device(sg_rope_t rope, sg_kv_cache_t cache, int layer, const float* q, int64_t ldq, const float* k,
+                             int64_t ldk, const float* v, int64_t ldv, float* out, int64_t ldo, const int32_t* pos,
+                             const int32_t* seq, int rows, int n_heads, void* stream) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  if (!rope || !cache || !q || !k || !v || !out || !pos) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (layer < 0 || layer >= cache->n_layers) return fail(SG_ERR_INVALID_ARG, "layer %d out of range", layer);
+  const int hd = cache->head_dim, nkv = cache->n_kv_heads;
+  if (rope->head_dim != hd) return fail(SG_ERR_INVALID_ARG, "RoPE head_dim %d != cache head_dim %d", rope->head_dim, hd);
+  if (hd != 64 && hd != 128 && hd != 256) return fail(SG_ERR_UNSUPPORTED, "head_dim %d (64, 128 or 256)", hd);
+  if (n_heads < nkv || n_heads % nkv || n_heads / nkv > ops::kMaxRep)
+    return fail(SG_ERR_UNSUPPORTED, "n_heads %d over %d KV heads (a multiple, at most %d per KV head)", n_heads, nkv,
+                ops::kMaxRep);
+  if (rows < 0 || ldq < (int64_t)n_heads * hd || ldo < (int64_t)n_heads * hd || ldk < (int64_t)nkv * hd ||
+      ldv < (int64_t)nkv * hd)
+    return fail(SG_ERR_INVALID_ARG, "bad rows or strides");
+  if (!aligned16(q) || (ldq & 3)) return fail(SG_ERR_INVALID_ARG, "q must be 16-byte aligned with ldq % 4 == 0");
+  if (rows > cache->n_seqs)
+    return fail(SG_ERR_INVALID_ARG, "%d rows > %d sequences (one row per sequence)", rows, cache->n_seqs);
+  if (rows == 0) return SG_OK;
+  ops::AttnArgs a = {};
+  a.kv = kv_view(cache);
+  a.layer = layer;
+  a.q = q;
+  a.ldq = ldq;
+  a.pos = pos;
+  a.seq_len = nullptr;
+  a.seq = seq;
+  a.n_heads = n_heads;
+  a.n_rep = n_heads / nkv;
+  a.n_split = (cache->max_seq + ops::kAttnP - 1) / ops::kAttnP;
+  a.scale = 1.0f / sqrtf((float)hd);  // ops.rs:93
+  a.lut = rope->lut;
+  a.max_context = rope->max_context;
+  a.k_new = k;
+  a.ldk = ldk;
+  a.v_new = v;
+  a.ldv = ldv;
+  a.out = out;
+  a.ldo = ldo;
+  rc = ensure_buf((void**)&d->attn_ws, &d->attn_ws_bytes, (size_t)rows * n_heads * a.n_split * (hd + 2) * sizeof(float));
+  if (rc) return rc;
+  a.ws = d->attn_ws;
+  // per-(row, KV head) split counters: zero between calls (the combining
+  // split resets its own); their place depends only on the row
+  const size_t cnt_need = (size_t)rows * nkv * sizeof(unsigned int);
+  if (d->attn_cnt_bytes < cnt_need) {
+    rc = ensure_buf(&d->attn_cnt, &d->attn_cnt_bytes, cnt_need);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemset(d->attn_cnt, 0, d->attn_cnt_bytes));
+  }
+  a.counters = static_cast<unsigned int*>(d->attn_cnt);
+  cudaStream_t st = (cudaStream_t)stream;
+  const dim3 g1(a.n_split, nkv, rows), g2(n_heads, rows);
+  switch (hd) {
+    case 64:
+      return attention_launch<64>(a, g1, g2, out, ldo, st);
+    case 128:
+      return attention_launch<128>(a, g1, g2, out, ldo, st);
+    default:
+      return attention_launch<256>(a, g1, g2, out, ldo, st);
+  }
 }
 
 int sg_silu_mul_device(float* g, int64_t ldg, const float* u, int64_t ldu, int n, int rows, void* stream) {

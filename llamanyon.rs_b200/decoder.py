@@ -139,9 +139,12 @@ class Decoder:
         self.seq[:n].copy_(t.as_tensor(np.asarray(seq, np.int32)))
         return n
 
-    def forward(self, rows: int, stream: int | None = None, logits_rows: slice | None = None):
+    def forward(self, rows: int, stream: int | None = None, logits_rows: slice | None = None,
+                decode: bool = False):
         """One forward pass of `rows` rows: logits (and the greedy pick in
-        `next`) for the rows in logits_rows (default: all)."""
+        `next`) for the rows in logits_rows (default: all). decode=True for
+        a step of one row per sequence: RoPE, the cache store and attention
+        then run as one kernel per layer."""
         c, o, g = self.cfg, self.ops, self.gpu
         p = lambda t: t.data_ptr()
         D, KV = c.d, c.n_kv_heads * c.head_dim
@@ -151,10 +154,14 @@ class Decoder:
             o.rmsnorm(p(self.x), D, p(self.m.attn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
             g.linear_multi_device([lw["attn_q"], lw["attn_k"], lw["attn_v"]], p(self.xn), D,
                                   [p(self.q), p(self.k), p(self.v)], [D, KV, KV], rows, stream=stream)
-            o.rope_kv(self.rope, self.cache, l, p(self.q), D, p(self.k), KV, p(self.v), KV, p(self.pos),
-                      p(self.seq), rows, c.n_heads, stream)
-            o.attention(self.cache, l, p(self.q), D, p(self.att), D, p(self.pos), None, p(self.seq), rows,
-                        c.n_heads, stream)
+            if decode:
+                o.rope_attention(self.rope, self.cache, l, p(self.q), D, p(self.k), KV, p(self.v), KV, p(self.att),
+                                 D, p(self.pos), p(self.seq), rows, c.n_heads, stream)
+            else:
+                o.rope_kv(self.rope, self.cache, l, p(self.q), D, p(self.k), KV, p(self.v), KV, p(self.pos),
+                          p(self.seq), rows, c.n_heads, stream)
+                o.attention(self.cache, l, p(self.q), D, p(self.att), D, p(self.pos), None, p(self.seq), rows,
+                            c.n_heads, stream)
             g.linear_device(lw["attn_output"], p(self.att), D, p(self.x), D, rows, stream=stream, flags=ACC)
             o.rmsnorm(p(self.x), D, p(self.m.ffn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
             g.linear_multi_device([lw["ffn_gate"], lw["ffn_up"]], p(self.xn), D, [p(self.gate), p(self.up)],

@@ -41,7 +41,7 @@ EXPORTS = (
     "sg_gguf_kv_int", "sg_gguf_kv_float", "sg_gguf_kv_string", "sg_gguf_register",
     "sg_synth_weight", "sg_synth_blocks", "sg_synth_x",
     "sg_rope_create", "sg_rope_free", "sg_rope_table", "sg_kv_cache_create", "sg_kv_cache_free", "sg_kv_cache_ptr",
-    "sg_rmsnorm_device", "sg_rope_kv_device", "sg_attention_device", "sg_silu_mul_device", "sg_add_device",
+    "sg_rmsnorm_device", "sg_rope_kv_device", "sg_attention_device", "sg_rope_attention_device", "sg_silu_mul_device", "sg_add_device",
     "sg_argmax_device", "sg_embed_device", "sg_allreduce_device", "sg_allreduce_path",
 )
 SG_ERR_FORMAT, SG_ERR_NOT_FOUND = -8, -9
@@ -102,6 +102,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     L.sg_rmsnorm_device.argtypes = [P, i64, P, P, i64, i32, i32, f32, P]
     L.sg_rope_kv_device.argtypes = [P, P, i32, P, i64, P, i64, P, i64, P, P, i32, i32, P]
     L.sg_attention_device.argtypes = [P, i32, P, i64, P, i64, P, P, P, i32, i32, P]
+    L.sg_rope_attention_device.argtypes = [P, P, i32, P, i64, P, i64, P, i64, P, i64, P, P, i32, i32, P]
     L.sg_silu_mul_device.argtypes = [P, i64, P, i64, i32, i32, P]
     L.sg_add_device.argtypes = [P, i64, P, i64, i32, i32, P]
     L.sg_argmax_device.argtypes = [P, i64, i32, i32, P, P]
@@ -363,6 +364,13 @@ class LayerOps:
                   seq_len: int | None, seq: int | None, rows: int, n_heads: int, stream: int | None = None):
         self.lib._check(self.L.sg_attention_device(cache.handle, layer, q, ldq, out, ldo, pos, seq_len or None,
                                                    seq or None, rows, n_heads, stream or None))
+
+    def rope_attention(self, rope: Rope, cache: KvCache, layer: int, q: int, ldq: int, k: int, ldk: int, v: int,
+                       ldv: int, out: int, ldo: int, pos: int, seq: int | None, rows: int, n_heads: int,
+                       stream: int | None = None):
+        """Decode form: RoPE, cache store and attention of one row per sequence."""
+        self.lib._check(self.L.sg_rope_attention_device(rope.handle, cache.handle, layer, q, ldq, k, ldk, v, ldv, out,
+                                                        ldo, pos, seq or None, rows, n_heads, stream or None))
 
     def silu_mul(self, g: int, ldg: int, u: int, ldu: int, n: int, rows: int, stream: int | None = None):
         self.lib._check(self.L.sg_silu_mul_device(g, ldg, u, ldu, n, rows, stream or None))

@@ -102,7 +102,7 @@ def test_decoder_prefill_then_greedy_decode(gpu, oracle, dtype):
         for step in range(n_new):
             pos = plen + step
             D.set_rows(cur, [pos] * n_seqs, list(range(n_seqs)))
-            D.forward(n_seqs)
+            D.forward(n_seqs, decode=True)  # one row per sequence: the fused decode attention
             torch.cuda.synchronize()
             gpu.synchronize()
             logits = D.logits[:n_seqs].cpu().numpy()
@@ -120,8 +120,9 @@ def test_decoder_prefill_then_greedy_decode(gpu, oracle, dtype):
 
 @pytest.mark.gpu
 def test_decoder_graph_replay_matches_eager(gpu, oracle):
-    """A decode step captured in a CUDA graph, replayed with the device-side
-    advance (token <- pick, position + 1), gives the eager steps' tokens."""
+    """A decode step captured in a CUDA graph (fused decode attention),
+    replayed with the device-side advance (token <- pick, position + 1),
+    gives the eager two-call steps' tokens."""
     import torch
     import decoder as dec
     cfg = dec.DecoderConfig(**CFG)
@@ -140,12 +141,12 @@ def test_decoder_graph_replay_matches_eager(gpu, oracle):
             st = torch.cuda.Stream()
             st.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(st):
-                D.forward(2, stream=st.cuda_stream)  # eager first use (workspaces)
+                D.forward(2, stream=st.cuda_stream, decode=True)  # eager first use (workspaces)
                 D.set_rows([5, 900], [0, 0], [0, 1])
                 st.synchronize()
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=st):
-                    D.forward(2, stream=st.cuda_stream)
+                    D.forward(2, stream=st.cuda_stream, decode=True)
                     D.advance(2)
                 for _ in range(6):
                     g.replay()

@@ -414,3 +414,54 @@ def test_host_validation(gpu, ops):
         c.free()
     with pytest.raises(sg.SwampGpuError):
         ops.rmsnorm(16, 4, 16, 16, 4, 8, 1, 1e-5)  # ldx < n
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("nq,nkv,hd", [(32, 8, 128), (8, 2, 64), (16, 2, 256)])
+def test_rope_attention_fused_matches_two_calls(gpu, oracle, ops, nq, nkv, hd):
+    """sg_rope_attention_device (one row per sequence) gives the same bits as
+    sg_rope_kv_device + sg_attention_device, output and cache, at positions
+    on and around the 64-position split edges, over two calls in a row."""
+    import torch
+    import swamp_gpu as sg
+    L, max_seq, ctx = 2, 200, 150
+    rope = sg.Rope(gpu, hd, ctx)
+    caches = [sg.KvCache(gpu, L, nkv, hd, max_seq, n_seqs=6) for _ in range(2)]
+    try:
+        # shared history: positions 0..199 of every sequence, stored in both caches
+        hist_k = oracle.gen_x(SEED, 700 + hd, (max_seq, nkv * hd))
+        hist_v = oracle.gen_x(SEED, 701 + hd, (max_seq, nkv * hd))
+        for c in caches:
+            for s in range(6):
+                _store(ops, c, 1, hist_k, hist_v, list(range(max_seq)), [s] * max_seq)
+        for call, pos in enumerate(([0, 63, 64, 65, 160, 199], [1, 127, 128, 129, 10, 198])):
+            rows = len(pos)
+            q = oracle.gen_x(SEED, 710 + call, (rows, nq * hd))
+            k = oracle.gen_x(SEED, 711 + call, (rows, nkv * hd))
+            v = oracle.gen_x(SEED, 712 + call, (rows, nkv * hd))
+            pd = _t(np.array(pos, np.int32))
+            sd = _t(np.array([5, 0, 3, 1, 2, 4], np.int32))
+            # two-call form on cache 0
+            q0, k0, v0 = _t(q), _t(k), _t(v)
+            out0 = torch.full((rows, nq * hd), float("nan"), device="cuda")
+            ops.rope_kv(rope, caches[0], 1, q0.data_ptr(), nq * hd, k0.data_ptr(), nkv * hd, v0.data_ptr(), nkv * hd,
+                        pd.data_ptr(), sd.data_ptr(), rows, nq)
+            ops.attention(caches[0], 1, q0.data_ptr(), nq * hd, out0.data_ptr(), nq * hd, pd.data_ptr(), None,
+                          sd.data_ptr(), rows, nq)
+            # fused form on cache 1
+            q1, k1, v1 = _t(q), _t(k), _t(v)
+            out1 = torch.full((rows, nq * hd), float("nan"), device="cuda")
+            ops.rope_attention(rope, caches[1], 1, q1.data_ptr(), nq * hd, k1.data_ptr(), nkv * hd, v1.data_ptr(),
+                               nkv * hd, out1.data_ptr(), nq * hd, pd.data_ptr(), sd.data_ptr(), rows, nq)
+            gpu.synchronize()
+            assert np.array_equal(out0.cpu().numpy().view(np.uint32), out1.cpu().numpy().view(np.uint32))
+            assert np.array_equal(q1.cpu().numpy(), q) and np.array_equal(k1.cpu().numpy(), k)
+            for s in range(6):
+                for h in range(nkv):
+                    a = [_read_f32(p, max_seq * hd) for p in caches[0].ptrs(s, 1, h)]
+                    b = [_read_f32(p, max_seq * hd) for p in caches[1].ptrs(s, 1, h)]
+                    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+    finally:
+        rope.free()
+        for c in caches:
+            c.free()
