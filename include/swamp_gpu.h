@@ -324,9 +324,8 @@ SG_API int sg_attention_device(sg_kv_cache_t cache, int layer, const float *q, i
  * sequence, so rows <= the cache's n_seqs) at position pos[r]; it rotates
  * q and k with the table row, stores k and v at pos[r], and attends
  * positions 0..pos[r]. q, k and v are read and left unchanged; out gets the
- * attention output. The results are the same bits as the two-call form. The
- * per-(row, KV head) split counters live in a per-device array that grows
- * on first use, like the attention workspace. */
+ * attention output. The results are the same bits as the two-call form.
+ * It shares the attention workspace (grows on first use). */
 SG_API int sg_rope_attention_device(sg_rope_t rope, sg_kv_cache_t cache, int layer, const float *q, int64_t ldq,
                                     const float *k, int64_t ldk, const float *v, int64_t ldv, float *out,
                                     int64_t ldo, const int32_t *pos, const int32_t *seq, int rows, int n_heads,

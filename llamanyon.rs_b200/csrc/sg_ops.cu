@@ -427,9 +427,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
       rec[1] = mls[2 * j + 1];
     }
   }
-  if constexpr (DECODE) {
+  if (DECODE && a.counters) {
     // the last split of this (row, KV head) to finish combines its heads:
-    // out = sum_s e_s acc_s / sum_s e_s l_s, e_s = exp(m_s - max_s m_s)
+    // out = sum_s e_s acc_s / sum_s e_s l_s, e_s = exp(m_s - max_s m_s),
+    // the same operations in the same order as attn_combine_kernel
     const int ns = valid_end / kAttnP + 1;
     __threadfence();
     __syncthreads();
@@ -437,19 +438,51 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
     __syncthreads();
     if (!last_flag) return;
     __threadfence();
-    for (int i = tid; i < n_rep * HD; i += kAttnThreads) {
-      const int j = i / HD, d = i - j * HD;
-      const int h = g * n_rep + j;
-      const float* rec = a.ws + ((int64_t)r * a.n_heads + h) * a.n_split * (HD + 2);
+    const float* rec0 = a.ws + ((int64_t)r * a.n_heads + g * n_rep) * a.n_split * (HD + 2);
+    const int64_t hstride = (int64_t)a.n_split * (HD + 2);
+    // per head: M (a warp max) and e_s for the first 64 splits in shared
+    // memory (later ones are recomputed), then L in split order
+    for (int j = warp; j < n_rep; j += kAttnThreads / 32) {
+      const float* rj = rec0 + j * hstride;
       float M = -INFINITY;
-      for (int q = 0; q < ns; ++q) M = fmaxf(M, __ldcg(rec + q * (HD + 2)));
-      float L = 0.f, acc = 0.f;
-      for (int q = 0; q < ns; ++q) {
-        const float e = expf(__ldcg(rec + q * (HD + 2)) - M);
-        L = fmaf(e, __ldcg(rec + q * (HD + 2) + 1), L);
-        acc = fmaf(e, __ldcg(rec + q * (HD + 2) + 2 + d), acc);
+      for (int q = lane; q < ns; q += 32) M = fmaxf(M, __ldcg(rj + q * (HD + 2)));
+      M = warp_max(M);
+      for (int q = lane; q < ns && q < kAttnP; q += 32) sc[j * kAttnP + q] = expf(__ldcg(rj + q * (HD + 2)) - M);
+      __syncwarp();
+      if (lane == 0) {
+        float L = 0.f;
+        for (int q = 0; q < ns; ++q) {
+          const float e = q < kAttnP ? sc[j * kAttnP + q] : expf(__ldcg(rj + q * (HD + 2)) - M);
+          L = fmaf(e, __ldcg(rj + q * (HD + 2) + 1), L);
+        }
+        mls[2 * j] = M;
+        mls[2 * j + 1] = L;
       }
-      a.out[(int64_t)r * a.ldo + (int64_t)h * HD + d] = acc / L;
+    }
+    __syncthreads();
+    // outputs four at a time per thread, so that four loads are in flight
+    for (int i0 = tid; i0 < n_rep * HD; i0 += 4 * kAttnThreads) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      int jj[4], dd[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = min(i0 + u * kAttnThreads, n_rep * HD - 1);
+        jj[u] = i / HD;
+        dd[u] = i - jj[u] * HD;
+      }
+      for (int q = 0; q < ns; ++q) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float* rq = rec0 + jj[u] * hstride + q * (HD + 2);  // split q's record of head jj[u]
+          const float e = q < kAttnP ? sc[jj[u] * kAttnP + q] : expf(__ldcg(rq) - mls[2 * jj[u]]);
+          acc[u] = fmaf(e, __ldcg(rq + 2 + dd[u]), acc[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * kAttnThreads;
+        if (i < n_rep * HD) a.out[(int64_t)r * a.ldo + (int64_t)(g * n_rep + jj[u]) * HD + dd[u]] = acc[u] / mls[2 * jj[u] + 1];
+      }
     }
     if (tid == 0) a.counters[r * a.kv.n_kv_heads + g] = 0;
   }
@@ -633,13 +666,14 @@ int attention_launch(const ops::AttnArgs& a, dim3 g1, dim3 g2, float* out, int64
                                   (int)ops::AttnSmem<HD>::kBytes));
     attr_done[dev] = 1;
   }
-  if (a.counters) {  // decode form: RoPE, cache store and combine inside the split kernel
+  if (a.lut) {  // decode form: RoPE and the cache store inside the split kernel
     CUDA_TRY(ops::launch(ops::attn_split_kernel<HD, true>, g1, dim3(ops::kAttnThreads), ops::AttnSmem<HD>::kBytes, st,
                          a));
-    return SG_OK;
+    if (a.counters) return SG_OK;  // the last split combined
+  } else {
+    CUDA_TRY(ops::launch(ops::attn_split_kernel<HD, false>, g1, dim3(ops::kAttnThreads), ops::AttnSmem<HD>::kBytes,
+                         st, a));
   }
-  CUDA_TRY(ops::launch(ops::attn_split_kernel<HD, false>, g1, dim3(ops::kAttnThreads), ops::AttnSmem<HD>::kBytes, st,
-                       a));
   CUDA_TRY(ops::launch(ops::attn_combine_kernel<HD>, g2, dim3(HD), 0, st, a, out, ldo));
   return SG_OK;
 }
@@ -901,6 +935,11 @@ int sg_rope_attention_device(sg_rope_t rope, sg_kv_cache_t cache, int layer, con
     CUDA_TRY(cudaMemset(d->attn_cnt, 0, d->attn_cnt_bytes));
   }
   a.counters = static_cast<unsigned int*>(d->attn_cnt);
+  // The split kernel can also combine in the last CTA of each (row, KV
+  // head) (a.counters); measured at 1 token per sequence that CTA's
+  // serialised loads cost more than a separate combine launch, so the
+  // combine runs as its own kernel.
+  a.counters = nullptr;
   cudaStream_t st = (cudaStream_t)stream;
   const dim3 g1(a.n_split, nkv, rows), g2(n_heads, rows);
   switch (hd) {

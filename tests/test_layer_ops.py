@@ -417,14 +417,16 @@ def test_host_validation(gpu, ops):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("nq,nkv,hd", [(32, 8, 128), (8, 2, 64), (16, 2, 256)])
-def test_rope_attention_fused_matches_two_calls(gpu, oracle, ops, nq, nkv, hd):
+@pytest.mark.parametrize("nq,nkv,hd,max_seq", [(32, 8, 128, 200), (8, 2, 64, 200), (16, 2, 256, 200),
+                                               (8, 2, 64, 4300)])
+def test_rope_attention_fused_matches_two_calls(gpu, oracle, ops, nq, nkv, hd, max_seq):
     """sg_rope_attention_device (one row per sequence) gives the same bits as
     sg_rope_kv_device + sg_attention_device, output and cache, at positions
-    on and around the 64-position split edges, over two calls in a row."""
+    on and around the 64-position split edges (and past 64 splits), over two
+    calls in a row."""
     import torch
     import swamp_gpu as sg
-    L, max_seq, ctx = 2, 200, 150
+    L, ctx = 2, 150
     rope = sg.Rope(gpu, hd, ctx)
     caches = [sg.KvCache(gpu, L, nkv, hd, max_seq, n_seqs=6) for _ in range(2)]
     try:
@@ -434,7 +436,10 @@ def test_rope_attention_fused_matches_two_calls(gpu, oracle, ops, nq, nkv, hd):
         for c in caches:
             for s in range(6):
                 _store(ops, c, 1, hist_k, hist_v, list(range(max_seq)), [s] * max_seq)
-        for call, pos in enumerate(([0, 63, 64, 65, 160, 199], [1, 127, 128, 129, 10, 198])):
+        plan = ([0, 63, 64, 65, 160, 199], [1, 127, 128, 129, 10, 198])
+        if max_seq > 4096:
+            plan = ([4290, 64, 4100, 0, 4160, 4299], [4291, 4095, 4096, 1, 2000, 4097])
+        for call, pos in enumerate(plan):
             rows = len(pos)
             q = oracle.gen_x(SEED, 710 + call, (rows, nq * hd))
             k = oracle.gen_x(SEED, 711 + call, (rows, nkv * hd))
