@@ -184,3 +184,56 @@ class Decoder:
     def free(self):
         self.rope.free()
         self.cache.free()
+
+
+def main(argv=None):
+    """Greedy generation with a random-init Llama-3-8B-shaped Q4_K model:
+    python llamanyon.rs_b200/decoder.py --layers 32 --batch 1 --prompt 512 --new 16
+    (one eager prefill pass, then eager decode steps; prints the device time
+    per decode step and the first sequence's tokens)."""
+    import argparse
+    import time
+
+    import torch
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--new", type=int, default=16)
+    ap.add_argument("--seed", type=int, default=0x5EED1A11)
+    a = ap.parse_args(argv)
+    gpu = sg.SwampGpu()
+    gpu.init(1)
+    cfg = DecoderConfig(n_layers=a.layers, d=4096, n_heads=32, n_kv_heads=8, ffn=14336, vocab=128256,
+                        max_seq=max(2048, a.prompt + a.new))
+    model = SynthModel(gpu, cfg, a.seed)
+    B, P = a.batch, a.prompt
+    D = Decoder(gpu, model, n_seqs=B, max_rows=B * P)
+    prompts = np.random.default_rng(a.seed).integers(0, cfg.vocab, size=(B, P))
+    # rows in (position, sequence) order: the last B rows are the last position
+    rows = D.set_rows(prompts.T.reshape(-1), np.repeat(np.arange(P), B), np.tile(np.arange(B), P))
+    D.forward(rows, logits_rows=slice(rows - B, rows))
+    out = [D.next[:B].cpu().tolist()]
+    D.tokens[:B].copy_(D.next[:B])
+    D.pos[:B].fill_(P)
+    D.seq[:B].copy_(torch.arange(B, dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(a.new - 1):
+        D.forward(B, decode=True)
+        D.advance(B)
+        out.append(D.tokens[:B].cpu().tolist())
+    torch.cuda.synchronize()
+    gpu.synchronize()
+    el = time.perf_counter() - t0
+    print(f"decode: {el * 1e3 / max(1, a.new - 1):.3f} ms per step (eager, host-launched), "
+          f"sequence 0: {[t[0] for t in out]}")
+    D.free()
+    model.free()
+    gpu.shutdown()
+    return 0
+
+
+if __name__ == "__main__":
+    import sys
+    sys.exit(main())
