@@ -96,14 +96,31 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 // out = (x * inv) * w, each step one IEEE operation as in ops.rs:190-199;
 // only the summation order of ss differs (a tree instead of a running sum).
 constexpr int kNormThreads = 512;
+constexpr int kNormRegs = 8;  // elements per thread kept in registers (rows up to 4096 read once)
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* x, int64_t ldx, const float* __restrict__ w,
                                                               float* out, int64_t ldo, int n, float eps) {
   __shared__ float red[kNormThreads / 32];
-  pdl_enter();
+  pdl_launch_dependents();
+  // the norm weights are constant: fetch them before waiting for the
+  // previous kernel, whose output x is
+  float wv[kNormRegs];
+#pragma unroll
+  for (int u = 0; u < kNormRegs; ++u) {
+    const int i = threadIdx.x + u * kNormThreads;
+    wv[u] = i < n ? w[i] : 0.f;
+  }
+  pdl_wait();
   const float* xr = x + (int64_t)blockIdx.x * ldx;
   float* orow = out + (int64_t)blockIdx.x * ldo;
+  float xv[kNormRegs];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += kNormThreads) ss = __fmaf_rn(xr[i], xr[i], ss);
+#pragma unroll
+  for (int u = 0; u < kNormRegs; ++u) {
+    const int i = threadIdx.x + u * kNormThreads;
+    xv[u] = i < n ? xr[i] : 0.f;
+    ss = __fmaf_rn(xv[u], xv[u], ss);
+  }
+  for (int i = threadIdx.x + kNormRegs * kNormThreads; i < n; i += kNormThreads) ss = __fmaf_rn(xr[i], xr[i], ss);
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
@@ -113,7 +130,13 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* x, i
   ss = __fdiv_rn(ss, (float)n);
   ss = __fadd_rn(ss, eps);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ss));
-  for (int i = threadIdx.x; i < n; i += kNormThreads) orow[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+#pragma unroll
+  for (int u = 0; u < kNormRegs; ++u) {
+    const int i = threadIdx.x + u * kNormThreads;
+    if (i < n) orow[i] = __fmul_rn(__fmul_rn(xv[u], inv), wv[u]);
+  }
+  for (int i = threadIdx.x + kNormRegs * kNormThreads; i < n; i += kNormThreads)
+    orow[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
 }
 
 // -------------------------------------------------------- RoPE + cache store
