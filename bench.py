@@ -558,12 +558,12 @@ def model_decode_bench(torch, gpu, args):
             def prefill_rows():
                 return D.set_rows(prompts.T.reshape(-1), np.repeat(np.arange(P), B), np.tile(np.arange(B), P))
             rows = prefill_rows()
-            D.forward(rows, stream=st.cuda_stream, logits_rows=slice(rows - B, rows))  # first use: workspaces
+            D.forward(rows, stream=st.cuda_stream, logits_rows=slice(rows - B, rows), prefill=(B, P, 1, B))  # first use: workspaces
             st.synchronize()
             e0, e1 = ev(), ev()
             e0.record(st)
             rows = prefill_rows()  # H2D of the prompt inside the timed region
-            D.forward(rows, stream=st.cuda_stream, logits_rows=slice(rows - B, rows))
+            D.forward(rows, stream=st.cuda_stream, logits_rows=slice(rows - B, rows), prefill=(B, P, 1, B))
             host_tok.copy_(D.next[:B], non_blocking=True)
             e1.record(st)
             st.synchronize()
@@ -619,7 +619,7 @@ def model_decode_bench(torch, gpu, args):
             "weight_bytes_per_step": wbytes_step, "runs": runs,
             "execution": "prefill: one eager pass; decode: one CUDA graph per token",
             "ops": "sg_embed / sg_rmsnorm / sg_linear_multi (QKV, gate+up) / sg_rope_attention (decode; "
-                   "sg_rope_kv + sg_attention at prefill) / "
+                   "sg_rope_kv + sg_attention_prefill at prefill) / "
                    "sg_linear + accumulate (O, down) / sg_silu_mul / sg_argmax"}
 
 

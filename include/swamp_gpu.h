@@ -331,6 +331,20 @@ SG_API int sg_rope_attention_device(sg_rope_t rope, sg_kv_cache_t cache, int lay
                                     int64_t ldo, const int32_t *pos, const int32_t *seq, int rows, int n_heads,
                                     void *stream);
 
+/* The batched prefill's attention (executor.rs:113-141): positions
+ * 0..n_tokens-1 of sequences 0..n_seqs-1, whose K and V rows the cache
+ * already holds (sg_rope_kv_device stored them), each attending positions
+ * 0..t of its own sequence. The row of (sequence s, position t) in q and out
+ * is s * row_stride_seq + t * row_stride_pos. Same results as
+ * sg_attention_device with pos = t and seq = s per row, within the attention
+ * tolerance (another summation order); one CTA serves a block of positions
+ * of one KV head, so each K/V tile is read once per block instead of once
+ * per position. head_dim 64 or 128; q and out 16-byte aligned with
+ * ldq, ldo multiples of 4. */
+SG_API int sg_attention_prefill_device(sg_kv_cache_t cache, int layer, const float *q, int64_t ldq, float *out,
+                                       int64_t ldo, int n_seqs, int n_tokens, int64_t row_stride_seq,
+                                       int64_t row_stride_pos, int n_heads, void *stream);
+
 /* silu then mul_in_place (ops.rs:203-214): g = g / (1 + exp(-g)) * u. */
 SG_API int sg_silu_mul_device(float *g, int64_t ldg, const float *u, int64_t ldu, int n, int rows, void *stream);
 /* add_in_place (ops.rs:216-220): x += y. (A linear's SG_FLAG_ACCUMULATE

@@ -536,6 +536,223 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(AttnArgs a, float* out
   o[d] = acc / L;
 }
 
+// ------------------------------------------------------- prefill attention
+// All prompt positions of a batch of sequences at once (the batched prefill,
+// executor.rs:113-141, where the reference attends each position in turn).
+// The row of (sequence s, position t) is s * row_stride_seq + t *
+// row_stride_pos; position t attends positions 0..t of its own sequence,
+// whose K and V rows the cache already holds.
+//
+// A CTA of 256 threads takes one (sequence, KV head) and a block of QB
+// consecutive positions for all n_rep query heads of that KV head (R = n_rep
+// x QB = 128 query rows, Q in shared memory), and walks the keys 0 .. last
+// position of the block in tiles of 32, each brought into shared memory by
+// two bulk copies. Per tile: scores S = Q K^T * scale for the 128 x 32 block
+// (a thread computes 4 rows x 4 keys; the 8 lanes of a shared-memory phase
+// start their walk over head_dim at different float4 columns, so the K and
+// Q reads of a phase fall in different banks), the causal mask, an online
+// softmax update per row (running max and sum; the O rows are rescaled when
+// the max moves), then O += P V (a thread holds 4 rows x 4 dims per tile of
+// O in registers). Everything in f32: the same products as the split
+// kernel, in another summation order.
+constexpr int kPfThreads = 256;
+constexpr int kPfRows = 128;  // query rows per CTA (n_rep x QB)
+constexpr int kPfKeys = 32;   // keys per tile
+
+template <int HD>
+struct PfSmem {
+  static constexpr size_t kQ = 0;                                            // [R][HD]
+  static constexpr size_t kK = kQ + (size_t)kPfRows * HD * 4;                // [32][HD]
+  static constexpr size_t kV = kK + (size_t)kPfKeys * HD * 4;                // [32][HD]
+  static constexpr size_t kS = kV + (size_t)kPfKeys * HD * 4;                // [R][32]
+  static constexpr size_t kM = kS + (size_t)kPfRows * kPfKeys * 4;           // running max [R]
+  static constexpr size_t kL = kM + (size_t)kPfRows * 4;                     // running sum [R]
+  static constexpr size_t kC = kL + (size_t)kPfRows * 4;                     // rescale [R]
+  static constexpr size_t kBar = kC + (size_t)kPfRows * 4;
+  static constexpr size_t kBytes = kBar + 16;
+};
+
+struct PfArgs {
+  KvView kv;
+  int layer;
+  const float* q;
+  int64_t ldq;
+  float* out;
+  int64_t ldo;
+  int n_tokens, n_heads, n_rep, qb;  // qb: positions per CTA (R / n_rep)
+  int64_t rs_seq, rs_pos;            // row strides
+  float scale;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(PfArgs a) {
+  using L = PfSmem<HD>;
+  constexpr int NC = HD / 4;
+  constexpr int OT = kPfRows * HD / 16 / kPfThreads;  // 4x4 O tiles per thread
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* Qs = reinterpret_cast<float*>(smem + L::kQ);
+  float* Ks = reinterpret_cast<float*>(smem + L::kK);
+  float* Vs = reinterpret_cast<float*>(smem + L::kV);
+  float* Ss = reinterpret_cast<float*>(smem + L::kS);
+  float* Ms = reinterpret_cast<float*>(smem + L::kM);
+  float* Ls = reinterpret_cast<float*>(smem + L::kL);
+  float* Cs = reinterpret_cast<float*>(smem + L::kC);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  __shared__ int ok_flag;
+  pdl_launch_dependents();
+  pdl_wait();  // q and the cache rows come from the previous kernels
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qblk = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+  const int n_rep = a.n_rep, qb = a.qb, R = n_rep * qb;
+  const int p0 = qblk * qb;
+  if (p0 >= a.n_tokens) return;
+  const int p1 = min(a.n_tokens, p0 + qb);  // positions p0 .. p1-1
+  // Q rows: row j * qb + i is query head g * n_rep + j at position p0 + i
+  for (int e = tid; e < kPfRows * NC; e += kPfThreads) {
+    const int row = e / NC, c = e - row * NC;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < R) {
+      const int j = row / qb, i = row - j * qb;
+      if (p0 + i < p1)
+        v = *reinterpret_cast<const float4*>(a.q + (int64_t)s * a.rs_seq * a.ldq + (int64_t)(p0 + i) * a.rs_pos * a.ldq +
+                                             (int64_t)(g * n_rep + j) * HD + 4 * c);
+    }
+    reinterpret_cast<float4*>(Qs)[e] = v;
+  }
+  for (int r = tid; r < kPfRows; r += kPfThreads) {
+    Ms[r] = -INFINITY;
+    Ls[r] = 0.f;
+  }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_fence_init();
+  }
+  float o[OT][16];
+#pragma unroll
+  for (int u = 0; u < OT; ++u)
+#pragma unroll
+    for (int e = 0; e < 16; ++e) o[u][e] = 0.f;
+  __syncthreads();
+  const size_t hoff = a.kv.head_off(s, a.layer, g);
+  const int n_tiles = (p1 + kPfKeys - 1) / kPfKeys;
+  for (int kt = 0; kt < n_tiles; ++kt) {
+    const int k0 = kt * kPfKeys, nk = min(kPfKeys, p1 - k0);
+    if (tid == 0) {
+      const uint32_t bytes = (uint32_t)nk * HD * 4;
+      mbar_arrive_expect_tx(bar, 2 * bytes);
+      bulk_g2s(Ks, a.kv.k + hoff + (size_t)k0 * HD, bytes, bar);
+      bulk_g2s(Vs, a.kv.v + hoff + (size_t)k0 * HD, bytes, bar);
+      ok_flag = mbar_wait(bar, kt & 1, 0x41) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!ok_flag) {  // the bounded wait gave up (error recorded): let the copies land, then leave
+      if (tid == 0) mbar_wait_drain(bar, kt & 1);
+      return;
+    }
+    mbar_test(bar, kt & 1);  // completed: acquire the copied rows in this thread
+    // S = Q K^T * scale: tile t -> rows 4 * (t / 8) .., keys 4 * (t % 8) ..
+    for (int t = tid; t < (R / 4) * (kPfKeys / 4); t += kPfThreads) {
+      const int rg = t >> 3, kg = t & 7;
+      float acc[4][4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
+      if (4 * kg < nk) {
+#pragma unroll 4
+        for (int i = 0; i < NC; ++i) {
+          const int c = (i + kg) & (NC - 1);
+          float4 qv[4], kv4[4];
+#pragma unroll
+          for (int x = 0; x < 4; ++x) qv[x] = reinterpret_cast<const float4*>(Qs + (4 * rg + x) * HD)[c];
+#pragma unroll
+          for (int y = 0; y < 4; ++y) kv4[y] = reinterpret_cast<const float4*>(Ks + (4 * kg + y) * HD)[c];
+#pragma unroll
+          for (int x = 0; x < 4; ++x)
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+              acc[x][y] = fmaf(qv[x].x, kv4[y].x, acc[x][y]);
+              acc[x][y] = fmaf(qv[x].y, kv4[y].y, acc[x][y]);
+              acc[x][y] = fmaf(qv[x].z, kv4[y].z, acc[x][y]);
+              acc[x][y] = fmaf(qv[x].w, kv4[y].w, acc[x][y]);
+            }
+        }
+      }
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const int row = 4 * rg + x;
+        const int qp = p0 + (row % qb);
+#pragma unroll
+        for (int y = 0; y < 4; ++y) {
+          const int kj = 4 * kg + y, kp = k0 + kj;
+          Ss[row * kPfKeys + kj] = (kj < nk && kp <= qp) ? acc[x][y] * a.scale : -INFINITY;
+        }
+      }
+    }
+    __syncthreads();
+    // online softmax: a warp per 16 rows, a lane per key
+    for (int row = warp; row < R; row += kPfThreads / 32) {
+      const float sv = Ss[row * kPfKeys + lane];
+      const float mt = warp_max(sv);
+      const float m_old = Ms[row];
+      const float m_new = fmaxf(m_old, mt);
+      const float pe = m_new == -INFINITY ? 0.f : expf(sv - m_new);
+      const float ls = warp_sum(pe);
+      Ss[row * kPfKeys + lane] = pe;
+      if (lane == 0) {
+        const float corr = m_new == -INFINITY ? 1.f : expf(m_old - m_new);  // exp(-inf) = 0 on the first tile
+        Cs[row] = corr;
+        Ls[row] = Ls[row] * corr + ls;
+        Ms[row] = m_new;
+      }
+    }
+    __syncthreads();
+    // O = O * corr + P V: O tile u of this thread -> rows 4 * (i / NC) .., dims 4 * (i % NC) ..
+#pragma unroll
+    for (int u = 0; u < OT; ++u) {
+      const int i = tid + u * kPfThreads;
+      const int rg = i / NC, dc = i - rg * NC;
+      if (4 * rg >= R) continue;
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const float cr = Cs[4 * rg + x];
+#pragma unroll
+        for (int y = 0; y < 4; ++y) o[u][4 * x + y] *= cr;
+      }
+      for (int kj = 0; kj < nk; ++kj) {
+        const float4 v4 = reinterpret_cast<const float4*>(Vs + kj * HD)[dc];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const float p = Ss[(4 * rg + x) * kPfKeys + kj];
+          o[u][4 * x + 0] = fmaf(p, v4.x, o[u][4 * x + 0]);
+          o[u][4 * x + 1] = fmaf(p, v4.y, o[u][4 * x + 1]);
+          o[u][4 * x + 2] = fmaf(p, v4.z, o[u][4 * x + 2]);
+          o[u][4 * x + 3] = fmaf(p, v4.w, o[u][4 * x + 3]);
+        }
+      }
+    }
+    __syncthreads();  // K, V and S are rewritten by the next tile
+  }
+  // out = O / l
+#pragma unroll
+  for (int u = 0; u < OT; ++u) {
+    const int i = tid + u * kPfThreads;
+    const int rg = i / NC, dc = i - rg * NC;
+    if (4 * rg >= R) continue;
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+      const int row = 4 * rg + x;
+      const int j = row / qb, qi = row - j * qb;
+      if (p0 + qi >= p1) continue;
+      const float l = Ls[row];
+      float* op = a.out + (int64_t)s * a.rs_seq * a.ldo + (int64_t)(p0 + qi) * a.rs_pos * a.ldo +
+                  (int64_t)(g * n_rep + j) * HD + 4 * dc;
+      *reinterpret_cast<float4*>(op) =
+          make_float4(o[u][4 * x] / l, o[u][4 * x + 1] / l, o[u][4 * x + 2] / l, o[u][4 * x + 3] / l);
+    }
+  }
+}
+
 // ------------------------------------------------------------- elementwise
 // g = silu(g) * u with silu(v) = v / (1 + exp(-v)) (ops.rs:203-214).
 __global__ void silu_mul_kernel(float* g, int64_t ldg, const float* u, int64_t ldu, int n, int64_t total) {
@@ -973,6 +1190,65 @@ int sg_rope_attention_device(sg_rope_t rope, sg_kv_cache_t cache, int layer, con
     default:
       return attention_launch<256>(a, g1, g2, out, ldo, st);
   }
+}
+
+int sg_attention_prefill_device(sg_kv_cache_t cache, int layer, const float* q, int64_t ldq, float* out, int64_t ldo,
+                                int n_seqs, int n_tokens, int64_t row_stride_seq, int64_t row_stride_pos, int n_heads,
+                                void* stream) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  DevState* d = nullptr;
+  int rc = op_device(&d);
+  if (rc) return rc;
+  if (!cache || !q || !out) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  if (layer < 0 || layer >= cache->n_layers) return fail(SG_ERR_INVALID_ARG, "layer %d out of range", layer);
+  const int hd = cache->head_dim, nkv = cache->n_kv_heads;
+  if (hd != 64 && hd != 128) return fail(SG_ERR_UNSUPPORTED, "prefill attention: head_dim %d (64 or 128)", hd);
+  if (n_heads < nkv || n_heads % nkv || n_heads / nkv > ops::kMaxRep)
+    return fail(SG_ERR_UNSUPPORTED, "n_heads %d over %d KV heads (a multiple, at most %d per KV head)", n_heads, nkv,
+                ops::kMaxRep);
+  if (n_seqs < 0 || n_seqs > cache->n_seqs || n_tokens < 0 || n_tokens > cache->max_seq)
+    return fail(SG_ERR_INVALID_ARG, "%d sequences x %d tokens outside the cache (%d x %d)", n_seqs, n_tokens,
+                cache->n_seqs, cache->max_seq);
+  if (row_stride_seq < 0 || row_stride_pos < 0 || ldq < (int64_t)n_heads * hd || ldo < (int64_t)n_heads * hd)
+    return fail(SG_ERR_INVALID_ARG, "bad strides");
+  if (!aligned16(q) || (ldq & 3) || !aligned16(out) || (ldo & 3))
+    return fail(SG_ERR_INVALID_ARG, "q and out must be 16-byte aligned with row strides that are multiples of 4");
+  if (n_seqs == 0 || n_tokens == 0) return SG_OK;
+  ops::PfArgs a = {};
+  a.kv = kv_view(cache);
+  a.layer = layer;
+  a.q = q;
+  a.ldq = ldq;
+  a.out = out;
+  a.ldo = ldo;
+  a.n_tokens = n_tokens;
+  a.n_heads = n_heads;
+  a.n_rep = n_heads / nkv;
+  a.qb = (ops::kPfRows / a.n_rep) & ~3;  // positions per CTA: n_rep x qb <= 128 rows, whole 4-row groups
+  a.rs_seq = row_stride_seq;
+  a.rs_pos = row_stride_pos;
+  a.scale = 1.0f / sqrtf((float)hd);  // ops.rs:93
+  const dim3 grid((unsigned)((n_tokens + a.qb - 1) / a.qb), (unsigned)nkv, (unsigned)n_seqs);
+  cudaStream_t st = (cudaStream_t)stream;
+  static int attr_done[64][2] = {};
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (hd == 64) {
+    if (dev < 64 && !attr_done[dev][0]) {
+      CUDA_TRY(cudaFuncSetAttribute(ops::attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)ops::PfSmem<64>::kBytes));
+      attr_done[dev][0] = 1;
+    }
+    CUDA_TRY(ops::launch(ops::attn_prefill_kernel<64>, grid, dim3(ops::kPfThreads), ops::PfSmem<64>::kBytes, st, a));
+  } else {
+    if (dev < 64 && !attr_done[dev][1]) {
+      CUDA_TRY(cudaFuncSetAttribute(ops::attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)ops::PfSmem<128>::kBytes));
+      attr_done[dev][1] = 1;
+    }
+    CUDA_TRY(ops::launch(ops::attn_prefill_kernel<128>, grid, dim3(ops::kPfThreads), ops::PfSmem<128>::kBytes, st, a));
+  }
+  return SG_OK;
 }
 
 int sg_silu_mul_device(float* g, int64_t ldg, const float* u, int64_t ldu, int n, int rows, void* stream) {

@@ -140,11 +140,15 @@ class Decoder:
         return n
 
     def forward(self, rows: int, stream: int | None = None, logits_rows: slice | None = None,
-                decode: bool = False):
+                decode: bool = False, prefill: tuple | None = None):
         """One forward pass of `rows` rows: logits (and the greedy pick in
         `next`) for the rows in logits_rows (default: all). decode=True for
         a step of one row per sequence: RoPE, the cache store and attention
-        then run as one kernel per layer."""
+        then run as one kernel per layer. prefill=(n_seqs, n_tokens,
+        row_stride_seq, row_stride_pos) for a prompt pass whose rows are
+        positions 0..n_tokens-1 of sequences 0..n_seqs-1 at those row
+        strides: attention then serves blocks of positions per CTA."""
+        use_pf = prefill is not None and self.cfg.head_dim in (64, 128)
         c, o, g = self.cfg, self.ops, self.gpu
         p = lambda t: t.data_ptr()
         D, KV = c.d, c.n_kv_heads * c.head_dim
@@ -160,8 +164,11 @@ class Decoder:
             else:
                 o.rope_kv(self.rope, self.cache, l, p(self.q), D, p(self.k), KV, p(self.v), KV, p(self.pos),
                           p(self.seq), rows, c.n_heads, stream)
-                o.attention(self.cache, l, p(self.q), D, p(self.att), D, p(self.pos), None, p(self.seq), rows,
-                            c.n_heads, stream)
+                if use_pf:
+                    o.attention_prefill(self.cache, l, p(self.q), D, p(self.att), D, *prefill, c.n_heads, stream)
+                else:
+                    o.attention(self.cache, l, p(self.q), D, p(self.att), D, p(self.pos), None, p(self.seq), rows,
+                                c.n_heads, stream)
             g.linear_device(lw["attn_output"], p(self.att), D, p(self.x), D, rows, stream=stream, flags=ACC)
             o.rmsnorm(p(self.x), D, p(self.m.ffn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
             g.linear_multi_device([lw["ffn_gate"], lw["ffn_up"]], p(self.xn), D, [p(self.gate), p(self.up)],
@@ -212,7 +219,7 @@ def main(argv=None):
     prompts = np.random.default_rng(a.seed).integers(0, cfg.vocab, size=(B, P))
     # rows in (position, sequence) order: the last B rows are the last position
     rows = D.set_rows(prompts.T.reshape(-1), np.repeat(np.arange(P), B), np.tile(np.arange(B), P))
-    D.forward(rows, logits_rows=slice(rows - B, rows))
+    D.forward(rows, logits_rows=slice(rows - B, rows), prefill=(B, P, 1, B))
     out = [D.next[:B].cpu().tolist()]
     D.tokens[:B].copy_(D.next[:B])
     D.pos[:B].fill_(P)

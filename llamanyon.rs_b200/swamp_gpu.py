@@ -41,7 +41,7 @@ EXPORTS = (
     "sg_gguf_kv_int", "sg_gguf_kv_float", "sg_gguf_kv_string", "sg_gguf_register",
     "sg_synth_weight", "sg_synth_blocks", "sg_synth_x",
     "sg_rope_create", "sg_rope_free", "sg_rope_table", "sg_kv_cache_create", "sg_kv_cache_free", "sg_kv_cache_ptr",
-    "sg_rmsnorm_device", "sg_rope_kv_device", "sg_attention_device", "sg_rope_attention_device", "sg_silu_mul_device", "sg_add_device",
+    "sg_rmsnorm_device", "sg_rope_kv_device", "sg_attention_device", "sg_rope_attention_device", "sg_attention_prefill_device", "sg_silu_mul_device", "sg_add_device",
     "sg_argmax_device", "sg_embed_device", "sg_allreduce_device", "sg_allreduce_path",
 )
 SG_ERR_FORMAT, SG_ERR_NOT_FOUND = -8, -9
@@ -103,6 +103,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     L.sg_rope_kv_device.argtypes = [P, P, i32, P, i64, P, i64, P, i64, P, P, i32, i32, P]
     L.sg_attention_device.argtypes = [P, i32, P, i64, P, i64, P, P, P, i32, i32, P]
     L.sg_rope_attention_device.argtypes = [P, P, i32, P, i64, P, i64, P, i64, P, i64, P, P, i32, i32, P]
+    L.sg_attention_prefill_device.argtypes = [P, i32, P, i64, P, i64, i32, i32, i64, i64, i32, P]
     L.sg_silu_mul_device.argtypes = [P, i64, P, i64, i32, i32, P]
     L.sg_add_device.argtypes = [P, i64, P, i64, i32, i32, P]
     L.sg_argmax_device.argtypes = [P, i64, i32, i32, P, P]
@@ -371,6 +372,13 @@ class LayerOps:
         """Decode form: RoPE, cache store and attention of one row per sequence."""
         self.lib._check(self.L.sg_rope_attention_device(rope.handle, cache.handle, layer, q, ldq, k, ldk, v, ldv, out,
                                                         ldo, pos, seq or None, rows, n_heads, stream or None))
+
+    def attention_prefill(self, cache: KvCache, layer: int, q: int, ldq: int, out: int, ldo: int, n_seqs: int,
+                          n_tokens: int, row_stride_seq: int, row_stride_pos: int, n_heads: int,
+                          stream: int | None = None):
+        """Causal attention of every prompt position of n_seqs sequences."""
+        self.lib._check(self.L.sg_attention_prefill_device(cache.handle, layer, q, ldq, out, ldo, n_seqs, n_tokens,
+                                                           row_stride_seq, row_stride_pos, n_heads, stream or None))
 
     def silu_mul(self, g: int, ldg: int, u: int, ldu: int, n: int, rows: int, stream: int | None = None):
         self.lib._check(self.L.sg_silu_mul_device(g, ldg, u, ldu, n, rows, stream or None))

@@ -87,7 +87,7 @@ def test_decoder_prefill_then_greedy_decode(gpu, oracle, dtype):
         prompts = rng.integers(0, cfg.vocab, size=(n_seqs, plen))
         refs = [OracleModel(oracle, cfg, SEED) for _ in range(n_seqs)]
         rows = D.set_rows(prompts.reshape(-1), np.tile(np.arange(plen), n_seqs), np.repeat(np.arange(n_seqs), plen))
-        D.forward(rows)
+        D.forward(rows, prefill=(n_seqs, plen, plen, 1))  # rows in (sequence, position) order
         torch.cuda.synchronize()
         gpu.synchronize()
         logits = D.logits[:rows].cpu().numpy()

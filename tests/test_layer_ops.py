@@ -343,7 +343,8 @@ def test_argmax_device(gpu, oracle, ops):
     rows.append(n)                                         # NaN: -1
     L = np.stack(rows)
     out = torch.full((len(rows),), -7, dtype=torch.int32, device="cuda")
-    ops.argmax(_t(L).data_ptr(), V, V, len(rows), out.data_ptr())
+    Ld = _t(L)
+    ops.argmax(Ld.data_ptr(), V, V, len(rows), out.data_ptr())
     assert out.cpu().tolist() == [oracle.argmax(r) for r in rows]
     assert out.cpu().tolist()[1] == 128255 and out.cpu().tolist()[-1] == -1
     # calls of other shapes reuse the per-row state: results stay exact
@@ -351,7 +352,8 @@ def test_argmax_device(gpu, oracle, ops):
         R, n = shape
         L2 = oracle.gen_x(SEED, 520 + n, (R, n))
         o2 = torch.full((R,), -7, dtype=torch.int32, device="cuda")
-        ops.argmax(_t(L2).data_ptr(), n, n, R, o2.data_ptr())
+        L2d = _t(L2)
+        ops.argmax(L2d.data_ptr(), n, n, R, o2.data_ptr())
         assert o2.cpu().tolist() == [oracle.argmax(r) for r in L2], shape
 
 
@@ -366,7 +368,8 @@ def test_embed_rows_bit_exact(gpu, oracle, ops, dtype):
         table = oracle.dequantize(dtype, raw, vocab * d).reshape(vocab, d)
         toks = np.array([0, 999, 128, 129, 5, 5], np.int32)
         out = torch.full((len(toks), d + 4), float("nan"), device="cuda")
-        ops.embed(W, _t(toks).data_ptr(), len(toks), out.data_ptr(), d + 4)
+        td = _t(toks)
+        ops.embed(W, td.data_ptr(), len(toks), out.data_ptr(), d + 4)
         gpu.synchronize()
         assert np.array_equal(out.cpu().numpy()[:, :d].view(np.uint32), table[toks].view(np.uint32))
     finally:
@@ -470,3 +473,50 @@ def test_rope_attention_fused_matches_two_calls(gpu, oracle, ops, nq, nkv, hd, m
         rope.free()
         for c in caches:
             c.free()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("nq,nkv,hd,n_seqs,n_tokens,seq_major", [(32, 8, 128, 1, 150, True), (8, 2, 64, 2, 77, False),
+                                                                 (8, 8, 64, 2, 130, True), (16, 8, 128, 3, 40, False)])
+def test_attention_prefill_matches_oracle(gpu, oracle, ops, nq, nkv, hd, n_seqs, n_tokens, seq_major):
+    """sg_attention_prefill_device over all prompt positions (row layouts
+    sequence-major and position-major) against the oracle's per-position
+    attention (|out - ref| <= 1e-4 * max |v|) and the per-row kernel."""
+    import torch
+    import swamp_gpu as sg
+    max_seq = 256
+    cache = sg.KvCache(gpu, 2, nkv, hd, max_seq, n_seqs)
+    try:
+        K = oracle.gen_x(SEED, 800 + hd, (n_seqs, nkv, max_seq, hd))
+        V = oracle.gen_x(SEED, 801 + hd, (n_seqs, nkv, max_seq, hd))
+        for s in range(n_seqs):
+            kk = np.ascontiguousarray(K[s].transpose(1, 0, 2).reshape(max_seq, nkv * hd))
+            vv = np.ascontiguousarray(V[s].transpose(1, 0, 2).reshape(max_seq, nkv * hd))
+            _store(ops, cache, 1, kk, vv, list(range(max_seq)), [s] * max_seq)
+        rows = n_seqs * n_tokens
+        rs_seq, rs_pos = (n_tokens, 1) if seq_major else (1, n_seqs)
+        seq_of = np.empty(rows, np.int32)
+        pos_of = np.empty(rows, np.int32)
+        for s in range(n_seqs):
+            for t in range(n_tokens):
+                seq_of[s * rs_seq + t * rs_pos] = s
+                pos_of[s * rs_seq + t * rs_pos] = t
+        q = oracle.gen_x(SEED, 802, (rows, nq * hd))
+        qd = _t(q)
+        out = torch.full((rows, nq * hd), float("nan"), device="cuda")
+        ops.attention_prefill(cache, 1, qd.data_ptr(), nq * hd, out.data_ptr(), nq * hd, n_seqs, n_tokens, rs_seq,
+                              rs_pos, nq)
+        out_rows = torch.full((rows, nq * hd), float("nan"), device="cuda")
+        pd, sd = _t(pos_of), _t(seq_of)  # held until the kernel has run
+        ops.attention(cache, 1, qd.data_ptr(), nq * hd, out_rows.data_ptr(), nq * hd, pd.data_ptr(), None,
+                      sd.data_ptr(), rows, nq)
+        gpu.synchronize()
+        got, got_rows = out.cpu().numpy(), out_rows.cpu().numpy()
+        for r in range(rows):
+            s, t = int(seq_of[r]), int(pos_of[r])
+            ref = oracle.attention(q[r], K[s], V[s], t + 1, t, nq, nkv, hd)
+            bound = 1e-4 * np.abs(V[s]).max()
+            assert np.abs(got[r] - ref).max() <= bound, (r, np.abs(got[r] - ref).max(), bound)
+            assert np.abs(got[r] - got_rows[r]).max() <= bound
+    finally:
+        cache.free()
