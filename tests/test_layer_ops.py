@@ -326,6 +326,18 @@ def test_silu_mul_and_add_device(gpu, oracle, ops):
     ops.add(big.data_ptr(), n + 8, ud.data_ptr(), n, n, rows)
     b = big.cpu().numpy()
     assert np.array_equal(b[:, :n], u) and np.all(b[:, n:] == 0)
+    # odd widths take the one-element path: same results
+    n2 = 7
+    g2, u2 = 4 * oracle.gen_x(SEED, 402, (rows, n2)), oracle.gen_x(SEED, 403, (rows, n2))
+    g2d, u2d = _t(g2), _t(u2)
+    ops.silu_mul(g2d.data_ptr(), n2, u2d.data_ptr(), n2, n2, rows)
+    got2 = g2d.cpu().numpy()
+    for r in range(rows):
+        ref = oracle.silu_mul(g2[r], u2[r])
+        assert np.all(np.abs(got2[r] - ref) <= 1e-6 * np.abs(ref) + 1e-37)
+    x2d = _t(g2)
+    ops.add(x2d.data_ptr(), n2, u2d.data_ptr(), n2, n2, rows)
+    assert np.array_equal(x2d.cpu().numpy(), g2 + u2)
 
 
 @pytest.mark.gpu
