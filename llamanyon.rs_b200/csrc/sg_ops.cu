@@ -545,7 +545,7 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(AttnArgs a, float* out
 //
 // A CTA of 256 threads takes one (sequence, KV head) and a block of QB
 // consecutive positions for all n_rep query heads of that KV head (R = n_rep
-// x QB = 128 query rows, Q in shared memory), and walks the keys 0 .. last
+// x QB <= 96 query rows, Q in shared memory), and walks the keys 0 .. last
 // position of the block in tiles of 32, each brought into shared memory by
 // two bulk copies. Per tile: scores S = Q K^T * scale for the 128 x 32 block
 // (a thread computes 4 rows x 4 keys; the 8 lanes of a shared-memory phase
@@ -556,7 +556,7 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(AttnArgs a, float* out
 // O in registers). Everything in f32: the same products as the split
 // kernel, in another summation order.
 constexpr int kPfThreads = 256;
-constexpr int kPfRows = 128;  // query rows per CTA (n_rep x QB)
+constexpr int kPfRows = 96;   // query rows per CTA (n_rep x QB): 2 CTAs fit an SM's shared memory
 constexpr int kPfKeys = 32;   // keys per tile
 
 template <int HD>
@@ -588,7 +588,7 @@ template <int HD>
 __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(PfArgs a) {
   using L = PfSmem<HD>;
   constexpr int NC = HD / 4;
-  constexpr int OT = kPfRows * HD / 16 / kPfThreads;  // 4x4 O tiles per thread
+  constexpr int OT = (kPfRows * HD / 16 + kPfThreads - 1) / kPfThreads;  // 4x4 O tiles per thread
   extern __shared__ __align__(128) uint8_t smem[];
   float* Qs = reinterpret_cast<float*>(smem + L::kQ);
   float* Ks = reinterpret_cast<float*>(smem + L::kK);
@@ -1255,7 +1255,7 @@ int sg_attention_prefill_device(sg_kv_cache_t cache, int layer, const float* q, 
   a.n_tokens = n_tokens;
   a.n_heads = n_heads;
   a.n_rep = n_heads / nkv;
-  a.qb = (ops::kPfRows / a.n_rep) & ~3;  // positions per CTA: n_rep x qb <= 128 rows, whole 4-row groups
+  a.qb = (ops::kPfRows / a.n_rep) & ~3;  // positions per CTA: n_rep x qb <= 96 rows, whole 4-row groups
   a.rs_seq = row_stride_seq;
   a.rs_pos = row_stride_pos;
   a.scale = 1.0f / sqrtf((float)hd);  // ops.rs:93
