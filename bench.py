@@ -10,7 +10,7 @@ copies of the layer rotate so every GEMV streams from HBM (the rotation
 footprint exceeds 4x the 126 MB L2).
 
 metric: whole-job algorithmic GB/s (weights N*K*18/32 bytes + activations in
-+ outputs out, per BASELINE.md section 4). With --gpus N (torchrun, one rank
++ outputs out). With --gpus N (torchrun, one rank
 per GPU) the model has N such layers, each tensor-parallel over the N ranks
 (column split Q/K/V/gate/up, row split O/down + NCCL all-reduce), so per-GPU
 bytes stay fixed (weak scaling).
@@ -48,8 +48,8 @@ def wbytes(k, n):
 
 
 def step_bytes(n_layers=1):
-    """algorithmic bytes of one step (114,148,352 /
-    115,085,312 / 118,833,152 per layer at batch 1/4/16)."""
+    """algorithmic bytes of one step (114,148,352 / 115,085,312 / 118,833,152
+    per layer at batch 1/4/16)."""
     tot = 0
     for b in BATCHES:
         for _, k, n in LAYER:

@@ -7,7 +7,7 @@ Column split (Q/K/V/gate/up) gives each rank a run of output rows; row split
 outputs with an all-reduce. Each rank computes its slice with the oracle (the
 reference's CPU route) on exactly the bytes the library would upload to its
 GPU; the gathered / reduced result must pass the parity gate against the
-untouched tensor (SURVEY-style TP parity: same values up to f32 sum order)."""
+untouched tensor (tensor-parallel parity: the same values up to the f32 sum order)."""
 import os
 import socket
 import sys
