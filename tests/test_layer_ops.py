@@ -532,3 +532,34 @@ def test_attention_prefill_matches_oracle(gpu, oracle, ops, nq, nkv, hd, n_seqs,
             assert np.abs(got[r] - got_rows[r]).max() <= bound
     finally:
         cache.free()
+
+
+@pytest.mark.gpu
+def test_prefill_and_fused_attention_reject_bad_shapes(gpu, ops):
+    """Host-side checks of the prefill and decode-form attention: nothing is
+    launched for shapes outside the cache or the kernels."""
+    import swamp_gpu as sg
+    c = sg.KvCache(gpu, 1, 2, 64, 32, n_seqs=2)
+    r = sg.Rope(gpu, 64, 32)
+    try:
+        bad = [
+            dict(n_seqs=3, n_tokens=8),    # more sequences than the cache holds
+            dict(n_seqs=1, n_tokens=33),   # more positions than the cache holds
+        ]
+        for b in bad:
+            with pytest.raises(sg.SwampGpuError):
+                ops.attention_prefill(c, 0, 16, 256, 16, 256, b["n_seqs"], b["n_tokens"], 1, 1, 4)
+        with pytest.raises(sg.SwampGpuError):  # 3 query heads over 2 KV heads
+            ops.attention_prefill(c, 0, 16, 256, 16, 256, 1, 8, 1, 1, 3)
+        with pytest.raises(sg.SwampGpuError):  # one row per sequence: 3 rows > 2 sequences
+            ops.rope_attention(r, c, 0, 16, 256, 16, 128, 16, 128, 16, 256, 16, None, 3, 4)
+        c256 = sg.KvCache(gpu, 1, 1, 256, 8)
+        try:
+            with pytest.raises(sg.SwampGpuError) as e:  # the prefill kernel covers head_dim 64 and 128
+                ops.attention_prefill(c256, 0, 16, 256, 16, 256, 1, 4, 1, 1, 1)
+            assert e.value.code == -5
+        finally:
+            c256.free()
+    finally:
+        r.free()
+        c.free()
