@@ -618,7 +618,7 @@ def model_decode_bench(torch, gpu, args):
                         f"{NEW} new tokens, greedy, batch 1 and 8",
             "weight_bytes_per_step": wbytes_step, "runs": runs,
             "execution": "prefill: one eager pass; decode: one CUDA graph per token",
-            "ops": "sg_embed / sg_rmsnorm / sg_linear_multi (QKV, gate+up) / sg_rope_attention (decode; "
+            "ops": "sg_embed / sg_rmsnorm / sg_linear (stacked QKV, stacked gate+up) / sg_rope_attention (decode; "
                    "sg_rope_kv + sg_attention_prefill at prefill) / "
                    "sg_linear + accumulate (O, down) / sg_silu_mul / sg_argmax"}
 

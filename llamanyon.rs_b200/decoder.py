@@ -67,14 +67,29 @@ def norm_vector(gpu: sg.SwampGpu, seed: int, tid: int, n: int) -> np.ndarray:
 
 
 class SynthModel:
-    """Random-init weights of the architecture, generated on the device."""
+    """Random-init weights of the architecture, generated on the device.
+
+    Q, K and V of a layer are registered as one tensor of d + 2 * kv rows
+    (their GGUF rows one after the other), and gate and up as one of
+    2 * ffn rows: each pair of projections that reads the same x is one
+    linear call, one prefill GEMM instead of three or two. The values are
+    exactly those of the separate tensors."""
 
     def __init__(self, gpu: sg.SwampGpu, cfg: DecoderConfig, seed: int):
         import torch
         self.cfg, self.seed = cfg, seed
         self.layers = []
         for l in range(cfg.n_layers):
-            self.layers.append({r: gpu.synth_weight(cfg.dtype, seed, tensor_id(r, l), *cfg.shape(r)) for r in ROLES})
+            def stacked(roles):
+                blocks = [gpu.synth_blocks(cfg.dtype, seed, tensor_id(r, l), *cfg.shape(r)) for r in roles]
+                rows = sum(cfg.shape(r)[0] for r in roles)
+                return gpu.register(np.concatenate(blocks), cfg.dtype, rows, cfg.d)
+            self.layers.append({
+                "qkv": stacked(("attn_q", "attn_k", "attn_v")),
+                "attn_output": gpu.synth_weight(cfg.dtype, seed, tensor_id("attn_output", l), *cfg.shape("attn_output")),
+                "gate_up": stacked(("ffn_gate", "ffn_up")),
+                "ffn_down": gpu.synth_weight(cfg.dtype, seed, tensor_id("ffn_down", l), *cfg.shape("ffn_down")),
+            })
         self.token_embd = gpu.synth_weight(cfg.dtype, seed, tensor_id("token_embd"), *cfg.shape("token_embd"))
         self.output = gpu.synth_weight(cfg.dtype, seed, tensor_id("output"), *cfg.shape("output"))
         dev = torch.device("cuda")
@@ -116,12 +131,11 @@ class Decoder:
         kv = c.n_kv_heads * c.head_dim
         self.x = torch.zeros(max_rows, c.d, **f)
         self.xn = torch.zeros(max_rows, c.d, **f)
-        self.q = torch.zeros(max_rows, c.d, **f)
-        self.k = torch.zeros(max_rows, kv, **f)
-        self.v = torch.zeros(max_rows, kv, **f)
+        self.qkv = torch.zeros(max_rows, c.d + 2 * kv, **f)  # [q | k | v] per row
+        self.q, self.k, self.v = self.qkv[:, :c.d], self.qkv[:, c.d:c.d + kv], self.qkv[:, c.d + kv:]
         self.att = torch.zeros(max_rows, c.d, **f)
-        self.gate = torch.zeros(max_rows, c.ffn, **f)
-        self.up = torch.zeros(max_rows, c.ffn, **f)
+        self.gu = torch.zeros(max_rows, 2 * c.ffn, **f)  # [gate | up] per row
+        self.gate, self.up = self.gu[:, :c.ffn], self.gu[:, c.ffn:]
         self.logits = torch.zeros(max_rows, c.vocab, **f)
         i32 = dict(device=dev, dtype=torch.int32)
         self.tokens = torch.zeros(max_rows, **i32)
@@ -152,29 +166,28 @@ class Decoder:
         c, o, g = self.cfg, self.ops, self.gpu
         p = lambda t: t.data_ptr()
         D, KV = c.d, c.n_kv_heads * c.head_dim
+        LQ, LG = D + 2 * KV, 2 * c.ffn  # row strides of [q | k | v] and [gate | up]
         ACC = sg.SG_FLAG_ACCUMULATE
         o.embed(self.m.token_embd, p(self.tokens), rows, p(self.x), D, stream)
         for l, lw in enumerate(self.m.layers):
             o.rmsnorm(p(self.x), D, p(self.m.attn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
-            g.linear_multi_device([lw["attn_q"], lw["attn_k"], lw["attn_v"]], p(self.xn), D,
-                                  [p(self.q), p(self.k), p(self.v)], [D, KV, KV], rows, stream=stream)
+            g.linear_device(lw["qkv"], p(self.xn), D, p(self.qkv), LQ, rows, stream=stream)
             if decode:
-                o.rope_attention(self.rope, self.cache, l, p(self.q), D, p(self.k), KV, p(self.v), KV, p(self.att),
+                o.rope_attention(self.rope, self.cache, l, p(self.q), LQ, p(self.k), LQ, p(self.v), LQ, p(self.att),
                                  D, p(self.pos), p(self.seq), rows, c.n_heads, stream)
             else:
-                o.rope_kv(self.rope, self.cache, l, p(self.q), D, p(self.k), KV, p(self.v), KV, p(self.pos),
+                o.rope_kv(self.rope, self.cache, l, p(self.q), LQ, p(self.k), LQ, p(self.v), LQ, p(self.pos),
                           p(self.seq), rows, c.n_heads, stream)
                 if use_pf:
-                    o.attention_prefill(self.cache, l, p(self.q), D, p(self.att), D, *prefill, c.n_heads, stream)
+                    o.attention_prefill(self.cache, l, p(self.q), LQ, p(self.att), D, *prefill, c.n_heads, stream)
                 else:
-                    o.attention(self.cache, l, p(self.q), D, p(self.att), D, p(self.pos), None, p(self.seq), rows,
+                    o.attention(self.cache, l, p(self.q), LQ, p(self.att), D, p(self.pos), None, p(self.seq), rows,
                                 c.n_heads, stream)
             g.linear_device(lw["attn_output"], p(self.att), D, p(self.x), D, rows, stream=stream, flags=ACC)
             o.rmsnorm(p(self.x), D, p(self.m.ffn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
-            g.linear_multi_device([lw["ffn_gate"], lw["ffn_up"]], p(self.xn), D, [p(self.gate), p(self.up)],
-                                  [c.ffn, c.ffn], rows, stream=stream)
-            o.silu_mul(p(self.gate), c.ffn, p(self.up), c.ffn, c.ffn, rows, stream)
-            g.linear_device(lw["ffn_down"], p(self.gate), c.ffn, p(self.x), D, rows, stream=stream, flags=ACC)
+            g.linear_device(lw["gate_up"], p(self.xn), D, p(self.gu), LG, rows, stream=stream)
+            o.silu_mul(p(self.gate), LG, p(self.up), LG, c.ffn, rows, stream)
+            g.linear_device(lw["ffn_down"], p(self.gate), LG, p(self.x), D, rows, stream=stream, flags=ACC)
         r0, r1 = (0, rows) if logits_rows is None else (logits_rows.start, logits_rows.stop)
         n = r1 - r0
         o.rmsnorm(p(self.x[r0]), D, p(self.m.output_norm), p(self.xn), D, D, n, c.eps, stream)
