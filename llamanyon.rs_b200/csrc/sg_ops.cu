@@ -582,6 +582,11 @@ struct PfArgs {
   int n_tokens, n_heads, n_rep, qb;  // qb: positions per CTA (R / n_rep)
   int64_t rs_seq, rs_pos;            // row strides
   float scale;
+  // key split: CTA (block, chunk) covers key tiles [chunk * chunk_tiles,
+  // (chunk + 1) * chunk_tiles); with n_chunks > 1 it writes (max, sum,
+  // unnormalised O) per row to ws and attn_prefill_combine_kernel merges
+  int n_blocks, n_chunks, chunk_tiles;
+  float* ws;  // [seq][kv head][block][chunk][row R][HD + 2]
 };
 
 template <int HD>
@@ -602,11 +607,14 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(PfArgs a) {
   pdl_launch_dependents();
   pdl_wait();  // q and the cache rows come from the previous kernels
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qblk = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+  const int qblk = blockIdx.x / a.n_chunks, ch = blockIdx.x - qblk * a.n_chunks;
+  const int g = blockIdx.y, s = blockIdx.z;
   const int n_rep = a.n_rep, qb = a.qb, R = n_rep * qb;
   const int p0 = qblk * qb;
   if (p0 >= a.n_tokens) return;
   const int p1 = min(a.n_tokens, p0 + qb);  // positions p0 .. p1-1
+  const int kt0 = ch * a.chunk_tiles;
+  if (kt0 * kPfKeys >= p1) return;  // no key of this chunk precedes the block's last position
   // Q rows: row j * qb + i is query head g * n_rep + j at position p0 + i
   for (int e = tid; e < kPfRows * NC; e += kPfThreads) {
     const int row = e / NC, c = e - row * NC;
@@ -634,22 +642,23 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(PfArgs a) {
     for (int e = 0; e < 16; ++e) o[u][e] = 0.f;
   __syncthreads();
   const size_t hoff = a.kv.head_off(s, a.layer, g);
-  const int n_tiles = (p1 + kPfKeys - 1) / kPfKeys;
-  for (int kt = 0; kt < n_tiles; ++kt) {
+  const int n_tiles = min((p1 + kPfKeys - 1) / kPfKeys, kt0 + a.chunk_tiles);
+  for (int kt = kt0; kt < n_tiles; ++kt) {
+    const uint32_t ph = (uint32_t)(kt - kt0) & 1u;  // this CTA's copy phase
     const int k0 = kt * kPfKeys, nk = min(kPfKeys, p1 - k0);
     if (tid == 0) {
       const uint32_t bytes = (uint32_t)nk * HD * 4;
       mbar_arrive_expect_tx(bar, 2 * bytes);
       bulk_g2s(Ks, a.kv.k + hoff + (size_t)k0 * HD, bytes, bar);
       bulk_g2s(Vs, a.kv.v + hoff + (size_t)k0 * HD, bytes, bar);
-      ok_flag = mbar_wait(bar, kt & 1, 0x41) ? 1 : 0;
+      ok_flag = mbar_wait(bar, ph, 0x41) ? 1 : 0;
     }
     __syncthreads();
     if (!ok_flag) {  // the bounded wait gave up (error recorded): let the copies land, then leave
-      if (tid == 0) mbar_wait_drain(bar, kt & 1);
+      if (tid == 0) mbar_wait_drain(bar, ph);
       return;
     }
-    mbar_test(bar, kt & 1);  // completed: acquire the copied rows in this thread
+    mbar_test(bar, ph);  // completed: acquire the copied rows in this thread
     // S = Q K^T * scale: tile t -> rows 4 * (t / 8) .., keys 4 * (t % 8) ..
     for (int t = tid; t < (R / 4) * (kPfKeys / 4); t += kPfThreads) {
       const int rg = t >> 3, kg = t & 7;
@@ -733,6 +742,27 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(PfArgs a) {
     }
     __syncthreads();  // K, V and S are rewritten by the next tile
   }
+  if (a.n_chunks > 1) {
+    // partial of this chunk: (m, l, unnormalised O) per row
+    float* rec0 = a.ws + ((((int64_t)s * a.kv.n_kv_heads + g) * a.n_blocks + qblk) * a.n_chunks + ch) * R * (HD + 2);
+#pragma unroll
+    for (int u = 0; u < OT; ++u) {
+      const int i = tid + u * kPfThreads;
+      const int rg = i / NC, dc = i - rg * NC;
+      if (4 * rg >= R) continue;
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        float* rec = rec0 + (int64_t)(4 * rg + x) * (HD + 2);
+        if (dc == 0) {
+          rec[0] = Ms[4 * rg + x];
+          rec[1] = Ls[4 * rg + x];
+        }
+#pragma unroll
+        for (int y = 0; y < 4; ++y) rec[2 + 4 * dc + y] = o[u][4 * x + y];
+      }
+    }
+    return;
+  }
   // out = O / l
 #pragma unroll
   for (int u = 0; u < OT; ++u) {
@@ -750,6 +780,38 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(PfArgs a) {
       *reinterpret_cast<float4*>(op) =
           make_float4(o[u][4 * x] / l, o[u][4 * x + 1] / l, o[u][4 * x + 2] / l, o[u][4 * x + 3] / l);
     }
+  }
+}
+
+// Merge the key chunks of the prefill: per row, M = max m_c, L = sum
+// exp(m_c - M) l_c, out = sum exp(m_c - M) O_c / L (chunks past a row's
+// position hold m = -inf, l = 0, O = 0 and add nothing).
+template <int HD>
+__global__ void __launch_bounds__(kPfThreads) attn_prefill_combine_kernel(PfArgs a) {
+  pdl_enter();
+  const int qblk = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+  const int n_rep = a.n_rep, qb = a.qb, R = n_rep * qb;
+  const int p0 = qblk * qb;
+  const int p1 = min(a.n_tokens, p0 + qb);
+  const int nch = min(a.n_chunks, ((p1 + kPfKeys - 1) / kPfKeys + a.chunk_tiles - 1) / a.chunk_tiles);
+  const float* base = a.ws + (((int64_t)s * a.kv.n_kv_heads + g) * a.n_blocks + qblk) * a.n_chunks * R * (HD + 2);
+  const int64_t cstride = (int64_t)R * (HD + 2);
+  for (int e = threadIdx.x; e < R * HD; e += kPfThreads) {
+    const int row = e / HD, d = e - row * HD;
+    const int j = row / qb, qi = row - j * qb;
+    if (p0 + qi >= p1) continue;
+    const float* rec = base + (int64_t)row * (HD + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, rec[c * cstride]);
+    float L = 0.f, acc = 0.f;
+    for (int c = 0; c < nch; ++c) {
+      const float m = rec[c * cstride];
+      const float w = m == -INFINITY ? 0.f : expf(m - M);
+      L = fmaf(w, rec[c * cstride + 1], L);
+      acc = fmaf(w, rec[c * cstride + 2 + d], acc);
+    }
+    a.out[(int64_t)s * a.rs_seq * a.ldo + (int64_t)(p0 + qi) * a.rs_pos * a.ldo + (int64_t)(g * n_rep + j) * HD + d] =
+        acc / L;
   }
 }
 
@@ -1259,7 +1321,24 @@ int sg_attention_prefill_device(sg_kv_cache_t cache, int layer, const float* q, 
   a.rs_seq = row_stride_seq;
   a.rs_pos = row_stride_pos;
   a.scale = 1.0f / sqrtf((float)hd);  // ops.rs:93
-  const dim3 grid((unsigned)((n_tokens + a.qb - 1) / a.qb), (unsigned)nkv, (unsigned)n_seqs);
+  // With fewer CTAs than two per SM, split the keys into chunks of 4 tiles
+  // (128 keys), so that the last query blocks (the longest causal rows)
+  // spread over several CTAs; with more, the blocks alone fill the GPU and
+  // the split only adds the partials' traffic (measured at 512 tokens: one
+  // sequence 282 -> 223 us per layer with the split, eight 956 -> 1175 us).
+  a.n_blocks = (n_tokens + a.qb - 1) / a.qb;
+  const int n_kt = (n_tokens + ops::kPfKeys - 1) / ops::kPfKeys;
+  const bool split = (int64_t)a.n_blocks * nkv * n_seqs < 2 * (int64_t)d->num_sms;
+  a.chunk_tiles = split ? 4 : n_kt;
+  a.n_chunks = (n_kt + a.chunk_tiles - 1) / a.chunk_tiles;
+  if (a.n_chunks > 1) {
+    const size_t need = (size_t)n_seqs * nkv * a.n_blocks * a.n_chunks * (a.n_rep * a.qb) * (hd + 2) * sizeof(float);
+    rc = ensure_buf((void**)&d->attn_ws, &d->attn_ws_bytes, need);
+    if (rc) return rc;
+    a.ws = d->attn_ws;
+  }
+  const dim3 grid((unsigned)(a.n_blocks * a.n_chunks), (unsigned)nkv, (unsigned)n_seqs);
+  const dim3 cgrid((unsigned)a.n_blocks, (unsigned)nkv, (unsigned)n_seqs);
   cudaStream_t st = (cudaStream_t)stream;
   static int attr_done[64][2] = {};
   int dev = 0;
@@ -1271,6 +1350,7 @@ int sg_attention_prefill_device(sg_kv_cache_t cache, int layer, const float* q, 
       attr_done[dev][0] = 1;
     }
     CUDA_TRY(ops::launch(ops::attn_prefill_kernel<64>, grid, dim3(ops::kPfThreads), ops::PfSmem<64>::kBytes, st, a));
+    if (a.n_chunks > 1) CUDA_TRY(ops::launch(ops::attn_prefill_combine_kernel<64>, cgrid, dim3(ops::kPfThreads), 0, st, a));
   } else {
     if (dev < 64 && !attr_done[dev][1]) {
       CUDA_TRY(cudaFuncSetAttribute(ops::attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1278,6 +1358,7 @@ int sg_attention_prefill_device(sg_kv_cache_t cache, int layer, const float* q, 
       attr_done[dev][1] = 1;
     }
     CUDA_TRY(ops::launch(ops::attn_prefill_kernel<128>, grid, dim3(ops::kPfThreads), ops::PfSmem<128>::kBytes, st, a));
+    if (a.n_chunks > 1) CUDA_TRY(ops::launch(ops::attn_prefill_combine_kernel<128>, cgrid, dim3(ops::kPfThreads), 0, st, a));
   }
   return SG_OK;
 }
