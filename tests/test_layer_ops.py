@@ -563,3 +563,28 @@ def test_prefill_and_fused_attention_reject_bad_shapes(gpu, ops):
     finally:
         r.free()
         c.free()
+
+
+def test_oracle_attention_and_norm_against_float64(oracle):
+    """The oracle's restatements against independent float64 numpy versions
+    of the same formulas (ops.rs:82-201): attention within 1e-5 * max |v|,
+    RMSNorm within 1e-5 relative, on GQA shapes and several positions."""
+    nq, nkv, hd, T = 8, 2, 64, 40
+    K = oracle.gen_x(SEED, 900, (nkv, T, hd)).astype(np.float32)
+    V = oracle.gen_x(SEED, 901, (nkv, T, hd)).astype(np.float32)
+    q = oracle.gen_x(SEED, 902, (nq * hd,))
+    for pos in (0, 1, 17, 39):
+        got = oracle.attention(q, K, V, pos + 1, pos, nq, nkv, hd)
+        want = np.empty(nq * hd)
+        for h in range(nq):
+            kh, vh = K[h // (nq // nkv)].astype(np.float64), V[h // (nq // nkv)].astype(np.float64)
+            s = kh[:pos + 1] @ q[h * hd:(h + 1) * hd].astype(np.float64) / np.sqrt(hd)
+            p = np.exp(s - s.max())
+            want[h * hd:(h + 1) * hd] = (p / p.sum()) @ vh[:pos + 1]
+        assert np.abs(got - want).max() <= 1e-5 * np.abs(V).max(), pos
+    x = oracle.gen_x(SEED, 903, (4096,))
+    w = (1 + 0.1 * oracle.gen_x(SEED, 904, (4096,))).astype(np.float32)
+    x64 = x.astype(np.float64)
+    want = x64 / np.sqrt(np.mean(x64 * x64) + 1e-5) * w
+    got = oracle.rmsnorm(x, w, 1e-5)
+    assert np.all(np.abs(got - want) <= 1e-5 * np.abs(want) + 1e-30)
