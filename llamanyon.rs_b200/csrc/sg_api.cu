@@ -89,8 +89,6 @@ struct DevState {
   size_t rbuf_bytes = 0;
   float* attn_ws = nullptr;  // attention split partials (sg_attention_device)
   size_t attn_ws_bytes = 0;
-  void* attn_cnt = nullptr;  // decode attention: per-(row, KV head) split counters
-  size_t attn_cnt_bytes = 0;
   void* argmax_ws = nullptr;  // argmax chunk keys, row counters and NaN flags
   size_t argmax_ws_bytes = 0;
   int argmax_rows = 0;  // rows the argmax counters and flags cover
@@ -296,7 +294,6 @@ void release_devices() {
     if (d.ybuf) cudaFree(d.ybuf);
     if (d.rbuf) cudaFree(d.rbuf);
     if (d.attn_ws) cudaFree(d.attn_ws);
-    if (d.attn_cnt) cudaFree(d.attn_cnt);
     if (d.argmax_ws) cudaFree(d.argmax_ws);
     if (d.hbuf) cudaFreeHost(d.hbuf);
     for (int i = 0; i < 2; ++i) {

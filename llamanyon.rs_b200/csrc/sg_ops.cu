@@ -229,17 +229,13 @@ struct AttnArgs {
   float scale;
   float* ws;  // [row][head][split][HD + 2]
   // decode form only (one row per sequence): RoPE and the cache store of
-  // the row's own k and v happen in the split that holds its position, and
-  // the last split of a (row, KV head) to finish combines
+  // the row's own k and v happen in the split that holds its position
   const float2* lut;
   int max_context;
   const float* k_new;
   int64_t ldk;
   const float* v_new;
   int64_t ldv;
-  unsigned int* counters;  // [row][kv head], zero between calls
-  float* out;
-  int64_t ldo;
 };
 
 template <int HD>
@@ -273,7 +269,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
   float* red = reinterpret_cast<float*>(smem + L::kRed);
   float* mls = reinterpret_cast<float*>(smem + L::kMl);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  __shared__ int ok_flag, last_flag;
+  __shared__ int ok_flag;
   pdl_launch_dependents();
   pdl_wait();  // q and the cache rows come from the previous kernels
   const int sp = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
@@ -449,65 +445,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
       rec[0] = mls[2 * j];
       rec[1] = mls[2 * j + 1];
     }
-  }
-  if (DECODE && a.counters) {
-    // the last split of this (row, KV head) to finish combines its heads:
-    // out = sum_s e_s acc_s / sum_s e_s l_s, e_s = exp(m_s - max_s m_s),
-    // the same operations in the same order as attn_combine_kernel
-    const int ns = valid_end / kAttnP + 1;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) last_flag = atomicAdd(&a.counters[r * a.kv.n_kv_heads + g], 1u) == (unsigned)(ns - 1);
-    __syncthreads();
-    if (!last_flag) return;
-    __threadfence();
-    const float* rec0 = a.ws + ((int64_t)r * a.n_heads + g * n_rep) * a.n_split * (HD + 2);
-    const int64_t hstride = (int64_t)a.n_split * (HD + 2);
-    // per head: M (a warp max) and e_s for the first 64 splits in shared
-    // memory (later ones are recomputed), then L in split order
-    for (int j = warp; j < n_rep; j += kAttnThreads / 32) {
-      const float* rj = rec0 + j * hstride;
-      float M = -INFINITY;
-      for (int q = lane; q < ns; q += 32) M = fmaxf(M, __ldcg(rj + q * (HD + 2)));
-      M = warp_max(M);
-      for (int q = lane; q < ns && q < kAttnP; q += 32) sc[j * kAttnP + q] = expf(__ldcg(rj + q * (HD + 2)) - M);
-      __syncwarp();
-      if (lane == 0) {
-        float L = 0.f;
-        for (int q = 0; q < ns; ++q) {
-          const float e = q < kAttnP ? sc[j * kAttnP + q] : expf(__ldcg(rj + q * (HD + 2)) - M);
-          L = fmaf(e, __ldcg(rj + q * (HD + 2) + 1), L);
-        }
-        mls[2 * j] = M;
-        mls[2 * j + 1] = L;
-      }
-    }
-    __syncthreads();
-    // outputs four at a time per thread, so that four loads are in flight
-    for (int i0 = tid; i0 < n_rep * HD; i0 += 4 * kAttnThreads) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      int jj[4], dd[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = min(i0 + u * kAttnThreads, n_rep * HD - 1);
-        jj[u] = i / HD;
-        dd[u] = i - jj[u] * HD;
-      }
-      for (int q = 0; q < ns; ++q) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float* rq = rec0 + jj[u] * hstride + q * (HD + 2);  // split q's record of head jj[u]
-          const float e = q < kAttnP ? sc[jj[u] * kAttnP + q] : expf(__ldcg(rq) - mls[2 * jj[u]]);
-          acc[u] = fmaf(e, __ldcg(rq + 2 + dd[u]), acc[u]);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = i0 + u * kAttnThreads;
-        if (i < n_rep * HD) a.out[(int64_t)r * a.ldo + (int64_t)(g * n_rep + jj[u]) * HD + dd[u]] = acc[u] / mls[2 * jj[u] + 1];
-      }
-    }
-    if (tid == 0) a.counters[r * a.kv.n_kv_heads + g] = 0;
   }
 }
 
@@ -1002,7 +939,6 @@ int attention_launch(const ops::AttnArgs& a, dim3 g1, dim3 g2, float* out, int64
   if (a.lut) {  // decode form: RoPE and the cache store inside the split kernel
     CUDA_TRY(ops::launch(ops::attn_split_kernel<HD, true>, g1, dim3(ops::kAttnThreads), ops::AttnSmem<HD>::kBytes, st,
                          a));
-    if (a.counters) return SG_OK;  // the last split combined
   } else {
     CUDA_TRY(ops::launch(ops::attn_split_kernel<HD, false>, g1, dim3(ops::kAttnThreads), ops::AttnSmem<HD>::kBytes,
                          st, a));
@@ -1254,25 +1190,9 @@ int sg_rope_attention_device(sg_rope_t rope, sg_kv_cache_t cache, int layer, con
   a.ldk = ldk;
   a.v_new = v;
   a.ldv = ldv;
-  a.out = out;
-  a.ldo = ldo;
   rc = ensure_buf((void**)&d->attn_ws, &d->attn_ws_bytes, (size_t)rows * n_heads * a.n_split * (hd + 2) * sizeof(float));
   if (rc) return rc;
   a.ws = d->attn_ws;
-  // per-(row, KV head) split counters: zero between calls (the combining
-  // split resets its own); their place depends only on the row
-  const size_t cnt_need = (size_t)rows * nkv * sizeof(unsigned int);
-  if (d->attn_cnt_bytes < cnt_need) {
-    rc = ensure_buf(&d->attn_cnt, &d->attn_cnt_bytes, cnt_need);
-    if (rc) return rc;
-    CUDA_TRY(cudaMemset(d->attn_cnt, 0, d->attn_cnt_bytes));
-  }
-  a.counters = static_cast<unsigned int*>(d->attn_cnt);
-  // The split kernel can also combine in the last CTA of each (row, KV
-  // head) (a.counters); measured at 1 token per sequence that CTA's
-  // serialised loads cost more than a separate combine launch, so the
-  // combine runs as its own kernel.
-  a.counters = nullptr;
   cudaStream_t st = (cudaStream_t)stream;
   const dim3 g1(a.n_split, nkv, rows), g2(n_heads, rows);
   switch (hd) {
