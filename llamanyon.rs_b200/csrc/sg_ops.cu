@@ -8,6 +8,10 @@
 //   sg_rope_kv_device    ops.rs:42-80     apply_rope_ufc, then
 //                        cache.rs:348-371,412-434  PagedKVCache::save / save_at
 //   sg_attention_device  ops.rs:82-186    attention (GQA, causal, softmax)
+//   sg_rope_attention_device              the decode step's RoPE + save +
+//                        attention for one row per sequence (executor.rs:447-481)
+//   sg_attention_prefill_device           the prefill's per-position attention
+//                        loop (executor.rs:135-141), blocks of positions per CTA
 //   sg_silu_mul_device   ops.rs:203-214   silu, mul_in_place
 //   sg_add_device        ops.rs:216-220   add_in_place
 //   sg_argmax_device     sampler.rs:94-95 greedy pick (the sampler's fallback)
