@@ -466,9 +466,12 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(AttnArgs a, float* out
   }
   const int ns = valid_end / kAttnP + 1;
   const float* rec = a.ws + ((int64_t)r * a.n_heads + h) * a.n_split * (HD + 2);
+  // unrolled so that the loads of several splits are in flight at once
   float M = -INFINITY;
+#pragma unroll 8
   for (int s = 0; s < ns; ++s) M = fmaxf(M, rec[s * (HD + 2)]);
   float L = 0.f, acc = 0.f;
+#pragma unroll 8
   for (int s = 0; s < ns; ++s) {
     const float e = expf(rec[s * (HD + 2)] - M);
     L = fmaf(e, rec[s * (HD + 2) + 1], L);
