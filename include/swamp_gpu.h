@@ -132,7 +132,7 @@ SG_API int sg_weight_shard(sg_weight_t w, int local_device, int64_t *n_rows, int
  * SG_FLAG_DEVICE_PTRS (single-device or rank mode only) xs/outs point at
  * this rank's device and hold this rank's shard: x of n_cols_local, out of
  * n_rows_local (column split) or n_rows (replicate / row split, all-reduced).
- * Batches of 1..16 run the decode GEMV; larger batches the prefill GEMM. */
+ * Batches of 1..32 run the decode GEMV; larger batches the prefill GEMM. */
 SG_API int sg_linear(sg_weight_t w, const float *const *xs, float *const *outs, int batch, int flags);
 
 /* forward_linear_multi (linear.rs:96-170): several tensors, same x (K). */
@@ -142,7 +142,10 @@ SG_API int sg_linear_multi(const sg_weight_t *ws, int n_weights, const float *x,
 /* Device-resident, stream-ordered form for engines that keep activations on
  * the GPU: x is [batch][ldx] (this rank's K-slice starts at x), y is
  * [batch][ldy]. stream is a cudaStream_t; NULL means CUDA's default stream.
- * Returns once the work is enqueued. */
+ * Returns once the work is enqueued. A row-split tensor's outputs are
+ * all-reduced in place; with SG_FLAG_ACCUMULATE every rank passes the same
+ * y (e.g. the replicated residual stream) and gets y + W x, the old y counted
+ * once. Batches of 1..32 run the decode GEMV, larger ones the prefill GEMM. */
 SG_API int sg_linear_device(sg_weight_t w, const float *x, int64_t ldx, float *y, int64_t ldy, int batch,
                      void *stream, int flags);
 SG_API int sg_linear_multi_device(const sg_weight_t *ws, int n_weights, const float *x, int64_t ldx,

@@ -20,6 +20,7 @@
 #include "../../include/swamp_gpu.h"
 #include "sg_gemm.cuh"
 #include "sg_gemv.cuh"
+#include "sg_gemv_q6k.cuh"
 #include "sg_peer.cuh"
 
 // ---------------------------------------------------------------- NCCL shim
@@ -218,15 +219,14 @@ int ensure_host(DevState& d, size_t need) {
 }
 
 // ------------------------------------------------------- GEMV workspace
-// The decode GEMV's workspace (sg_gemv.cuh): zeroing flags, then activation
-// images. Up to kStaticWsCols columns it is a fixed array per device inside
-// the library, so no decode call allocates; wider tensors use a buffer that
-// grows on demand (flags zeroed when it is allocated). Flags hold per-call
-// epochs, so no state carries over from one call (or a failed one) to the
+// The decode GEMV's workspace (sg_gemv.cuh): the activation images of a
+// call. Up to kStaticWsCols columns at 16 tokens (wider at fewer tokens) it
+// is a fixed array per device inside the library, so no decode call
+// allocates; larger calls use a buffer that grows on demand. Every call
+// rewrites what it reads, so no state carries over from one call to the
 // next.
 constexpr int64_t kStaticWsCols = 32768;
-constexpr size_t kStaticWsBytes =
-    gemv_tc::kFlagsBytes + (size_t)((kStaticWsCols / 64 + gemv_tc::kUC - 1) / gemv_tc::kUC) * gemv_tc::Cfg<16>::XU;
+constexpr size_t kStaticWsBytes = gemv_mma::ws_bytes<2>(kStaticWsCols / 256);
 static __device__ __align__(256) uint8_t g_gemv_ws[kStaticWsBytes];
 std::mutex g_ws_mu;
 void* g_ws_ptr[64] = {nullptr};
@@ -333,7 +333,6 @@ int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* 
           return fail(SG_ERR_OOM, "cudaMalloc(%zu) failed", gws_bytes);
         }
         d.gemv_ws_bytes = gws_bytes;
-        CUDA_TRY(cudaMemsetAsync(d.gemv_ws, 0, gemv_tc::kFlagsBytes, st));
       }
       gws = d.gemv_ws;
       gws_bytes = d.gemv_ws_bytes;
@@ -342,7 +341,15 @@ int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* 
     // matrix, on its own kernel)
     for (int i0 = 0; i0 < n_w;) {
       if (ws[i0]->dtype == SG_DTYPE_Q6_K) {
-        CUDA_TRY(sg_gemv_q6k(ws[i0], x, ldx, ys[i0], ldys[i0], batch, accumulate, d.num_sms, st));
+        if (batch <= SG_GEMV_Q6K_MAX_BATCH) {
+          CUDA_TRY(sg_gemv_q6k(ws[i0], x, ldx, ys[i0], ldys[i0], batch, accumulate, d.num_sms, st));
+        } else {
+          const size_t need = sg_gemm_scratch_bytes(batch, K);
+          int rc = need ? ensure_buf(&d.scratch, &d.scratch_bytes, need) : SG_OK;
+          if (rc) return rc;
+          CUDA_TRY(sg_gemm(ws[i0], x, ldx, ys[i0], ldys[i0], batch, accumulate, d.scratch, d.scratch_bytes,
+                           d.num_sms, st));
+        }
         ++i0;
         continue;
       }
@@ -900,8 +907,6 @@ int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x,
       return fail(SG_ERR_INVALID_ARG, "multi: tensors must share dtype, n_cols and tp_mode");
     const int64_t need = ws[i]->tp_mode == SG_TP_ROW ? ws[i]->n_rows : sw[i]->n_rows;
     if (!ys[i] || ldys[i] < need) return fail(SG_ERR_INVALID_ARG, "y[%d]: ldy %lld < %lld rows", i, (long long)ldys[i], (long long)need);
-    if (acc && ws[i]->tp_mode == SG_TP_ROW && g_ctx.world > 1)
-      return fail(SG_ERR_UNSUPPORTED, "SG_FLAG_ACCUMULATE with a row-split tensor");
   }
   if (ldx < sw[0]->n_cols) return fail(SG_ERR_INVALID_ARG, "ldx %lld < n_cols %lld", (long long)ldx, (long long)sw[0]->n_cols);
   DevState& d = g_ctx.devs[0];
@@ -913,7 +918,11 @@ int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x,
   // Row split: every rank holds a partial sum of all n_rows outputs. They are
   // written packed ([batch][n_rows] per tensor, back to back) so that one
   // all-reduce covers the call, then copied into strided outputs if needed.
+  // With SG_FLAG_ACCUMULATE rank 0 adds its partial onto y's current values
+  // and the other ranks overwrite theirs, so the sum holds y once (every rank
+  // passes the same y, e.g. a replicated residual stream).
   if (!g_nccl.AllReduce) return fail(SG_ERR_NCCL, "NCCL not initialised");
+  const bool lead = g_ctx.rank_base == 0;
   bool packed = true;
   size_t count = 0;
   for (int i = 0; i < n_weights; ++i) {
@@ -937,7 +946,11 @@ int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x,
       off += (size_t)batch * ws[i]->n_rows;
     }
   }
-  int rc = run_linear(d, sw, n_weights, x, ldx, yp, lp, batch, st, false);
+  if (!packed && acc && lead)
+    for (int i = 0; i < n_weights; ++i)
+      CUDA_TRY(cudaMemcpy2DAsync(yp[i], (size_t)lp[i] * sizeof(float), ys[i], (size_t)ldys[i] * sizeof(float),
+                                 (size_t)lp[i] * sizeof(float), batch, cudaMemcpyDeviceToDevice, st));
+  int rc = run_linear(d, sw, n_weights, x, ldx, yp, lp, batch, st, acc && lead);
   if (rc) return rc;
   rc = allreduce_rank(d, yp[0], count, st);
   if (rc) return rc;

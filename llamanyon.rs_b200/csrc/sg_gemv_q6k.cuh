@@ -2,6 +2,8 @@
 #pragma once
 #include "sg_layout.cuh"
 
+#define SG_GEMV_Q6K_MAX_BATCH 16  // larger batches of a Q6_K tensor run the prefill GEMM
+
 // y[t][r] (ldy) = sum_k W[r][k] x[t][k] (ldx) for t < batch (1..16), or
 // y += W x with accumulate. With several K ranges per row-block the rows of
 // y are zeroed first (stream-ordered) and the ranges reduced with red.add.

@@ -1,13 +1,15 @@
 // sg_noalloc.cu -- sg_linear_device_noalloc: the decode GEMV (batch 1..16,
 // device pointers) for callers that must never trigger a device allocation.
 //
-// The decode GEMV's workspace (zeroing flags, and from 3 tokens on the
+// The decode GEMV's workspace (hand-over flags, partial-sum slots and the
 // activation images) is the library's fixed per-device array (g_gemv_ws in
-// sg_api.cu), sized for n_cols <= kStaticWsCols, so a call only launches
-// kernels (plus the all-reduce of a row-split tensor). Its address is looked
-// up once per device on the first call that uses the device. The workspace
-// is shared by all decode calls on a device, so two calls whose kernels
-// overlap in time (different streams, no ordering between them) race on it.
+// sg_api.cu), sized for n_cols <= kStaticWsCols at 16 tokens, so a call only
+// launches kernels (plus the all-reduce of a row-split tensor). Its address
+// is looked up once per device on the first call that uses the device. The
+// workspace is shared by all decode calls on a device, so two calls whose
+// kernels overlap in time (different streams, no ordering between them) race
+// on it.
+constexpr int kNoallocMaxBatch = 16;
 
 int sg_linear_device_noalloc(sg_weight_t w, const float* x, int64_t ldx, float* y, int64_t ldy, int batch,
                              void* stream, int flags) {
@@ -16,9 +18,9 @@ int sg_linear_device_noalloc(sg_weight_t w, const float* x, int64_t ldx, float* 
   if (rc) return rc;
   if (!x || !y) return fail(SG_ERR_INVALID_ARG, "null pointer");
   if (g_ctx.devs.size() != 1) return fail(SG_ERR_INVALID_ARG, "device entry points need one device per process");
-  if (batch < 1 || batch > SG_GEMV_MAX_BATCH)
-    return fail(SG_ERR_UNSUPPORTED, "sg_linear_device_noalloc: batch %d outside the decode range 1..%d", batch,
-                SG_GEMV_MAX_BATCH);
+  if (batch < 1 || batch > kNoallocMaxBatch)
+    return fail(SG_ERR_UNSUPPORTED, "sg_linear_device_noalloc: batch %d outside the range 1..%d of the fixed workspace",
+                batch, kNoallocMaxBatch);
   const SgDevWeight* sw = &w->shards[0].w;
   if (sw->dtype != SG_DTYPE_Q6_K && sg_gemv_scratch_bytes(sw->n_cols, batch) > kStaticWsBytes)
     return fail(SG_ERR_UNSUPPORTED, "sg_linear_device_noalloc: n_cols %lld above %lld at batch %d (the fixed workspace)",

@@ -4,7 +4,7 @@
 // (the per-device error flag) have exactly one definition without relocatable
 // device code.
 #include "sg_layout.cu"
-#include "sg_gemv.cu"
+#include "sg_gemv_mma.cu"
 #include "sg_gemv_q6k.cu"
 #include "sg_gemm.cu"
 #include "sg_api.cu"

@@ -35,6 +35,9 @@ def gpu():
     lib.shutdown()
 
 
+PARITY_LOG = []  # (test, gated worst ratio, strict max, strict 99.9th percentile, share of strict > 1e-3, elements)
+
+
 def reference_gate(y, ref, l2dot, rtol=1e-3):
     """Per-element parity bound used by every GEMV/GEMM test:
 
@@ -44,16 +47,37 @@ def reference_gate(y, ref, l2dot, rtol=1e-3):
     route); ||w.*x||_2 is the natural magnitude of the dot product (a sum of
     K terms of random sign has |ref| of about that size), so elements whose
     true value cancels to ~0 are judged against the scale of their terms
-    instead of an arbitrarily small |ref|. Returns the worst ratio."""
+    instead of an arbitrarily small |ref|. Returns the worst ratio.
+
+    Beside it the north star's strict metric, max |y - ref| / |ref| per
+    element (ref != 0), is recorded with its 99.9th percentile and the share
+    of elements above rtol; the session summary prints them per test."""
     y = np.asarray(y, np.float64)
     ref = np.asarray(ref, np.float64)
     denom = np.maximum(np.abs(ref), np.asarray(l2dot, np.float64))
     denom = np.where(denom == 0, 1.0, denom)
     ratio = np.abs(y - ref) / denom
     worst = float(ratio.max()) if ratio.size else 0.0
+    nz = ref != 0
+    strict = np.abs(y - ref)[nz] / np.abs(ref)[nz]
+    if strict.size:
+        PARITY_LOG.append((os.environ.get("PYTEST_CURRENT_TEST", "?").split(" ")[0], worst, float(strict.max()),
+                           float(np.quantile(strict, 0.999)), float(np.mean(strict > rtol)), int(strict.size)))
     assert np.all(np.isfinite(y)), "non-finite outputs"
     assert worst <= rtol, f"parity bound exceeded: max |y-ref|/max(|ref|,||w.*x||) = {worst:.3e} > {rtol}"
     return worst
+
+
+def pytest_terminal_summary(terminalreporter):
+    if not PARITY_LOG:
+        return
+    tr = terminalreporter
+    tr.section("parity: gated bound and the strict per-element relative error")
+    tr.write_line(f"{'test':<90} {'gate':>9} {'strict max':>11} {'strict p99.9':>12} {'>1e-3':>8} {'elements':>9}")
+    for name, worst, smax, sq, frac, n in PARITY_LOG:
+        tr.write_line(f"{name[-90:]:<90} {worst:9.2e} {smax:11.2e} {sq:12.2e} {frac:8.1e} {n:9d}")
+    allmax = max(r[1] for r in PARITY_LOG)
+    tr.write_line(f"worst gated ratio over {len(PARITY_LOG)} checks: {allmax:.3e}")
 
 
 def reference_outputs(orc, dtype, w, x, n_rows, n_cols):

@@ -68,7 +68,7 @@ def test_reference_test_fixtures_on_gpu(gpu, oracle):
         assert np.all(np.abs(y - ref) < 0.01)  # the reference test's own bound (:765)
 
 
-@pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8, 13, 16])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8, 13, 16, 17, 24, 31, 32])
 @pytest.mark.parametrize("dtype,n,k", [(Q40, 300, 1024), (Q4K, 300, 1024), (Q40, 64, 96)])
 def test_gemv_batches(gpu, oracle, dtype, n, k, batch):
     w = _weights(oracle, dtype, n, k, tid=3)
@@ -82,7 +82,7 @@ def test_gemv_batches(gpu, oracle, dtype, n, k, batch):
         W.free()
 
 
-@pytest.mark.parametrize("batch", [17, 40, 64])
+@pytest.mark.parametrize("batch", [33, 40, 64])
 @pytest.mark.parametrize("dtype", [Q40, Q4K])
 def test_prefill_batches(gpu, oracle, dtype, batch):
     n, k = 160, 512
@@ -117,7 +117,7 @@ def test_prefill_shapes(gpu, oracle, dtype, n, k, m):
 
 @pytest.mark.parametrize("dtype", [Q40, Q4K])
 def test_prefill_device_strided_accumulate(gpu, oracle, dtype):
-    """Device entry, batch > 16: padded leading dimensions, y += W x (split-K
+    """Device entry, batch > 32: padded leading dimensions, y += W x (split-K
     reduction onto existing values), and two calls in a row on one stream."""
     torch = pytest.importorskip("torch")
     n, k, m = 256, 2048, 40
@@ -257,6 +257,68 @@ def test_host_validation_errors(gpu):
     finally:
         W.free()
     gpu.synchronize()
+
+
+@pytest.mark.parametrize("dtype,n,k,batch", [(Q40, 4096, 4096, 1), (Q40, 4096, 4096, 4), (Q4K, 1024, 4096, 2),
+                                             (Q4K, 640, 2048, 9), (Q40, 300, 11008, 32)])
+def test_gemv_graph_replay(gpu, oracle, dtype, n, k, batch):
+    """One decode call captured alone in a CUDA graph and replayed with new
+    activations: rows shared by several CTAs are handed over through flags
+    that each launch sets and clears, so every replay must match the
+    reference (y is poisoned with NaN before each replay)."""
+    torch = pytest.importorskip("torch")
+    w = _weights(oracle, dtype, n, k, tid=40)
+    W = gpu.register(w, dtype, n, k)
+    try:
+        xd = torch.zeros((batch, k), dtype=torch.float32, device="cuda")
+        yd = torch.zeros((batch, n), dtype=torch.float32, device="cuda")
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            gpu.linear_device(W, xd.data_ptr(), k, yd.data_ptr(), n, batch, stream=st.cuda_stream)  # warm-up
+        st.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            gpu.linear_device(W, xd.data_ptr(), k, yd.data_ptr(), n, batch, stream=st.cuda_stream)
+        rows = np.arange(0, n, max(1, n // 97))
+        rb = oracle.row_bytes(dtype, k)
+        sub = np.concatenate([w[r * rb:(r + 1) * rb] for r in rows])
+        for rep in range(6):
+            x = oracle.gen_x(SEED, 41 + rep, (batch, k))
+            xd.copy_(torch.from_numpy(x))
+            yd.fill_(float("nan"))
+            g.replay()
+            torch.cuda.synchronize()
+            y = yd.cpu().numpy()
+            assert np.all(np.isfinite(y)), f"replay {rep}: rows left unwritten"
+            ref, l2 = reference_outputs(oracle, dtype, sub, x, len(rows), k)
+            reference_gate(y[:, rows], ref, l2)
+        del g
+    finally:
+        W.free()
+
+
+@pytest.mark.parametrize("batch", [1, 3, 16, 32])
+def test_gemv_multi_device_shared(gpu, oracle, batch):
+    """Three tensors sharing x in one call (the stacked Q/K/V pattern) with
+    widths that make CTA ranges cross matrix boundaries; strided outputs."""
+    torch = pytest.importorskip("torch")
+    k = 2048
+    ns = (1000, 136, 136)
+    ws = [_weights(oracle, Q4K, n, k, tid=50 + i) for i, n in enumerate(ns)]
+    Ws = [gpu.register(w, Q4K, n, k) for w, n in zip(ws, ns)]
+    try:
+        x = oracle.gen_x(SEED, 51, (batch, k))
+        xd = torch.from_numpy(x).cuda()
+        ys = [torch.full((batch, n + 5), float("nan"), device="cuda") for n in ns]
+        gpu.linear_multi_device(Ws, xd.data_ptr(), k, [y.data_ptr() for y in ys], [n + 5 for n in ns], batch)
+        torch.cuda.synchronize()
+        for w, n, y in zip(ws, ns, ys):
+            assert torch.isnan(y[:, n:]).all()
+            ref, l2 = reference_outputs(oracle, Q4K, w, x, n, k)
+            reference_gate(y[:, :n].cpu().numpy(), ref, l2)
+    finally:
+        for W in Ws:
+            W.free()
 
 
 # --------------------------------------------------------------- full sizes
