@@ -428,6 +428,7 @@ def gpu_arm(args):
     upload = gguf_upload_bench(torch, gpu) if world == 1 and not args.no_prefill else None
     q6k = q6k_bench(torch, gpu, st) if world == 1 and not args.no_prefill else None
     decode = model_decode_bench(torch, gpu, args) if world == 1 and not args.no_model else None
+    tp_model = tp_model_bench(torch, gpu, args, dist, world) if not args.no_tp_model else None
 
     # -------------------------------------------------------------- e2e
     # the public host-pointer C ABI: x copied in and y read back on every call
@@ -501,6 +502,7 @@ def gpu_arm(args):
             "gguf_upload": upload,
             "q6k": q6k,
             "model_decode": decode,
+            "tp_model": tp_model,
         }
         if decode and cpu:
             # the CPU engine streams the same weight bytes per token at the
@@ -520,6 +522,111 @@ def gpu_arm(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def tp_model_bench(torch, gpu, args, dist, world):
+    """a random-init Llama-3-70B-architecture model in Q4_0 (80
+    layers, d 8192, 64 query / 8 KV heads, FFN 28672, vocab 128256)
+    tensor-parallel over the job's ranks (column split Q/K/V/gate/up, row
+    split O/down with the in-place all-reduce of each row-split call), through
+    llamanyon.rs_b200/decoder.py. The workload: a 2048-token prefill (32
+    sequences x 64 prompt tokens, one pass) followed by batch-32 greedy
+    decoding of 128 tokens, each decode step one CUDA graph. Device time with
+    CUDA events, max over ranks. Weights are generated on the device (each
+    rank its own shards, from the same seeds at every degree)."""
+    import numpy as np
+    import decoder as dec
+    B, P, NEW = 32, 64, args.tp_new
+    cfg = dec.DecoderConfig(n_layers=args.tp_layers, d=8192, n_heads=64, n_kv_heads=8, ffn=28672, vocab=128256,
+                            dtype=Q40, context_len=1024, max_seq=P + NEW + 64)
+    model = dec.SynthModel(gpu, cfg, SEED, stacked=False)
+    D = dec.Decoder(gpu, model, n_seqs=B, max_rows=B * P)
+    rng = np.random.default_rng(SEED + 70)
+    prompts = rng.integers(0, cfg.vocab, size=(B, P))
+    st = torch.cuda.Stream()
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def maxr(ms):
+        if not dist:
+            return ms
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def prefill_rows():
+        return D.set_rows(prompts.T.reshape(-1), np.repeat(np.arange(P), B), np.tile(np.arange(B), P))
+    with torch.cuda.stream(st):
+        rows = prefill_rows()
+        D.forward(rows, stream=st.cuda_stream, logits_rows=slice(rows - B, rows), prefill=(B, P, 1, B))  # workspaces
+        st.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = ev(), ev()
+        e0.record(st)
+        rows = prefill_rows()
+        D.forward(rows, stream=st.cuda_stream, logits_rows=slice(rows - B, rows), prefill=(B, P, 1, B))
+        e1.record(st)
+        st.synchronize()
+    prefill_ms = maxr(e0.elapsed_time(e1))
+    first = D.next[:B].clone()
+    seqs = torch.arange(B, dtype=torch.int32, device="cuda")
+    with torch.cuda.stream(st):
+        def start():
+            D.tokens[:B].copy_(first)
+            D.pos[:B].fill_(P)
+            D.seq[:B].copy_(seqs)
+        start()
+        D.forward(B, stream=st.cuda_stream, decode=True)  # first use of the decode shapes
+        start()
+        st.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            D.forward(B, stream=st.cuda_stream, decode=True)
+            D.advance(B)
+        for _ in range(3):
+            g.replay()
+        start()
+        st.synchronize()
+        if dist:
+            dist.barrier()
+        steps = NEW - 1
+        e2, e3 = ev(), ev()
+        e2.record(st)
+        for _ in range(steps):
+            g.replay()
+        e3.record(st)
+        st.synchronize()
+        toks = D.tokens[:B].cpu().tolist()
+        del g
+    dec_ms = maxr(e2.elapsed_time(e3))
+    step_ms = dec_ms / steps
+    peak, peak_kind = measured_peaks()
+    tburst, tsust, tkind = measured_tensor_peak()
+    mean_len = P + 1 + (steps - 1) / 2
+    kv_bytes = 2 * B * cfg.n_layers * (cfg.n_kv_heads // world) * cfg.head_dim * 4 * mean_len
+    by = model.weight_bytes() + kv_bytes  # per rank
+    gbs = by / (step_ms * 1e-3) / 1e9
+    flops = 2 * B * P * (sum(cfg.shape(r)[0] * cfg.shape(r)[1] for r in dec.ROLES) * cfg.n_layers
+                         + cfg.d * cfg.vocab / P)  # the head runs on the last position only
+    tflops_gpu = flops / world / (prefill_ms * 1e-3) / 1e12
+    out = {
+        "workload": f"configs[4]: random-init Llama-3-70B-architecture Q4_0, {cfg.n_layers} layers, TP{world}; "
+                    f"prefill {B * P} tokens ({B} sequences x {P}), then batch-{B} greedy decode of {NEW} tokens",
+        "tp": world,
+        "prefill_ms": round(prefill_ms, 2), "prefill_tok_s": round(B * P / (prefill_ms * 1e-3), 1),
+        "prefill_roofline": {"bound": "tensor", "achieved": round(tflops_gpu, 1), "peak": tburst, "unit": "TFLOP/s",
+                             "frac": round(tflops_gpu / tburst, 4), "per": "GPU", "peak_kind": tkind + " bf16 burst"},
+        "decode_ms_per_step": round(step_ms, 4), "decode_tok_s": round(B / (step_ms * 1e-3), 1),
+        "e2e_tok_s": round(B * NEW / ((prefill_ms + dec_ms) * 1e-3), 1),
+        "decode_roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                            "frac": round(gbs / peak, 4), "per": "GPU", "bytes_per_step_per_gpu": int(by),
+                            "peak_kind": peak_kind},
+        "allreduce": "NCCL in-place all-reduce after each row-split linear (O, down): 2 per layer",
+        "tokens_seq0": [t for t in toks[:1]],
+    }
+    D.free()
+    model.free()
+    return out
 
 
 def model_decode_bench(torch, gpu, args):
@@ -792,6 +899,9 @@ def main():
     ap.add_argument("--no-model", action="store_true", help="skip the configs[3] model decode measurement")
     ap.add_argument("--model-layers", type=int, default=32, help="configs[3] layers (32 = the named model)")
     ap.add_argument("--model-new", type=int, default=256, help="configs[3] generated tokens")
+    ap.add_argument("--no-tp-model", action="store_true", help="skip the configs[4] tensor-parallel model")
+    ap.add_argument("--tp-layers", type=int, default=80, help="configs[4] layers (80 = the named model)")
+    ap.add_argument("--tp-new", type=int, default=128, help="configs[4] generated tokens")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

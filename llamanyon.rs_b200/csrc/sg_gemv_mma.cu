@@ -320,16 +320,14 @@ __global__ void __launch_bounds__(128) xprep_kernel(XParams p) {
   using C = Cfg<NTG>;
   pdl_launch_dependents();
   pdl_wait();  // x may come from the previous kernel, which may also still read the images
-  // zero the outputs: every thread of the grid takes a stride of them
+  // zero the outputs: every thread of the grid takes a stride of each row
   {
-    const int64_t nth = (int64_t)gridDim.x * blockDim.x, tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    for (int m = 0; m < p.n_zero; ++m) {
-      const int64_t n = (int64_t)p.batch * p.n_rows[m];
-      for (int64_t i = tid; i < n; i += nth) {
-        const int64_t b = i / p.n_rows[m], r = i - b * p.n_rows[m];
-        p.y[m][b * p.ldy[m] + r] = 0.f;
+    const int nth = gridDim.x * blockDim.x, tid = blockIdx.x * blockDim.x + threadIdx.x;
+    for (int m = 0; m < p.n_zero; ++m)
+      for (int b = 0; b < p.batch; ++b) {
+        float* yr = p.y[m] + (int64_t)b * p.ldy[m];
+        for (int r = tid; r < p.n_rows[m]; r += nth) yr[r] = 0.f;
       }
-    }
   }
   const int lane = threadIdx.x & 31;
   const int wg = blockIdx.x * 4 + (threadIdx.x >> 5);

@@ -69,27 +69,52 @@ def norm_vector(gpu: sg.SwampGpu, seed: int, tid: int, n: int) -> np.ndarray:
 class SynthModel:
     """Random-init weights of the architecture, generated on the device.
 
-    Q, K and V of a layer are registered as one tensor of d + 2 * kv rows
-    (their GGUF rows one after the other), and gate and up as one of
-    2 * ffn rows: each pair of projections that reads the same x is one
-    linear call, one prefill GEMM instead of three or two. The values are
-    exactly those of the separate tensors."""
+    Single GPU (stacked=True): Q, K and V of a layer are registered as one
+    tensor of d + 2 * kv rows (their GGUF rows one after the other), and gate
+    and up as one of 2 * ffn rows: each pair of projections that reads the
+    same x is one linear call, one prefill GEMM instead of three or two. The
+    values are exactly those of the separate tensors.
 
-    def __init__(self, gpu: sg.SwampGpu, cfg: DecoderConfig, seed: int):
+    Tensor parallel (stacked=False, the job's world from gpu.topology()):
+    Q, K, V, gate and up are column-split (each rank holds its heads' rows and
+    its FFN slice, generated on the device from the same seeds, so the model
+    is the same at every degree) and called as one multi-tensor linear; O and
+    down are row-split over the same head / FFN slices, their partial sums
+    all-reduced into the replicated residual stream (executor.rs:436-505 with
+    the layout of linear.rs:31-45 generalised to ranks)."""
+
+    def __init__(self, gpu: sg.SwampGpu, cfg: DecoderConfig, seed: int, stacked: bool = True):
         import torch
         self.cfg, self.seed = cfg, seed
+        _, self.world, _ = gpu.topology()
+        self.stacked = stacked and self.world == 1
+        W = self.world
+        if cfg.n_heads % W or cfg.n_kv_heads % W or cfg.ffn % W:
+            raise ValueError(f"heads {cfg.n_heads}/{cfg.n_kv_heads} and ffn {cfg.ffn} must split over {W} ranks")
         self.layers = []
         for l in range(cfg.n_layers):
-            def stacked(roles):
+            def stacked_t(roles):
                 blocks = [gpu.synth_blocks(cfg.dtype, seed, tensor_id(r, l), *cfg.shape(r)) for r in roles]
                 rows = sum(cfg.shape(r)[0] for r in roles)
                 return gpu.register(np.concatenate(blocks), cfg.dtype, rows, cfg.d)
-            self.layers.append({
-                "qkv": stacked(("attn_q", "attn_k", "attn_v")),
-                "attn_output": gpu.synth_weight(cfg.dtype, seed, tensor_id("attn_output", l), *cfg.shape("attn_output")),
-                "gate_up": stacked(("ffn_gate", "ffn_up")),
-                "ffn_down": gpu.synth_weight(cfg.dtype, seed, tensor_id("ffn_down", l), *cfg.shape("ffn_down")),
-            })
+
+            def synth(role, mode):
+                return gpu.synth_weight(cfg.dtype, seed, tensor_id(role, l), *cfg.shape(role), mode)
+            if self.stacked:
+                self.layers.append({
+                    "qkv": stacked_t(("attn_q", "attn_k", "attn_v")),
+                    "attn_output": synth("attn_output", sg.SG_TP_REPLICATE),
+                    "gate_up": stacked_t(("ffn_gate", "ffn_up")),
+                    "ffn_down": synth("ffn_down", sg.SG_TP_REPLICATE),
+                })
+            else:
+                self.layers.append({
+                    "q": synth("attn_q", sg.SG_TP_COLUMN), "k": synth("attn_k", sg.SG_TP_COLUMN),
+                    "v": synth("attn_v", sg.SG_TP_COLUMN),
+                    "attn_output": synth("attn_output", sg.SG_TP_ROW),
+                    "gate": synth("ffn_gate", sg.SG_TP_COLUMN), "up": synth("ffn_up", sg.SG_TP_COLUMN),
+                    "ffn_down": synth("ffn_down", sg.SG_TP_ROW),
+                })
         self.token_embd = gpu.synth_weight(cfg.dtype, seed, tensor_id("token_embd"), *cfg.shape("token_embd"))
         self.output = gpu.synth_weight(cfg.dtype, seed, tensor_id("output"), *cfg.shape("output"))
         dev = torch.device("cuda")
@@ -100,10 +125,11 @@ class SynthModel:
         self.output_norm = torch.from_numpy(norm_vector(gpu, seed, tensor_id("output_norm"), cfg.d)).to(dev)
 
     def weight_bytes(self) -> int:
-        """GGUF bytes of every quantized tensor one decode step reads (the
+        """GGUF bytes of every quantized tensor one decode step reads on one
+        rank (the layers' shards and the replicated output head; the
         embedding table contributes one row per token, not counted)."""
         c = self.cfg
-        tot = sum(sg.row_bytes(c.dtype, c.shape(r)[1]) * c.shape(r)[0] for r in ROLES) * c.n_layers
+        tot = sum(sg.row_bytes(c.dtype, c.shape(r)[1]) * c.shape(r)[0] for r in ROLES) * c.n_layers // self.world
         return tot + sg.row_bytes(c.dtype, c.d) * c.vocab
 
     def free(self):
@@ -123,19 +149,23 @@ class Decoder:
         self.gpu, self.m, self.cfg = gpu, model, model.cfg
         self.ops = sg.LayerOps(gpu)
         c = self.cfg
+        W = model.world
+        # this rank's heads, KV heads and FFN slice
+        self.n_heads, self.n_kv, self.ffn = c.n_heads // W, c.n_kv_heads // W, c.ffn // W
         self.rope = sg.Rope(gpu, c.head_dim, c.context_len)
-        self.cache = sg.KvCache(gpu, c.n_layers, c.n_kv_heads, c.head_dim, c.max_seq, n_seqs)
+        self.cache = sg.KvCache(gpu, c.n_layers, self.n_kv, c.head_dim, c.max_seq, n_seqs)
         self.max_rows = max_rows
         dev = torch.device("cuda")
         f = dict(device=dev, dtype=torch.float32)
-        kv = c.n_kv_heads * c.head_dim
+        dq, kv = self.n_heads * c.head_dim, self.n_kv * c.head_dim
+        self.dq = dq
         self.x = torch.zeros(max_rows, c.d, **f)
         self.xn = torch.zeros(max_rows, c.d, **f)
-        self.qkv = torch.zeros(max_rows, c.d + 2 * kv, **f)  # [q | k | v] per row
-        self.q, self.k, self.v = self.qkv[:, :c.d], self.qkv[:, c.d:c.d + kv], self.qkv[:, c.d + kv:]
-        self.att = torch.zeros(max_rows, c.d, **f)
-        self.gu = torch.zeros(max_rows, 2 * c.ffn, **f)  # [gate | up] per row
-        self.gate, self.up = self.gu[:, :c.ffn], self.gu[:, c.ffn:]
+        self.qkv = torch.zeros(max_rows, dq + 2 * kv, **f)  # [q | k | v] per row
+        self.q, self.k, self.v = self.qkv[:, :dq], self.qkv[:, dq:dq + kv], self.qkv[:, dq + kv:]
+        self.att = torch.zeros(max_rows, dq, **f)
+        self.gu = torch.zeros(max_rows, 2 * self.ffn, **f)  # [gate | up] per row
+        self.gate, self.up = self.gu[:, :self.ffn], self.gu[:, self.ffn:]
         self.logits = torch.zeros(max_rows, c.vocab, **f)
         i32 = dict(device=dev, dtype=torch.int32)
         self.tokens = torch.zeros(max_rows, **i32)
@@ -165,28 +195,39 @@ class Decoder:
         use_pf = prefill is not None and self.cfg.head_dim in (64, 128)
         c, o, g = self.cfg, self.ops, self.gpu
         p = lambda t: t.data_ptr()
-        D, KV = c.d, c.n_kv_heads * c.head_dim
-        LQ, LG = D + 2 * KV, 2 * c.ffn  # row strides of [q | k | v] and [gate | up]
+        D, DQ, KV, F = c.d, self.dq, self.n_kv * c.head_dim, self.ffn
+        H = self.n_heads
+        LQ, LG = DQ + 2 * KV, 2 * F  # row strides of [q | k | v] and [gate | up]
         ACC = sg.SG_FLAG_ACCUMULATE
         o.embed(self.m.token_embd, p(self.tokens), rows, p(self.x), D, stream)
         for l, lw in enumerate(self.m.layers):
             o.rmsnorm(p(self.x), D, p(self.m.attn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
-            g.linear_device(lw["qkv"], p(self.xn), D, p(self.qkv), LQ, rows, stream=stream)
+            if self.m.stacked:
+                g.linear_device(lw["qkv"], p(self.xn), D, p(self.qkv), LQ, rows, stream=stream)
+            else:
+                g.linear_multi_device([lw["q"], lw["k"], lw["v"]], p(self.xn), D,
+                                      [p(self.q), p(self.k), p(self.v)], [LQ] * 3, rows, stream=stream)
             if decode:
                 o.rope_attention(self.rope, self.cache, l, p(self.q), LQ, p(self.k), LQ, p(self.v), LQ, p(self.att),
-                                 D, p(self.pos), p(self.seq), rows, c.n_heads, stream)
+                                 DQ, p(self.pos), p(self.seq), rows, H, stream)
             else:
                 o.rope_kv(self.rope, self.cache, l, p(self.q), LQ, p(self.k), LQ, p(self.v), LQ, p(self.pos),
-                          p(self.seq), rows, c.n_heads, stream)
+                          p(self.seq), rows, H, stream)
                 if use_pf:
-                    o.attention_prefill(self.cache, l, p(self.q), LQ, p(self.att), D, *prefill, c.n_heads, stream)
+                    o.attention_prefill(self.cache, l, p(self.q), LQ, p(self.att), DQ, *prefill, H, stream)
                 else:
-                    o.attention(self.cache, l, p(self.q), LQ, p(self.att), D, p(self.pos), None, p(self.seq), rows,
-                                c.n_heads, stream)
-            g.linear_device(lw["attn_output"], p(self.att), D, p(self.x), D, rows, stream=stream, flags=ACC)
+                    o.attention(self.cache, l, p(self.q), LQ, p(self.att), DQ, p(self.pos), None, p(self.seq), rows,
+                                H, stream)
+            # O: row-split over this rank's heads; the all-reduce adds every
+            # rank's part (and the residual, once) into x
+            g.linear_device(lw["attn_output"], p(self.att), DQ, p(self.x), D, rows, stream=stream, flags=ACC)
             o.rmsnorm(p(self.x), D, p(self.m.ffn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
-            g.linear_device(lw["gate_up"], p(self.xn), D, p(self.gu), LG, rows, stream=stream)
-            o.silu_mul(p(self.gate), LG, p(self.up), LG, c.ffn, rows, stream)
+            if self.m.stacked:
+                g.linear_device(lw["gate_up"], p(self.xn), D, p(self.gu), LG, rows, stream=stream)
+            else:
+                g.linear_multi_device([lw["gate"], lw["up"]], p(self.xn), D, [p(self.gate), p(self.up)], [LG] * 2,
+                                      rows, stream=stream)
+            o.silu_mul(p(self.gate), LG, p(self.up), LG, F, rows, stream)
             g.linear_device(lw["ffn_down"], p(self.gate), LG, p(self.x), D, rows, stream=stream, flags=ACC)
         r0, r1 = (0, rows) if logits_rows is None else (logits_rows.start, logits_rows.stop)
         n = r1 - r0
