@@ -277,6 +277,15 @@ int init_devices(const std::vector<int>& devices, int rank_base, int world) {
     d.num_sms = prop.multiProcessorCount;
     CUDA_TRY(cudaSetDevice(dev));
     CUDA_TRY(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
+    // bounded device waits: SG_WAIT_NS in the environment (nanoseconds,
+    // 1 ms .. 60 s) replaces the built-in 4 s, e.g. for a test that lets a
+    // wait run out
+    unsigned long long wait_ns = SG_WAIT_NS;
+    if (const char* e = std::getenv("SG_WAIT_NS")) {
+      const unsigned long long v = strtoull(e, nullptr, 10);
+      if (v >= 1000000ull && v <= 60000000000ull) wait_ns = v;
+    }
+    CUDA_TRY(cudaMemcpyToSymbol(g_sg_wait_ns, &wait_ns, sizeof wait_ns));
     g_ctx.devs.push_back(d);
   }
   g_ctx.rank_base = rank_base;

@@ -1,6 +1,6 @@
 // sg_common.cuh -- shared device helpers for the swamp-gpu B200 kernels.
 //
-// Every spin-wait in these kernels is bounded: after SG_WAIT_NS of wall time
+// Every spin-wait in these kernels is bounded: after g_sg_wait_ns of wall time
 // (%globaltimer) the waiting thread records an error code in the per-device
 // flag g_sg_error and returns false, and the caller abandons its loop. The
 // host reads the flag after a call (SG_ERR_DEVICE_FAULT) instead of the GPU
@@ -108,6 +108,9 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 #ifndef SG_WAIT_NS
 #define SG_WAIT_NS 4000000000ull
 #endif
+// The limit in force, per device: SG_WAIT_NS unless the host set another one
+// at initialisation (SG_WAIT_NS in the environment of sg_init / sg_init_rank).
+__device__ unsigned long long g_sg_wait_ns = SG_WAIT_NS;
 #ifndef SG_WAIT_QUIET_CYCLES
 #define SG_WAIT_QUIET_CYCLES (1ll << 17)
 #endif
@@ -120,7 +123,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int ta
     if (clock64() - c0 > SG_WAIT_QUIET_CYCLES) {  // a long wait: watch the error flag and the wall clock
       if (t0 == 0) t0 = globaltimer_ns();
       if (*(volatile int*)&g_sg_error != 0) return false;
-      if (globaltimer_ns() - t0 > SG_WAIT_NS) break;
+      if (globaltimer_ns() - t0 > g_sg_wait_ns) break;
     }
   }
   sg_set_error(SG_DEVERR_WAIT_TIMEOUT | tag);
@@ -134,7 +137,7 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > SG_WAIT_NS) return false;
+    if (globaltimer_ns() - t0 > g_sg_wait_ns) return false;
   }
 }
 

@@ -58,9 +58,11 @@ __global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(const float*
   const uint32_t e = e_sh, par = e & 1u;
   const int64_t i0 = (int64_t)c * kArChunk, n = (count - i0 < kArChunk) ? count - i0 : (int64_t)kArChunk;
   const bool vec = ((count & 3) == 0) && (((uintptr_t)src & 15) == 0);
-  // 1. this rank's chunk into slot [par][rank] of every peer
-  for (int p = 0; p < world; ++p) {
-    if (p == rank) continue;
+  // 1. this rank's chunk into slot [par][rank] of every peer (the peers in
+  // an order that starts after this rank, so the ranks' stores spread over
+  // the links)
+  for (int j = 1; j < world; ++j) {
+    const int p = (rank + j) % world;
     float* slot = pp.buf[p] + ((int64_t)par * world + rank) * cap + i0;
     if (vec) {
       for (int64_t i = 4 * tid; i < n; i += 4 * kArThreads)
@@ -69,21 +71,26 @@ __global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(const float*
       for (int64_t i = tid; i < n; i += kArThreads) slot[i] = src[i0 + i];
     }
   }
-  __threadfence_system();
+  // one system-scope fence after the CTA barrier orders every thread's
+  // stores (the barrier makes them visible to thread 0) before the flags
   __syncthreads();
-  if (tid == 0)
-    for (int p = 0; p < world; ++p)
-      if (p != rank) st_release_sys_u32(pp.flags[p] + ((int64_t)par * world + rank) * kArMaxChunks + c, e);
-  // 2. wait for every peer's chunk (one thread per peer, bounded)
+  if (tid == 0) {
+    __threadfence_system();
+    for (int j = 1; j < world; ++j) {
+      const int p = (rank + j) % world;
+      *(volatile uint32_t*)(pp.flags[p] + ((int64_t)par * world + rank) * kArMaxChunks + c) = e;
+    }
+  }
+  // 2. wait for every peer's chunk (one thread per peer polls its flag in
+  // this rank's own memory, bounded)
   if (tid < world && tid != rank) {
     const uint32_t* f = pp.flags[rank] + ((int64_t)par * world + tid) * kArMaxChunks + c;
     const uint64_t t0 = globaltimer_ns();
     while (ld_acquire_sys_u32(f) != e) {
-      if (globaltimer_ns() - t0 > SG_WAIT_NS) {
+      if (globaltimer_ns() - t0 > g_sg_wait_ns) {
         sg_set_error(SG_DEVERR_WAIT_TIMEOUT | 0x50);
         break;
       }
-      __nanosleep(64);
     }
   }
   __syncthreads();
