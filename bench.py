@@ -128,7 +128,7 @@ def measured_peaks():
 # capture of the current kernels (profiles/): decode GEMV 4096->11008 batch 1
 # (algorithmic 25,406,976 B); prefill GEMM Q4_K 4096->14336 M=512
 # (algorithmic weight + activation bytes 41,418,752 B).
-NCU_TRAFFIC = {"gemv_4096x11008_b1": 25_442_048, "gemm_q4k_4096x14336_m512": 54_764_032}
+NCU_TRAFFIC = {"gemv_4096x11008_b1": 25_465_088, "gemm_q4k_4096x14336_m512": 54_764_032}
 
 
 def measured_tensor_peak():
@@ -492,7 +492,7 @@ def gpu_arm(args):
                          "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC["gemv_4096x11008_b1"],
                          "traffic_launch": "4096x11008 batch 1 (algorithmic 25,406,976 B)", "peak_kind": peak_kind,
                          "traffic_note": "ncu dram bytes of one launch of that shape, per launch like achieved",
-                         "kernel": "gemv_kernel (one launch per GEMV), back-to-back launches in a CUDA graph",
+                         "kernel": "gemv_kernel (mma.sync u8 x s8, one launch per GEMV, + xprep_kernel), back-to-back in a CUDA graph",
                          "per_shape_gbs": per_shape},
             "e2e": e2e,
             "cpu_baseline": cpu,
