@@ -202,6 +202,54 @@ def cpu_prefill_sample(threads, seconds_budget=8.0):
                                f"configs[2] shape) in {el:.1f} s on {threads} host threads")
 
 
+def cpu_q4k_decode_variants(threads, seconds_each=3.0):
+    """The reference's other Q4_K decode routes on the host, each timed on the
+    configs[1] layer's 7 shapes quantized as Q4_K, batch 1 (GB/s of weight +
+    activation bytes, like the headline):
+      - forward_linear's Q4_K arm with the scalar kernel (fused_gemv_q4k.rs:466-508;
+        the parity target), on `threads` threads and on 1;
+      - the same arm as the reference dispatches it on this CPU
+        (fused_gemv_q4k.rs:59-82 -> VNNI :101-317 or AVX2 :325-392), on `threads`
+        threads and on 1: numerically divergent from the reference's
+        dequantizer, timing only."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.build()
+    ws = [(k, n, oracle.gen_weight(Q4K, SEED, 520 + i, n, k)) for i, (_, k, n) in enumerate(LAYER)]
+    x = {k: oracle.gen_x(SEED, 920 + k, (k,)) for _, k, _ in LAYER}
+    layer_b = sum(oracle.row_bytes(Q4K, k) * n + (k + n) * 4 for k, n, _ in ws)
+    path = oracle.simd_path()
+
+    def run(fn, nthr):
+        for k, n, w in ws[:1]:
+            fn(w, x[k], n, k, nthr)  # page-in
+        t0, layers = time.perf_counter(), 0
+        while True:
+            for k, n, w in ws:
+                fn(w, x[k], n, k, nthr)
+            layers += 1
+            el = time.perf_counter() - t0
+            if el > seconds_each:
+                return layer_b * layers / el / 1e9, layers, el
+
+    scalar = lambda w, xx, n, k, t: oracle.forward_linear(Q4K, w, xx, n, k, t)
+    disp = lambda w, xx, n, k, t: oracle.forward_linear_dispatched(w, xx, n, k, t)
+    out = []
+    variants = [("scalar", scalar, "fused_gemv_q4k_scalar (fused_gemv_q4k.rs:466-508), the parity target")]
+    if path != "none":
+        variants.append(("as-dispatched", disp, f"fused_gemv_q4k as dispatched on this CPU: {path} "
+                         f"({'fused_gemv_q4k.rs:101-317' if path == 'avx512-vnni' else 'fused_gemv_q4k.rs:325-392'}); "
+                         "numerically divergent, timing only"))
+    for name, fn, what in variants:
+        for nthr in sorted({threads, 1}, reverse=True):
+            gbs, layers, el = run(fn, nthr)
+            out.append({"variant": f"q4_k {name}", "value": round(gbs, 3), "unit": "GB/s", "cores": nthr,
+                        "kind": "port", "sample": f"{layers} passes over the configs[1] layer's 7 shapes as Q4_K, "
+                                                  f"batch 1, through forward_linear's Q4_K arm (linear.rs:28-46) "
+                                                  f"with {what}, {el:.1f} s on {nthr} host threads"})
+    return out
+
+
 def reference_arm(args):
     """The reference's CPU route on the host cores, same metric and config.
 
@@ -472,7 +520,8 @@ def gpu_arm(args):
         gbs, ncalls, el = cpu_sample(threads, seconds_budget=args.cpu_seconds)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"{ncalls} forward_linear calls (Q4_0 engine route, batch 1) over the layer's 7 "
-                         f"tensors in {el:.1f} s on {threads} host threads"}
+                         f"tensors in {el:.1f} s on {threads} host threads",
+               "variants": cpu_q4k_decode_variants(threads)}
 
     if rank == 0:
         line = {

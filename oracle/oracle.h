@@ -95,6 +95,18 @@ int orc_forward_linear_batch(int dtype, const uint8_t *w, const float *const *xs
                              float *const *outs, int64_t batch, int64_t n_rows,
                              int64_t n_cols, int n_threads);
 
+/* oracle_simd.c: the reference's dispatched SIMD Q4_K paths, for CPU timing
+ * only (numerically divergent from the reference's dequantizer; see that
+ * file). orc_simd_path: 2 = AVX-512 VNNI, 1 = AVX2+FMA, 0 = neither.
+ * orc_gemv_q4k_vnni accumulates into out, orc_gemv_q4k_avx2 overwrites;
+ * both return -1 when the CPU lacks the path. orc_forward_linear_dispatched
+ * zeroes out, partitions rows as linear.rs:31-45 and returns the path used. */
+int orc_simd_path(void);
+int orc_gemv_q4k_vnni(const uint8_t *w, const float *x, float *out, int64_t n_rows, int64_t n_cols);
+int orc_gemv_q4k_avx2(const uint8_t *w, const float *x, float *out, int64_t n_rows, int64_t n_cols);
+int orc_forward_linear_dispatched(const uint8_t *w, const float *x, float *out, int64_t n_rows,
+                                  int64_t n_cols, int n_threads);
+
 /* The reference's test block packer, fused_gemv_q4k.rs:708-724 (inverse of
  * unpack_scales). d and dmin go through f16 round-to-nearest-even. */
 void orc_make_q4k_block(float d, float dmin, const uint8_t scales[8],

@@ -81,6 +81,13 @@ def lib() -> ctypes.CDLL:
     L.orc_add.argtypes = [P, P, i64]
     L.orc_argmax.argtypes = [P, i64]
     L.orc_argmax.restype = i64
+    L.orc_simd_path.restype = ctypes.c_int
+    L.orc_gemv_q4k_vnni.argtypes = [P, P, P, i64, i64]
+    L.orc_gemv_q4k_vnni.restype = ctypes.c_int
+    L.orc_gemv_q4k_avx2.argtypes = [P, P, P, i64, i64]
+    L.orc_gemv_q4k_avx2.restype = ctypes.c_int
+    L.orc_forward_linear_dispatched.argtypes = [P, P, P, i64, i64, ctypes.c_int]
+    L.orc_forward_linear_dispatched.restype = ctypes.c_int
     _lib = L
     return L
 
@@ -183,6 +190,42 @@ def forward_linear(dtype, w, x, n_rows, n_cols, n_threads) -> np.ndarray:
     if rc:
         raise ValueError(rc)
     return out
+
+
+SIMD_PATHS = {0: "none", 1: "avx2", 2: "avx512-vnni"}
+
+
+def simd_path() -> str:
+    """The SIMD path the reference's fused_gemv_q4k dispatcher
+    (fused_gemv_q4k.rs:59-82) takes on this CPU."""
+    return SIMD_PATHS[lib().orc_simd_path()]
+
+
+def gemv_q4k_simd(path: str, w, x, n_rows, n_cols) -> np.ndarray:
+    """The reference's SIMD Q4_K GEMV ("avx512-vnni": fused_gemv_q4k.rs:101-317,
+    "avx2": :325-392), single-threaded. TIMING ONLY: these paths do not compute
+    the reference's dequantized dot product (the VNNI path drops the sub-block
+    scales from the integer quire and quantizes x to int8), so their outputs
+    are not a parity target."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(n_rows, np.float32)
+    fn = lib().orc_gemv_q4k_vnni if path == "avx512-vnni" else lib().orc_gemv_q4k_avx2
+    if fn(_p(w), _p(x), _p(out), n_rows, n_cols):
+        raise RuntimeError(f"{path} not supported on this CPU")
+    return out
+
+
+def forward_linear_dispatched(w, x, n_rows, n_cols, n_threads):
+    """forward_linear's Q4_K arm (linear.rs:28-46) as the reference runs it on
+    this CPU: rows over n_threads threads, each chunk through the dispatched
+    SIMD kernel. TIMING ONLY (numerically divergent, see gemv_q4k_simd).
+    Returns (out, path)."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(n_rows, np.float32)
+    rc = lib().orc_forward_linear_dispatched(_p(w), _p(x), _p(out), n_rows, n_cols, n_threads)
+    if rc < 1:
+        raise RuntimeError("no SIMD path on this CPU")
+    return out, SIMD_PATHS[rc]
 
 
 def forward_linear_batch(dtype, w, xs: np.ndarray, n_rows, n_cols, n_threads) -> np.ndarray:
