@@ -159,3 +159,66 @@ def test_decoder_graph_replay_matches_eager(gpu, oracle):
     finally:
         D.free()
         model.free()
+
+
+# configs[3]'s layer at full width (Llama-3-8B: d 4096, 32 query / 8 KV heads
+# of 128, FFN 14336, Q4_K), one layer and a small vocabulary.
+CFG3_LAYER = dict(n_layers=1, d=4096, n_heads=32, n_kv_heads=8, ffn=14336, vocab=512, context_len=64, max_seq=64)
+
+
+class WideOracleModel(OracleModel):
+    """OracleModel with forward_linear on every host thread (the row split
+    leaves each row's result unchanged)."""
+
+    def lin(self, role, layer, x):
+        import os
+        c = self.c
+        n, k = c.shape(role)
+        w = self.out_w if role == "output" else self.w[layer][role]
+        return self.o.forward_linear(c.dtype, w, x, n, k, os.cpu_count() or 4)
+
+
+@pytest.mark.gpu
+def test_decoder_configs3_full_width_layer(gpu, oracle):
+    """One configs[3]-width layer: a 40-row prefill (2 sequences of 20, the
+    prefill GEMM) and 3 two-row decode steps (the decode GEMV and fused decode
+    attention), logits and greedy tokens against the oracle's engine loop."""
+    import torch
+    import decoder as dec
+    cfg = dec.DecoderConfig(dtype=12, **CFG3_LAYER)
+    model = dec.SynthModel(gpu, cfg, SEED)
+    n_seqs, plen, n_new = 2, 20, 3
+    D = dec.Decoder(gpu, model, n_seqs=n_seqs, max_rows=n_seqs * plen)
+    try:
+        rng = np.random.default_rng(SEED + 3)
+        prompts = rng.integers(0, cfg.vocab, size=(n_seqs, plen))
+        refs = [WideOracleModel(oracle, cfg, SEED) for _ in range(n_seqs)]
+        rows = D.set_rows(prompts.reshape(-1), np.tile(np.arange(plen), n_seqs), np.repeat(np.arange(n_seqs), plen))
+        D.forward(rows, prefill=(n_seqs, plen, plen, 1))
+        torch.cuda.synchronize()
+        gpu.synchronize()
+        logits = D.logits[:rows].cpu().numpy()
+        picks = D.next[:rows].cpu().numpy()
+        cur = []
+        for s in range(n_seqs):
+            for t in range(plen):
+                ref, tok = refs[s].step(int(prompts[s, t]), t)
+                _check_logits(logits[s * plen + t], ref, int(picks[s * plen + t]), tok)
+            cur.append(tok)
+        for step in range(n_new):
+            pos = plen + step
+            D.set_rows(cur, [pos] * n_seqs, list(range(n_seqs)))
+            D.forward(n_seqs, decode=True)
+            torch.cuda.synchronize()
+            gpu.synchronize()
+            logits = D.logits[:n_seqs].cpu().numpy()
+            picks = D.next[:n_seqs].cpu().numpy()
+            nxt = []
+            for s in range(n_seqs):
+                ref, tok = refs[s].step(cur[s], pos)
+                _check_logits(logits[s], ref, int(picks[s]), tok)
+                nxt.append(tok)
+            cur = nxt
+    finally:
+        D.free()
+        model.free()

@@ -1,5 +1,6 @@
 """sg_linear_device_noalloc through the C ABI: same results as
-sg_linear_device, two calls in a row, prefill batches rejected with a clear
+sg_linear_device and within the parity bound of the oracle's restatement of
+the reference, two calls in a row, prefill batches rejected with a clear
 error, and no device memory taken by the calls themselves.
 
 Collected last (file name) so it also runs after every other GPU test; it
@@ -7,7 +8,7 @@ needs nothing from them and passes alone."""
 import numpy as np
 import pytest
 
-from conftest import SEED
+from conftest import SEED, reference_gate, reference_outputs
 
 pytestmark = pytest.mark.gpu
 
@@ -29,6 +30,8 @@ def test_noalloc_matches_device_entry(gpu, oracle, dtype, n, k, batch):
         torch.cuda.synchronize()
         ref = y_ref.cpu().numpy()
         scale = np.abs(ref).max() + 1e-30
+        x_host = x.cpu().numpy()
+        orc, l2 = reference_outputs(oracle, dtype, w, x_host, n, k)
         for _ in range(2):  # two calls in a row on the shared scratch
             y = torch.full((batch, n), float("nan"), device="cuda")
             gpu.linear_device_noalloc(W, x.data_ptr(), k, y.data_ptr(), n, batch)
@@ -36,6 +39,7 @@ def test_noalloc_matches_device_entry(gpu, oracle, dtype, n, k, batch):
             got = y.cpu().numpy()
             assert np.all(np.isfinite(got))
             assert np.max(np.abs(got - ref)) <= 1e-6 * scale
+            reference_gate(got, orc, l2)
     finally:
         W.free()
 
