@@ -26,11 +26,14 @@
 //     f32 is 1.5*2^23 + D exactly and one subtraction gives D; per column
 //     acc += d_row * D; each column is scaled by 2^(-7*digit)/s per unit and
 //     the digit columns of a token are summed at the end of a row segment.
-//   batch 3-32 (combined): 8 tokens per MMA, one MMA per digit, and the
-//     three s32 results of a (row, token) are combined exactly into
-//     V_sum = (D0*128 + D1)*128 + D2 (Q4_0: the digit-2 accumulator starts at
-//     -8*sum V, |V_sum| < 2^30), one conversion to f32 and one FMA with the
-//     block scale.
+//   batch 3-32 (combined): 8 tokens per MMA, one MMA per digit, every
+//     accumulator starting at the bits of 1.5*2^23 (Q4_0: minus 8*sum of the
+//     column's digit) as above; per (row, token) the three digit sums D_i
+//     come out exactly by one subtraction each, (D0*128 + D1)*128 + D2 is
+//     formed by two FMAs (exact up to the last, which rounds once to f32)
+//     and one FMA applies the block scale. Pairs of values (rows g, g+8 of a
+//     column) go through the packed f32x2 instructions, and no integer to
+//     float conversion is needed.
 // Q4_K keeps the min term apart: per (row, block) m * (sum of the block's x).
 //
 // Weight layout: the repacked tiles of sg_layout.cuh, unchanged. A warp takes
@@ -78,7 +81,7 @@ struct Cfg {
   static constexpr bool P = NTG == 0;
   static constexpr int NTOK = P ? 2 : 8 * NTG;     // token slots
   static constexpr int NM = P ? 1 : 3 * NTG;       // MMAs per (16 rows, 32-block)
-  static constexpr int NCA = P ? 1 : NTG;          // accumulator-start areas per block
+  static constexpr int NCA = P ? 1 : 3 * NTG;      // accumulator-start areas per block
   static constexpr int PB = NM * 256 + NCA * 32;   // image bytes per 32-block
   static constexpr int INV_OFF = 8 * PB;           // per-unit scales after the 8 blocks
   static constexpr int XU = 8 * PB + 128;          // image bytes per unit
@@ -88,10 +91,12 @@ struct Cfg {
   static constexpr int RT = 1;
   static constexpr int NCW = 8 / RT;               // consumer warps
   static constexpr int THREADS = 32 * (1 + NCW);
-  // two CTAs per SM; ring depth as shared memory allows (at least ~64 KB of
-  // weights in flight per SM)
+  // two CTAs per SM, two ring slots each: about 80 KB of weights in flight
+  // per SM. Deeper rings measured slower: when every CTA requests all its
+  // tiles at once, they arrive together at the end and the compute cannot
+  // overlap the stream.
   static constexpr int CPS = 2;
-  static constexpr int R = P || NTG == 1 ? 4 : NTG == 2 ? 3 : 2;
+  static constexpr int R = 2;
   static constexpr int SMEM = R * SLOT + 128;
   // registers: leave room beside the GEMV CTAs for one CTA of the next
   // call's activation prep kernel (128 threads x 40 registers), which under
@@ -179,6 +184,21 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
 }
 
 __device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
+// f16 half h (0: low, 1: high) of a scale word, as the pair (v, v)
+__device__ __forceinline__ float2 h2f_pair(uint32_t w, int h) {
+  return __half22float2(__half2half2(__ushort_as_half((unsigned short)(w >> (16 * h)))));
+}
+// byte i of a scale word as the float pair (v, v), exact: the byte is placed
+// in the mantissa of 2^23, then 2^23 is subtracted
+__device__ __forceinline__ float2 byte_pair(uint32_t w, int i) {
+  const float a = __uint_as_float(__byte_perm(w, 0x4B000000u, (uint32_t)i | 0x7650u));
+  return __fadd2_rn(make_float2(a, a), make_float2(-8388608.f, -8388608.f));
+}
+// the pair (c[2*q], c[2*q+1]) of MMA results read as floats: row g (q = 0) or
+// g+8 (q = 1) at columns 2t, 2t+1 (adjacent registers)
+__device__ __forceinline__ float2 res_pair(const int (&c)[4], int q) {
+  return make_float2(__int_as_float(c[2 * q]), __int_as_float(c[2 * q + 1]));
+}
 
 // ------------------------------------------------------ activation images
 // Image of one unit (256 K), for the plan of Cfg<NTG>:
@@ -188,8 +208,10 @@ __device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__us
 //     [NCA][t 4][2 words]     per-column accumulator starts (lane t holds
 //                             columns 2t, 2t+1):
 //        per-column plan  Q4_0: bits 1.5*2^23 - 8*sum(digits); Q4_K: sum(digits)
-//        combined plan    Q4_0: -8*sum(V) of token (8*tg + 2t + i);
-//                         Q4_K: sum(V) as f32 (the min term)
+//        combined plan    area 3*tg + i, column c = token 8*tg + c:
+//                         Q4_0: bits 1.5*2^23 - 8*sum(digit i);
+//                         Q4_K: area 3*tg only, sum(V) as f32 (the min
+//                         term); the digit MMAs start at 1.5*2^23
 //   INV_OFF: per-column plan: f32 [col 8] = 2^(-7*digit)/s of the column's
 //            token; combined plan: f32 [token 32] = 2^-14/s. NaN when the
 //            unit's x holds inf or NaN.
@@ -304,8 +326,13 @@ __device__ __forceinline__ void store_unit(uint8_t* unit, const UnitX& u, int to
     for (int i = 0; i < 3; ++i)
       *reinterpret_cast<uint2*>(blk + ((3 * tg + i) * 32 + 4 * cc + t) * 8) = make_uint2(u.dig[i][0], u.dig[i][1]);
     if (t == 0) {
-      uint32_t* ca = reinterpret_cast<uint32_t*>(blk + C::NM * 256 + tg * 32);
-      ca[cc] = DT == SG_DTYPE_Q4_0 ? (uint32_t)(-8 * u.vsum) : __float_as_uint((float)u.vsum);
+      uint32_t* ca = reinterpret_cast<uint32_t*>(blk + C::NM * 256 + 3 * tg * 32);
+      if constexpr (DT == SG_DTYPE_Q4_0) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i) ca[8 * i + cc] = kMagic - 8u * (uint32_t)u.dsum[i];
+      } else {
+        ca[cc] = __float_as_uint((float)u.vsum);
+      }
     }
     if (lane == 0) inv[tok] = inv_scale(u, 6.103515625e-05f);
   }
@@ -373,8 +400,9 @@ __device__ __forceinline__ void seg_coords(int lane, int j, int& rr, int& tok) {
 template <int DT, int NTG, typename C = Cfg<NTG>>
 __global__ void __launch_bounds__(C::THREADS, C::CPS) __maxnreg__(C::MAXREG) gemv_kernel(Params p) {
   constexpr int RT = C::RT;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
+  // a shared-space array (not a generic pointer): every shared-memory access
+  // below is a 32-bit shared address, most of them a constant offset
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[C::R], empty[C::R];
 
   pdl_launch_dependents();  // the next kernel may start its prologue as SMs free up
@@ -437,19 +465,24 @@ __global__ void __launch_bounds__(C::THREADS, C::CPS) __maxnreg__(C::MAXREG) gem
   }
   pdl_wait();  // the images are built and y is zeroed (the prep kernel completed)
 
-  // per-unit accumulators (reset at every piece end) and per-segment sums
-  constexpr int NA = C::P ? 4 : 4 * NTG;
-  float acc[RT][NA];
-  float accu[RT][NA];
-  float accm[RT][NA];       // Q4_K min term (combined plan)
-  int iacc[RT][4], iacm[RT][4];  // Q4_K per-column plan: integer sums over the unit
+  // Sums as pairs of columns (2t, 2t+1) of one row: pair q = row g + 8q
+  // (per-column plan: columns; combined plan, at 2*tg + q: tokens 8*tg + 2t
+  // and 8*tg + 2t + 1). Per-unit sums are reset at every piece end,
+  // per-segment sums at every segment end; the pairs go through the packed
+  // f32x2 instructions (an MMA's two results of a row sit in adjacent
+  // registers).
+  constexpr int NP = C::P ? 2 : 2 * NTG;
+  float2 acc[RT][NP], accu[RT][NP], accm[RT][NP];  // accm: Q4_K min term (combined plan)
+  int iacc[RT][4], iacm[RT][4];                    // Q4_K per-column plan: integer sums over the unit
 #pragma unroll
   for (int r = 0; r < RT; ++r) {
 #pragma unroll
-    for (int i = 0; i < NA; ++i) acc[r][i] = accu[r][i] = accm[r][i] = 0.f;
+    for (int i = 0; i < NP; ++i) acc[r][i] = accu[r][i] = accm[r][i] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < 4; ++i) iacc[r][i] = iacm[r][i] = 0;
   }
+  const float2 neg_magic = make_float2(-kMagicF, -kMagicF);
+  const float2 f128 = make_float2(128.f, 128.f);
 
   Cursor cur;
   cur.init(p, g0, g1);
@@ -460,8 +493,8 @@ __global__ void __launch_bounds__(C::THREADS, C::CPS) __maxnreg__(C::MAXREG) gem
     const uint8_t* slot = smem + s * C::SLOT;
     const uint8_t* xim = slot + kXOff;
     const int cnt = cur.cnt(p), ci0 = cur.c & 3;
-#pragma unroll 1
-    for (int j = 0; j < cnt; ++j) {
+    // one 64-K chunk of the piece: j = its tile in the slot, cj = its place in the unit
+    auto chunk = [&](const int j, const int cj) {
       const uint8_t* tile = slot + j * SG_TILE_BYTES;
       uint32_t sw0[RT], sw1[RT];
 #pragma unroll
@@ -481,7 +514,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CPS) __maxnreg__(C::MAXREG) gem
           a[r][2] = (w0 >> 4) & kNib;
           a[r][3] = (w1 >> 4) & kNib;
         }
-        const uint8_t* xb = xim + (2 * (ci0 + j) + h) * C::PB;
+        const uint8_t* xb = xim + (2 * cj + h) * C::PB;
         if constexpr (C::P) {
           const uint2 b = *reinterpret_cast<const uint2*>(xb + lane * 8);
           const uint2 ci = *reinterpret_cast<const uint2*>(xb + 256 + t * 8);
@@ -491,11 +524,8 @@ __global__ void __launch_bounds__(C::THREADS, C::CPS) __maxnreg__(C::MAXREG) gem
             mma_u8s8(d, a[r][0], a[r][1], a[r][2], a[r][3], b.x, b.y, DT == SG_DTYPE_Q4_0 ? ci.x : 0u,
                      DT == SG_DTYPE_Q4_0 ? ci.y : 0u);
             if constexpr (DT == SG_DTYPE_Q4_0) {
-              const float d0 = h2f(sw0[r] >> (16 * h)), d1 = h2f(sw1[r] >> (16 * h));
-              accu[r][0] = fmaf(d0, __int_as_float(d[0]) - kMagicF, accu[r][0]);
-              accu[r][1] = fmaf(d0, __int_as_float(d[1]) - kMagicF, accu[r][1]);
-              accu[r][2] = fmaf(d1, __int_as_float(d[2]) - kMagicF, accu[r][2]);
-              accu[r][3] = fmaf(d1, __int_as_float(d[3]) - kMagicF, accu[r][3]);
+              accu[r][0] = __ffma2_rn(h2f_pair(sw0[r], h), __fadd2_rn(res_pair(d, 0), neg_magic), accu[r][0]);
+              accu[r][1] = __ffma2_rn(h2f_pair(sw1[r], h), __fadd2_rn(res_pair(d, 1), neg_magic), accu[r][1]);
             } else {
               const int sc0 = (sw0[r] >> (8 * h)) & 0xFF, sc1 = (sw1[r] >> (8 * h)) & 0xFF;
               const int m0 = (sw0[r] >> (16 + 8 * h)) & 0xFF, m1 = (sw1[r] >> (16 + 8 * h)) & 0xFF;
@@ -510,91 +540,108 @@ __global__ void __launch_bounds__(C::THREADS, C::CPS) __maxnreg__(C::MAXREG) gem
             }
           }
         } else {
-          float f0[RT], f1[RT];  // row scales (Q4_0: d; Q4_K: sc)
-          float n0[RT], n1[RT];  // Q4_K: m
+          float2 fs[RT][2], ns[RT][2];  // scales of rows g, g+8 as pairs: Q4_0 d; Q4_K sc and m
 #pragma unroll
           for (int r = 0; r < RT; ++r) {
             if constexpr (DT == SG_DTYPE_Q4_0) {
-              f0[r] = h2f(sw0[r] >> (16 * h));
-              f1[r] = h2f(sw1[r] >> (16 * h));
-              n0[r] = n1[r] = 0.f;
+              fs[r][0] = h2f_pair(sw0[r], h);
+              fs[r][1] = h2f_pair(sw1[r], h);
             } else {
-              f0[r] = (float)((sw0[r] >> (8 * h)) & 0xFF);
-              f1[r] = (float)((sw1[r] >> (8 * h)) & 0xFF);
-              n0[r] = (float)((sw0[r] >> (16 + 8 * h)) & 0xFF);
-              n1[r] = (float)((sw1[r] >> (16 + 8 * h)) & 0xFF);
+              fs[r][0] = byte_pair(sw0[r], h);  // sc
+              fs[r][1] = byte_pair(sw1[r], h);
+              ns[r][0] = byte_pair(sw0[r], 2 + h);  // m
+              ns[r][1] = byte_pair(sw1[r], 2 + h);
             }
           }
 #pragma unroll
           for (int tg = 0; tg < NTG; ++tg) {
-            const uint2 ca = *reinterpret_cast<const uint2*>(xb + C::NM * 256 + tg * 32 + t * 8);
-            uint2 b[3];
+            const uint8_t* cab = xb + C::NM * 256 + 3 * tg * 32 + t * 8;
+            uint2 b[3], st[3];
 #pragma unroll
-            for (int i = 0; i < 3; ++i) b[i] = *reinterpret_cast<const uint2*>(xb + (3 * tg + i) * 256 + lane * 8);
+            for (int i = 0; i < 3; ++i) {
+              b[i] = *reinterpret_cast<const uint2*>(xb + (3 * tg + i) * 256 + lane * 8);
+              st[i] = DT == SG_DTYPE_Q4_0 ? *reinterpret_cast<const uint2*>(cab + i * 32) : make_uint2(kMagic, kMagic);
+            }
+            float2 vs;  // Q4_K: the block's sums of V of tokens 2t, 2t+1
+            if constexpr (DT == SG_DTYPE_Q4_K) vs = *reinterpret_cast<const float2*>(cab);
 #pragma unroll
             for (int r = 0; r < RT; ++r) {
               int dd[3][4];
 #pragma unroll
-              for (int i = 0; i < 3; ++i) {
-                const bool c2 = DT == SG_DTYPE_Q4_0 && i == 2;
-                mma_u8s8(dd[i], a[r][0], a[r][1], a[r][2], a[r][3], b[i].x, b[i].y, c2 ? ca.x : 0u, c2 ? ca.y : 0u);
-              }
+              for (int i = 0; i < 3; ++i)
+                mma_u8s8(dd[i], a[r][0], a[r][1], a[r][2], a[r][3], b[i].x, b[i].y, st[i].x, st[i].y);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int vs = (dd[0][q] * 128 + dd[1][q]) * 128 + dd[2][q];
-                accu[r][4 * tg + q] = fmaf(q < 2 ? f0[r] : f1[r], (float)vs, accu[r][4 * tg + q]);
-                if constexpr (DT == SG_DTYPE_Q4_K)
-                  accm[r][4 * tg + q] =
-                      fmaf(q < 2 ? n0[r] : n1[r], __uint_as_float((q & 1) ? ca.y : ca.x), accm[r][4 * tg + q]);
+              for (int q = 0; q < 2; ++q) {
+                // digit sums D_i = result - 1.5*2^23 (exact); (D0*128 + D1) is exact,
+                // *128 + D2 rounds once to f32 (the value sum_k q_k V_k of the pair)
+                float2 e[3];
+#pragma unroll
+                for (int i = 0; i < 3; ++i) e[i] = __fadd2_rn(res_pair(dd[i], q), neg_magic);
+                const float2 val = __ffma2_rn(__ffma2_rn(e[0], f128, e[1]), f128, e[2]);
+                accu[r][2 * tg + q] = __ffma2_rn(fs[r][q], val, accu[r][2 * tg + q]);
+                if constexpr (DT == SG_DTYPE_Q4_K) accm[r][2 * tg + q] = __ffma2_rn(ns[r][q], vs, accm[r][2 * tg + q]);
               }
             }
           }
         }
       }
+    };
+    bool whole = false;
+    if constexpr (NTG <= 2) {
+      // a whole unit (the common case): straight-line code, every shared-memory
+      // address a constant offset from the slot
+      if (cnt == kUC) {
+#pragma unroll
+        for (int j = 0; j < kUC; ++j) chunk(j, j);
+        whole = true;
+      }
+    }
+    if (!whole) {
+#pragma unroll 1
+      for (int j = 0; j < cnt; ++j) chunk(j, ci0 + j);
     }
     // ---- piece end: apply the unit's 1/s (and Q4_K's d, dmin)
     const float* inv = reinterpret_cast<const float*>(xim + C::INV_OFF);
 #pragma unroll
     for (int r = 0; r < RT; ++r) {
-      float dA = 0.f, mA = 0.f, dB = 0.f, mB = 0.f;
+      float2 dm[2], nm[2];  // Q4_K: d and -dmin of rows g (0) and g+8 (1), as pairs
       if constexpr (DT == SG_DTYPE_Q4_K) {
-        const uint32_t q0 = *reinterpret_cast<const uint32_t*>(slot + kDdOff + r0[r] * 4);
-        const uint32_t q1 = *reinterpret_cast<const uint32_t*>(slot + kDdOff + r1[r] * 4);
-        dA = h2f(q0 & 0xFFFFu);
-        mA = h2f(q0 >> 16);
-        dB = h2f(q1 & 0xFFFFu);
-        mB = h2f(q1 >> 16);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(slot + kDdOff + (q ? r1[r] : r0[r]) * 4);
+          dm[q] = h2f_pair(w, 0);
+          const float2 mn = h2f_pair(w, 1);
+          nm[q] = make_float2(-mn.x, -mn.y);
+        }
       }
       if constexpr (C::P) {
-        const float2 iv = *reinterpret_cast<const float2*>(inv + 2 * t);
+        const float2 iv = *reinterpret_cast<const float2*>(inv + 2 * t);  // columns 2t, 2t+1
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float ivc = (i & 1) ? iv.y : iv.x;
+        for (int q = 0; q < 2; ++q) {
           if constexpr (DT == SG_DTYPE_Q4_0) {
-            acc[r][i] = fmaf(ivc, accu[r][i], acc[r][i]);
-            accu[r][i] = 0.f;
+            acc[r][q] = __ffma2_rn(iv, accu[r][q], acc[r][q]);
+            accu[r][q] = make_float2(0.f, 0.f);
           } else {
-            const float dr = i < 2 ? dA : dB, mr = i < 2 ? mA : mB;
-            acc[r][i] = fmaf(ivc, fmaf(dr, (float)iacc[r][i], -(mr * (float)iacm[r][i])), acc[r][i]);
-            iacc[r][i] = iacm[r][i] = 0;
+            const float2 ia = make_float2((float)iacc[r][2 * q], (float)iacc[r][2 * q + 1]);
+            const float2 im = make_float2((float)iacm[r][2 * q], (float)iacm[r][2 * q + 1]);
+            acc[r][q] = __ffma2_rn(iv, __ffma2_rn(dm[q], ia, __fmul2_rn(nm[q], im)), acc[r][q]);
+            iacc[r][2 * q] = iacc[r][2 * q + 1] = iacm[r][2 * q] = iacm[r][2 * q + 1] = 0;
           }
         }
       } else {
 #pragma unroll
         for (int tg = 0; tg < NTG; ++tg) {
-          const float2 iv = *reinterpret_cast<const float2*>(inv + 8 * tg + 2 * t);
+          const float2 iv = *reinterpret_cast<const float2*>(inv + 8 * tg + 2 * t);  // tokens 2t, 2t+1 of the group
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float ivc = (q & 1) ? iv.y : iv.x;
-            const int i = 4 * tg + q;
+          for (int q = 0; q < 2; ++q) {
+            const int i = 2 * tg + q;
             if constexpr (DT == SG_DTYPE_Q4_0) {
-              acc[r][i] = fmaf(ivc, accu[r][i], acc[r][i]);
+              acc[r][i] = __ffma2_rn(iv, accu[r][i], acc[r][i]);
             } else {
-              const float dr = q < 2 ? dA : dB, mr = q < 2 ? mA : mB;
-              acc[r][i] = fmaf(ivc, fmaf(dr, accu[r][i], -(mr * accm[r][i])), acc[r][i]);
-              accm[r][i] = 0.f;
+              acc[r][i] = __ffma2_rn(iv, __ffma2_rn(dm[q], accu[r][i], __fmul2_rn(nm[q], accm[r][i])), acc[r][i]);
+              accm[r][i] = make_float2(0.f, 0.f);
             }
-            accu[r][i] = 0.f;
+            accu[r][i] = make_float2(0.f, 0.f);
           }
         }
       }
@@ -610,13 +657,13 @@ __global__ void __launch_bounds__(C::THREADS, C::CPS) __maxnreg__(C::MAXREG) gem
     for (int r = 0; r < RT; ++r) {
       Seg<NTG> sv;
       if constexpr (C::P) {
-        // column c = 3*token + digit; lane t holds columns 2t (acc 0, 2) and 2t+1 (acc 1, 3)
+        // column c = 3*token + digit; lane t holds columns 2t (.x) and 2t+1 (.y)
         const int ca = 2 * t, cb = 2 * t + 1;
         float pv[4];
-        pv[0] = (ca / 3 == 0 ? acc[r][0] : 0.f) + (cb / 3 == 0 ? acc[r][1] : 0.f);  // row g, token 0
-        pv[1] = (ca / 3 == 1 ? acc[r][0] : 0.f) + (cb / 3 == 1 ? acc[r][1] : 0.f);  // row g, token 1
-        pv[2] = (ca / 3 == 0 ? acc[r][2] : 0.f) + (cb / 3 == 0 ? acc[r][3] : 0.f);  // row g+8, token 0
-        pv[3] = (ca / 3 == 1 ? acc[r][2] : 0.f) + (cb / 3 == 1 ? acc[r][3] : 0.f);  // row g+8, token 1
+        pv[0] = (ca / 3 == 0 ? acc[r][0].x : 0.f) + (cb / 3 == 0 ? acc[r][0].y : 0.f);  // row g, token 0
+        pv[1] = (ca / 3 == 1 ? acc[r][0].x : 0.f) + (cb / 3 == 1 ? acc[r][0].y : 0.f);  // row g, token 1
+        pv[2] = (ca / 3 == 0 ? acc[r][1].x : 0.f) + (cb / 3 == 0 ? acc[r][1].y : 0.f);  // row g+8, token 0
+        pv[3] = (ca / 3 == 1 ? acc[r][1].x : 0.f) + (cb / 3 == 1 ? acc[r][1].y : 0.f);  // row g+8, token 1
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           pv[i] += __shfl_xor_sync(0xffffffffu, pv[i], 1);
@@ -625,10 +672,13 @@ __global__ void __launch_bounds__(C::THREADS, C::CPS) __maxnreg__(C::MAXREG) gem
         sv.v[0] = t == 0 ? pv[0] : t == 1 ? pv[1] : t == 2 ? pv[2] : pv[3];
       } else {
 #pragma unroll
-        for (int i = 0; i < Seg<NTG>::NV; ++i) sv.v[i] = acc[r][i];
+        for (int i = 0; i < NP; ++i) {
+          sv.v[2 * i] = acc[r][i].x;
+          sv.v[2 * i + 1] = acc[r][i].y;
+        }
       }
 #pragma unroll
-      for (int i = 0; i < NA; ++i) acc[r][i] = 0.f;
+      for (int i = 0; i < NP; ++i) acc[r][i] = make_float2(0.f, 0.f);
       const int tile_row0 = r0[r] - g;  // first row of the 16-row tile
       // a row-block run by this CTA alone is stored; one shared with other
       // CTAs (zeroed by the prep kernel unless the call accumulates) is added to
