@@ -21,19 +21,22 @@
 //
 // Two column plans:
 //   batch 1-2 (per-column): column 3*token + digit, one MMA per block. The
-//     accumulator starts at the bits of 1.5*2^23 (Q4_0: minus 8*sum of the
-//     column's digits, which turns q into q-8), so the s32 result read as an
-//     f32 is 1.5*2^23 + D exactly and one subtraction gives D; per column
-//     acc += d_row * D; each column is scaled by 2^(-7*digit)/s per unit and
-//     the digit columns of a token are summed at the end of a row segment.
+//     accumulators start at the bits of 1.5*2^23 (Q4_0; Q4_K at 0), so the
+//     s32 result read as an f32 is 1.5*2^23 + sum q*digit exactly; adding
+//     the column's -1.5*2^23 - 8*sum(digits) (from the activation image)
+//     gives sum (q-8)*digit exactly; per column acc += d_row * D; each
+//     column is scaled by 2^(-7*digit)/s per unit and the digit columns of a
+//     token are summed at the end of a row segment.
 //   batch 3-32 (combined): 8 tokens per MMA, one MMA per digit, every
-//     accumulator starting at the bits of 1.5*2^23 (Q4_0: minus 8*sum of the
-//     column's digit) as above; per (row, token) the three digit sums D_i
-//     come out exactly by one subtraction each, (D0*128 + D1)*128 + D2 is
-//     formed by two FMAs (exact up to the last, which rounds once to f32)
-//     and one FMA applies the block scale. Pairs of values (rows g, g+8 of a
-//     column) go through the packed f32x2 instructions, and no integer to
-//     float conversion is needed.
+//     accumulator starting at the bits of 1.5*2^23. Per (row, token) one
+//     subtraction per digit gives D_i exactly (Q4_0's digit 2 takes the
+//     token's -1.5*2^23 - 8*sum V instead, rounded once), two FMAs form
+//     (D0*128 + D1)*128 + D2 (exact up to the last, which rounds once to
+//     f32) and one FMA applies the block scale.
+// Pairs of values (the two columns of a row that an MMA leaves in adjacent
+// registers) go through the packed f32x2 add/FMA; the loop has no
+// integer-to-float conversion and the MMAs' accumulator input is one
+// loop-invariant register quad.
 // Q4_K keeps the min term apart: per (row, block) m * (sum of the block's x).
 //
 // Weight layout: the repacked tiles of sg_layout.cuh, unchanged. A warp takes
@@ -81,7 +84,7 @@ struct Cfg {
   static constexpr bool P = NTG == 0;
   static constexpr int NTOK = P ? 2 : 8 * NTG;     // token slots
   static constexpr int NM = P ? 1 : 3 * NTG;       // MMAs per (16 rows, 32-block)
-  static constexpr int NCA = P ? 1 : 3 * NTG;      // accumulator-start areas per block
+  static constexpr int NCA = P ? 1 : NTG;          // per-column value areas per block
   static constexpr int PB = NM * 256 + NCA * 32;   // image bytes per 32-block
   static constexpr int INV_OFF = 8 * PB;           // per-unit scales after the 8 blocks
   static constexpr int XU = 8 * PB + 128;          // image bytes per unit
@@ -183,6 +186,14 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
 }
 
+// the same, every accumulator starting at c (a loop-invariant register quad)
+__device__ __forceinline__ void mma_u8s8_c(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1, uint32_t c) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
+}
+
 __device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
 // f16 half h (0: low, 1: high) of a scale word, as the pair (v, v)
 __device__ __forceinline__ float2 h2f_pair(uint32_t w, int h) {
@@ -205,13 +216,13 @@ __device__ __forceinline__ float2 res_pair(const int (&c)[4], int q) {
 //   block bu (0..7) at bu*PB:
 //     [NM][lane 32][2 words]  B fragments: MMA m, lane (g, t) = the digits of
 //                             column g at K offsets 8t+{0,4,1,5} | 8t+{2,6,3,7}
-//     [NCA][t 4][2 words]     per-column accumulator starts (lane t holds
-//                             columns 2t, 2t+1):
-//        per-column plan  Q4_0: bits 1.5*2^23 - 8*sum(digits); Q4_K: sum(digits)
-//        combined plan    area 3*tg + i, column c = token 8*tg + c:
-//                         Q4_0: bits 1.5*2^23 - 8*sum(digit i);
-//                         Q4_K: area 3*tg only, sum(V) as f32 (the min
-//                         term); the digit MMAs start at 1.5*2^23
+//     [NCA][t 4][2 words]     a value per column (lane t holds columns 2t, 2t+1):
+//        per-column plan  Q4_0: f32 -1.5*2^23 - 8*sum(digits), added to the
+//                         MMA result (which started at 1.5*2^23) to give
+//                         sum (q-8)*digit; Q4_K: sum(digits) (the min term)
+//        combined plan    area tg, column c = token 8*tg + c:
+//                         Q4_0: f32 -1.5*2^23 - 8*sum(V), added to the
+//                         digit-2 result; Q4_K: sum(V) as f32 (the min term)
 //   INV_OFF: per-column plan: f32 [col 8] = 2^(-7*digit)/s of the column's
 //            token; combined plan: f32 [token 32] = 2^-14/s. NaN when the
 //            unit's x holds inf or NaN.
@@ -315,9 +326,9 @@ __device__ __forceinline__ void store_unit(uint8_t* unit, const UnitX& u, int to
     for (int i = 0; i < 3; ++i) {
       const int col = 3 * tok + i;
       *reinterpret_cast<uint2*>(blk + (4 * col + t) * 8) = make_uint2(u.dig[i][0], u.dig[i][1]);
-      if (t == 0)
+      if (t == 0)  // Q4_0: exact (|8 * sum| <= 2^14)
         reinterpret_cast<uint32_t*>(blk + 256)[col] =
-            DT == SG_DTYPE_Q4_0 ? kMagic - 8u * (uint32_t)u.dsum[i] : (uint32_t)u.dsum[i];
+            DT == SG_DTYPE_Q4_0 ? __float_as_uint(-kMagicF - (float)(8 * u.dsum[i])) : (uint32_t)u.dsum[i];
       if (lane == 0) inv[col] = inv_scale(u, i == 0 ? 1.f : i == 1 ? 0.0078125f : 6.103515625e-05f);
     }
   } else {
@@ -325,14 +336,10 @@ __device__ __forceinline__ void store_unit(uint8_t* unit, const UnitX& u, int to
 #pragma unroll
     for (int i = 0; i < 3; ++i)
       *reinterpret_cast<uint2*>(blk + ((3 * tg + i) * 32 + 4 * cc + t) * 8) = make_uint2(u.dig[i][0], u.dig[i][1]);
-    if (t == 0) {
-      uint32_t* ca = reinterpret_cast<uint32_t*>(blk + C::NM * 256 + 3 * tg * 32);
-      if constexpr (DT == SG_DTYPE_Q4_0) {
-#pragma unroll
-        for (int i = 0; i < 3; ++i) ca[8 * i + cc] = kMagic - 8u * (uint32_t)u.dsum[i];
-      } else {
-        ca[cc] = __float_as_uint((float)u.vsum);
-      }
+    if (t == 0) {  // Q4_0: rounded once (|8 * sum V| <= 2^28)
+      uint32_t* ca = reinterpret_cast<uint32_t*>(blk + C::NM * 256 + tg * 32);
+      ca[cc] = DT == SG_DTYPE_Q4_0 ? __float_as_uint((float)(-12582912.0 - 8.0 * (double)u.vsum))
+                                   : __float_as_uint((float)u.vsum);
     }
     if (lane == 0) inv[tok] = inv_scale(u, 6.103515625e-05f);
   }
@@ -368,7 +375,7 @@ __global__ void __launch_bounds__(128) xprep_kernel(XParams p) {
       const int bu = i >> 3, col = 6 + ((i >> 2) & 1), t = i & 3;
       uint8_t* blk = p.ximg + (size_t)u * C::XU + bu * C::PB;
       *reinterpret_cast<uint2*>(blk + (4 * col + t) * 8) = make_uint2(0u, 0u);
-      if (t == 0) reinterpret_cast<uint32_t*>(blk + 256)[col] = DT == SG_DTYPE_Q4_0 ? kMagic : 0u;
+      if (t == 0) reinterpret_cast<uint32_t*>(blk + 256)[col] = DT == SG_DTYPE_Q4_0 ? __float_as_uint(-kMagicF) : 0u;
       if (bu == 0 && t == 0) reinterpret_cast<float*>(p.ximg + (size_t)u * C::XU + C::INV_OFF)[col] = 0.f;
     }
 }
@@ -521,11 +528,12 @@ __global__ void __launch_bounds__(C::THREADS, C::CPS) __maxnreg__(C::MAXREG) gem
 #pragma unroll
           for (int r = 0; r < RT; ++r) {
             int d[4];
-            mma_u8s8(d, a[r][0], a[r][1], a[r][2], a[r][3], b.x, b.y, DT == SG_DTYPE_Q4_0 ? ci.x : 0u,
-                     DT == SG_DTYPE_Q4_0 ? ci.y : 0u);
+            mma_u8s8_c(d, a[r][0], a[r][1], a[r][2], a[r][3], b.x, b.y, DT == SG_DTYPE_Q4_0 ? kMagic : 0u);
             if constexpr (DT == SG_DTYPE_Q4_0) {
-              accu[r][0] = __ffma2_rn(h2f_pair(sw0[r], h), __fadd2_rn(res_pair(d, 0), neg_magic), accu[r][0]);
-              accu[r][1] = __ffma2_rn(h2f_pair(sw1[r], h), __fadd2_rn(res_pair(d, 1), neg_magic), accu[r][1]);
+              // result + (-1.5*2^23 - 8*sum digits) = sum (q-8)*digit, exact
+              const float2 corr = make_float2(__uint_as_float(ci.x), __uint_as_float(ci.y));
+              accu[r][0] = __ffma2_rn(h2f_pair(sw0[r], h), __fadd2_rn(res_pair(d, 0), corr), accu[r][0]);
+              accu[r][1] = __ffma2_rn(h2f_pair(sw1[r], h), __fadd2_rn(res_pair(d, 1), corr), accu[r][1]);
             } else {
               const int sc0 = (sw0[r] >> (8 * h)) & 0xFF, sc1 = (sw1[r] >> (8 * h)) & 0xFF;
               const int m0 = (sw0[r] >> (16 + 8 * h)) & 0xFF, m1 = (sw1[r] >> (16 + 8 * h)) & 0xFF;
@@ -555,31 +563,28 @@ __global__ void __launch_bounds__(C::THREADS, C::CPS) __maxnreg__(C::MAXREG) gem
           }
 #pragma unroll
           for (int tg = 0; tg < NTG; ++tg) {
-            const uint8_t* cab = xb + C::NM * 256 + 3 * tg * 32 + t * 8;
-            uint2 b[3], st[3];
+            uint2 b[3];
 #pragma unroll
-            for (int i = 0; i < 3; ++i) {
-              b[i] = *reinterpret_cast<const uint2*>(xb + (3 * tg + i) * 256 + lane * 8);
-              st[i] = DT == SG_DTYPE_Q4_0 ? *reinterpret_cast<const uint2*>(cab + i * 32) : make_uint2(kMagic, kMagic);
-            }
-            float2 vs;  // Q4_K: the block's sums of V of tokens 2t, 2t+1
-            if constexpr (DT == SG_DTYPE_Q4_K) vs = *reinterpret_cast<const float2*>(cab);
+            for (int i = 0; i < 3; ++i) b[i] = *reinterpret_cast<const uint2*>(xb + (3 * tg + i) * 256 + lane * 8);
+            // tokens 2t, 2t+1: Q4_0 -1.5*2^23 - 8*sum V (the digit-2 offset); Q4_K sum V
+            const float2 cv = *reinterpret_cast<const float2*>(xb + C::NM * 256 + tg * 32 + t * 8);
 #pragma unroll
             for (int r = 0; r < RT; ++r) {
               int dd[3][4];
 #pragma unroll
               for (int i = 0; i < 3; ++i)
-                mma_u8s8(dd[i], a[r][0], a[r][1], a[r][2], a[r][3], b[i].x, b[i].y, st[i].x, st[i].y);
+                mma_u8s8_c(dd[i], a[r][0], a[r][1], a[r][2], a[r][3], b[i].x, b[i].y, kMagic);
 #pragma unroll
               for (int q = 0; q < 2; ++q) {
-                // digit sums D_i = result - 1.5*2^23 (exact); (D0*128 + D1) is exact,
-                // *128 + D2 rounds once to f32 (the value sum_k q_k V_k of the pair)
-                float2 e[3];
-#pragma unroll
-                for (int i = 0; i < 3; ++i) e[i] = __fadd2_rn(res_pair(dd[i], q), neg_magic);
-                const float2 val = __ffma2_rn(__ffma2_rn(e[0], f128, e[1]), f128, e[2]);
+                // digit sums D_i = result - 1.5*2^23 (exact; Q4_0's digit 2 also
+                // takes -8*sum V, rounded once); (D0*128 + D1) is exact, *128 + D2
+                // rounds once: the pair's sum_k q_k V_k (Q4_0: (q_k - 8) V_k)
+                const float2 e0 = __fadd2_rn(res_pair(dd[0], q), neg_magic);
+                const float2 e1 = __fadd2_rn(res_pair(dd[1], q), neg_magic);
+                const float2 e2 = __fadd2_rn(res_pair(dd[2], q), DT == SG_DTYPE_Q4_0 ? cv : neg_magic);
+                const float2 val = __ffma2_rn(__ffma2_rn(e0, f128, e1), f128, e2);
                 accu[r][2 * tg + q] = __ffma2_rn(fs[r][q], val, accu[r][2 * tg + q]);
-                if constexpr (DT == SG_DTYPE_Q4_K) accm[r][2 * tg + q] = __ffma2_rn(ns[r][q], vs, accm[r][2 * tg + q]);
+                if constexpr (DT == SG_DTYPE_Q4_K) accm[r][2 * tg + q] = __ffma2_rn(ns[r][q], cv, accm[r][2 * tg + q]);
               }
             }
           }
