@@ -12,7 +12,7 @@ footprint exceeds 4x the 126 MB L2).
 metric: whole-job algorithmic GB/s (weights N*K*18/32 bytes + activations in
 + outputs out). With --gpus N (torchrun, one rank
 per GPU) the model has N such layers, each tensor-parallel over the N ranks
-(column split Q/K/V/gate/up, row split O/down + NCCL all-reduce), so per-GPU
+(column split Q/K/V/gate/up, row split O/down + all-reduce), so per-GPU
 bytes stay fixed (weak scaling).
 
 --impl reference times the reference's CPU path (the C restatement of
@@ -533,6 +533,7 @@ def gpu_arm(args):
             "config": {"workload": "configs[1]: Llama-2-7B layer Q4_0 linears (4x 4096->4096, 2x 4096->11008, "
                                    "11008->4096) at decode batch 1, 4, 16",
                        "layers_per_step": n_layers, "parallelism": f"tp{world}" if world > 1 else "none",
+                       "allreduce": gpu.allreduce_path() if world > 1 else None,
                        "execution": "eager" if args.eager else "CUDA graph per step (PDL edges kept)",
                        "l2_policy": f"inputs larger than L2: {copies} rotating layer copies "
                                     f"({copies * layer_b / world / 1e6:.0f} MB per GPU vs L2 {l2 / 1e6:.0f} MB)",
@@ -670,7 +671,8 @@ def tp_model_bench(torch, gpu, args, dist, world):
         "decode_roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                             "frac": round(gbs / peak, 4), "per": "GPU", "bytes_per_step_per_gpu": int(by),
                             "peak_kind": peak_kind},
-        "allreduce": "NCCL in-place all-reduce after each row-split linear (O, down): 2 per layer",
+        "allreduce": (("library peer kernel over NVLink (values with epochs, no fence)" if gpu.allreduce_path() == "peer"
+                       else "NCCL") + " in-place all-reduce after each row-split linear (O, down): 2 per layer"),
         "tokens_seq0": [t for t in toks[:1]],
     }
     D.free()
@@ -937,6 +939,51 @@ def profile_arm(args):
     return 0
 
 
+def ar_latency_arm(args):
+    """Latency of the row-split all-reduce (sg_allreduce_device) per call:
+    20 back-to-back calls captured in a CUDA graph, replayed 10 times, device
+    time, max over ranks; one JSON line from rank 0 (not a bench line)."""
+    torch, gpu, dist, rank, world, local = setup_gpu(args)
+    res = {}
+    st = torch.cuda.Stream()
+    for n in (4096, 16384, 65536, 262144):
+        buf = torch.ones(n, device="cuda")
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                gpu.allreduce_device(buf.data_ptr(), n, stream=st.cuda_stream)
+            st.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                for _ in range(20):
+                    gpu.allreduce_device(buf.data_ptr(), n, stream=st.cuda_stream)
+            g.replay()
+            st.synchronize()
+            if dist:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(10):
+                g.replay()
+            e1.record(st)
+            st.synchronize()
+        us = torch.tensor([e0.elapsed_time(e1) * 1e3 / 200], device="cuda")
+        if dist:
+            dist.all_reduce(us, op=dist.ReduceOp.MAX)
+        res[f"{n * 4 // 1024}KB"] = round(float(us), 2)
+        del g
+    path = gpu.allreduce_path() if world > 1 else "none"
+    gpu.synchronize()
+    if dist:
+        dist.barrier()
+    gpu.shutdown()
+    if rank == 0:
+        print(json.dumps({"allreduce_latency_us": res, "n_gpus": world, "path": path,
+                          "method": "20 calls per CUDA graph, 10 replays, device time, max over ranks"}), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -949,6 +996,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--profile", default=None, help="K,N,B: single-shape eager launches (for ncu)")
     ap.add_argument("--dtype", default="q4_0", choices=["q4_0", "q4k"])
+    ap.add_argument("--ar-latency", action="store_true", help="all-reduce latency per call (under torchrun)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] prefill measurement")
     ap.add_argument("--prefill-reps", type=int, default=20)
     ap.add_argument("--no-model", action="store_true", help="skip the configs[3] model decode measurement")
@@ -962,6 +1010,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return reference_arm(args)
+    if args.ar_latency:
+        return ar_latency_arm(args)
     if args.profile:
         return profile_arm(args)
     return gpu_arm(args)

@@ -183,15 +183,15 @@ SG_API int sg_fused_gemv_q4k(const uint8_t *w_raw, const float *x, float *out, i
 
 /* Sum all-reduce of `count` floats in place across the ranks of a
  * one-process-per-GPU job (every rank calls it with the same count; the
- * row-split linears use it for their outputs). Up to 1 Mi floats it runs the
- * library's peer kernel: each rank stores its partial straight into every
- * peer's receive buffer over NVLink (CUDA IPC mappings made at
- * sg_init_rank), raises a flag there, waits (bounded) for the peers' flags
- * and sums in rank order, so every rank gets the same bits. Larger vectors,
- * or jobs where any rank could not map its peers, use ncclAllReduce.
- * Stream-ordered and graph-capturable. The peer kernel is enabled by
- * SG_PEER_ALLREDUCE=1 in the environment at sg_init_rank; otherwise every
- * call uses NCCL.
+ * row-split linears use it for their outputs). Up to 512 Ki floats it runs
+ * the library's peer kernel: each rank stores its partial straight into
+ * every peer's receive buffer over NVLink (CUDA IPC mappings made at
+ * sg_init_rank), every value beside the call's epoch in one 8-byte word,
+ * reads the peers' values from its own buffer as their epochs arrive
+ * (bounded waits) and sums in rank order, so every rank gets the same bits.
+ * Larger vectors, or jobs where any rank could not map its peers, use
+ * ncclAllReduce. Stream-ordered and graph-capturable. SG_PEER_ALLREDUCE=0
+ * in the environment at sg_init_rank makes every call use NCCL.
  * sg_allreduce_path reports which one this job uses (1: peer kernel). */
 SG_API int sg_allreduce_device(float *buf, int64_t count, void *stream);
 SG_API int sg_allreduce_path(int *peer);

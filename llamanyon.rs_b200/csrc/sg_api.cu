@@ -98,7 +98,7 @@ struct DevState {
   uint8_t* upbuf[2] = {nullptr, nullptr};  // pinned double buffer of weight uploads
   cudaEvent_t upev[2] = {nullptr, nullptr};
   // peer all-reduce (one process per GPU, sg_peer.cuh): this rank's receive
-  // buffer and flags (one allocation, exported by CUDA IPC), the mappings of
+  // buffer (values with their epochs, exported by CUDA IPC), the mappings of
   // every rank's, and the per-chunk epoch counters
   bool peer_on = false;
   void* peer_base = nullptr;
@@ -416,13 +416,13 @@ int peer_setup(DevState& d) {
   const int W = g_ctx.world, R = g_ctx.rank_base;
   int ok = W <= SG_PEER_MAX;
   const char* env = std::getenv("SG_PEER_ALLREDUCE");
-  if (!env || env[0] != '1') ok = 0;  // opt-in until validated on a multi-GPU box
-  const size_t buf_bytes = (size_t)2 * W * kPeerCap * sizeof(float);
-  const size_t flag_bytes = (size_t)2 * W * kArMaxChunks * sizeof(uint32_t);
+  if (env && env[0] == '0') ok = 0;  // SG_PEER_ALLREDUCE=0: NCCL for every all-reduce
+  // [2 parities][W ranks][kPeerCap / 2] words of {v0, epoch, v1, epoch}
+  const size_t buf_bytes = (size_t)2 * W * (kPeerCap / 2) * sizeof(uint4);
   cudaIpcMemHandle_t mine = {};
-  if (ok && (cudaMalloc(&d.peer_base, buf_bytes + flag_bytes) != cudaSuccess ||
+  if (ok && (cudaMalloc(&d.peer_base, buf_bytes) != cudaSuccess ||
              cudaMalloc((void**)&d.peer_ctr, kArMaxChunks * sizeof(uint32_t)) != cudaSuccess ||
-             cudaMemset(d.peer_base, 0, buf_bytes + flag_bytes) != cudaSuccess ||
+             cudaMemset(d.peer_base, 0, buf_bytes) != cudaSuccess ||
              cudaMemset(d.peer_ctr, 0, kArMaxChunks * sizeof(uint32_t)) != cudaSuccess ||
              cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&mine, d.peer_base) != cudaSuccess)) {
     cudaGetLastError();
@@ -442,15 +442,14 @@ int peer_setup(DevState& d) {
   CUDA_TRY(cudaMemcpy(all.data(), dev, (size_t)W * sizeof mine, cudaMemcpyDeviceToHost));
   for (int p = 0; p < W && ok; ++p) {
     if (p == R) {
-      d.peer.buf[p] = static_cast<float*>(d.peer_base);
+      d.peer.buf[p] = static_cast<uint4*>(d.peer_base);
     } else if (cudaIpcOpenMemHandle(&d.peer_mapped[p], all[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
       cudaGetLastError();
       ok = 0;
       break;
     } else {
-      d.peer.buf[p] = static_cast<float*>(d.peer_mapped[p]);
+      d.peer.buf[p] = static_cast<uint4*>(d.peer_mapped[p]);
     }
-    d.peer.flags[p] = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(d.peer.buf[p]) + buf_bytes);
   }
   // every rank must take the same path
   int* dok = reinterpret_cast<int*>(dev);

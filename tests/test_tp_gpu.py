@@ -1,4 +1,4 @@
-"""Tensor parallelism on the default NCCL path, on 2 GPUs.
+"""Tensor parallelism on 2 GPUs.
 
 One process per GPU (sg_init_rank, as bench.py under torchrun uses it):
 column-split (Q/K/V/gate/up style) and row-split (O/down style) linears at
@@ -11,9 +11,11 @@ loop, and one configs[4]-width layer (d 8192, FFN 28672, Q4_0).
 One process driving both GPUs (sg_init(2), ncclCommInitAll), as the
 single-process Rust engine would: column and row split through sg_linear.
 
-Skipped below 2 GPUs (ranks whose collectives wait for one another must each
-have their own GPU). No peer all-reduce here: SG_PEER_ALLREDUCE is unset, so
-every row-split call uses ncclAllReduce.
+The one-process-per-GPU linears run on both all-reduce paths: the default
+peer kernel over NVLink (sg_peer.cuh) and ncclAllReduce (SG_PEER_ALLREDUCE=0);
+the decoder and the configs[4]-width layer on the default. sg_init(2) always
+uses NCCL. Skipped below 2 GPUs (ranks whose collectives wait for one another
+must each have their own GPU).
 """
 import json
 import os
@@ -45,12 +47,15 @@ def _paths():
             sys.path.insert(0, p)
 
 
-def _rank(rank, world, port, outdir, part):
+def _rank(rank, world, port, outdir, part, path="peer"):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
     _paths()
-    os.environ.pop("SG_PEER_ALLREDUCE", None)
+    if path == "nccl":
+        os.environ["SG_PEER_ALLREDUCE"] = "0"
+    else:
+        os.environ.pop("SG_PEER_ALLREDUCE", None)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import swamp_gpu as sg
     import oracle
@@ -180,21 +185,22 @@ def _decoder(g, sg, oracle, torch, dist, rank, world, out, part):
             out["checks"].append([f"decoder dt{dtype} d{cfg.d} tp{world}", worst])
 
 
-def _spawn(tmp_path, part):
+def _spawn(tmp_path, part, path="peer"):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs (one per rank)")
     import torch.multiprocessing as mp
-    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), part), nprocs=2, join=True,
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), part, path), nprocs=2, join=True,
                        start_method="spawn")
     return [json.load(open(tmp_path / f"out{r}.json")) for r in range(2)]
 
 
 @pytest.mark.gpu
-def test_tp_linears_nccl_two_ranks(tmp_path):
-    outs = _spawn(tmp_path, "linears")
+@pytest.mark.parametrize("path", ["peer", "nccl"])
+def test_tp_linears_two_ranks(tmp_path, path):
+    outs = _spawn(tmp_path, "linears", path)
     for o in outs:
-        assert o["path"] == "nccl"
+        assert o["path"] == path
         names = [c[0] for c in o["checks"]]
         assert len(names) == 2 * 3 * 5
         assert max(c[1] for c in o["checks"]) <= 1e-3
