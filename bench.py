@@ -128,7 +128,7 @@ def measured_peaks():
 # capture of the current kernels (profiles/): decode GEMV 4096->11008 batch 1
 # (algorithmic 25,406,976 B); prefill GEMM Q4_K 4096->14336 M=512
 # (algorithmic weight + activation bytes 41,418,752 B).
-NCU_TRAFFIC = {"gemv_4096x11008_b1": 25_465_088, "gemm_q4k_4096x14336_m512": 54_764_032}
+NCU_TRAFFIC = {"gemv_4096x11008_b1": 25_466_624, "gemm_q4k_4096x14336_m512": 54_764_032}
 
 
 def measured_tensor_peak():
