@@ -115,7 +115,8 @@ __global__ void __launch_bounds__(256) gemm_xprep_kernel(const float* __restrict
     *reinterpret_cast<uint4*>(xl + t * K + k) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
   // zero the tiles that a stream-K boundary cuts (reduced with red.add):
-  // one warp per (boundary, 32-token slice of the tile)
+  // one warp per (boundary, 32-token slice of the tile); a tile that several
+  // boundaries cut is zeroed by the first of them only
   if (!p.accumulate && p.rem_iters > 0) {
     const int lane = threadIdx.x & 31;
     const int64_t nwarp = stride >> 5;
@@ -124,6 +125,10 @@ __global__ void __launch_bounds__(256) gemm_xprep_kernel(const float* __restrict
       const int cb = 1 + (int)(i / (BN / 32)), ts = (int)(i % (BN / 32));
       const int64_t it = (int64_t)cb * p.rem_iters / G;
       if (it % p.n_ch == 0) continue;
+      if (cb > 1) {
+        const int64_t prev = (int64_t)(cb - 1) * p.rem_iters / G;
+        if (prev % p.n_ch != 0 && prev / p.n_ch == it / p.n_ch) continue;  // an earlier boundary cuts this tile
+      }
       const int tile = p.dp * G + (int)(it / p.n_ch);
       const int rb = tile / p.n_tt, tt = tile % p.n_tt;
       const int nr = min(BM, p.n_rows - rb * BM);
