@@ -157,11 +157,11 @@ SG_API int sg_linear_multi_device(const sg_weight_t *ws, int n_weights, const fl
  * streams. Same arguments and results as sg_linear_device for one tensor at
  * decode batch 1..16 (larger batches are rejected with SG_ERR_UNSUPPORTED:
  * they run the prefill GEMM, whose activation scratch is allocated on first
- * use). The decode kernel's workspace (cross-CTA flags and, from 3 tokens
- * on, the converted activation operands) is a fixed per-device array inside
- * the library, so the call allocates nothing: any n_cols at batch 1..2,
- * n_cols up to 32768 at batch 16 (more at fewer tokens; wider tensors are
- * rejected with SG_ERR_UNSUPPORTED and a message naming the limit). The first call on a
+ * use). The decode kernel's workspace (the call's activations converted to
+ * the MMA operand layout) is a fixed 1.65 MB per-device array inside the
+ * library, so the call allocates nothing: n_cols up to 174080 at batch 1..2,
+ * 64768 at 3..8 and 32768 at 9..16 (wider tensors are rejected with
+ * SG_ERR_UNSUPPORTED and a message naming the limit). The first call on a
  * device looks up that workspace's address once; make it before any stream
  * capture begins. All decode calls on a device share the workspace: calls
  * whose work may overlap in time (different streams with no ordering between

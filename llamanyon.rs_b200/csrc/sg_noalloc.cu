@@ -1,14 +1,14 @@
 // sg_noalloc.cu -- sg_linear_device_noalloc: the decode GEMV (batch 1..16,
 // device pointers) for callers that must never trigger a device allocation.
 //
-// The decode GEMV's workspace (hand-over flags, partial-sum slots and the
-// activation images) is the library's fixed per-device array (g_gemv_ws in
-// sg_api.cu), sized for n_cols <= kStaticWsCols at 16 tokens, so a call only
-// launches kernels (plus the all-reduce of a row-split tensor). Its address
-// is looked up once per device on the first call that uses the device. The
-// workspace is shared by all decode calls on a device, so two calls whose
-// kernels overlap in time (different streams, no ordering between them) race
-// on it.
+// The decode GEMV's workspace (the call's activations converted to the MMA
+// operand layout, rewritten by every call) is the library's fixed per-device
+// array (g_gemv_ws in sg_api.cu), sized for n_cols <= kStaticWsCols at 16
+// tokens (more at fewer tokens), so a call only launches kernels (plus the
+// all-reduce of a row-split tensor). Its address is looked up once per device
+// on the first call that uses the device. The workspace is shared by all
+// decode calls on a device, so two calls whose kernels overlap in time
+// (different streams, no ordering between them) race on it.
 constexpr int kNoallocMaxBatch = 16;
 
 int sg_linear_device_noalloc(sg_weight_t w, const float* x, int64_t ldx, float* y, int64_t ldy, int batch,
@@ -22,9 +22,11 @@ int sg_linear_device_noalloc(sg_weight_t w, const float* x, int64_t ldx, float* 
     return fail(SG_ERR_UNSUPPORTED, "sg_linear_device_noalloc: batch %d outside the range 1..%d of the fixed workspace",
                 batch, kNoallocMaxBatch);
   const SgDevWeight* sw = &w->shards[0].w;
-  if (sw->dtype != SG_DTYPE_Q6_K && sg_gemv_scratch_bytes(sw->n_cols, batch) > kStaticWsBytes)
+  if (sw->dtype != SG_DTYPE_Q6_K && sg_gemv_scratch_bytes(sw->n_cols, batch) > kStaticWsBytes) {
+    const long long limit = (long long)(kStaticWsBytes / sg_gemv_scratch_bytes(256, batch)) * 256;
     return fail(SG_ERR_UNSUPPORTED, "sg_linear_device_noalloc: n_cols %lld above %lld at batch %d (the fixed workspace)",
-                (long long)sw->n_cols, (long long)kStaticWsCols, batch);
+                (long long)sw->n_cols, limit, batch);
+  }
   const bool acc = (flags & SG_FLAG_ACCUMULATE) != 0;
   const bool row_split = w->tp_mode == SG_TP_ROW && g_ctx.world > 1;
   const int64_t need = w->tp_mode == SG_TP_ROW ? w->n_rows : sw->n_rows;
