@@ -457,9 +457,48 @@ int peer_setup(DevState& d) {
   r = g_nccl.AllReduce(dok, dok, 1, kNcclInt32, kNcclMin, d.comm, d.stream);
   CUDA_TRY(cudaStreamSynchronize(d.stream));
   CUDA_TRY(cudaMemcpy(&ok, dok, sizeof ok, cudaMemcpyDeviceToHost));
-  cudaFree(dev);
-  if (r) return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
+  if (r) {
+    cudaFree(dev);
+    return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
+  }
   d.peer_on = ok != 0;
+  if (d.peer_on) {
+    // self-test: one all-reduce of small integers through the peer kernel,
+    // which must come out exact on every rank; any rank that sees a wrong sum
+    // or a wait that gave up sends the whole job to NCCL
+    const int64_t n = 2 * kArChunk + 3;
+    std::vector<float> h(n, (float)(R + 1));
+    float* t = nullptr;
+    int pass = cudaMalloc(&t, n * sizeof(float)) == cudaSuccess &&
+               cudaMemcpy(t, h.data(), n * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess;
+    if (pass) pass = allreduce_rank(d, t, (size_t)n, d.stream) == SG_OK &&
+                     cudaStreamSynchronize(d.stream) == cudaSuccess &&
+                     cudaMemcpy(h.data(), t, n * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess;
+    const float want = (float)W * (W + 1) / 2;
+    for (int64_t i = 0; pass && i < n; ++i) pass = h[i] == want;
+    int err = 0;
+    cudaMemcpyFromSymbol(&err, g_sg_error, sizeof(int));
+    if (err) {
+      pass = 0;
+      const int z = 0;
+      cudaMemcpyToSymbol(g_sg_error, &z, sizeof(int));
+    }
+    if (t) cudaFree(t);
+    cudaGetLastError();
+    CUDA_TRY(cudaMemcpy(dok, &pass, sizeof pass, cudaMemcpyHostToDevice));
+    r = g_nccl.AllReduce(dok, dok, 1, kNcclInt32, kNcclMin, d.comm, d.stream);
+    CUDA_TRY(cudaStreamSynchronize(d.stream));
+    CUDA_TRY(cudaMemcpy(&pass, dok, sizeof pass, cudaMemcpyDeviceToHost));
+    if (r) {
+      cudaFree(dev);
+      return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
+    }
+    if (!pass) {
+      std::fprintf(stderr, "swamp_gpu: the peer all-reduce self-test failed; using NCCL\n");
+      d.peer_on = false;
+    }
+  }
+  cudaFree(dev);
   return SG_OK;
 }
 
