@@ -350,6 +350,28 @@ SG_API int sg_attention_prefill_device(sg_kv_cache_t cache, int layer, const flo
 
 /* silu then mul_in_place (ops.rs:203-214): g = g / (1 + exp(-g)) * u. */
 SG_API int sg_silu_mul_device(float *g, int64_t ldg, const float *u, int64_t ldu, int n, int rows, void *stream);
+
+/* Fused forms of two engine sequences, for decode: the op runs on the way
+ * into the decode GEMV's activation operands, so its output rows are never
+ * written and one kernel per call is saved. Results are bit-identical to
+ * running the op then the linear (the same arithmetic, RMSNorm's summation
+ * order included). Batches above the decode range, and Q6_K tensors, run the
+ * two steps (the op's rows go to a library buffer allocated on first use).
+ * No reference counterparts: the engine calls rmsnorm then
+ * forward_linear_multi (executor.rs:436-445 / :493-499), and silu,
+ * mul_in_place then forward_linear (:499-505).
+ *
+ * sg_rmsnorm_linear_multi_device: ys[i] = W_i rmsnorm(x) with weight
+ * `norm_weight` [n_cols] and eps, otherwise as sg_linear_multi_device (x is
+ * not modified).
+ * sg_silu_mul_linear_device: y = W (silu(g) * u), otherwise as
+ * sg_linear_device (g and u [batch][n_cols] with strides ldg / ldu; neither
+ * is modified). */
+SG_API int sg_rmsnorm_linear_multi_device(const sg_weight_t *ws, int n_weights, const float *x, int64_t ldx,
+                                          const float *norm_weight, float eps, float *const *ys,
+                                          const int64_t *ldys, int batch, void *stream, int flags);
+SG_API int sg_silu_mul_linear_device(sg_weight_t w, const float *g, int64_t ldg, const float *u, int64_t ldu,
+                                     float *y, int64_t ldy, int batch, void *stream, int flags);
 /* add_in_place (ops.rs:216-220): x += y. (A linear's SG_FLAG_ACCUMULATE
  * adds its result into the residual stream in the same kernel.) */
 SG_API int sg_add_device(float *x, int64_t ldx, const float *y, int64_t ldy, int n, int rows, void *stream);

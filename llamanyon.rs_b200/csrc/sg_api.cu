@@ -95,6 +95,9 @@ struct DevState {
   int argmax_rows = 0;  // rows the argmax counters and flags cover
   float* hbuf = nullptr;  // pinned host staging
   size_t hbuf_bytes = 0;
+  int* err_host = nullptr;  // pinned copy of the device error word (host-pointer calls)
+  float* pbuf = nullptr;    // rows of a prologue (RMSNorm / SiLU-mul) run ahead of a GEMM or Q6_K call
+  size_t pbuf_bytes = 0;
   uint8_t* upbuf[2] = {nullptr, nullptr};  // pinned double buffer of weight uploads
   cudaEvent_t upev[2] = {nullptr, nullptr};
   // peer all-reduce (one process per GPU, sg_peer.cuh): this rank's receive
@@ -244,6 +247,26 @@ cudaError_t static_workspace(int device, void** out) {
   return cudaSuccess;
 }
 
+// Host-pointer calls read the device error word in the same stream as their
+// output (no extra synchronous copy per call): enqueue the read before the
+// final synchronisation, check it after.
+int read_error_async(DevState& d, cudaStream_t st) {
+  if (!d.err_host && cudaMallocHost((void**)&d.err_host, 64) != cudaSuccess) {
+    cudaGetLastError();
+    d.err_host = nullptr;
+    return fail(SG_ERR_OOM, "cudaMallocHost(64) failed");
+  }
+  CUDA_TRY(cudaMemcpyFromSymbolAsync(d.err_host, g_sg_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st));
+  return SG_OK;
+}
+
+int check_device_error(DevState& d);
+
+int error_after_sync(DevState& d) {
+  if (d.err_host && *(volatile int*)d.err_host == 0) return SG_OK;
+  return check_device_error(d);  // reads it again, clears it and reports
+}
+
 int check_device_error(DevState& d) {
   int v = 0;
   CUDA_TRY(cudaSetDevice(d.device));
@@ -305,6 +328,8 @@ void release_devices() {
     if (d.attn_ws) cudaFree(d.attn_ws);
     if (d.argmax_ws) cudaFree(d.argmax_ws);
     if (d.hbuf) cudaFreeHost(d.hbuf);
+    if (d.err_host) cudaFreeHost(d.err_host);
+    if (d.pbuf) cudaFree(d.pbuf);
     for (int i = 0; i < 2; ++i) {
       if (d.upbuf[i]) cudaFreeHost(d.upbuf[i]);
       if (d.upev[i]) cudaEventDestroy(d.upev[i]);
@@ -321,11 +346,32 @@ void release_devices() {
 
 // ---------------------------------------------------------- the core launch
 // y[b][*] (ldy) = W_shard x[b][*] (ldx) on one device, stream-ordered.
+// the prologue's rows into out [batch][K] (sg_ops.cu: the same kernels as
+// sg_rmsnorm_device / sg_silu_mul_device)
+int apply_prologue(DevState& d, const SgGemvPrologue& pro, const float* x, int64_t ldx, int64_t K, int batch,
+                   float* out, cudaStream_t st);
+
 int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* x, int64_t ldx,
-               float* const* ys, const int64_t* ldys, int batch, cudaStream_t st, bool accumulate) {
+               float* const* ys, const int64_t* ldys, int batch, cudaStream_t st, bool accumulate,
+               const SgGemvPrologue* pro = nullptr) {
   const int64_t K = ws[0]->n_cols;
   if (((uintptr_t)x & 15) || (ldx & 3))
     return fail(SG_ERR_INVALID_ARG, "x must be 16-byte aligned with a row stride that is a multiple of 4 floats");
+  if (pro && pro->kind != SG_PRO_NONE) {
+    // the decode GEMV (Q4_0 / Q4_K, up to SG_GEMV_MAX_BATCH tokens) applies
+    // the prologue on its own way in; anything else gets the rows first
+    bool fused = batch <= SG_GEMV_MAX_BATCH;
+    for (int i = 0; i < n_w; ++i) fused = fused && ws[i]->dtype != SG_DTYPE_Q6_K;
+    if (!fused) {
+      int rc = ensure_buf((void**)&d.pbuf, &d.pbuf_bytes, (size_t)batch * K * sizeof(float));
+      if (rc) return rc;
+      rc = apply_prologue(d, *pro, x, ldx, K, batch, d.pbuf, st);
+      if (rc) return rc;
+      x = d.pbuf;
+      ldx = K;
+      pro = nullptr;
+    }
+  }
   if (batch <= SG_GEMV_MAX_BATCH) {
     void* gws = nullptr;
     size_t gws_bytes = sg_gemv_scratch_bytes(K, batch);
@@ -366,7 +412,7 @@ int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* 
       while (i1 < n_w && i1 - i0 < SG_GEMV_MAX_MATS && ws[i1]->dtype == ws[i0]->dtype) ++i1;
       SgGemvMat mats[SG_GEMV_MAX_MATS];
       for (int i = i0; i < i1; ++i) mats[i - i0] = {ws[i], ys[i], ldys[i]};
-      CUDA_TRY(sg_gemv(mats, i1 - i0, x, ldx, batch, accumulate, gws, gws_bytes, d.num_sms, st));
+      CUDA_TRY(sg_gemv(mats, i1 - i0, x, ldx, batch, accumulate, gws, gws_bytes, d.num_sms, st, pro));
       i0 = i1;
     }
     return SG_OK;
@@ -586,8 +632,10 @@ int linear_host(const sg_weight_t* ws, int n_w, const float* const* xs, float* c
     int64_t tot = 0;
     for (int i = 0; i < n_w; ++i) tot += (int64_t)batch * ld[di][i];
     CUDA_TRY(cudaMemcpyAsync(d.hbuf, d.ybuf, (size_t)tot * sizeof(float), cudaMemcpyDeviceToHost, d.stream));
+    int rc = read_error_async(d, d.stream);
+    if (rc) return rc;
     CUDA_TRY(cudaStreamSynchronize(d.stream));
-    int rc = check_device_error(d);
+    rc = error_after_sync(d);
     if (rc) return rc;
     int64_t off = 0;
     for (int i = 0; i < n_w; ++i) {
@@ -936,9 +984,8 @@ int sg_linear_device(sg_weight_t w, const float* x, int64_t ldx, float* y, int64
   return sg_linear_multi_device(&w, 1, x, ldx, &y, ldys, batch, stream, flags);
 }
 
-int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x, int64_t ldx, float* const* ys,
-                           const int64_t* ldys, int batch, void* stream, int flags) {
-  std::lock_guard<std::mutex> lk(g_ctx.mu);
+int linear_multi_device_impl(const sg_weight_t* ws, int n_weights, const float* x, int64_t ldx, float* const* ys,
+                             const int64_t* ldys, int batch, void* stream, int flags, const SgGemvPrologue* pro) {
   if (!ws || !x || !ys || !ldys || n_weights < 1 || n_weights > SG_GEMV_MAX_MATS)
     return fail(SG_ERR_INVALID_ARG, "bad arguments");
   if (g_ctx.devs.size() != 1) return fail(SG_ERR_INVALID_ARG, "device entry points need one device per process");
@@ -961,7 +1008,8 @@ int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x,
   // a NULL stream is CUDA's default stream (the CUDA convention), not the
   // library's internal stream, so callers on the default stream stay ordered
   cudaStream_t st = (cudaStream_t)stream;
-  if (ws[0]->tp_mode != SG_TP_ROW || g_ctx.world == 1) return run_linear(d, sw, n_weights, x, ldx, ys, ldys, batch, st, acc);
+  if (ws[0]->tp_mode != SG_TP_ROW || g_ctx.world == 1)
+    return run_linear(d, sw, n_weights, x, ldx, ys, ldys, batch, st, acc, pro);
   // Row split: every rank holds a partial sum of all n_rows outputs. They are
   // written packed ([batch][n_rows] per tensor, back to back) so that one
   // all-reduce covers the call, then copied into strided outputs if needed.
@@ -997,7 +1045,7 @@ int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x,
     for (int i = 0; i < n_weights; ++i)
       CUDA_TRY(cudaMemcpy2DAsync(yp[i], (size_t)lp[i] * sizeof(float), ys[i], (size_t)ldys[i] * sizeof(float),
                                  (size_t)lp[i] * sizeof(float), batch, cudaMemcpyDeviceToDevice, st));
-  int rc = run_linear(d, sw, n_weights, x, ldx, yp, lp, batch, st, acc && lead);
+  int rc = run_linear(d, sw, n_weights, x, ldx, yp, lp, batch, st, acc && lead, pro);
   if (rc) return rc;
   rc = allreduce_rank(d, yp[0], count, st);
   if (rc) return rc;
@@ -1006,6 +1054,34 @@ int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x,
       CUDA_TRY(cudaMemcpy2DAsync(ys[i], (size_t)ldys[i] * sizeof(float), yp[i], (size_t)lp[i] * sizeof(float),
                                  (size_t)lp[i] * sizeof(float), batch, cudaMemcpyDeviceToDevice, st));
   return SG_OK;
+}
+
+int sg_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x, int64_t ldx, float* const* ys,
+                           const int64_t* ldys, int batch, void* stream, int flags) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  return linear_multi_device_impl(ws, n_weights, x, ldx, ys, ldys, batch, stream, flags, nullptr);
+}
+
+int sg_rmsnorm_linear_multi_device(const sg_weight_t* ws, int n_weights, const float* x, int64_t ldx,
+                                   const float* norm_weight, float eps, float* const* ys, const int64_t* ldys,
+                                   int batch, void* stream, int flags) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!norm_weight) return fail(SG_ERR_INVALID_ARG, "null norm weight");
+  const SgGemvPrologue pro = {SG_PRO_RMSNORM, norm_weight, eps, nullptr, 0};
+  return linear_multi_device_impl(ws, n_weights, x, ldx, ys, ldys, batch, stream, flags, &pro);
+}
+
+int sg_silu_mul_linear_device(sg_weight_t w, const float* g, int64_t ldg, const float* u, int64_t ldu, float* y,
+                              int64_t ldy, int batch, void* stream, int flags) {
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (!u) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  int rc = validate_weight(w);
+  if (rc) return rc;
+  if (ldu < w->shards[0].w.n_cols)
+    return fail(SG_ERR_INVALID_ARG, "ldu %lld < n_cols %lld", (long long)ldu, (long long)w->shards[0].w.n_cols);
+  const SgGemvPrologue pro = {SG_PRO_SILU_MUL, nullptr, 0.f, u, ldu};
+  const int64_t ldys[1] = {ldy};
+  return linear_multi_device_impl(&w, 1, g, ldg, &y, ldys, batch, stream, flags, &pro);
 }
 
 int sg_dequant_f32(sg_weight_t w, float* dst, int flags) {

@@ -135,6 +135,7 @@ struct XParams {
   int64_t ldy[SG_GEMV_MAX_MATS];
   int n_rows[SG_GEMV_MAX_MATS];
   int n_zero;
+  SgGemvPrologue pro;
 };
 
 __device__ __forceinline__ int find_mat(const Params& p, int rbg) {
@@ -247,6 +248,65 @@ __device__ __forceinline__ void load_x8(const float* x, int64_t ldx, int K, int 
   } else {
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = 0.f;
+  }
+}
+
+// 1/sqrt(mean(x^2) + eps) of a row, in sg_rmsnorm_device's order: that
+// kernel's thread t (of kSgNormThreads) sums x_i^2 for i = t, t + 512, ... in
+// one FMA chain, each warp of 32 chains is reduced by the xor-shuffle tree,
+// and the 16 warp sums are added in warp order. The 4 warps of a prep CTA
+// replay it together: warp w runs the chain groups w, w + 4, w + 8, w + 12,
+// their loads interleaved. Every thread of the CTA must call it (a CTA
+// barrier); `active` is false for a padding token slot (result 1).
+__device__ __forceinline__ float cta_inv_rms(const float* xr, int n, float eps, bool active, int warp, int lane) {
+  constexpr int NG = kSgNormThreads / 32, G4 = NG / 4;
+  __shared__ float red[NG];
+  if (active) {
+    float c[G4];
+#pragma unroll
+    for (int j = 0; j < G4; ++j) c[j] = 0.f;
+    for (int m = 0; m * kSgNormThreads < n; ++m) {
+#pragma unroll
+      for (int j = 0; j < G4; ++j) {
+        const int i = m * kSgNormThreads + 32 * (warp + 4 * j) + lane;
+        if (i < n) c[j] = __fmaf_rn(xr[i], xr[i], c[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < G4; ++j) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) c[j] += __shfl_xor_sync(0xffffffffu, c[j], o);
+      if (lane == 0) red[warp + 4 * j] = c[j];
+    }
+  }
+  __syncthreads();
+  if (!active) return 1.f;
+  float ss = 0.f;
+#pragma unroll
+  for (int w = 0; w < NG; ++w) ss += red[w];
+  ss = __fdiv_rn(ss, (float)n);
+  ss = __fadd_rn(ss, eps);
+  return __fdiv_rn(1.0f, __fsqrt_rn(ss));
+}
+
+// silu(v) * u, v / (1 + exp(-v)) with each step rounded (sg_silu_mul_device)
+__device__ __forceinline__ float silu_mul_pro(float v, float u) {
+  return __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+}
+
+// load_x8 with the call's prologue applied (inv: the token's RMSNorm factor)
+__device__ __forceinline__ void load_x8_pro(const float* x, int64_t ldx, int K, int u, int tok, int batch, int lane,
+                                            const SgGemvPrologue& pro, float inv, float (&v)[8]) {
+  load_x8(x, ldx, K, u, tok, batch, lane, v);
+  const int k0 = 256 * u + 8 * lane;
+  if (pro.kind == SG_PRO_NONE || tok >= batch || k0 >= K) return;
+  if (pro.kind == SG_PRO_RMSNORM) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], inv), pro.w[k0 + e]);
+  } else {
+    const float* ur = pro.x2 + (int64_t)tok * pro.ldx2 + k0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = silu_mul_pro(v[e], ur[e]);
   }
 }
 
@@ -363,12 +423,25 @@ __global__ void __launch_bounds__(128) xprep_kernel(XParams p) {
         for (int r = tid; r < p.n_rows[m]; r += nth) yr[r] = 0.f;
       }
   }
-  const int lane = threadIdx.x & 31;
-  const int wg = blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (wg >= p.n_units * C::NTOK) return;
-  const int u = wg / C::NTOK, tok = wg - u * C::NTOK;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int u, tok;
+  float inv = 1.f;
+  if (p.pro.kind == SG_PRO_RMSNORM) {
+    // CTA = (token slot, 4 consecutive units): its warps share the token and
+    // compute its RMSNorm factor together
+    const int gpt = (p.n_units + 3) / 4;
+    tok = blockIdx.x / gpt;
+    u = (blockIdx.x - tok * gpt) * 4 + warp;
+    inv = cta_inv_rms(p.x + (int64_t)min(tok, p.batch - 1) * p.ldx, p.K, p.pro.eps, tok < p.batch, warp, lane);
+    if (u >= p.n_units) return;
+  } else {
+    const int wg = blockIdx.x * 4 + warp;
+    if (wg >= p.n_units * C::NTOK) return;
+    u = wg / C::NTOK;
+    tok = wg - u * C::NTOK;
+  }
   float v[8];
-  load_x8(p.x, p.ldx, p.K, u, tok, p.batch, lane, v);
+  load_x8_pro(p.x, p.ldx, p.K, u, tok, p.batch, lane, p.pro, inv, v);
   store_unit<DT, NTG>(p.ximg + (size_t)u * C::XU, unit_x(v), tok, lane);
   if (C::P && tok == 0)  // columns 6 and 7 hold no token: zero digits, a plain start value, zero scale
     for (int i = lane; i < 8 * 2 * 4; i += 32) {
@@ -742,7 +815,8 @@ cudaError_t launch(Params p, XParams xp, int rb_total, int num_sms, cudaStream_t
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = sg_pdl_enabled() ? 1 : 0;
   cudaLaunchConfig_t x = {};  // the activation images and zeroed outputs
-  x.gridDim = dim3((unsigned)((xp.n_units * C::NTOK + 3) / 4));
+  x.gridDim = dim3((unsigned)(xp.pro.kind == SG_PRO_RMSNORM ? C::NTOK * ((xp.n_units + 3) / 4)
+                                                             : (xp.n_units * C::NTOK + 3) / 4));
   x.blockDim = dim3(128);
   x.stream = st;
   x.attrs = attr;
@@ -774,7 +848,7 @@ size_t sg_gemv_scratch_bytes(int64_t n_cols, int batch) {
 }
 
 cudaError_t sg_gemv(const SgGemvMat* mats, int n_mats, const float* x, int64_t ldx, int batch, bool accumulate,
-                    void* scratch, size_t scratch_bytes, int num_sms, cudaStream_t st) {
+                    void* scratch, size_t scratch_bytes, int num_sms, cudaStream_t st, const SgGemvPrologue* pro) {
   using namespace gemv_mma;
   if (n_mats < 1 || n_mats > SG_GEMV_MAX_MATS || batch < 1 || batch > SG_GEMV_MAX_BATCH || !x || !scratch)
     return cudaErrorInvalidValue;
@@ -808,6 +882,12 @@ cudaError_t sg_gemv(const SgGemvMat* mats, int n_mats, const float* x, int64_t l
   xp.n_units = (int)((K + 255) / 256);
   xp.ximg = static_cast<uint8_t*>(scratch);
   xp.n_zero = accumulate ? 0 : n_mats;
+  if (pro && pro->kind != SG_PRO_NONE) {
+    if ((pro->kind == SG_PRO_RMSNORM && !pro->w) || (pro->kind == SG_PRO_SILU_MUL && (!pro->x2 || pro->ldx2 < K)) ||
+        pro->kind > SG_PRO_SILU_MUL)
+      return cudaErrorInvalidValue;
+    xp.pro = *pro;
+  }
 #define SG_GEMV_LAUNCH(DT)                                       \
   switch (ntg) {                                                 \
     case 0: return launch<DT, 0>(p, xp, rb, num_sms, st);        \

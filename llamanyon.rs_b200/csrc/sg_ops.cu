@@ -99,7 +99,7 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 // One CTA per row: ss = sum x^2, ss /= n, ss += eps, inv = 1 / sqrt(ss),
 // out = (x * inv) * w, each step one IEEE operation as in ops.rs:190-199;
 // only the summation order of ss differs (a tree instead of a running sum).
-constexpr int kNormThreads = 512;
+constexpr int kNormThreads = kSgNormThreads;  // the decode GEMV's RMSNorm prologue replays this order
 constexpr int kNormRegs = 8;  // elements per thread kept in registers (rows up to 4096 read once)
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* x, int64_t ldx, const float* __restrict__ w,
                                                               float* out, int64_t ldo, int n, float eps) {
@@ -953,6 +953,28 @@ int attention_launch(const ops::AttnArgs& a, dim3 g1, dim3 g2, float* out, int64
   CUDA_TRY(ops::launch(ops::attn_combine_kernel<HD>, g2, dim3(HD), 0, st, a, out, ldo));
   return SG_OK;
 }
+// (declared beside run_linear in sg_api.cu)
+// The rows of a GEMV prologue, for the calls that do not fuse it (prefill
+// GEMM, Q6_K): the same kernels as sg_rmsnorm_device / sg_silu_mul_device.
+int apply_prologue(DevState& d, const SgGemvPrologue& pro, const float* x, int64_t ldx, int64_t K, int batch,
+                   float* out, cudaStream_t st) {
+  if (pro.kind == SG_PRO_RMSNORM) {
+    CUDA_TRY(ops::launch(ops::rmsnorm_kernel, dim3(batch), dim3(ops::kNormThreads), 0, st, x, ldx, pro.w, out,
+                         (int64_t)K, (int)K, pro.eps));
+    return SG_OK;
+  }
+  CUDA_TRY(cudaMemcpy2DAsync(out, (size_t)K * sizeof(float), x, (size_t)ldx * sizeof(float), (size_t)K * sizeof(float),
+                             batch, cudaMemcpyDeviceToDevice, st));
+  const int64_t total = K * batch;
+  if (K % 4 == 0 && pro.ldx2 % 4 == 0 && aligned16(pro.x2))
+    CUDA_TRY(ops::launch(ops::silu_mul_kernel<4>, dim3(ops::ew_grid(total / 4, d.num_sms)), dim3(256), 0, st, out,
+                         (int64_t)K, pro.x2, pro.ldx2, (int)K, total));
+  else
+    CUDA_TRY(ops::launch(ops::silu_mul_kernel<1>, dim3(ops::ew_grid(total, d.num_sms)), dim3(256), 0, st, out,
+                         (int64_t)K, pro.x2, pro.ldx2, (int)K, total));
+  return SG_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1083,6 +1105,7 @@ int sg_rmsnorm_device(const float* x, int64_t ldx, const float* weight, float* o
                        out, ldo, n, eps));
   return SG_OK;
 }
+
 
 int sg_rope_kv_device(sg_rope_t rope, sg_kv_cache_t cache, int layer, float* q, int64_t ldq, float* k, int64_t ldk,
                       const float* v, int64_t ldv, const int32_t* pos, const int32_t* seq, int rows, int n_q_heads,

@@ -143,9 +143,18 @@ class SynthModel:
 class Decoder:
     """Buffers and the forward pass for up to max_rows query rows."""
 
-    def __init__(self, gpu: sg.SwampGpu, model: SynthModel, n_seqs: int, max_rows: int):
+    def __init__(self, gpu: sg.SwampGpu, model: SynthModel, n_seqs: int, max_rows: int,
+                 fuse_norm: bool = False, fuse_silu: bool = True):
+        """fuse_norm / fuse_silu: RMSNorm / SiLU-mul run inside the following
+        linear's operand build (sg_rmsnorm_linear_multi_device /
+        sg_silu_mul_linear_device, the same rows as the separate calls);
+        False runs the engine's two calls. Measured on configs[3] at batch 1:
+        the SiLU fusion saves 1.4% of a decode step, the RMSNorm fusion costs
+        0.7% (each prep CTA re-reads its token's row for the norm), so only
+        the former is on by default."""
         import torch
         self.torch = torch
+        self.fuse_norm, self.fuse_silu = fuse_norm, fuse_silu
         self.gpu, self.m, self.cfg = gpu, model, model.cfg
         self.ops = sg.LayerOps(gpu)
         c = self.cfg
@@ -200,13 +209,21 @@ class Decoder:
         LQ, LG = DQ + 2 * KV, 2 * F  # row strides of [q | k | v] and [gate | up]
         ACC = sg.SG_FLAG_ACCUMULATE
         o.embed(self.m.token_embd, p(self.tokens), rows, p(self.x), D, stream)
-        for l, lw in enumerate(self.m.layers):
-            o.rmsnorm(p(self.x), D, p(self.m.attn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
-            if self.m.stacked:
-                g.linear_device(lw["qkv"], p(self.xn), D, p(self.qkv), LQ, rows, stream=stream)
+        def norm_linear(norm, ws, ys, ld):
+            """ys = W rmsnorm(x): fused (the norm runs inside the GEMV's operand
+            build) or as the engine's two calls."""
+            if self.fuse_norm:
+                g.rmsnorm_linear_multi_device(ws, p(self.x), D, p(norm), c.eps, ys, [ld] * len(ws), rows,
+                                              stream=stream)
             else:
-                g.linear_multi_device([lw["q"], lw["k"], lw["v"]], p(self.xn), D,
-                                      [p(self.q), p(self.k), p(self.v)], [LQ] * 3, rows, stream=stream)
+                o.rmsnorm(p(self.x), D, p(norm), p(self.xn), D, D, rows, c.eps, stream)
+                g.linear_multi_device(ws, p(self.xn), D, ys, [ld] * len(ws), rows, stream=stream)
+
+        for l, lw in enumerate(self.m.layers):
+            if self.m.stacked:
+                norm_linear(self.m.attn_norm[l], [lw["qkv"]], [p(self.qkv)], LQ)
+            else:
+                norm_linear(self.m.attn_norm[l], [lw["q"], lw["k"], lw["v"]], [p(self.q), p(self.k), p(self.v)], LQ)
             if decode:
                 o.rope_attention(self.rope, self.cache, l, p(self.q), LQ, p(self.k), LQ, p(self.v), LQ, p(self.att),
                                  DQ, p(self.pos), p(self.seq), rows, H, stream)
@@ -221,14 +238,16 @@ class Decoder:
             # O: row-split over this rank's heads; the all-reduce adds every
             # rank's part (and the residual, once) into x
             g.linear_device(lw["attn_output"], p(self.att), DQ, p(self.x), D, rows, stream=stream, flags=ACC)
-            o.rmsnorm(p(self.x), D, p(self.m.ffn_norm[l]), p(self.xn), D, D, rows, c.eps, stream)
             if self.m.stacked:
-                g.linear_device(lw["gate_up"], p(self.xn), D, p(self.gu), LG, rows, stream=stream)
+                norm_linear(self.m.ffn_norm[l], [lw["gate_up"]], [p(self.gu)], LG)
             else:
-                g.linear_multi_device([lw["gate"], lw["up"]], p(self.xn), D, [p(self.gate), p(self.up)], [LG] * 2,
-                                      rows, stream=stream)
-            o.silu_mul(p(self.gate), LG, p(self.up), LG, F, rows, stream)
-            g.linear_device(lw["ffn_down"], p(self.gate), LG, p(self.x), D, rows, stream=stream, flags=ACC)
+                norm_linear(self.m.ffn_norm[l], [lw["gate"], lw["up"]], [p(self.gate), p(self.up)], LG)
+            if self.fuse_silu:
+                g.silu_mul_linear_device(lw["ffn_down"], p(self.gate), LG, p(self.up), LG, p(self.x), D, rows,
+                                         stream=stream, flags=ACC)
+            else:
+                o.silu_mul(p(self.gate), LG, p(self.up), LG, F, rows, stream)
+                g.linear_device(lw["ffn_down"], p(self.gate), LG, p(self.x), D, rows, stream=stream, flags=ACC)
         r0, r1 = (0, rows) if logits_rows is None else (logits_rows.start, logits_rows.stop)
         n = r1 - r0
         o.rmsnorm(p(self.x[r0]), D, p(self.m.output_norm), p(self.xn), D, D, n, c.eps, stream)

@@ -42,6 +42,7 @@ EXPORTS = (
     "sg_synth_weight", "sg_synth_blocks", "sg_synth_x",
     "sg_rope_create", "sg_rope_free", "sg_rope_table", "sg_kv_cache_create", "sg_kv_cache_free", "sg_kv_cache_ptr",
     "sg_rmsnorm_device", "sg_rope_kv_device", "sg_attention_device", "sg_rope_attention_device", "sg_attention_prefill_device", "sg_silu_mul_device", "sg_add_device",
+    "sg_rmsnorm_linear_multi_device", "sg_silu_mul_linear_device",
     "sg_argmax_device", "sg_embed_device", "sg_allreduce_device", "sg_allreduce_path",
 )
 SG_ERR_FORMAT, SG_ERR_NOT_FOUND = -8, -9
@@ -72,6 +73,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     L.sg_linear_multi.argtypes = [P, i32, P, P, i32]
     L.sg_linear_device.argtypes = [P, P, i64, P, i64, i32, P, i32]
     L.sg_linear_multi_device.argtypes = [P, i32, P, i64, P, P, i32, P, i32]
+    L.sg_rmsnorm_linear_multi_device.argtypes = [P, i32, P, i64, P, ctypes.c_float, P, P, i32, P, i32]
+    L.sg_silu_mul_linear_device.argtypes = [P, P, i64, P, i64, P, i64, i32, P, i32]
     L.sg_linear_device_noalloc.argtypes = [P, P, i64, P, i64, i32, P, i32]
     L.sg_dequant_f32.argtypes = [P, P, i32]
     L.sg_fused_gemv_q4k.argtypes = [P, P, P, i32, i32]
@@ -244,6 +247,23 @@ class SwampGpu:
                               stream: int = 0, flags: int = 0):
         """linear_device without any device allocation (decode batch 1..16)."""
         self._check(self.L.sg_linear_device_noalloc(w.handle, x_ptr, ldx, y_ptr, ldy, batch, stream or None, flags))
+
+    def rmsnorm_linear_multi_device(self, ws: Sequence[Weight], x_ptr: int, ldx: int, norm_ptr: int, eps: float,
+                                    y_ptrs: Sequence[int], ldys: Sequence[int], batch: int, stream: int = 0,
+                                    flags: int = 0):
+        """ys[i] = W_i rmsnorm(x) (RMSNorm fused into the decode GEMV's operand build)."""
+        n = len(ws)
+        hp = (ctypes.c_void_p * n)(*[w.handle for w in ws])
+        yp = (ctypes.c_void_p * n)(*y_ptrs)
+        lp = (ctypes.c_int64 * n)(*ldys)
+        self._check(self.L.sg_rmsnorm_linear_multi_device(hp, n, x_ptr, ldx, norm_ptr, eps, yp, lp, batch,
+                                                          stream or None, flags))
+
+    def silu_mul_linear_device(self, w: Weight, g_ptr: int, ldg: int, u_ptr: int, ldu: int, y_ptr: int, ldy: int,
+                               batch: int, stream: int = 0, flags: int = 0):
+        """y = W (silu(g) * u) (SiLU-mul fused into the decode GEMV's operand build)."""
+        self._check(self.L.sg_silu_mul_linear_device(w.handle, g_ptr, ldg, u_ptr, ldu, y_ptr, ldy, batch,
+                                                     stream or None, flags))
 
     def linear_multi_device(self, ws: Sequence[Weight], x_ptr: int, ldx: int, y_ptrs: Sequence[int],
                             ldys: Sequence[int], batch: int, stream: int = 0, flags: int = 0):

@@ -330,6 +330,31 @@ pub fn silu_mul_device(g: *mut f32, ldg: i64, u: *const f32, ldu: i64, n: usize,
     check(lib, unsafe { f(g, ldg, u, ldu, n as c_int, rows as c_int, stream) })
 }
 
+/// `rmsnorm_device` then `linear_multi_device` on its rows as one call: at
+/// decode batch the norm runs inside the GEMV's activation prep (the rows are
+/// never written), bit-identical to the two calls.
+pub fn rmsnorm_linear_multi_device(ws: &[SgWeight], x: *const f32, ldx: i64, norm_weight: *const f32, eps: f32,
+                                   ys: &[*mut f32], ldys: &[i64], batch: usize, stream: Stream, flags: c_int)
+                                   -> Result<()> {
+    let lib = try_lib()?;
+    let f = sym!(lib, "sg_rmsnorm_linear_multi_device",
+                 unsafe extern "C" fn(*const SgWeight, c_int, *const f32, i64, *const f32, f32, *const *mut f32,
+                                      *const i64, c_int, Stream, c_int) -> c_int);
+    check(lib, unsafe { f(ws.as_ptr(), ws.len() as c_int, x, ldx, norm_weight, eps, ys.as_ptr(), ldys.as_ptr(),
+                          batch as c_int, stream, flags) })
+}
+
+/// `silu_mul_device` then `linear_device` on its rows as one call (g and u
+/// are not modified).
+pub fn silu_mul_linear_device(w: SgWeight, g: *const f32, ldg: i64, u: *const f32, ldu: i64, y: *mut f32, ldy: i64,
+                              batch: usize, stream: Stream, flags: c_int) -> Result<()> {
+    let lib = try_lib()?;
+    let f = sym!(lib, "sg_silu_mul_linear_device",
+                 unsafe extern "C" fn(SgWeight, *const f32, i64, *const f32, i64, *mut f32, i64, c_int, Stream,
+                                      c_int) -> c_int);
+    check(lib, unsafe { f(w, g, ldg, u, ldu, y, ldy, batch as c_int, stream, flags) })
+}
+
 pub fn argmax_device(logits: *const f32, ld: i64, n: usize, rows: usize, out: *mut i32, stream: Stream)
                      -> Result<()> {
     let lib = try_lib()?;
