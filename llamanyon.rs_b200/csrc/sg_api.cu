@@ -106,6 +106,8 @@ struct DevState {
   bool peer_on = false;
   void* peer_base = nullptr;
   uint32_t* peer_ctr = nullptr;
+  uint32_t* peer_ctr2 = nullptr;  // the two-shot kernel's per-chunk epoch counters
+  bool two_shot_on = false;
   SgPeerPtrs peer = {};
   void* peer_mapped[SG_PEER_MAX] = {};
 };
@@ -338,6 +340,7 @@ void release_devices() {
       if (d.peer_mapped[p]) cudaIpcCloseMemHandle(d.peer_mapped[p]);
     if (d.peer_base) cudaFree(d.peer_base);
     if (d.peer_ctr) cudaFree(d.peer_ctr);
+    if (d.peer_ctr2) cudaFree(d.peer_ctr2);
     if (d.stream) cudaStreamDestroy(d.stream);
   }
   g_ctx.devs.clear();
@@ -428,11 +431,43 @@ int run_linear(DevState& d, const SgDevWeight* const* ws, int n_w, const float* 
 }
 
 constexpr int64_t kPeerCap = (int64_t)kArChunk * kArMaxChunks;  // floats per slot
+constexpr int64_t kPeerCap2 = kPeerCap / 2;                        // floats per two-shot part slot
+constexpr int kAr2MaxChunks = (int)(kPeerCap2 / kAr2Chunk);
+
+// -1: the size rule below; 0: never two-shot; 1: always (when set up)
+int two_shot_mode() {
+  static const int m = [] {
+    const char* v = std::getenv("SG_AR_TWO_SHOT");
+    return v ? (v[0] == '1' ? 1 : 0) : -1;
+  }();
+  return m;
+}
 
 // Sum all-reduce of `count` floats in place on this rank's device: the peer
 // kernel when it is set up and the vector fits a slot, else NCCL.
-int allreduce_rank(DevState& d, float* buf, size_t count, cudaStream_t st) {
+// path: 0 by the rules below, 1 the one-shot peer kernel, 2 the two-shot one
+int allreduce_rank(DevState& d, float* buf, size_t count, cudaStream_t st, int path = 0) {
   if (g_ctx.world <= 1 || count == 0) return SG_OK;
+  const int tsm = two_shot_mode();
+  const bool two = path == 2 || (path == 0 && d.two_shot_on &&
+                                 (tsm == 1 || (tsm == -1 && g_ctx.world >= 4 && count >= ((size_t)1 << 17))));
+  if (d.peer_on && two && (int64_t)count <= kPeerCap) {
+    // large vectors on 4+ ranks: reduce-scatter + all-gather (each rank sends
+    // 2 (W-1)/W of the vector instead of (W-1) times it)
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = sg_pdl_enabled() ? 1 : 0;
+    const int64_t part = (((int64_t)count + g_ctx.world - 1) / g_ctx.world + 1) & ~(int64_t)1;
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3((unsigned)((part + kAr2Chunk - 1) / kAr2Chunk));
+    c.blockDim = dim3(kAr2Threads);
+    c.stream = st;
+    c.attrs = attr;
+    c.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&c, peer_allreduce2_kernel, (const float*)buf, buf, (int64_t)count, g_ctx.world,
+                                g_ctx.rank_base, d.peer, d.peer_ctr2, part, kPeerCap2));
+    return SG_OK;
+  }
   if (d.peer_on && (int64_t)count <= kPeerCap) {
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -463,11 +498,15 @@ int peer_setup(DevState& d) {
   int ok = W <= SG_PEER_MAX;
   const char* env = std::getenv("SG_PEER_ALLREDUCE");
   if (env && env[0] == '0') ok = 0;  // SG_PEER_ALLREDUCE=0: NCCL for every all-reduce
-  // [2 parities][W ranks][kPeerCap / 2] words of {v0, epoch, v1, epoch}
-  const size_t buf_bytes = (size_t)2 * W * (kPeerCap / 2) * sizeof(uint4);
+  // [2 parities][W ranks][kPeerCap / 2] words of {v0, epoch, v1, epoch}, then
+  // the two-shot slots [2 parities][2 phases][W ranks][kPeerCap2 / 2]
+  const size_t buf1_bytes = (size_t)2 * W * (kPeerCap / 2) * sizeof(uint4);
+  const size_t buf_bytes = buf1_bytes + (size_t)2 * 2 * W * (kPeerCap2 / 2) * sizeof(uint4);
   cudaIpcMemHandle_t mine = {};
   if (ok && (cudaMalloc(&d.peer_base, buf_bytes) != cudaSuccess ||
              cudaMalloc((void**)&d.peer_ctr, kArMaxChunks * sizeof(uint32_t)) != cudaSuccess ||
+             cudaMalloc((void**)&d.peer_ctr2, kAr2MaxChunks * sizeof(uint32_t)) != cudaSuccess ||
+             cudaMemset(d.peer_ctr2, 0, kAr2MaxChunks * sizeof(uint32_t)) != cudaSuccess ||
              cudaMemset(d.peer_base, 0, buf_bytes) != cudaSuccess ||
              cudaMemset(d.peer_ctr, 0, kArMaxChunks * sizeof(uint32_t)) != cudaSuccess ||
              cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&mine, d.peer_base) != cudaSuccess)) {
@@ -489,12 +528,14 @@ int peer_setup(DevState& d) {
   for (int p = 0; p < W && ok; ++p) {
     if (p == R) {
       d.peer.buf[p] = static_cast<uint4*>(d.peer_base);
+      d.peer.buf2[p] = reinterpret_cast<uint4*>(static_cast<uint8_t*>(d.peer_base) + buf1_bytes);
     } else if (cudaIpcOpenMemHandle(&d.peer_mapped[p], all[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
       cudaGetLastError();
       ok = 0;
       break;
     } else {
       d.peer.buf[p] = static_cast<uint4*>(d.peer_mapped[p]);
+      d.peer.buf2[p] = reinterpret_cast<uint4*>(static_cast<uint8_t*>(d.peer_mapped[p]) + buf1_bytes);
     }
   }
   // every rank must take the same path
@@ -509,40 +550,48 @@ int peer_setup(DevState& d) {
   }
   d.peer_on = ok != 0;
   if (d.peer_on) {
-    // self-test: one all-reduce of small integers through the peer kernel,
-    // which must come out exact on every rank; any rank that sees a wrong sum
-    // or a wait that gave up sends the whole job to NCCL
-    const int64_t n = 2 * kArChunk + 3;
-    std::vector<float> h(n, (float)(R + 1));
-    float* t = nullptr;
-    int pass = cudaMalloc(&t, n * sizeof(float)) == cudaSuccess &&
-               cudaMemcpy(t, h.data(), n * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess;
-    if (pass) pass = allreduce_rank(d, t, (size_t)n, d.stream) == SG_OK &&
-                     cudaStreamSynchronize(d.stream) == cudaSuccess &&
-                     cudaMemcpy(h.data(), t, n * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess;
-    const float want = (float)W * (W + 1) / 2;
-    for (int64_t i = 0; pass && i < n; ++i) pass = h[i] == want;
-    int err = 0;
-    cudaMemcpyFromSymbol(&err, g_sg_error, sizeof(int));
-    if (err) {
-      pass = 0;
-      const int z = 0;
-      cudaMemcpyToSymbol(g_sg_error, &z, sizeof(int));
-    }
-    if (t) cudaFree(t);
-    cudaGetLastError();
-    CUDA_TRY(cudaMemcpy(dok, &pass, sizeof pass, cudaMemcpyHostToDevice));
-    r = g_nccl.AllReduce(dok, dok, 1, kNcclInt32, kNcclMin, d.comm, d.stream);
+    // self-test: an all-reduce of small integers through each peer kernel
+    // (one-shot, then two-shot), which must come out exact on every rank; a
+    // wrong sum or a wait that gave up on any rank turns that kernel off for
+    // the whole job (NCCL, or the one-shot kernel, instead)
+    auto selftest = [&](int path, int64_t n) -> int {
+      std::vector<float> h(n, (float)(R + 1));
+      float* t = nullptr;
+      int pass = cudaMalloc(&t, n * sizeof(float)) == cudaSuccess &&
+                 cudaMemcpy(t, h.data(), n * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess;
+      if (pass) pass = allreduce_rank(d, t, (size_t)n, d.stream, path) == SG_OK &&
+                       cudaStreamSynchronize(d.stream) == cudaSuccess &&
+                       cudaMemcpy(h.data(), t, n * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess;
+      const float want = (float)W * (W + 1) / 2;
+      for (int64_t i = 0; pass && i < n; ++i) pass = h[i] == want;
+      int err = 0;
+      cudaMemcpyFromSymbol(&err, g_sg_error, sizeof(int));
+      if (err) {
+        pass = 0;
+        const int z = 0;
+        cudaMemcpyToSymbol(g_sg_error, &z, sizeof(int));
+      }
+      if (t) cudaFree(t);
+      cudaGetLastError();
+      return pass;
+    };
+    int pass[2];
+    pass[0] = selftest(1, 2 * kArChunk + 3);
+    pass[1] = pass[0] && selftest(2, 2 * (int64_t)W * kAr2Chunk + 3);
+    CUDA_TRY(cudaMemcpy(dok, pass, sizeof pass, cudaMemcpyHostToDevice));
+    r = g_nccl.AllReduce(dok, dok, 2, kNcclInt32, kNcclMin, d.comm, d.stream);
     CUDA_TRY(cudaStreamSynchronize(d.stream));
-    CUDA_TRY(cudaMemcpy(&pass, dok, sizeof pass, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(pass, dok, sizeof pass, cudaMemcpyDeviceToHost));
     if (r) {
       cudaFree(dev);
       return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
     }
-    if (!pass) {
+    if (!pass[0]) {
       std::fprintf(stderr, "swamp_gpu: the peer all-reduce self-test failed; using NCCL\n");
       d.peer_on = false;
     }
+    d.two_shot_on = pass[0] && pass[1];
+    if (pass[0] && !pass[1]) std::fprintf(stderr, "swamp_gpu: the two-shot all-reduce self-test failed; not used\n");
   }
   cudaFree(dev);
   return SG_OK;

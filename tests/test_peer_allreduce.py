@@ -1,7 +1,8 @@
 """The row-split all-reduce over NVLink peer memory (sg_allreduce_device, used
-by every row-split linear in one-process-per-GPU mode) against exact sums and
-NCCL, on 2 GPUs as 2 processes. Skipped when fewer than 2 GPUs are visible:
-ranks whose kernels wait for one another must each have their own GPU.
+by every row-split linear in one-process-per-GPU mode; the one-shot and the
+two-shot kernel) against exact sums and NCCL, on 2 GPUs as 2 processes.
+Skipped when fewer than 2 GPUs are visible: ranks whose kernels wait for one
+another must each have their own GPU.
 
 Exactness: the inputs are small integers, so every order of summation gives
 the same float and the result must equal the integer sum exactly.
@@ -28,7 +29,7 @@ def _free_port():
     return p
 
 
-def _rank(rank, world, port, outdir):
+def _rank(rank, world, port, outdir, two_shot="0"):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -36,7 +37,8 @@ def _rank(rank, world, port, outdir):
         sys.path.insert(0, p)
     import swamp_gpu as sg
     import oracle
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), SG_PEER_ALLREDUCE="1")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), SG_PEER_ALLREDUCE="1",
+                      SG_AR_TWO_SHOT=two_shot)
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
@@ -109,13 +111,18 @@ def _rank(rank, world, port, outdir):
 
 
 @pytest.mark.gpu
-def test_peer_allreduce_two_gpus(tmp_path):
+@pytest.mark.parametrize("two_shot", ["0", "1"])
+def test_peer_allreduce_two_gpus(tmp_path, two_shot):
+    """two_shot "1" (SG_AR_TWO_SHOT=1) sends every call through the
+    reduce-scatter + all-gather kernel, which by default only large vectors
+    on 4 or more ranks take."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs (one per rank)")
     import json
     import torch.multiprocessing as mp
-    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), two_shot), nprocs=2, join=True,
+                       start_method="spawn")
     out = json.load(open(tmp_path / "out.json"))
     assert out["path"] == "peer"
     assert out["exact"] and out["graph"]
