@@ -207,11 +207,11 @@ def cpu_q4k_decode_variants(threads, seconds_each=3.0):
     configs[1] layer's 7 shapes quantized as Q4_K, batch 1 (GB/s of weight +
     activation bytes, like the headline):
       - forward_linear's Q4_K arm with the scalar kernel (fused_gemv_q4k.rs:466-508;
-        the parity target), on `threads` threads and on 1;
+        the parity target), on `threads` threads, on the engine's cap of 6 and on 1;
       - the same arm as the reference dispatches it on this CPU
-        (fused_gemv_q4k.rs:59-82 -> VNNI :101-317 or AVX2 :325-392), on `threads`
-        threads and on 1: numerically divergent from the reference's
-        dequantizer, timing only."""
+        (fused_gemv_q4k.rs:59-82 -> VNNI :101-317 or AVX2 :325-392), on the same
+        thread counts: numerically divergent from the reference's dequantizer,
+        timing only."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     oracle.build()
@@ -241,7 +241,8 @@ def cpu_q4k_decode_variants(threads, seconds_each=3.0):
                          f"({'fused_gemv_q4k.rs:101-317' if path == 'avx512-vnni' else 'fused_gemv_q4k.rs:325-392'}); "
                          "numerically divergent, timing only"))
     for name, fn, what in variants:
-        for nthr in sorted({threads, 1}, reverse=True):
+        # all host threads, the reference engine's own cap of 6 (executor.rs:31), one
+        for nthr in sorted({threads, min(6, threads), 1}, reverse=True):
             gbs, layers, el = run(fn, nthr)
             out.append({"variant": f"q4_k {name}", "value": round(gbs, 3), "unit": "GB/s", "cores": nthr,
                         "kind": "port", "sample": f"{layers} passes over the configs[1] layer's 7 shapes as Q4_K, "
