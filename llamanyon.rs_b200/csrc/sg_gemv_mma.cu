@@ -180,14 +180,8 @@ struct Cursor {
   }
 };
 
-__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1, uint32_t c0, uint32_t c1) {
-  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
-      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
-}
-
-// the same, every accumulator starting at c (a loop-invariant register quad)
+// D = A (16 x 32 u8) * B (32 x 8 s8) + C, every accumulator starting at c
+// (one loop-invariant register quad)
 __device__ __forceinline__ void mma_u8s8_c(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                            uint32_t b0, uint32_t b1, uint32_t c) {
   asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
@@ -195,7 +189,6 @@ __device__ __forceinline__ void mma_u8s8_c(int (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
 }
 
-__device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
 // f16 half h (0: low, 1: high) of a scale word, as the pair (v, v)
 __device__ __forceinline__ float2 h2f_pair(uint32_t w, int h) {
   return __half22float2(__half2half2(__ushort_as_half((unsigned short)(w >> (16 * h)))));
