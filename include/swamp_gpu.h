@@ -166,7 +166,12 @@ SG_API int sg_linear_multi_device(const sg_weight_t *ws, int n_weights, const fl
  * capture begins. All decode calls on a device share the workspace: calls
  * whose work may overlap in time (different streams with no ordering between
  * them) race, so order them. A row-split tensor in one-process-per-GPU mode
- * needs ldy == n_rows and no SG_FLAG_ACCUMULATE.
+ * needs ldy == n_rows and no SG_FLAG_ACCUMULATE; its all-reduce is the peer
+ * kernel over the buffers sg_init_rank mapped (batch * n_rows up to 512 Ki
+ * floats), which allocates nothing. With that kernel off
+ * (SG_PEER_ALLREDUCE=0, or a set-up that failed: sg_allreduce_path) or a
+ * longer vector it is ncclAllReduce, and NCCL may set up connections and
+ * their buffers on its first collective of a kind.
  * The reference has no counterpart: its CPU path allocates per call. */
 SG_API int sg_linear_device_noalloc(sg_weight_t w, const float *x, int64_t ldx, float *y, int64_t ldy, int batch,
                                     void *stream, int flags);

@@ -4,9 +4,11 @@
 // The decode GEMV's workspace (the call's activations converted to the MMA
 // operand layout, rewritten by every call) is the library's fixed per-device
 // array (g_gemv_ws in sg_api.cu), sized for n_cols <= kStaticWsCols at 16
-// tokens (more at fewer tokens), so a call only launches kernels (plus the
-// all-reduce of a row-split tensor). Its address is looked up once per device
-// on the first call that uses the device. The workspace is shared by all
+// tokens (more at fewer tokens), so a call only launches kernels. A row-split
+// tensor's all-reduce is the peer kernel over the receive buffers that
+// sg_init_rank mapped (vectors up to 512 Ki floats) or, with that kernel off
+// or for longer vectors, ncclAllReduce. The workspace's address is looked up
+// once per device on the first call that uses the device. The workspace is shared by all
 // decode calls on a device, so two calls whose kernels overlap in time
 // (different streams, no ordering between them) race on it.
 constexpr int kNoallocMaxBatch = 16;
@@ -48,10 +50,7 @@ int sg_linear_device_noalloc(sg_weight_t w, const float* x, int64_t ldx, float* 
     SgGemvMat m = {sw, y, ldy};
     CUDA_TRY(sg_gemv(&m, 1, x, ldx, batch, acc, ws, kStaticWsBytes, d.num_sms, st));
   }
-  if (row_split) {
-    if (!g_nccl.AllReduce) return fail(SG_ERR_NCCL, "NCCL not initialised");
-    const ncclResult_t r = g_nccl.AllReduce(y, y, (size_t)batch * w->n_rows, kNcclFloat, kNcclSum, d.comm, st);
-    if (r) return fail(SG_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
-  }
-  return SG_OK;
+  // the peer all-reduce kernel (receive buffers mapped by sg_init_rank) for
+  // vectors within its slot, else ncclAllReduce
+  return row_split ? allreduce_rank(d, y, (size_t)batch * w->n_rows, st) : SG_OK;
 }

@@ -122,6 +122,13 @@ def _linears(g, sg, oracle, torch, rank, world, out):
             st.synchronize()
             g.synchronize()
             _gate(out, f"row dt{dtype} b{b} device", yd.cpu().numpy(), ref, l2)
+            if b <= 16:  # the entry point with no device allocation, same all-reduce
+                yd = torch.full((b, nr), float("nan"), device="cuda")
+                with torch.cuda.stream(st):
+                    g.linear_device_noalloc(W, xs.data_ptr(), nc, yd.data_ptr(), nr, b, stream=st.cuda_stream)
+                st.synchronize()
+                g.synchronize()
+                _gate(out, f"row dt{dtype} b{b} noalloc", yd.cpu().numpy(), ref, l2)
             # row split onto a replicated y (the residual stream): y0 counted once
             y0 = np.linspace(-2, 2, b * nr).astype(np.float32).reshape(b, nr)
             yd = torch.from_numpy(y0.copy()).cuda()
