@@ -102,6 +102,13 @@ SG_API const char *sg_last_error(void);
 /* rank / world size / number of devices driven by this process */
 SG_API int sg_topology(int *rank, int *world, int *local_devices);
 
+/* Page-locked host memory for the xs / outs of the host-pointer entry
+ * points (copied by DMA without the staging copy). bytes == 0 gives NULL.
+ * No sg_init needed. The reference has no counterpart: its buffers are
+ * ordinary Vec<f32>. */
+SG_API int sg_host_alloc(size_t bytes, void **out);
+SG_API int sg_host_free(void *p);
+
 /* ---------------------------------------------------------------- weights */
 
 /* Upload one GGUF tensor (host pointer to its raw block bytes, row-major:
@@ -132,7 +139,12 @@ SG_API int sg_weight_shard(sg_weight_t w, int local_device, int64_t *n_rows, int
  * SG_FLAG_DEVICE_PTRS (single-device or rank mode only) xs/outs point at
  * this rank's device and hold this rank's shard: x of n_cols_local, out of
  * n_rows_local (column split) or n_rows (replicate / row split, all-reduced).
- * Batches of 1..32 run the decode GEMV; larger batches the prefill GEMM. */
+ * Batches of 1..32 run the decode GEMV; larger batches the prefill GEMM.
+ * Host rows one fixed stride apart in page-locked memory (sg_host_alloc, or
+ * the caller's own cudaHostAlloc) are copied by DMA straight from xs and into
+ * outs (one device per process, no SG_FLAG_ACCUMULATE for outs); other host
+ * rows pass through the library's page-locked staging buffer with one extra
+ * host copy. Either way the call returns with the results in outs. */
 SG_API int sg_linear(sg_weight_t w, const float *const *xs, float *const *outs, int batch, int flags);
 
 /* forward_linear_multi (linear.rs:96-170): several tensors, same x (K). */

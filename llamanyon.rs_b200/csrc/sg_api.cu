@@ -619,6 +619,29 @@ int validate_weight(sg_weight_t w) {
   return SG_OK;
 }
 
+// Rows rows[0..n) + off, `width` floats each, that sit in page-locked host
+// memory one fixed stride apart (a caller's cudaHostAlloc or sg_host_alloc
+// buffer): the copy engine moves them straight from or to the caller with one
+// 2D copy instead of through the library's staging buffer. Returns that
+// stride in floats, or 0 when the rows are pageable, ragged or overlapping.
+int64_t pinned_stride(const float* const* rows, int n, int64_t off, int64_t width) {
+  const uintptr_t base = (uintptr_t)rows[0];
+  const intptr_t step = n > 1 ? (intptr_t)((uintptr_t)rows[1] - base) : (intptr_t)(width * sizeof(float));
+  if (step % (intptr_t)sizeof(float) || step < (intptr_t)(width * sizeof(float))) return 0;
+  for (int b = 2; b < n; ++b)
+    if ((uintptr_t)rows[b] != base + (uintptr_t)step * (uintptr_t)b) return 0;
+  const float* ends[2] = {rows[0] + off, rows[n - 1] + off + width - 1};
+  for (const float* p : ends) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    if (a.type != cudaMemoryTypeHost) return 0;
+  }
+  return (int64_t)(step / (intptr_t)sizeof(float));
+}
+
 // host-pointer linear over all local devices (also the multi form)
 int linear_host(const sg_weight_t* ws, int n_w, const float* const* xs, float* const* outs, int batch, int flags) {
   const int64_t K = ws[0]->n_cols;
@@ -651,8 +674,14 @@ int linear_host(const sg_weight_t* ws, int n_w, const float* const* xs, float* c
     rc = ensure_host(d, std::max(hx, (size_t)ytot * sizeof(float)));
     if (rc) return rc;
     CUDA_TRY(cudaStreamSynchronize(d.stream));  // pinned staging reuse
-    for (int b = 0; b < batch; ++b) memcpy(d.hbuf + (size_t)b * kl, xs[b] + c0, (size_t)kl * sizeof(float));
-    CUDA_TRY(cudaMemcpyAsync(d.xbuf, d.hbuf, hx, cudaMemcpyHostToDevice, d.stream));
+    const int64_t xpitch = nd == 1 ? pinned_stride(xs, batch, c0, kl) : 0;
+    if (xpitch) {
+      CUDA_TRY(cudaMemcpy2DAsync(d.xbuf, (size_t)kl * sizeof(float), xs[0] + c0, (size_t)xpitch * sizeof(float),
+                                 (size_t)kl * sizeof(float), (size_t)batch, cudaMemcpyHostToDevice, d.stream));
+    } else {
+      for (int b = 0; b < batch; ++b) memcpy(d.hbuf + (size_t)b * kl, xs[b] + c0, (size_t)kl * sizeof(float));
+      CUDA_TRY(cudaMemcpyAsync(d.xbuf, d.hbuf, hx, cudaMemcpyHostToDevice, d.stream));
+    }
     int64_t off = 0;
     const SgDevWeight* sw[SG_GEMV_MAX_MATS];
     for (int i = 0; i < n_w; ++i) {
@@ -678,9 +707,24 @@ int linear_host(const sg_weight_t* ws, int n_w, const float* const* xs, float* c
     if (tp != SG_TP_COLUMN && di > 0) break;
     DevState& d = g_ctx.devs[di];
     CUDA_TRY(cudaSetDevice(d.device));
-    int64_t tot = 0;
-    for (int i = 0; i < n_w; ++i) tot += (int64_t)batch * ld[di][i];
-    CUDA_TRY(cudaMemcpyAsync(d.hbuf, d.ybuf, (size_t)tot * sizeof(float), cudaMemcpyDeviceToHost, d.stream));
+    // one device and no accumulation: outputs in page-locked memory are
+    // written by the copy engine directly, the rest through the staging buffer
+    int64_t tot = 0, staged = 0;
+    int64_t opitch[SG_GEMV_MAX_MATS];
+    for (int i = 0; i < n_w; ++i) {
+      const int64_t r0 = tp == SG_TP_COLUMN ? ws[i]->shards[di].row0 : 0;
+      opitch[i] = nd == 1 && !accumulate ? pinned_stride(outs + (size_t)i * batch, batch, r0, ld[di][i]) : 0;
+      if (opitch[i]) {
+        CUDA_TRY(cudaMemcpy2DAsync(outs[(size_t)i * batch] + r0, (size_t)opitch[i] * sizeof(float), d.ybuf + tot,
+                                   (size_t)ld[di][i] * sizeof(float), (size_t)ld[di][i] * sizeof(float),
+                                   (size_t)batch, cudaMemcpyDeviceToHost, d.stream));
+      } else {
+        staged = tot + (int64_t)batch * ld[di][i];
+      }
+      tot += (int64_t)batch * ld[di][i];
+    }
+    if (staged)  // the staged tensors lie within the first `staged` floats
+      CUDA_TRY(cudaMemcpyAsync(d.hbuf, d.ybuf, (size_t)staged * sizeof(float), cudaMemcpyDeviceToHost, d.stream));
     int rc = read_error_async(d, d.stream);
     if (rc) return rc;
     CUDA_TRY(cudaStreamSynchronize(d.stream));
@@ -691,6 +735,10 @@ int linear_host(const sg_weight_t* ws, int n_w, const float* const* xs, float* c
       const Shard& s = ws[i]->shards[di];
       const int64_t r0 = tp == SG_TP_COLUMN ? s.row0 : 0;
       const int64_t nr = ld[di][i];
+      if (opitch[i]) {
+        off += (int64_t)batch * nr;
+        continue;
+      }
       for (int b = 0; b < batch; ++b) {
         float* dst = outs[(size_t)i * batch + b] + r0;
         const float* src = d.hbuf + off + (size_t)b * nr;
@@ -1193,6 +1241,23 @@ int sg_allreduce_path(int* peer) {
   if (!g_ctx.inited) return fail(SG_ERR_NOT_INITIALIZED, "sg_init not called");
   if (!peer) return fail(SG_ERR_INVALID_ARG, "null pointer");
   *peer = g_ctx.devs.size() == 1 && g_ctx.devs[0].peer_on ? 1 : 0;
+  return SG_OK;
+}
+
+int sg_host_alloc(size_t bytes, void** out) {
+  if (!out) return fail(SG_ERR_INVALID_ARG, "null pointer");
+  *out = nullptr;
+  if (bytes == 0) return SG_OK;
+  if (cudaHostAlloc(out, bytes, cudaHostAllocPortable) != cudaSuccess) {
+    cudaGetLastError();
+    *out = nullptr;
+    return fail(SG_ERR_OOM, "cudaHostAlloc(%zu) failed", bytes);
+  }
+  return SG_OK;
+}
+
+int sg_host_free(void* p) {
+  if (p) CUDA_TRY(cudaFreeHost(p));
   return SG_OK;
 }
 

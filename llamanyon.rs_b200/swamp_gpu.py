@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import weakref
 from dataclasses import dataclass
 from typing import Sequence
 
@@ -44,6 +45,7 @@ EXPORTS = (
     "sg_rmsnorm_device", "sg_rope_kv_device", "sg_attention_device", "sg_rope_attention_device", "sg_attention_prefill_device", "sg_silu_mul_device", "sg_add_device",
     "sg_rmsnorm_linear_multi_device", "sg_silu_mul_linear_device",
     "sg_argmax_device", "sg_embed_device", "sg_allreduce_device", "sg_allreduce_path",
+    "sg_host_alloc", "sg_host_free",
 )
 SG_ERR_FORMAT, SG_ERR_NOT_FOUND = -8, -9
 
@@ -113,6 +115,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     L.sg_embed_device.argtypes = [P, P, i32, P, i64, P]
     L.sg_allreduce_device.argtypes = [P, i64, P]
     L.sg_allreduce_path.argtypes = [P]
+    L.sg_host_alloc.argtypes = [ctypes.c_size_t, P]
+    L.sg_host_free.argtypes = [P]
     for name in EXPORTS:
         getattr(L, name).restype = ctypes.c_char_p if name == "sg_last_error" else ctypes.c_int
     return L
@@ -210,33 +214,73 @@ class SwampGpu:
         return Weight(self, h.value, dtype, n_rows, n_cols, tp_mode)
 
     # --------------------------------------------------------- compute
-    def linear(self, w: Weight, xs: np.ndarray, accumulate_into: np.ndarray | None = None) -> np.ndarray:
-        """outs[b] = W xs[b] (host arrays); xs is (K,) or (B, K)."""
-        xs = np.ascontiguousarray(xs, dtype=np.float32)
+    def host_array(self, shape, dtype=np.float32) -> np.ndarray:
+        """A numpy array in page-locked host memory (sg_host_alloc), freed with
+        its last view. xs and outs of linear / linear_multi held in such arrays
+        are copied by DMA without the library's staging copy."""
+        dt = np.dtype(dtype)
+        n = int(np.prod(shape)) * dt.itemsize
+        p = ctypes.c_void_p()
+        self._check(self.L.sg_host_alloc(max(n, 1), ctypes.byref(p)))
+        buf = (ctypes.c_ubyte * max(n, 1)).from_address(p.value)
+        weakref.finalize(buf, self.L.sg_host_free, p.value)
+        return np.frombuffer(buf, dtype=np.uint8, count=n).view(dt).reshape(shape)
+
+    @staticmethod
+    def _rows(a: np.ndarray, n: int):
+        """Row pointers of a 2D float32 array whose rows are contiguous."""
+        base, step = a.ctypes.data, a.strides[0]
+        return (ctypes.c_void_p * n)(*[base + b * step for b in range(n)])
+
+    @staticmethod
+    def _out_rows(out: np.ndarray, shape) -> np.ndarray:
+        if out.dtype != np.float32 or out.shape != shape or (out.ndim and out.strides[-1] != 4):
+            raise SwampGpuError(-1, f"out must be float32 {shape} with contiguous rows")
+        return out
+
+    def linear(self, w: Weight, xs: np.ndarray, accumulate_into: np.ndarray | None = None,
+               out: np.ndarray | None = None) -> np.ndarray:
+        """outs[b] = W xs[b] (host arrays); xs is (K,) or (B, K), its rows may be
+        strided (a column slice of a wider array). The result goes to `out`
+        when given (float32, the shape of the result, contiguous rows; a
+        column-split rank writes only its rows of it), else to a new array."""
+        xs = np.asarray(xs, dtype=np.float32)
         single = xs.ndim == 1
         if single:
             xs = xs[None]
+        if xs.ndim != 2 or xs.strides[1] != 4:
+            xs = np.ascontiguousarray(xs)
         B = xs.shape[0]
         if xs.shape[1] < w.n_cols:
             raise SwampGpuError(-1, "forward_linear shape mismatch")  # linear.rs:23
         if accumulate_into is not None:
             outs = np.ascontiguousarray(accumulate_into, dtype=np.float32).reshape(B, w.n_rows)
             flags = SG_FLAG_ACCUMULATE
+        elif out is not None:
+            outs = self._out_rows(out, (w.n_rows,) if single else (B, w.n_rows))
+            if single:
+                outs = outs[None]
+            flags = 0
         else:
             outs = np.zeros((B, w.n_rows), np.float32)
             flags = 0
-        xp = (ctypes.c_void_p * B)(*[xs[b].ctypes.data for b in range(B)])
-        op = (ctypes.c_void_p * B)(*[outs[b].ctypes.data for b in range(B)])
-        self._check(self.L.sg_linear(w.handle, xp, op, B, flags))
+        self._check(self.L.sg_linear(w.handle, self._rows(xs, B), self._rows(outs, B), B, flags))
         return outs[0] if single else outs
 
-    def linear_multi(self, ws: Sequence[Weight], x: np.ndarray) -> list:
+    def linear_multi(self, ws: Sequence[Weight], x: np.ndarray, outs: Sequence[np.ndarray] | None = None) -> list:
+        """outs[i] = W_i x for one vector x; `outs` (float32 (n_rows_i,)
+        arrays) receive the results when given."""
         x = np.ascontiguousarray(x, dtype=np.float32)
-        outs = [np.zeros(w.n_rows, np.float32) for w in ws]
+        if outs is None:
+            outs = [np.zeros(w.n_rows, np.float32) for w in ws]
+        else:
+            outs = [self._out_rows(o, (w.n_rows,)) for o, w in zip(outs, ws)]
+            if len(outs) != len(ws):
+                raise SwampGpuError(-1, "one output per tensor")
         hp = (ctypes.c_void_p * len(ws))(*[w.handle for w in ws])
         op = (ctypes.c_void_p * len(ws))(*[o.ctypes.data for o in outs])
         self._check(self.L.sg_linear_multi(hp, len(ws), x.ctypes.data, op, 0))
-        return outs
+        return list(outs)
 
     def linear_device(self, w: Weight, x_ptr: int, ldx: int, y_ptr: int, ldy: int, batch: int,
                       stream: int = 0, flags: int = 0):

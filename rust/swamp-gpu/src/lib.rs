@@ -205,6 +205,40 @@ pub fn tp_shard(dtype: c_int, n_rows: usize, n_cols: usize, tp: c_int, world: us
     Ok((r0, r, c0, c))
 }
 
+/// f32 host memory from sg_host_alloc (page-locked): `linear` / `linear_multi`
+/// copy rows held here by DMA without the library's staging copy.
+pub struct PinnedBuf {
+    ptr: *mut f32,
+    len: usize,
+}
+
+impl PinnedBuf {
+    pub fn new(len: usize) -> Result<Self> {
+        let lib = try_lib()?;
+        let f = sym!(lib, "sg_host_alloc", unsafe extern "C" fn(usize, *mut *mut c_void) -> c_int);
+        let mut p: *mut c_void = std::ptr::null_mut();
+        check(lib, unsafe { f(len.max(1) * std::mem::size_of::<f32>(), &mut p) })?;
+        unsafe { std::ptr::write_bytes(p as *mut f32, 0, len) };
+        Ok(PinnedBuf { ptr: p as *mut f32, len })
+    }
+    pub fn as_slice(&self) -> &[f32] {
+        unsafe { std::slice::from_raw_parts(self.ptr, self.len) }
+    }
+    pub fn as_mut_slice(&mut self) -> &mut [f32] {
+        unsafe { std::slice::from_raw_parts_mut(self.ptr, self.len) }
+    }
+}
+
+impl Drop for PinnedBuf {
+    fn drop(&mut self) {
+        if let Ok(lib) = try_lib() {
+            if let Ok(f) = unsafe { lib.get::<unsafe extern "C" fn(*mut c_void) -> c_int>(b"sg_host_free\0") } {
+                unsafe { f(self.ptr as *mut c_void) };
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------- compute
 
 /// forward_linear / forward_linear_batch on host buffers: outs[b] = W xs[b]
