@@ -2,8 +2,9 @@
 
 One process per GPU (sg_init_rank, as bench.py under torchrun uses it):
 column-split (Q/K/V/gate/up style) and row-split (O/down style) linears at
-decode and prefill batch sizes, through the device and the host-pointer
-entry points, against the CPU oracle; row split with SG_FLAG_ACCUMULATE on
+decode and prefill batch sizes, through the device entry points (and the
+one with no device allocation) and the host-pointer ones (ordinary and
+page-locked host rows), against the CPU oracle; row split with SG_FLAG_ACCUMULATE on
 a replicated y (the residual stream). Then the tensor-parallel decoder
 (llamanyon.rs_b200/decoder.py, stacked=False) against the oracle's engine
 loop, and one configs[4]-width layer (d 8192, FFN 28672, Q4_0).
@@ -111,6 +112,15 @@ def _linears(g, sg, oracle, torch, rank, world, out):
                   l2[:, r0:r0 + rows])
             yh = g.linear(W, x)  # host pointers: this rank's rows of the whole output
             _gate(out, f"column dt{dtype} b{b} host", yh[:, r0:r0 + rows], ref[:, r0:r0 + rows], l2[:, r0:r0 + rows])
+            # page-locked rows: x and this rank's rows of out move by DMA
+            xp = g.host_array((b, k))
+            xp[:] = x
+            yp = g.host_array((b, nr))
+            yp[:] = np.nan
+            g.linear(W, xp, out=yp)
+            assert np.isnan(yp[:, :r0]).all() and np.isnan(yp[:, r0 + rows:]).all()
+            _gate(out, f"column dt{dtype} b{b} pinned", yp[:, r0:r0 + rows], ref[:, r0:r0 + rows],
+                  l2[:, r0:r0 + rows])
             W.free()
             # row split: this rank's K slice, all-reduced outputs
             W = g.register(w, dtype, nr, k, sg.SG_TP_ROW)
@@ -140,6 +150,9 @@ def _linears(g, sg, oracle, torch, rank, world, out):
             _gate(out, f"row+acc dt{dtype} b{b} device", yd.cpu().numpy() - y0, ref, l2)
             yh = g.linear(W, x)
             _gate(out, f"row dt{dtype} b{b} host", yh, ref, l2)
+            yp[:] = np.nan
+            g.linear(W, xp, out=yp)
+            _gate(out, f"row dt{dtype} b{b} pinned", yp, ref, l2)
             W.free()
 
 
@@ -209,7 +222,9 @@ def test_tp_linears_two_ranks(tmp_path, path):
     for o in outs:
         assert o["path"] == path
         names = [c[0] for c in o["checks"]]
-        assert len(names) == 2 * 3 * 5 + 2 * 2  # + the no-allocation entry point at batch 1 and 16
+        # 5 checks per (dtype, batch), 2 with page-locked host rows, the
+        # no-allocation entry point at batch 1 and 16
+        assert len(names) == 2 * 3 * 7 + 2 * 2
         assert max(c[1] for c in o["checks"]) <= 1e-3
 
 
