@@ -86,3 +86,21 @@ def reference_outputs(orc, dtype, w, x, n_rows, n_cols):
     ref = orc.reference_linear(dtype, w, x, n_rows, n_cols)
     l2 = np.stack([orc.gemv_f64(dtype, w, x[b], n_rows, n_cols)[2] for b in range(x.shape[0])])
     return ref, l2
+
+
+def reference_outputs_batch(orc, dtype, w, x, n_rows, n_cols):
+    """reference_outputs for whole full-size tensors, in seconds: ref is the
+    engine's batched route (forward_linear_batch, linear.rs:176-239) on all
+    host threads -- for Q4_0 the same dequantized-row dots as the per-token
+    route, bit for bit; for Q4_K fused_gemv_q4k_batched's scalar order
+    (fused_gemv_q4k.rs:650-698), the kernel the reference runs at prefill --
+    and ||w.*x||_2 comes from the dequantized rows in f64 with numpy."""
+    x = np.atleast_2d(np.asarray(x, np.float32))
+    ref = orc.forward_linear_batch(dtype, w, x, n_rows, n_cols, os.cpu_count() or 1)
+    W = orc.dequantize(dtype, w, n_rows * n_cols).reshape(n_rows, n_cols)
+    x2 = x.astype(np.float64) ** 2
+    l2 = np.empty((x.shape[0], n_rows))
+    for r0 in range(0, n_rows, 2048):
+        wc = W[r0:r0 + 2048].astype(np.float64)
+        l2[:, r0:r0 + 2048] = np.sqrt(x2 @ (wc * wc).T)
+    return ref, l2

@@ -131,6 +131,24 @@ def test_forward_linear_batch_matches_batched_kernel(oracle):
     assert np.all(np.abs(got - single) < 1e-3 * (np.abs(single) + 1))
 
 
+def test_reference_outputs_batch_matches_per_token(oracle):
+    """The full-size parity tests' fast reference (batched route on all host
+    threads, ||w.*x||_2 from numpy) against the per-token one: Q4_0 bit for
+    bit, Q4_K within rounding of the other summation order; the l2 norms
+    agree to f64 rounding."""
+    from conftest import reference_outputs, reference_outputs_batch
+    for dtype, n, k, B in ((oracle.DTYPE_Q4_0, 2100, 352, 3), (oracle.DTYPE_Q4_K, 2050, 512, 4)):
+        w = oracle.gen_weight(dtype, 13, 3, n, k)
+        xs = oracle.gen_x(13, 5, (B, k))
+        ref, l2 = reference_outputs(oracle, dtype, w, xs, n, k)
+        ref_b, l2_b = reference_outputs_batch(oracle, dtype, w, xs, n, k)
+        if dtype == oracle.DTYPE_Q4_0:
+            assert np.array_equal(ref_b, ref)
+        else:
+            assert np.all(np.abs(ref_b - ref) <= 1e-5 * np.maximum(np.abs(ref), l2))
+        assert np.allclose(l2_b, l2, rtol=1e-12, atol=0)
+
+
 def test_generator_distributions(oracle):
     w = oracle.gen_weight(oracle.DTYPE_Q4_0, 5, 1, 64, 4096)
     blocks = w.reshape(-1, 18)
