@@ -47,6 +47,16 @@ def wbytes(k, n):
     return n * k * 18 // 32
 
 
+def decode_config(world):
+    """The configs[1] workload both arms report (the reference arm times a
+    bounded sample of it): N layers at N GPUs, TP N."""
+    return {"workload": "configs[1]: Llama-2-7B layer Q4_0 linears (4x 4096->4096, 2x 4096->11008, "
+                        "11008->4096) at decode batch 1, 4, 16",
+            "batches": list(BATCHES), "layers_per_step": world, "parallelism": f"tp{world}" if world > 1 else "none",
+            "l2_policy": "inputs larger than L2: rotating copies of the layer weights, over 4.5x L2 per GPU",
+            "bytes_per_step": step_bytes(world)}
+
+
 def step_bytes(n_layers=1):
     """algorithmic bytes of one step (114,148,352 / 115,085,312 / 118,833,152
     per layer at batch 1/4/16)."""
@@ -153,28 +163,60 @@ def prefill_flops():
 # reference arm / CPU baseline
 # ---------------------------------------------------------------------------
 
-def cpu_sample(threads, seconds_budget=20.0, max_calls=None):
-    """The reference CPU path on the layer at batch 1 (one token), repeated
-    while inside the time budget. Returns (GB/s, calls, seconds, sample)."""
+def ref_layer(oracle):
+    """The configs[1] layer's 7 seeded Q4_0 tensors and the activations of
+    each batch, as the reference CPU path consumes them."""
+    ws = [(k, n, oracle.gen_weight(Q40, SEED, 500 + i, n, k)) for i, (_, k, n) in enumerate(LAYER)]
+    xb = {(b, k): oracle.gen_x(SEED, 900 + 16 * b + k, (b, k)) for b in BATCHES for _, k, _ in LAYER}
+    return ws, xb
+
+
+def ref_step(oracle, sl, xb, threads):
+    """One configs[1] step through the routes the reference takes: batch 1
+    forward_linear's Q4_0 route (whole-slice dequant + f32 row dots,
+    linear.rs:68-87); batches 4 and 16 forward_linear_batch, which sends a
+    Q4_0 tensor to fallback_gemv (linear.rs:233-236,336-364): tokens over
+    threads, each a dispatched fused_gemv_q4k over the tensor (timed as it
+    runs; it does not decode Q4_0). sl: (K, rows, blocks) per tensor."""
+    simd = oracle.simd_path() != "none"
+    for b in BATCHES:
+        for k, r, w in sl:
+            if b == 1 or not simd:
+                for t in range(b):
+                    oracle.forward_linear(Q40, w, xb[(b, k)][t], r, k, threads)
+            else:
+                oracle.fallback_gemv_dispatched(w, xb[(b, k)], r, k, threads)
+
+
+def ref_route(oracle):
+    if oracle.simd_path() == "none":
+        return "batches 4 and 16 as per-token forward_linear calls (no SIMD path on this CPU)"
+    return (f"batches 4 and 16 through forward_linear_batch -> fallback_gemv with the dispatched "
+            f"{oracle.simd_path()} fused_gemv_q4k (the reference's batched Q4_0 route, linear.rs:233-236,336-364; "
+            f"numerically divergent, timed as it runs)")
+
+
+def cpu_sample(threads, seconds_budget=20.0):
+    """The reference CPU path on the whole configs[1] step (batches 1, 4, 16),
+    repeated while inside the time budget. Returns (GB/s, steps, seconds,
+    sample)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
-    import numpy as np
     oracle.build()
-    ws = [(k, n, oracle.gen_weight(Q40, SEED, 500 + i, n, k)) for i, (_, k, n) in enumerate(LAYER)]
-    x = {k: oracle.gen_x(SEED, 900 + k, (k,)) for _, k, _ in LAYER}
-    # one warm call (page-in)
-    oracle.forward_linear(Q40, ws[0][2], x[ws[0][0]], ws[0][1], ws[0][0], threads)
+    ws, xb = ref_layer(oracle)
+    ref_step(oracle, ws, xb, threads)  # warm (page-in)
     t0 = time.perf_counter()
-    calls, nbytes = 0, 0
+    steps = 0
     while True:
-        for k, n, w in ws:
-            oracle.forward_linear(Q40, w, x[k], n, k, threads)
-            calls += 1
-            nbytes += wbytes(k, n) + (k + n) * 4
+        ref_step(oracle, ws, xb, threads)
+        steps += 1
         el = time.perf_counter() - t0
-        if el > seconds_budget or (max_calls and calls >= max_calls):
+        if el > seconds_budget:
             break
-    return nbytes / el / 1e9, calls, el
+    sample = (f"{steps} whole configs[1] steps (7 Q4_0 tensors at batch 1, 4, 16) in {el:.1f} s: batch 1 "
+              f"through forward_linear's Q4_0 route (full-tensor dequant + f32 row dots, "
+              f"swamp-engine/src/linear.rs:68-87), {ref_route(oracle)}; {threads} host threads")
+    return step_bytes(1) * steps / el / 1e9, steps, el, sample
 
 
 def cpu_prefill_sample(threads, seconds_budget=8.0):
@@ -254,10 +296,11 @@ def cpu_q4k_decode_variants(threads, seconds_each=3.0):
 def reference_arm(args):
     """The reference's CPU route on the host cores, same metric and config.
 
-    Each step runs the layer's 7 tensors through forward_linear at batch 1
-    (one token, the engine's decode call) on a row slice sized so that the
-    whole --steps/--warmup run stays within about two minutes; GB/s counts the
-    sliced bytes. Rank 0 only."""
+    Each step is a bounded sample of the configs[1] step: the layer's 7 Q4_0
+    tensors, cut to their first rows, at batch 1, 4 and 16 through the
+    routes the reference takes (ref_step). The row cut keeps the whole
+    --steps/--warmup run within about two minutes; GB/s counts the sampled
+    bytes. Rank 0 only."""
     rank = env_int("RANK", 0)
     if rank != 0:
         return 0
@@ -265,42 +308,37 @@ def reference_arm(args):
     import oracle
     oracle.build()
     threads = os.cpu_count() or 1
-    ws = [(k, n, oracle.gen_weight(Q40, SEED, 500 + i, n, k)) for i, (_, k, n) in enumerate(LAYER)]
-    x = {k: oracle.gen_x(SEED, 900 + k, (k,)) for _, k, _ in LAYER}
+    world = env_int("WORLD_SIZE", 1)
+    ws, xb = ref_layer(oracle)
     t0 = time.perf_counter()
-    for k, n, w in ws:  # calibration pass (also pages the weights in)
-        oracle.forward_linear(Q40, w, x[k], n, k, threads)
-    t_layer = time.perf_counter() - t0
+    ref_step(oracle, ws, xb, threads)  # calibration pass (also pages the weights in)
+    t_full = time.perf_counter() - t0
     budget = 120.0 / max(1, args.steps + args.warmup)
-    frac = min(1.0, budget / t_layer)
+    frac = min(1.0, budget / t_full)
     sl = []
     for k, n, w in ws:
-        rows = max(128, int(n * frac) // 128 * 128)
-        rb = oracle.row_bytes(Q40, k)
-        sl.append((k, rows, w[: rows * rb]))
-    step_b = sum(wbytes(k, r) + (k + r) * 4 for k, r, _ in sl)
+        rows = min(n, max(128, int(n * frac) // 128 * 128))
+        sl.append((k, rows, w[: rows * oracle.row_bytes(Q40, k)]))
+    step_b = sum(wbytes(k, r) + b * (k + r) * 4 for b in BATCHES for k, r, _ in sl)
     for _ in range(args.warmup):
-        for k, r, w in sl:
-            oracle.forward_linear(Q40, w, x[k], r, k, threads)
+        ref_step(oracle, sl, xb, threads)
     per_step = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        for k, r, w in sl:
-            oracle.forward_linear(Q40, w, x[k], r, k, threads)
+        ref_step(oracle, sl, xb, threads)
         per_step.append(time.perf_counter() - t0)
     tot = sum(per_step)
     value = step_b * len(per_step) / tot / 1e9
     sample = (f"per step: the layer's 7 Q4_0 tensors, first {sl[0][1]}/{LAYER[0][2]} .. rows "
-              f"({100 * frac:.1f}% of each), batch 1, through forward_linear's Q4_0 route "
-              f"(full-slice dequant + f32 row dots, swamp-engine/src/linear.rs:68-87) on {threads} threads")
+              f"({100 * frac:.1f}% of each), batch 1 through forward_linear's Q4_0 route (full-slice dequant + "
+              f"f32 row dots, swamp-engine/src/linear.rs:68-87), {ref_route(oracle)}; {threads} host threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * tot / len(per_step), 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "configs[1]: Llama-2-7B layer Q4_0 linears at decode (CPU sample: batch 1)",
-                   "host_threads": threads, "bytes_per_step": step_b},
+        "config": decode_config(world),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "sampled_bytes_per_step": step_b},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -544,10 +582,8 @@ def gpu_arm(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        gbs, ncalls, el = cpu_sample(threads, seconds_budget=args.cpu_seconds)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{ncalls} forward_linear calls (Q4_0 engine route, batch 1) over the layer's 7 "
-                         f"tensors in {el:.1f} s on {threads} host threads",
+        gbs, _, _, sample = cpu_sample(threads, seconds_budget=args.cpu_seconds)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample,
                "variants": cpu_q4k_decode_variants(threads)}
 
     if rank == 0:
@@ -557,14 +593,11 @@ def gpu_arm(args):
             "scaling": "weak", "vs_baseline": None,
             "dtype": "u4 weights x s8 activation digits (3 per value), s32 tensor-core accumulate, f32 epilogue",
             "data": "synthetic (seeded random-init Q4_0 blocks, N(0,1) activations)",
-            "config": {"workload": "configs[1]: Llama-2-7B layer Q4_0 linears (4x 4096->4096, 2x 4096->11008, "
-                                   "11008->4096) at decode batch 1, 4, 16",
-                       "layers_per_step": n_layers, "parallelism": f"tp{world}" if world > 1 else "none",
-                       "allreduce": gpu.allreduce_path() if world > 1 else None,
-                       "execution": "eager" if args.eager else "CUDA graph per step (PDL edges kept)",
-                       "l2_policy": f"inputs larger than L2: {copies} rotating layer copies "
-                                    f"({copies * layer_b / world / 1e6:.0f} MB per GPU vs L2 {l2 / 1e6:.0f} MB)",
-                       "bytes_per_step": step_bytes(n_layers)},
+            "config": decode_config(world),
+            "run": {"allreduce": gpu.allreduce_path() if world > 1 else None,
+                    "execution": "eager" if args.eager else "CUDA graph per step (PDL edges kept)",
+                    "l2": f"{copies} rotating layer copies ({copies * layer_b / world / 1e6:.0f} MB per GPU vs L2 "
+                          f"{l2 / 1e6:.0f} MB)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC["gemv_4096x11008_b1"],
                          "traffic_launch": "4096x11008 batch 1 (algorithmic 25,406,976 B)", "peak_kind": peak_kind,
@@ -581,13 +614,20 @@ def gpu_arm(args):
             "model_decode": decode,
             "tp_model": tp_model,
         }
-        if decode and cpu:
-            # the CPU engine streams the same weight bytes per token at the
-            # GEMV route's measured rate (a full 32-layer CPU run would take
-            # minutes per token)
-            for key, run in decode["runs"].items():
-                run["cpu_extrapolated_tok_s"] = round(
-                    int(key[1:]) * cpu["value"] * 1e9 / decode["weight_bytes_per_step"], 4)
+        if decode and cpu and cpu.get("variants"):
+            # the CPU engine runs every token of a step through the Q4_K decode
+            # kernel it dispatches (the batched VNNI route loops that kernel
+            # over the tokens), so one token costs the model's weight bytes at
+            # that kernel's measured rate on all host threads (a full 32-layer
+            # CPU run would take minutes per token)
+            by = {(v["variant"], v["cores"]): v["value"] for v in cpu["variants"]}
+            rate = by.get(("q4_k as-dispatched", cpu["cores"]),
+                          by.get(("q4_k scalar", cpu["cores"])))
+            if rate:
+                for run in decode["runs"].values():
+                    run["cpu_extrapolated_tok_s"] = round(rate * 1e9 / decode["weight_bytes_per_step"], 4)
+                decode["cpu_extrapolation"] = (f"one token = the model's weight bytes at the host's Q4_K decode "
+                                               f"rate ({rate} GB/s, {cpu['cores']} threads)")
         print(json.dumps(line), flush=True)
     graphs = None
     torch.cuda.synchronize()

@@ -106,6 +106,10 @@ int orc_gemv_q4k_vnni(const uint8_t *w, const float *x, float *out, int64_t n_ro
 int orc_gemv_q4k_avx2(const uint8_t *w, const float *x, float *out, int64_t n_rows, int64_t n_cols);
 int orc_forward_linear_dispatched(const uint8_t *w, const float *x, float *out, int64_t n_rows,
                                   int64_t n_cols, int n_threads);
+/* forward_linear_batch's non-Q4_K route, fallback_gemv (linear.rs:336-364),
+ * over the dispatched kernel: returns the path used, or < 0. */
+int orc_fallback_gemv_dispatched(const uint8_t *w, const float *const *xs, float *const *outs, int64_t batch,
+                                 int64_t n_rows, int64_t n_cols, int n_threads);
 
 /* The reference's test block packer, fused_gemv_q4k.rs:708-724 (inverse of
  * unpack_scales). d and dmin go through f16 round-to-nearest-even. */

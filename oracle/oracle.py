@@ -88,6 +88,8 @@ def lib() -> ctypes.CDLL:
     L.orc_gemv_q4k_avx2.restype = ctypes.c_int
     L.orc_forward_linear_dispatched.argtypes = [P, P, P, i64, i64, ctypes.c_int]
     L.orc_forward_linear_dispatched.restype = ctypes.c_int
+    L.orc_fallback_gemv_dispatched.argtypes = [P, P, P, i64, i64, i64, ctypes.c_int]
+    L.orc_fallback_gemv_dispatched.restype = ctypes.c_int
     _lib = L
     return L
 
@@ -226,6 +228,25 @@ def forward_linear_dispatched(w, x, n_rows, n_cols, n_threads):
     if rc < 1:
         raise RuntimeError("no SIMD path on this CPU")
     return out, SIMD_PATHS[rc]
+
+
+def fallback_gemv_dispatched(w, xs: np.ndarray, n_rows, n_cols, n_threads):
+    """forward_linear_batch's route for tensors that are not Q4_K
+    (linear.rs:233-236 -> fallback_gemv, :336-364) as the reference runs it
+    on this CPU: tokens over n_threads threads, each a whole-tensor
+    dispatched fused_gemv_q4k. For Q4_0 bytes that is the reference's
+    batched Q4_0 route. TIMING ONLY (the Q4_K kernel does not decode Q4_0).
+    Returns (outs, path)."""
+    xs = np.ascontiguousarray(xs, np.float32)
+    B = xs.shape[0]
+    outs = np.empty((B, n_rows), np.float32)
+    xp = (ctypes.c_void_p * B)(*[xs[t].ctypes.data for t in range(B)])
+    op = (ctypes.c_void_p * B)(*[outs[t].ctypes.data for t in range(B)])
+    rc = lib().orc_fallback_gemv_dispatched(_p(w), ctypes.addressof(xp), ctypes.addressof(op), B, n_rows,
+                                            n_cols, n_threads)
+    if rc < 1:
+        raise RuntimeError("no SIMD path on this CPU" if rc == -1 else f"orc_fallback_gemv_dispatched rc={rc}")
+    return outs, SIMD_PATHS[rc]
 
 
 def forward_linear_batch(dtype, w, xs: np.ndarray, n_rows, n_cols, n_threads) -> np.ndarray:

@@ -22,8 +22,17 @@
  *    (swamp-engine/src/linear.rs:31-45) over the dispatcher of
  *    fused_gemv_q4k (:59-82): VNNI where the CPU has it, else AVX2. out is
  *    zeroed first (the VNNI path accumulates).
+ *  - orc_fallback_gemv_dispatched: forward_linear_batch for a tensor that
+ *    is not Q4_K (swamp-engine/src/linear.rs:233-236), i.e. fallback_gemv
+ *    (:336-364): tokens split over threads in runs of ceil(batch/threads),
+ *    each token a whole-tensor fused_gemv_q4k on one thread into a zeroed
+ *    row buffer that is then copied to its output. For a Q4_0 tensor this
+ *    runs the Q4_K kernel over Q4_0 bytes (both are 0.5625 B per weight,
+ *    so the kernel's length check passes): the reference's batched Q4_0
+ *    route, timed here as it runs.
  */
 #include <immintrin.h>
+#include <stdlib.h>
 #include <pthread.h>
 #include <stdint.h>
 #include <string.h>
@@ -216,4 +225,56 @@ int orc_forward_linear_dispatched(const uint8_t *w, const float *x, float *out, 
     if (th[t]) pthread_join(th[t], NULL);
   (void)started;
   return path;
+}
+
+struct fallback_job {
+  const uint8_t *w;
+  const float *const *xs;
+  float *const *outs;
+  int64_t b0, b1, n_rows, n_blocks;
+  int path, rc;
+};
+
+static void *fallback_worker(void *arg) {
+  struct fallback_job *j = (struct fallback_job *)arg;
+  if (j->b1 <= j->b0) return NULL;
+  float *lo = (float *)malloc((size_t)j->n_rows * sizeof(float));
+  if (!lo) {
+    j->rc = -3;
+    return NULL;
+  }
+  for (int64_t b = j->b0; b < j->b1; ++b) {
+    memset(lo, 0, (size_t)j->n_rows * sizeof(float));
+    if (j->path == 2)
+      gemv_q4k_vnni(j->w, j->xs[b], lo, j->n_rows, j->n_blocks);
+    else
+      gemv_q4k_avx2(j->w, j->xs[b], lo, j->n_rows, j->n_blocks);
+    memcpy(j->outs[b], lo, (size_t)j->n_rows * sizeof(float));
+  }
+  free(lo);
+  return NULL;
+}
+
+int orc_fallback_gemv_dispatched(const uint8_t *w, const float *const *xs, float *const *outs, int64_t batch,
+                                 int64_t n_rows, int64_t n_cols, int n_threads) {
+  const int path = orc_simd_path();
+  if (n_cols % Q4K_BS || path < 1 || n_threads < 1 || n_threads > 1024 || batch < 0) return -1;
+  if (batch == 0) return path;
+  const int64_t cs = (batch + n_threads - 1) / n_threads;  // linear.rs:340
+  pthread_t th[1024];
+  struct fallback_job jobs[1024];
+  for (int t = 0; t < n_threads; ++t) {
+    const int64_t b0 = t * cs, b1 = b0 + cs < batch ? b0 + cs : batch;
+    jobs[t] = (struct fallback_job){w, xs, outs, b0, b1, n_rows, n_cols / Q4K_BS, path, 0};
+    if (b1 <= b0 || pthread_create(&th[t], NULL, fallback_worker, &jobs[t]) != 0) {
+      fallback_worker(&jobs[t]);
+      th[t] = 0;
+    }
+  }
+  int rc = path;
+  for (int t = 0; t < n_threads; ++t) {
+    if (th[t]) pthread_join(th[t], NULL);
+    if (jobs[t].rc) rc = jobs[t].rc;
+  }
+  return rc;
 }

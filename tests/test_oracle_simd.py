@@ -104,3 +104,21 @@ def test_dispatched_row_partition(oracle, case, threads):
     got, path = oracle.forward_linear_dispatched(w, x, n, k, threads)
     want = oracle.gemv_q4k_simd(path, w, x, n, k)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("threads", [1, 3, 8])
+@pytest.mark.parametrize("batch", [1, 4, 5])
+def test_fallback_gemv_token_split(oracle, threads, batch):
+    """forward_linear_batch's non-Q4_K route (fallback_gemv, linear.rs:336-364)
+    over Q4_0 bytes: tokens split over threads, each token the whole-tensor
+    dispatched kernel, so every output row equals that kernel's single call on
+    the same bytes."""
+    if oracle.simd_path() == "none":
+        pytest.skip("no SIMD path")
+    n, k = 37, 512
+    w = oracle.gen_weight(2, SEED, 40, n, k)  # Q4_0: 18 B per 32, read as 144 B per 256
+    xs = oracle.gen_x(SEED, 41, (batch, k))
+    outs, path = oracle.fallback_gemv_dispatched(w, xs, n, k, threads)
+    for b in range(batch):
+        # Q4_0 bytes read as Q4_K scales can decode to inf / NaN: NaN matches NaN
+        assert np.array_equal(outs[b], oracle.gemv_q4k_simd(path, w, xs[b], n, k), equal_nan=True)
