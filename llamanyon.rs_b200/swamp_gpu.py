@@ -274,9 +274,9 @@ class SwampGpu:
         if outs is None:
             outs = [np.zeros(w.n_rows, np.float32) for w in ws]
         else:
-            outs = [self._out_rows(o, (w.n_rows,)) for o, w in zip(outs, ws)]
             if len(outs) != len(ws):
                 raise SwampGpuError(-1, "one output per tensor")
+            outs = [self._out_rows(o, (w.n_rows,)) for o, w in zip(outs, ws)]
         hp = (ctypes.c_void_p * len(ws))(*[w.handle for w in ws])
         op = (ctypes.c_void_p * len(ws))(*[o.ctypes.data for o in outs])
         self._check(self.L.sg_linear_multi(hp, len(ws), x.ctypes.data, op, 0))
