@@ -72,3 +72,32 @@ def test_no_cpu_fallback_without_gpu(lib):
     assert rc != 0
     msg = lib.sg_last_error().decode()
     assert "CPU fallback" in msg or "CUDA" in msg or "device" in msg
+
+
+def test_host_alloc_argument_checks(lib):
+    """sg_host_alloc: a null out pointer is rejected, zero bytes give NULL
+    with no CUDA call, and freeing NULL is a no-op."""
+    assert lib.sg_host_alloc(16, None) == -1
+    p = ctypes.c_void_p(1)
+    assert lib.sg_host_alloc(0, ctypes.byref(p)) == 0 and p.value is None
+    assert lib.sg_host_free(None) == 0
+
+
+def test_binding_checks_output_arrays_on_the_host(lib):
+    """linear / linear_multi reject an output array of the wrong shape,
+    dtype or row layout (and a wrong count) before calling the library."""
+    import numpy as np
+    import swamp_gpu as sg
+    g = sg.SwampGpu()
+    W = sg.Weight(g, None, 12, 8, 256, 0)
+    x = np.zeros((2, 256), np.float32)
+    for bad in (np.zeros((2, 9), np.float32), np.zeros((2, 8), np.float64), np.zeros((8, 2), np.float32).T):
+        with pytest.raises(sg.SwampGpuError) as e:
+            g.linear(W, x, out=bad)
+        assert e.value.code == -1
+    with pytest.raises(sg.SwampGpuError) as e:
+        g.linear_multi([W, W], x[0], outs=[np.zeros(8, np.float32)])
+    assert e.value.code == -1
+    with pytest.raises(sg.SwampGpuError) as e:  # a valid call reaches the library, which rejects the handle
+        g.linear(W, x, out=np.zeros((2, 8), np.float32))
+    assert e.value.code in (-6, -1)  # not initialised, or (after an init in this process) a null handle
